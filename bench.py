@@ -1,0 +1,450 @@
+"""Benchmark of the B200 hot path (one JSON line on stdout from rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2] [--impl ours|reference]
+
+Workload (default): the Ming LM token loop with
+MLX-style affine 4-bit g64 weights, batch 1, a 128-token prefill, then decode
+steps feeding each step's output hidden state back as the next input. A
+"step" is one decode step of the batch (one token per sequence). Other
+configs: 1 (bf16 LM, batch 1), 3 (4-bit, batch 32, ragged prompts),
+4 (adaLN DiT head, one CFM sample of 10 Euler steps per step).
+
+value  : device-timed throughput with inputs resident in HBM (CUDA events on
+         the library's stream around exactly K steps, max over ranks).
+e2e    : the same metric through the public C ABI call a user makes
+         (ming_cuda_lm_decode with pinned host buffers: each step copies its
+         input in and reads its hidden state + stop probability back).
+--impl reference: the reference's CPU path restated (the oracle port,
+         OpenMP on the host cores) on the same workload; rank 0 only.
+
+Multi-GPU (torchrun): one independent replica per GPU (the path does not
+shard); value is the sum over replicas of tokens / the max time over ranks.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ming-tts-serve_b200"))
+
+METRIC = "LM decode tokens/s (batch 1 & 32) per B200 and at 1/2/4/8 GPUs; % HBM roofline"
+
+CONFIGS = {
+    1: dict(name="LM token loop, bf16, batch 1, 64-token prefill + 256 decode steps (BASELINE configs[0])",
+            bits=16, batch=1, prefill=64, decode=256, seed=0),
+    2: dict(name="LM token loop, MLX affine 4-bit g64, batch 1, 128-token prefill + 1024 decode steps (BASELINE configs[1])",
+            bits=4, batch=1, prefill=128, decode=1024, seed=0),
+    3: dict(name="LM batched decode, 4-bit g64, 32 sequences, prompts U[32,512], 512 decode steps, 16-token pages (BASELINE configs[2])",
+            bits=4, batch=32, prefill=None, decode=512, seed=0),
+    4: dict(name="DiT adaLN flow head, 6x768, 4x64 latent patch, 10 Euler steps, CFG, batch 1 (BASELINE configs[3])",
+            dit=True, batch=1, seed=1),
+    41: dict(name="DiT adaLN flow head, 6x768, 4x64 latent patch, 10 Euler steps, CFG, batch 32 (BASELINE configs[3])",
+             dit=True, batch=32, seed=1),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """Samples nvidia-smi during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = max(smax, float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        import torch
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    return ws, rank, local
+
+
+def dist_max(x, ws):
+    """Max of a per-rank scalar over all ranks (device time is the max over ranks)."""
+    if ws == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def aggregate_throughput(local_ms, rows_per_rank, steps, ws):
+    """Whole-job throughput of independent replicas: every rank processed
+    rows_per_rank * steps units; the job took the slowest rank's time."""
+    ms = dist_max(local_ms, ws)
+    return ws * rows_per_rank * steps / (ms / 1e3), ms
+
+
+def dist_barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def lm_workload(cfgid, local, steps, warmup):
+    import ming_b200 as M
+    from ming_b200 import synth
+    c = CONFIGS[cfgid]
+    B = c["batch"]
+    if c["prefill"] is None:  # ragged prompts U[32, 512]
+        rng = np.random.default_rng(c["seed"])
+        lens = rng.integers(32, 513, size=B).tolist()
+    else:
+        lens = [c["prefill"]] * B
+    max_ctx = ((max(lens) + warmup + steps + 2 + 255) // 256) * 256
+    pages = sum((L + warmup + steps + 2 + 15) // 16 for L in lens) + 16
+    t0 = time.time()
+    W = synth.lm_weights(seed=c["seed"], bits=c["bits"], layers=24)
+    log(f"[bench] weights generated in {time.time() - t0:.1f}s ({synth.nbytes(W) / 1e6:.1f} MB)")
+    cfg = M.default_cfg(weight_bits=c["bits"], dit_mode=M.DIT_NONE, agg_blocks=0, max_ctx=max_ctx, max_pages=pages,
+                        max_batch=max(B, 1), max_seqs=max(B, 1), max_prefill=512)
+    ctx = M.Context(cfg, device=local, weights=W)
+    seqs = []
+    last = []
+    for b, L in enumerate(lens):
+        s = ctx.seq_alloc()
+        x = synth.normal_bf16(c["seed"], f"bench.prompt.{b}", (L, 896))
+        out, _ = ctx.prefill(s, x)
+        seqs.append(s)
+        last.append(out[-1])
+    return ctx, seqs, lens, np.stack(last), W
+
+
+def algorithmic_bytes_lm(W, lens_now, B):
+    """Bytes a decode step must move: every weight once, the KV cache of
+    every sequence (K and V, all layers) once, activations negligible."""
+    w = sum(v.nbytes for k, v in W.items() if k.startswith("model.model.layers.")) + W["model.model.norm.weight"].nbytes \
+        + W["stop_head.weight"].nbytes
+    kv = sum(12288 * (L + 1) for L in lens_now)  # 24 layers x (K+V) x 2 heads x 64 x 2 B per position
+    return w, kv
+
+
+def run_ours(args, ws, rank, local):
+    import torch
+
+    import ming_b200 as M
+    cfgid = args.config
+    c = CONFIGS[cfgid]
+    torch.cuda.set_device(local)
+    if c.get("dit"):
+        return run_dit(args, ws, rank, local)
+    ctx, seqs, lens, x_last, W = lm_workload(cfgid, local, args.steps, args.warmup)
+    B = len(seqs)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=local)
+    xdev = torch.from_numpy(x_last.view(np.int16).copy()).to(f"cuda:{local}")
+    nmax = max(args.steps, args.warmup)
+    outdev = torch.empty((nmax, B, 896), dtype=torch.int16, device=f"cuda:{local}")
+    stopdev = torch.empty((nmax, B), dtype=torch.float32, device=f"cuda:{local}")
+    # warm-up (graph capture happens here)
+    ctx.generate(seqs, xdev, args.warmup, kind=M.PTR_DEVICE, out=outdev, stop=stopdev)
+    ctx.sync()
+    lens_start = [ctx.seq_len(s) for s in seqs]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local)
+    dist_barrier(ws)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    ev0.record(stream)
+    ctx.generate(seqs, xdev, args.steps, kind=M.PTR_DEVICE, out=outdev, stop=stopdev)
+    ev1.record(stream)
+    ev1.synchronize()
+    torch.cuda.synchronize()
+    dist_barrier(ws)
+    ck = clocks.stop()
+    ms_local = ev0.elapsed_time(ev1)
+    value, ms = aggregate_throughput(ms_local, B, args.steps, ws)
+    ms_step = ms / args.steps
+    # roofline of the decode step (the captured graph): algorithmic bytes / step time
+    wbytes, _ = algorithmic_bytes_lm(W, lens_start, B)
+    kv_avg = sum(12288 * (L + args.steps / 2.0 + 1) for L in lens_start)
+    step_bytes = wbytes + kv_avg
+    hbm, tf, peak_kind = load_peaks()
+    achieved = step_bytes / (ms_local / args.steps / 1e3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tp):
+        traffic = json.load(open(tp)).get(f"config{cfgid}")
+    # ---- e2e through the C ABI with pinned host buffers, one call per step ----
+    xin = torch.from_numpy(x_last.view(np.int16).copy()).pin_memory()
+    hout = torch.empty((B, 896), dtype=torch.int16).pin_memory()
+    hstop = torch.empty((B,), dtype=torch.float32).pin_memory()
+    for s, L in zip(seqs, lens_start):
+        ctx.seq_truncate(s, L)
+    ids = (M.ctypes.c_int * B)(*seqs)
+    L_ = M.lib()
+    for _ in range(min(args.warmup, 8)):
+        M._check(L_.ming_cuda_lm_decode(ctx._h, B, ids, M.ctypes.c_void_p(xin.data_ptr()), M.ctypes.c_void_p(hout.data_ptr()),
+                                        M.ctypes.c_void_p(hstop.data_ptr()), M.PTR_HOST))
+    for s, L in zip(seqs, lens_start):
+        ctx.seq_truncate(s, L)
+    dist_barrier(ws)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        M._check(L_.ming_cuda_lm_decode(ctx._h, B, ids, M.ctypes.c_void_p(xin.data_ptr()), M.ctypes.c_void_p(hout.data_ptr()),
+                                        M.ctypes.c_void_p(hstop.data_ptr()), M.PTR_HOST))
+        xin.copy_(hout)  # feed the step's output back (host side, as a caller would)
+    e2e_s = time.perf_counter() - t0
+    e2e_s = dist_max(e2e_s, ws)
+    e2e = {"value": ws * B * args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * 896 * 2,
+           "d2h_bytes_per_step": B * 896 * 2 + B * 4, "api": "ming_cuda_lm_decode (pinned host buffers)"}
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(cfgid, W, lens, x_last, args.cpu_seconds)
+    ctx.close()
+    launches_per_step = 1 + 24 * 5 + 1
+    res = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 act / " + ("u4-g64" if c["bits"] == 4 else "u8-g64" if c["bits"] == 8 else "bf16") + " weights, f32 acc",
+        "data": "synthetic (seeded random-init weights and N(0,1) embeddings, SplitMix64/Box-Muller)",
+        "config": {"workload": c["name"], "batch_per_gpu": B, "prompt_lens": lens if len(lens) <= 4 else f"U[32,512] x{len(lens)}",
+                   "kv_positions_at_start": lens_start, "parallelism": f"replicas x{ws} (no collective)",
+                   "l2": "inputs larger than L2: every step streams all weights (%.0f MB) from HBM" % (wbytes / 1e6)},
+        "roofline": {"bound": "hbm", "kernel": "decode step (captured graph: %d kernels)" % launches_per_step,
+                     "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
+                     "algorithmic_bytes_per_step": step_bytes, "traffic": traffic},
+        "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": ck, "cpu_baseline": cpu,
+    }
+    return res
+
+
+def cpu_baseline(cfgid, W, lens, x_last, budget_s=20.0):
+    """The oracle port (OpenMP, all host threads) on a bounded sample of the
+    same workload: prefill (untimed) then decode steps until ~budget_s."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from ming_b200 import synth
+    c = CONFIGS[cfgid]
+    lm = O.Lm(W)
+    B = len(lens)
+    nb = min(B, 2)  # sequences sampled on the CPU
+    caches, xs = [], []
+    for b in range(nb):
+        x = synth.normal_bf16(c["seed"], f"bench.prompt.{b}", (lens[b], 896))
+        cch = lm.new_cache(lens[b] + 4096)
+        out, _ = lm.forward(cch, x)
+        caches.append(cch)
+        xs.append(out[-1:])
+    n = 0
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < budget_s and n < 1024:
+        for b in range(nb):
+            xs[b], _ = lm.forward(caches[b], xs[b])
+        n += 1
+    dt = time.perf_counter() - t0
+    return {"value": n * nb / dt, "unit": "tokens/s", "cores": O.threads(), "kind": "port",
+            "sample": f"{n} decode steps x {nb} sequence(s) after an untimed {lens[0]}-token prefill, "
+                      f"24 layers, same weights (CPU restatement, not MLX)"}
+
+
+def run_dit(args, ws, rank, local):
+    import torch
+
+    import ming_b200 as M
+    from ming_b200 import synth
+    c = CONFIGS[args.config]
+    B = c["batch"]
+    W = synth.ada_weights(seed=c["seed"])
+    cfg = M.default_cfg(layers=0, dit_mode=M.DIT_ADALN, dit_hidden=768, dit_blocks=6, dit_heads=12, dit_ff=3072,
+                        dit_frames=4, dit_max_batch=max(B, 1), agg_blocks=0)
+    ctx = M.Context(cfg, device=local, weights=W)
+    z = synth.normal_bf16(c["seed"], "bench.dit.z", (B, 896))
+    noise = synth.normal_bf16(c["seed"], "bench.dit.noise", (B, 4, 64))
+    stream = torch.cuda.ExternalStream(ctx.stream, device=local)
+    zd = torch.from_numpy(z.view(np.int16).copy()).cuda()
+    nd = torch.from_numpy(noise.view(np.int16).copy()).cuda()
+    yd = torch.empty_like(nd)
+    L_ = M.lib()
+    P = lambda t: M.ctypes.c_void_p(t.data_ptr())
+
+    def step():
+        M._check(L_.ming_cuda_cfm_sample(ctx._h, B, P(zd), None, P(nd), None, M.ctypes.c_float(2.0), M.ctypes.c_float(0.0),
+                                         P(yd), M.PTR_DEVICE))
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local)
+    dist_barrier(ws)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    ev1.synchronize()
+    dist_barrier(ws)
+    ck = clocks.stop()
+    ms_local = ev0.elapsed_time(ev1)
+    ms = dist_max(ms_local, ws)
+    wbytes = synth.nbytes(W)
+    hbm, tf, peak_kind = load_peaks()
+    per_sample_bytes = 10 * wbytes  # weights once per Euler step
+    achieved = per_sample_bytes / (ms_local / args.steps / 1e3) / 1e9
+    hz = np.empty_like(noise)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        hz = ctx.cfm_sample(z, None, noise)
+    e2e_s = dist_max(time.perf_counter() - t0, ws)
+    ctx.close()
+    return {"metric": "DiT flow-head CFM samples/s (10 Euler steps, CFG)", "value": ws * B * args.steps / (ms / 1e3),
+            "unit": "samples/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded random init)", "config": {"workload": c["name"], "batch_per_gpu": B},
+            "roofline": {"bound": "hbm" if B < 16 else "tensor", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": None},
+            "e2e": {"value": ws * B * args.steps / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": z.nbytes + noise.nbytes,
+                    "d2h_bytes_per_step": noise.nbytes},
+            "gpu_launches": None, "clocks": ck, "cpu_baseline": None}
+
+
+def run_reference(args, ws, rank, local):
+    """The reference's CPU path restated (oracle port, all host threads)."""
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from ming_b200 import synth
+    cfgid = args.config
+    c = CONFIGS[cfgid]
+    if c.get("dit"):
+        return {"impl": "reference", "unavailable": "reference arm implemented for the LM configs only"}
+    B = c["batch"]
+    lens = [c["prefill"]] * B if c["prefill"] else np.random.default_rng(c["seed"]).integers(32, 513, size=B).tolist()
+    W = synth.lm_weights(seed=c["seed"], bits=c["bits"], layers=24)
+    lm = O.Lm(W)
+    nb = min(B, 2)
+    caches, xs = [], []
+    for b in range(nb):
+        x = synth.normal_bf16(c["seed"], f"bench.prompt.{b}", (lens[b], 896))
+        cch = lm.new_cache(lens[b] + args.warmup + args.steps + 8)
+        out, _ = lm.forward(cch, x)
+        caches.append(cch)
+        xs.append(out[-1:])
+
+    def step():
+        for b in range(nb):
+            xs[b], _ = lm.forward(caches[b], xs[b])
+
+    for _ in range(args.warmup):
+        step()
+    budget = float(os.environ.get("MING_REF_BUDGET_S", "150"))
+    n = 0
+    t0 = time.perf_counter()
+    while n < args.steps and (time.perf_counter() - t0) < budget:
+        step()
+        n += 1
+    dt = time.perf_counter() - t0
+    v = n * nb / dt
+    return {"metric": METRIC, "value": v, "unit": "tokens/s", "impl": "reference", "n_gpus": ws, "steps": n,
+            "warmup": args.warmup, "ms_per_step": dt / n * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 act / f32 acc (CPU)", "data": "synthetic",
+            "config": {"workload": c["name"], "batch_per_gpu": B, "sequences_sampled": nb},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": O.threads(), "kind": "port",
+                             "sample": f"{n} decode steps x {nb} sequence(s) of the workload (time-bounded at {budget:.0f}s)"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1024)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--config", type=int, default=2)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=20.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    ws, rank, local = dist_setup(args) if args.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),
+                                                                   int(os.environ.get("RANK", "0")),
+                                                                   int(os.environ.get("LOCAL_RANK", "0")))
+    if args.impl == "reference":
+        res = run_reference(args, ws, rank, local)
+    else:
+        res = run_ours(args, ws, rank, local)
+    if rank == 0 and res is not None:
+        print(json.dumps(res), flush=True)
+    if args.impl == "ours" and ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,141 @@
+/*
+ * ming_cuda.h — C ABI of the B200 (sm_100a) implementation of ming-tts-serve's
+ * per-step hot path: the KV-cached Qwen2 LM decode step and the DiT
+ * flow-matching head.
+ *
+ * Plain C types only (bf16 values travel as uint16_t bit patterns). Every call
+ * returns MING_OK (0) or an error code; ming_cuda_last_error() gives the
+ * message of the calling thread's last failure. This mirrors mlx-c's
+ * convention that the reference binds (src/mlx.zig:8-17, `check()` at
+ * src/mlx.zig:431): an int status plus out-pointers.
+ *
+ * Threading: one context per GPU; calls on one context come from one thread
+ * (the reference runs all GPU work on one engine thread,
+ * src/ming_service.zig:11-14). Work is queued on the context's stream;
+ * calls that return data to host memory synchronise that stream.
+ *
+ * Pointer kinds: functions taking `ptr_kind` accept host pointers
+ * (MING_PTR_HOST, copied through the context's staging buffers) or device
+ * pointers on the context's GPU (MING_PTR_DEVICE, no copies, asynchronous).
+ */
+#ifndef MING_CUDA_H
+#define MING_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MING_OK 0
+#define MING_ERR_INVALID 1  /* bad argument, shape or state */
+#define MING_ERR_CUDA 2     /* a CUDA call failed */
+#define MING_ERR_NOMEM 3    /* device memory or KV pages exhausted */
+#define MING_ERR_MISSING 4  /* a required weight was not loaded */
+
+enum { MING_DTYPE_BF16 = 0, MING_DTYPE_F32 = 1, MING_DTYPE_U32 = 2 };
+enum { MING_PTR_HOST = 0, MING_PTR_DEVICE = 1 };
+enum { MING_DIT_NONE = 0, MING_DIT_TOKEN = 1, MING_DIT_ADALN = 2 };
+
+typedef struct ming_ctx ming_ctx;
+
+/* Model and runtime shape. ming_cuda_default_cfg() fills the Qwen2-0.5B LM of
+ * Ming-3.0-tts (src/ming_model.zig:37-53,500-504) with the reference's
+ * token-conditioned flow head (8 blocks x 1024) and aggregator. */
+typedef struct ming_cfg {
+    /* LM */
+    int hidden, layers, heads, kv_heads, head_dim, ff;
+    float rope_theta, rms_eps;
+    int weight_bits; /* 16 (bf16), 8 or 4 (MLX affine, group_size) */
+    int group_size;
+    /* KV cache and batching */
+    int page_size;    /* positions per page; must be 16 */
+    int max_seqs;     /* sequences alive at once */
+    int max_pages;    /* pages in the pool */
+    int max_ctx;      /* positions per sequence */
+    int max_batch;    /* rows per decode step */
+    int max_prefill;  /* rows per prefill chunk */
+    /* flow head */
+    int dit_mode; /* MING_DIT_NONE / TOKEN / ADALN */
+    int dit_hidden, dit_blocks, dit_heads, dit_ff, dit_latent, dit_frames, dit_cond_dim, dit_freq_dim;
+    int dit_max_batch;
+    /* aggregator (token mode only; 0 blocks = none) */
+    int agg_blocks;
+} ming_cfg;
+
+void ming_cuda_default_cfg(ming_cfg* cfg);
+
+/* Replaces Model.load's device side (src/ming_model.zig:923): creates the
+ * context on `device`. Weights follow with ming_cuda_load_tensor. */
+int ming_cuda_create(int device, const ming_cfg* cfg, ming_ctx** out);
+
+/* One tensor of model.safetensors under the reference's names
+ * (src/ming_model.zig:546-561,728-741,938-965), e.g.
+ * "model.model.layers.3.self_attn.q_proj.weight". Quantized linears come as
+ * "<prefix>.weight" (U32, [out, in*bits/32]) + ".scales" + ".biases" (BF16,
+ * [out, in/group]), MLX's QuantizedLinear layout. The data is copied. */
+int ming_cuda_load_tensor(ming_ctx* ctx, const char* name, int dtype, const int64_t* shape, int ndim, const void* host);
+
+/* Checks that every weight is present, repacks them into the kernels' tile
+ * layout on the device, precomputes the flow schedule tables, frees the
+ * staged copies. Must precede any compute call. */
+int ming_cuda_finalize(ming_ctx* ctx);
+
+/* Sequences own KV pages (KvCache.init/deinit, src/ming_model.zig:638-662). */
+int ming_cuda_seq_alloc(ming_ctx* ctx, int* seq_id);
+int ming_cuda_seq_free(ming_ctx* ctx, int seq_id);
+int ming_cuda_seq_len(ming_ctx* ctx, int seq_id, int* len);
+/* Truncates a sequence to `len` positions (pages are kept for reuse). */
+int ming_cuda_seq_truncate(ming_ctx* ctx, int seq_id, int len);
+
+/* Model.lmForward for a multi-row prompt (QStack.forward with L > 1,
+ * src/ming_model.zig:566-614): x [L][hidden] at positions len..len+L-1,
+ * appends K/V. out [L][hidden] post-norm hidden (may be NULL), stop [L]
+ * p(stop) of each row (may be NULL). */
+int ming_cuda_lm_prefill(ming_ctx* ctx, int seq_id, const uint16_t* x, int L, uint16_t* out, float* stop, int ptr_kind);
+
+/* One decode step for B sequences (QStack.forward decode branch ->
+ * decodeFused -> fused.lmLayer x 24, src/ming_model.zig:529-544,566-575,
+ * src/ming_fused.zig:597-614; stopProb src/ming_model.zig:1033-1038):
+ * x [B][hidden] -> out [B][hidden], stop [B]. Runs one captured CUDA graph. */
+int ming_cuda_lm_decode(ming_ctx* ctx, int B, const int* seq_ids, const uint16_t* x, uint16_t* out, float* stop,
+                        int ptr_kind);
+
+/* `steps` decode steps feeding each step's output hidden state back as the
+ * next input (BASELINE's LM token loop): out [steps][B][hidden],
+ * stop [steps][B] (either may be NULL). */
+int ming_cuda_lm_generate(ming_ctx* ctx, int B, const int* seq_ids, const uint16_t* x0, int steps, uint16_t* out,
+                          float* stop, int ptr_kind);
+
+/* Model.cfmSample (src/ming_model.zig:1143-1215): 10 Euler steps with CFG.
+ * Token mode: z [B][cond_dim], hist [B][latent], noise [B][latent],
+ * sde [10][B][latent] or NULL. adaLN mode: hist unused, noise/y
+ * [B][frames][latent], sde [10][B][frames][latent] or NULL.
+ * shift = sigma * sqrt(temperature) (0 disables the SDE term). */
+int ming_cuda_cfm_sample(ming_ctx* ctx, int B, const uint16_t* z, const uint16_t* hist, const uint16_t* noise,
+                         const uint16_t* sde, float cfg, float shift, uint16_t* y, int ptr_kind);
+
+/* Model.aggregate (src/ming_model.zig:1040-1053,1153-1157): latent [B][latent]
+ * -> next LM input rows [B][hidden]. */
+int ming_cuda_aggregate(ming_ctx* ctx, int B, const uint16_t* latent, uint16_t* out, int ptr_kind);
+
+/* The context's CUDA stream (a cudaStream_t), for event timing by callers. */
+int ming_cuda_get_stream(ming_ctx* ctx, void** stream);
+int ming_cuda_sync(ming_ctx* ctx);
+int ming_cuda_destroy(ming_ctx* ctx);
+const char* ming_cuda_last_error(void);
+
+/* ---- inspection (tests) ---- */
+/* Reads positions [pos0, pos0+n) of one layer's cache through the block
+ * table: k, v host [kv_heads][n][head_dim] bf16. */
+int ming_cuda_kv_read(ming_ctx* ctx, int seq_id, int layer, int pos0, int n, uint16_t* k, uint16_t* v);
+/* Dequantizes a loaded linear back from its device tiles (the kernels' own
+ * unpack path): out host [out][in] f32 in the reference's row order. */
+int ming_cuda_unpack_linear(ming_ctx* ctx, const char* weight_name, float* out);
+/* Timestep embeddings [10][dit_hidden] bf16 the flow head uses (host). */
+int ming_cuda_flow_temb(ming_ctx* ctx, uint16_t* te);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,339 @@
+// linear.cuh — the tiled linear kernel every projection of the step runs on.
+//
+// out[row][feature] = sum_k W[feature][k] * y[row][k], with:
+//   * W streamed once from HBM as packed 16-row tiles (pack.h), dequantised in
+//     registers (4/8-bit: exact fp16 integer codes, the MLX group scale/bias
+//     applied per 64-group in f32; bf16: used as is);
+//   * y, the activations, built by a prologue functor straight into shared
+//     memory in mma B-fragment order (RMSNorm, attention split combine,
+//     LayerNorm + adaLN modulation, or plain copy);
+//   * tensor-core mma.sync m16n8k16 with f32 accumulation;
+//   * an epilogue functor that receives each (tile row r, r+8) pair so RoPE
+//     halves, rotary neighbours and gate/up pairs land in one thread.
+//
+// Grid: x = tile, y = block of 8*NT activation rows. 4 warps per CTA split the
+// 64-wide groups of K round robin and meet in shared memory.
+#pragma once
+
+#include "common.cuh"
+
+namespace ming {
+
+constexpr int LIN_WARPS = 4;
+constexpr int LIN_THREADS = LIN_WARPS * 32;
+constexpr int LIN_KC = 1024;  // K chunk staged in shared memory at a time
+
+struct PackedW {
+    const uint8_t* tiles = nullptr;
+    const float* bias = nullptr;  // [ntiles*16] in packed row order, or null
+    int ntiles = 0, K = 0, fmt = 16;
+};
+
+MING_DEV constexpr int chunk_b(int fmt) { return fmt == 4 ? 576 : (fmt == 8 ? 1088 : 2048); }
+
+template <int NT>
+struct LinSmem {
+    // B fragments of one K chunk: [kstep][NT][lane] uint2
+    static constexpr int B_BYTES = (LIN_KC / 16) * NT * 32 * 8;
+    static constexpr int YS_BYTES = (LIN_KC / 64) * 8 * NT * 4;   // per (group,row) sum of y
+    static constexpr int RED_BYTES = LIN_WARPS * 16 * 8 * NT * 4;
+    static constexpr int AUX_FLOATS = 8 * NT * 32;                  // prologue per-row scratch
+    static constexpr int TOTAL = B_BYTES + YS_BYTES + RED_BYTES + AUX_FLOATS * 4;
+};
+
+// Writes the B-fragment entry for (kstep, ntile j, lane) from 4 y values.
+// b0 = (y[row][k0+2t], y[row][k0+2t+1]), b1 = the same at +8; row = 8j + lane/4.
+template <bool F16>
+MING_DEV uint2 make_bfrag(float y0, float y1, float y8, float y9) {
+    if (F16) return make_uint2(pack_f16x2(y0, y1), pack_f16x2(y8, y9));
+    return make_uint2(pack_bf16x2(y0, y1), pack_bf16x2(y8, y9));
+}
+
+// Stages one K chunk: for each (kstep, ntile, lane) entry asks the prologue
+// for the 4 values. Prologue API: float y(int row_in_block, int k) (row < nrows).
+template <int NT, bool F16, class Pro>
+MING_DEV void stage_chunk(const Pro& pro, int nrows, int kc, int kcl, uint2* sB, float* sYs, bool need_ysum) {
+    const int nent = (kcl / 16) * NT * 32;
+    for (int e = threadIdx.x; e < nent; e += LIN_THREADS) {
+        const int lane = e & 31, j = (e >> 5) % NT, ks = (e >> 5) / NT;
+        const int row = j * 8 + (lane >> 2), k0 = kc + ks * 16 + 2 * (lane & 3);
+        float y0 = 0.f, y1 = 0.f, y8 = 0.f, y9 = 0.f;
+        if (row < nrows) {
+            y0 = pro.y(row, k0);
+            y1 = pro.y(row, k0 + 1);
+            y8 = pro.y(row, k0 + 8);
+            y9 = pro.y(row, k0 + 9);
+        }
+        sB[e] = make_bfrag<F16>(y0, y1, y8, y9);
+    }
+    if (!need_ysum) return;
+    __syncthreads();
+    // per (group, row) sum of the rounded y the tensor cores will see
+    const int ng = kcl / 64;
+    for (int e = threadIdx.x; e < ng * 8 * NT; e += LIN_THREADS) {
+        const int gi = e / (8 * NT), row = e % (8 * NT), j = row / 8, gr = row % 8;
+        float s = 0.f;
+        for (int ks = 0; ks < 4; ks++)
+            for (int tq = 0; tq < 4; tq++) {
+                const uint2 v = sB[((gi * 4 + ks) * NT + j) * 32 + gr * 4 + tq];
+                if (F16) {
+                    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+                    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+                    s += (a.x + a.y) + (b.x + b.y);
+                } else {
+                    const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y);
+                    s += (a.x + a.y) + (b.x + b.y);
+                }
+            }
+        sYs[e] = s;
+    }
+}
+
+// One 64-group of one tile for NT n-tiles: acc[j][4] += W_group . y_group.
+template <int FMT, int NT>
+MING_DEV void group_mma(const uint8_t* chunk, const uint2* sB /*at group's first kstep*/, const float* sYs /*group row sums*/,
+                        float (&acc)[NT][4], int lane) {
+    if constexpr (FMT == 16) {
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+            const uint4 w = ldg_nc16(chunk + ((size_t)ks * 32 + lane) * 16);
+            const uint32_t a[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                const uint2 b = sB[(ks * NT + j) * 32 + lane];
+                mma_bf16(acc[j], a, b.x, b.y);
+            }
+        }
+    } else {
+        uint32_t words[8];
+        if constexpr (FMT == 4) {
+            const uint4 w = ldg_nc16(chunk + (size_t)lane * 16);
+            words[0] = w.x; words[1] = w.y; words[2] = w.z; words[3] = w.w;
+        } else {
+            const uint4 w0 = ldg_nc16(chunk + (size_t)lane * 16);
+            const uint4 w1 = ldg_nc16(chunk + (size_t)(32 + lane) * 16);
+            words[0] = w0.x; words[1] = w0.y; words[2] = w0.z; words[3] = w0.w;
+            words[4] = w1.x; words[5] = w1.y; words[6] = w1.z; words[7] = w1.w;
+        }
+        const uint2 sc = ldg_nc8(chunk + (FMT == 4 ? 512 : 1024) + (lane >> 2) * 8);
+        const float s_lo = __uint_as_float(sc.x << 16), b_lo = __uint_as_float(sc.x & 0xffff0000u);
+        const float s_hi = __uint_as_float(sc.y << 16), b_hi = __uint_as_float(sc.y & 0xffff0000u);
+        float t[NT][4];
+#pragma unroll
+        for (int j = 0; j < NT; j++) t[j][0] = t[j][1] = t[j][2] = t[j][3] = 0.f;
+#pragma unroll
+        for (int ks = 0; ks < 4; ks++) {
+            uint32_t a[4];
+            if constexpr (FMT == 4) dq4(words[ks], a);
+            else dq8(words[(ks >> 1) * 4 + (ks & 1) * 2], words[(ks >> 1) * 4 + (ks & 1) * 2 + 1], a);
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                const uint2 b = sB[(ks * NT + j) * 32 + lane];
+                mma_f16(t[j], a, b.x, b.y);
+            }
+        }
+        const int c = 2 * (lane & 3);
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+            const float y0 = sYs[j * 8 + c], y1 = sYs[j * 8 + c + 1];
+            acc[j][0] += s_lo * t[j][0] + b_lo * y0;
+            acc[j][1] += s_lo * t[j][1] + b_lo * y1;
+            acc[j][2] += s_hi * t[j][2] + b_hi * y0;
+            acc[j][3] += s_hi * t[j][3] + b_hi * y1;
+        }
+    }
+}
+
+// Prologue API:
+//   MING_DEV void init(int r0, int nrows, float* aux) const;   // per-row stats into aux
+//   MING_DEV float y(int row, int k) const;                    // after init
+// Epilogue API:
+//   MING_DEV void operator()(int tile, int r8, int row /*absolute*/, float lo, float hi) const;
+template <int FMT, int NT, class Pro, class Epi>
+__global__ void __launch_bounds__(LIN_THREADS) linear_kernel(PackedW W, Pro pro, Epi epi, int rows) {
+    using S = LinSmem<NT>;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint2* sB = reinterpret_cast<uint2*>(smem);
+    float* sYs = reinterpret_cast<float*>(smem + S::B_BYTES);
+    float* sRed = reinterpret_cast<float*>(smem + S::B_BYTES + S::YS_BYTES);
+    float* sAux = reinterpret_cast<float*>(smem + S::B_BYTES + S::YS_BYTES + S::RED_BYTES);
+    constexpr bool F16 = FMT != 16;
+    const int tile = blockIdx.x, r0 = blockIdx.y * 8 * NT;
+    const int nrows = min(8 * NT, rows - r0);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ng_total = W.K / 64;
+    Pro p = pro;
+    p.init(r0, nrows, sAux);
+    __syncthreads();
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    const uint8_t* tbase = W.tiles + (size_t)tile * ng_total * chunk_b(FMT);
+    for (int kc = 0; kc < W.K; kc += LIN_KC) {
+        const int kcl = min(LIN_KC, W.K - kc);
+        __syncthreads();
+        stage_chunk<NT, F16>(p, nrows, kc, kcl, sB, sYs, FMT != 16);
+        __syncthreads();
+        const int ng = kcl / 64;
+#pragma unroll 2
+        for (int gi = warp; gi < ng; gi += LIN_WARPS) {
+            const uint8_t* ch = tbase + (size_t)(kc / 64 + gi) * chunk_b(FMT);
+            group_mma<FMT, NT>(ch, sB + (size_t)gi * 4 * NT * 32, sYs + gi * 8 * NT, acc, lane);
+        }
+    }
+    // warps -> shared: sRed[warp][row 0..15][col 0..8NT)
+    {
+        const int g = lane >> 2, c = 2 * (lane & 3);
+        float* r = sRed + warp * 16 * 8 * NT;
+#pragma unroll
+        for (int j = 0; j < NT; j++) {
+            r[g * 8 * NT + j * 8 + c] = acc[j][0];
+            r[g * 8 * NT + j * 8 + c + 1] = acc[j][1];
+            r[(g + 8) * 8 * NT + j * 8 + c] = acc[j][2];
+            r[(g + 8) * 8 * NT + j * 8 + c + 1] = acc[j][3];
+        }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < 8 * 8 * NT; e += LIN_THREADS) {
+        const int r8 = e / (8 * NT), col = e % (8 * NT);
+        if (col >= nrows) continue;
+        float lo = 0.f, hi = 0.f;
+#pragma unroll
+        for (int w = 0; w < LIN_WARPS; w++) {
+            lo += sRed[(w * 16 + r8) * 8 * NT + col];
+            hi += sRed[(w * 16 + r8 + 8) * 8 * NT + col];
+        }
+        epi(tile, r8, r0 + col, lo, hi);
+    }
+}
+
+// ---------------------------------------------------------------------
+// Prologues
+// ---------------------------------------------------------------------
+
+// Plain activations y = x (bf16 rows, leading dimension ld).
+struct ProPlain {
+    const uint16_t* x;
+    int ld;
+    int r0;
+    MING_DEV void init(int r0_, int, float*) { r0 = r0_; }
+    MING_DEV float y(int row, int k) const { return bf2f(x[(size_t)(r0 + row) * ld + k]); }
+};
+
+// RMSNorm folded in: y = x * rsqrt(mean(x^2) + eps) * nw (the reference's
+// LA/LD/A/C prologue, src/ming_fused.zig:100-142; the tensor-core operand
+// needs 16-bit y, so 1/rms is applied before the product).
+struct ProRms {
+    const uint16_t* x;
+    const uint16_t* nw;
+    int ld, K;
+    float eps;
+    int r0;
+    float* inv;
+    MING_DEV void init(int r0_, int nrows, float* aux) {
+        r0 = r0_;
+        inv = aux;
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int r = warp; r < nrows; r += LIN_WARPS) {
+            const uint16_t* xr = x + (size_t)(r0 + r) * ld;
+            float s = 0.f;
+            for (int k = lane * 2; k < K; k += 64) {
+                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(xr + k));
+                s += v.x * v.x + v.y * v.y;
+            }
+            s = warp_sum(s);
+            if (lane == 0) aux[r] = rsqrtf(s / (float)K + eps);
+        }
+    }
+    MING_DEV float y(int row, int k) const {
+        return bf2f(x[(size_t)(r0 + row) * ld + k]) * inv[row] * bf2f(nw[k]);
+    }
+};
+
+// LayerNorm (no affine, eps 1e-6) + adaLN modulation, evaluated in f32 and
+// rounded to bf16 once: y = rb(LN(x) * (1 + scale) + shift). Rows of one
+// condition share its modulation row (rows_per_cond consecutive rows).
+struct ProLnMod {
+    const uint16_t* x;
+    const uint16_t* shift;  // [cond rows][mod_ld]
+    const uint16_t* scale;
+    int ld, mod_ld, K, rows_per_cond;
+    int r0;
+    float* st;  // [row][2] mean, inv
+    MING_DEV void init(int r0_, int nrows, float* aux) {
+        r0 = r0_;
+        st = aux;
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int r = warp; r < nrows; r += LIN_WARPS) {
+            const uint16_t* xr = x + (size_t)(r0 + r) * ld;
+            float s = 0.f;
+            for (int k = lane; k < K; k += 32) s += bf2f(xr[k]);
+            const float mu = warp_sum(s) / (float)K;
+            float v = 0.f;
+            for (int k = lane; k < K; k += 32) { const float d = bf2f(xr[k]) - mu; v += d * d; }
+            v = warp_sum(v) / (float)K;
+            if (lane == 0) { aux[2 * r] = mu; aux[2 * r + 1] = rsqrtf(v + 1e-6f); }
+        }
+    }
+    MING_DEV float y(int row, int k) const {
+        const int ar = r0 + row, c = ar / rows_per_cond;
+        const float n = (bf2f(x[(size_t)ar * ld + k]) - st[2 * row]) * st[2 * row + 1];
+        return rb(n * (1.0f + bf2f(scale[(size_t)c * mod_ld + k])) + bf2f(shift[(size_t)c * mod_ld + k]));
+    }
+};
+
+// ---------------------------------------------------------------------
+// Generic epilogues
+// ---------------------------------------------------------------------
+
+// Plain row order (tile row r -> feature 16*tile + r).
+// out[row][f] = rb(res[row][f] + rb(v + bias)).
+struct EpiResidual {
+    const uint16_t* res;
+    uint16_t* out;
+    const float* bias;
+    int ld;
+    MING_DEV void operator()(int tile, int r8, int row, float lo, float hi) const {
+        const int f0 = tile * 16 + r8, f1 = f0 + 8;
+        const float b0 = bias ? bias[f0] : 0.f, b1 = bias ? bias[f1] : 0.f;
+        const size_t i0 = (size_t)row * ld + f0, i1 = (size_t)row * ld + f1;
+        out[i0] = f2bf(bf2f(res[i0]) + rb(lo + b0));
+        out[i1] = f2bf(bf2f(res[i1]) + rb(hi + b1));
+    }
+};
+
+// out[row][f] = act(rb(v + bias)); act 0 = none, 1 = gelu_approx chain,
+// 2 = SiLU chain (each bf16 op rounded), 3 = store f32 unrounded.
+MING_DEV float gelu_chain(float x) {
+    // mlx.nn.gelu_approx with every bf16 op rounded (src/ming_fused.zig:229-236)
+    const float c1 = 0.044677734375f;  // rb(0.044715)
+    const float c2 = 0.796875f;        // rb(0.7978845608)
+    const float x3 = rb(x * x * x);
+    const float inner = rb(x + rb(c1 * x3));
+    const float th = rb(tanhf(rb(c2 * inner)));
+    return rb(rb(0.5f * x) * rb(1.0f + th));
+}
+MING_DEV float silu_chain(float x) { return rb(x * rb(1.0f / (1.0f + __expf(-x)))); }
+
+struct EpiAct {
+    uint16_t* out;
+    float* out_f32;
+    const float* bias;
+    int ld, act, nvalid;  // features >= nvalid are padding and dropped
+    MING_DEV float f(float v, int fi) const {
+        const float x = rb(v + (bias ? bias[fi] : 0.f));
+        return act == 1 ? gelu_chain(x) : (act == 2 ? silu_chain(x) : x);
+    }
+    MING_DEV void operator()(int tile, int r8, int row, float lo, float hi) const {
+        const int f0 = tile * 16 + r8, f1 = f0 + 8;
+        if (act == 3) {
+            if (f0 < nvalid) out_f32[(size_t)row * ld + f0] = lo + (bias ? bias[f0] : 0.f);
+            if (f1 < nvalid) out_f32[(size_t)row * ld + f1] = hi + (bias ? bias[f1] : 0.f);
+            return;
+        }
+        if (f0 < nvalid) out[(size_t)row * ld + f0] = f2bf(f(lo, f0));
+        if (f1 < nvalid) out[(size_t)row * ld + f1] = f2bf(f(hi, f1));
+    }
+};
+
+}  // namespace ming

@@ -1,0 +1,1174 @@
+// runtime.cu — the context behind include/ming_cuda.h: weight staging and
+// repacking, the paged KV allocator, captured decode graphs, the flow head.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/ming_cuda.h"
+#include "dit.cuh"
+#include "lm.cuh"
+#include "pack.h"
+
+using namespace ming;
+
+// ---------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------
+
+static thread_local std::string g_err;
+
+namespace {
+
+struct Err {
+    int code;
+    std::string msg;
+};
+
+int fail(int code, const std::string& m) {
+    g_err = m;
+    return code;
+}
+
+#define CK(call)                                                                                      \
+    do {                                                                                              \
+        cudaError_t e_ = (call);                                                                      \
+        if (e_ != cudaSuccess)                                                                        \
+            return fail(MING_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));           \
+    } while (0)
+
+struct HostTensor {
+    int dtype = 0;
+    std::vector<int64_t> shape;
+    std::vector<uint8_t> data;
+    int64_t dim(int i) const { return i < (int)shape.size() ? shape[i] : 1; }
+};
+
+// A device allocation freed with the context.
+struct DevMem {
+    std::vector<void*> ptrs;
+    ~DevMem() {
+        for (void* p : ptrs) cudaFree(p);
+    }
+    template <class T>
+    T* alloc(size_t count, int* rc) {
+        void* p = nullptr;
+        if (count == 0) count = 1;
+        cudaError_t e = cudaMalloc(&p, count * sizeof(T));
+        if (e != cudaSuccess) {
+            *rc = fail(MING_ERR_NOMEM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
+            return nullptr;
+        }
+        cudaMemset(p, 0, count * sizeof(T));
+        ptrs.push_back(p);
+        return static_cast<T*>(p);
+    }
+};
+
+struct PackedLin {
+    PackedW w;
+    std::vector<std::string> src_names;  // weight names of the sources
+    std::vector<RowRef> rows;
+    std::vector<int> src_out, src_in;
+};
+
+struct DitBlockW {
+    PackedLin ada, qkv, o, ff1, ff2;
+    uint16_t* norm1 = nullptr;
+    uint16_t* norm2 = nullptr;
+};
+
+struct SeqInfo {
+    bool live = false;
+    int len = 0;
+};
+
+}  // namespace
+
+struct ming_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    ming_cfg cfg{};
+    bool finalized = false;
+    std::map<std::string, HostTensor> staged;
+    DevMem mem;
+    std::vector<PackedLin*> all_lins;
+
+    // LM
+    struct Layer {
+        PackedLin qkv, o, gu, down;
+        uint16_t* ln1 = nullptr;
+        uint16_t* ln2 = nullptr;
+    };
+    std::vector<Layer> layers;
+    uint16_t* norm = nullptr;
+    uint16_t* stop_w = nullptr;
+    uint16_t* stop_b = nullptr;
+    float log2_theta = 0;
+
+    // KV
+    uint16_t* pool = nullptr;
+    int* bt = nullptr;
+    int bt_ld = 0;
+    std::vector<int> bt_host;
+    std::vector<int> free_pages;
+    std::vector<SeqInfo> seqs;
+
+    // activations / step state
+    int maxr = 0, nsplit = 0;
+    uint16_t *x = nullptr, *x1 = nullptr, *q = nullptr, *h = nullptr, *z = nullptr;
+    float* stop = nullptr;
+    float* part = nullptr;
+    int *seq_len = nullptr, *row_seq = nullptr, *row_pos = nullptr, *step_counter = nullptr;
+    uint16_t** out_cell = nullptr;
+    float** stop_cell = nullptr;
+    std::vector<int> row_seq_host;
+    std::map<int, cudaGraphExec_t> decode_graphs;
+    uint16_t* gen_out = nullptr;
+    size_t gen_out_elems = 0;
+    float* gen_stop = nullptr;
+    size_t gen_stop_elems = 0;
+
+    // flow head
+    std::vector<DitBlockW> dit;
+    PackedLin t_mlp0, t_mlp2, x_emb, c_emb, final_ada, final_lin;
+    uint16_t* final_norm = nullptr;
+    uint16_t* final_w = nullptr;  // token final linear, raw bf16 [latent][H]
+    uint16_t* final_b = nullptr;
+    float* inv_freq = nullptr;
+    uint16_t* temb = nullptr;  // [10][H]
+    float flow_dt[10] = {0}, flow_sq[10] = {0};
+    uint16_t *f_z = nullptr, *f_zc = nullptr, *f_hist = nullptr, *f_y = nullptr, *f_sde = nullptr;
+    uint16_t *f_ce = nullptr, *f_xh = nullptr, *f_xy = nullptr, *f_rows = nullptr, *f_x1 = nullptr, *f_qkv = nullptr;
+    uint16_t *f_att = nullptr, *f_hh = nullptr, *f_sc = nullptr, *f_mod = nullptr;
+    float* f_vel = nullptr;
+    std::map<std::pair<int, int>, cudaGraphExec_t> cfm_graphs;  // (B, sde?) -> graph
+    float cfm_cfg = NAN, cfm_shift = NAN;
+
+    // aggregator
+    std::vector<DitBlockW> agg;
+    PackedLin agg_x_emb, agg_final;
+    uint16_t* agg_cls = nullptr;
+    uint16_t* agg_norm = nullptr;
+    float* agg_inv_freq = nullptr;
+    uint16_t *a_lat = nullptr, *a_rows = nullptr, *a_x1 = nullptr, *a_qkv = nullptr, *a_att = nullptr, *a_hh = nullptr,
+             *a_xe = nullptr, *a_out = nullptr;
+
+    ~ming_ctx() {
+        for (auto& kv : decode_graphs) cudaGraphExecDestroy(kv.second);
+        for (auto& kv : cfm_graphs) cudaGraphExecDestroy(kv.second);
+        for (PackedLin* l : all_lins) (void)l;
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+// ---------------------------------------------------------------------
+// linear launch dispatch
+// ---------------------------------------------------------------------
+
+namespace {
+
+template <int FMT, int NT, class Pro, class Epi>
+void launch_lin_t(const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
+    static unsigned attr_devices = 0;  // bit d: attribute set on device d
+    constexpr int smem = LinSmem<NT>::TOTAL;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_devices & (1u << (dev & 31)))) {
+        cudaFuncSetAttribute(linear_kernel<FMT, NT, Pro, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        attr_devices |= 1u << (dev & 31);
+    }
+    dim3 grid(W.ntiles, (rows + 8 * NT - 1) / (8 * NT));
+    linear_kernel<FMT, NT, Pro, Epi><<<grid, LIN_THREADS, smem, s>>>(W, p, e, rows);
+}
+
+template <int FMT, class Pro, class Epi>
+void launch_lin_f(const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
+    if (rows <= 8) launch_lin_t<FMT, 1>(W, p, e, rows, s);
+    else if (rows <= 16) launch_lin_t<FMT, 2>(W, p, e, rows, s);
+    else launch_lin_t<FMT, 4>(W, p, e, rows, s);
+}
+
+template <class Pro, class Epi>
+void run_linear(const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
+    if (rows <= 0) return;
+    if (W.fmt == 4) launch_lin_f<4>(W, p, e, rows, s);
+    else if (W.fmt == 8) launch_lin_f<8>(W, p, e, rows, s);
+    else launch_lin_f<16>(W, p, e, rows, s);
+}
+
+// Dequantizes every tile of a packed linear to f32 [ntiles*16][K] (the
+// kernels' unpack functions; used by ming_cuda_unpack_linear).
+__global__ void unpack_tiles_kernel(PackedW W, float* out) {
+    const int tile = blockIdx.x, gi = blockIdx.y, lane = threadIdx.x;
+    const int ng = W.K / 64, cb = chunk_b(W.fmt);
+    const uint8_t* ch = W.tiles + ((size_t)tile * ng + gi) * cb;
+    const int g = lane >> 2, t = lane & 3;
+    float s_lo = 1.f, b_lo = 0.f, s_hi = 1.f, b_hi = 0.f;
+    if (W.fmt != 16) {
+        const uint2 sc = *reinterpret_cast<const uint2*>(ch + (W.fmt == 4 ? 512 : 1024) + g * 8);
+        s_lo = __uint_as_float(sc.x << 16);
+        b_lo = __uint_as_float(sc.x & 0xffff0000u);
+        s_hi = __uint_as_float(sc.y << 16);
+        b_hi = __uint_as_float(sc.y & 0xffff0000u);
+    }
+    for (int ks = 0; ks < 4; ks++) {
+        uint32_t a[4];
+        if (W.fmt == 16) {
+            const uint4 w = *reinterpret_cast<const uint4*>(ch + ((size_t)ks * 32 + lane) * 16);
+            a[0] = w.x; a[1] = w.y; a[2] = w.z; a[3] = w.w;
+        } else if (W.fmt == 4) {
+            const uint32_t w = reinterpret_cast<const uint32_t*>(ch + (size_t)lane * 16)[ks];
+            dq4(w, a);
+        } else {
+            const uint32_t* p = reinterpret_cast<const uint32_t*>(ch + ((size_t)(ks >> 1) * 32 + lane) * 16 + (ks & 1) * 8);
+            dq8(p[0], p[1], a);
+        }
+        const int k0 = gi * 64 + ks * 16 + 2 * t;
+        const int rr[4] = {g, g + 8, g, g + 8};
+        const int kk[4] = {k0, k0, k0 + 8, k0 + 8};
+        for (int i = 0; i < 4; i++) {
+            float lo, hi;
+            if (W.fmt == 16) {
+                const float2 v = unpack_bf16x2(a[i]);
+                lo = v.x;
+                hi = v.y;
+            } else {
+                const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&a[i]));
+                const float s = rr[i] < 8 ? s_lo : s_hi, b = rr[i] < 8 ? b_lo : b_hi;
+                lo = s * v.x + b;
+                hi = s * v.y + b;
+            }
+            float* o = out + (size_t)(tile * 16 + rr[i]) * W.K + kk[i];
+            o[0] = lo;
+            o[1] = hi;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------
+// staging helpers
+// ---------------------------------------------------------------------
+
+const HostTensor* find(ming_ctx* c, const std::string& n) {
+    auto it = c->staged.find(n);
+    return it == c->staged.end() ? nullptr : &it->second;
+}
+
+int lin_src(ming_ctx* c, const std::string& prefix, LinearSrc& s, bool want_bias) {
+    const HostTensor* w = find(c, prefix + ".weight");
+    if (!w) return fail(MING_ERR_MISSING, "missing weight " + prefix + ".weight");
+    const HostTensor* sc = find(c, prefix + ".scales");
+    const HostTensor* bi = find(c, prefix + ".biases");
+    if (w->shape.size() != 2) return fail(MING_ERR_INVALID, prefix + ".weight is not 2-D");
+    s = LinearSrc{};
+    s.out = (int)w->shape[0];
+    if (sc) {
+        if (!bi) return fail(MING_ERR_MISSING, "missing " + prefix + ".biases");
+        if (w->dtype != MING_DTYPE_U32 || sc->dtype != MING_DTYPE_BF16 || bi->dtype != MING_DTYPE_BF16)
+            return fail(MING_ERR_INVALID, prefix + ": quantized weight must be U32 with BF16 scales/biases");
+        if (sc->shape.size() != 2 || sc->shape[0] != s.out || bi->shape != sc->shape)
+            return fail(MING_ERR_INVALID, prefix + ": scales/biases shape mismatch");
+        s.group = c->cfg.group_size;
+        s.in = (int)sc->shape[1] * s.group;
+        const int64_t words = w->shape[1];
+        if (s.in == 0 || (words * 32) % s.in) return fail(MING_ERR_INVALID, prefix + ": cannot infer bit width");
+        s.fmt = (int)(words * 32 / s.in);
+        if (s.fmt != 4 && s.fmt != 8) return fail(MING_ERR_INVALID, prefix + ": only 4/8-bit quantization is supported");
+        s.q = reinterpret_cast<const uint32_t*>(w->data.data());
+        s.scales = reinterpret_cast<const uint16_t*>(sc->data.data());
+        s.biases = reinterpret_cast<const uint16_t*>(bi->data.data());
+    } else {
+        if (w->dtype != MING_DTYPE_BF16) return fail(MING_ERR_INVALID, prefix + ".weight must be BF16 (or U32 + scales)");
+        s.fmt = 16;
+        s.in = (int)w->shape[1];
+        s.w = reinterpret_cast<const uint16_t*>(w->data.data());
+    }
+    if (want_bias) {
+        const HostTensor* b = find(c, prefix + ".bias");
+        if (!b) return fail(MING_ERR_MISSING, "missing " + prefix + ".bias");
+        if (b->dtype != MING_DTYPE_BF16 || b->data.size() != (size_t)s.out * 2)
+            return fail(MING_ERR_INVALID, prefix + ".bias must be BF16 [out]");
+        s.bias = reinterpret_cast<const uint16_t*>(b->data.data());
+    }
+    return MING_OK;
+}
+
+int upload_packed(ming_ctx* c, const std::vector<LinearSrc>& srcs, const std::vector<std::string>& names,
+                  const std::vector<RowRef>& rows, PackedLin& pl) {
+    const int fmt = srcs[0].fmt, K = srcs[0].in;
+    std::vector<uint8_t> tiles;
+    std::vector<float> bias;
+    std::string e = pack_tiles(srcs, rows, fmt, K, tiles, bias);
+    if (!e.empty()) return fail(MING_ERR_INVALID, names[0] + ": " + e);
+    int rc = MING_OK;
+    uint8_t* dt = c->mem.alloc<uint8_t>(tiles.size(), &rc);
+    if (!dt) return rc;
+    float* db = c->mem.alloc<float>(bias.size(), &rc);
+    if (!db) return rc;
+    CK(cudaMemcpy(dt, tiles.data(), tiles.size(), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(db, bias.data(), bias.size() * 4, cudaMemcpyHostToDevice));
+    pl.w.tiles = dt;
+    pl.w.bias = db;
+    pl.w.ntiles = (int)rows.size() / 16;
+    pl.w.K = K;
+    pl.w.fmt = fmt;
+    pl.src_names = names;
+    pl.rows = rows;
+    for (auto& s : srcs) {
+        pl.src_out.push_back(s.out);
+        pl.src_in.push_back(s.in);
+    }
+    c->all_lins.push_back(&pl);
+    return MING_OK;
+}
+
+// Plain row order: tile row r -> source row 16t + r (zero rows past `out`).
+int pack_plain(ming_ctx* c, const std::string& prefix, bool bias, PackedLin& pl, int* out_dim = nullptr) {
+    LinearSrc s;
+    int rc = lin_src(c, prefix, s, bias);
+    if (rc) return rc;
+    if (out_dim) *out_dim = s.out;
+    std::vector<RowRef> rows(((s.out + 15) / 16) * 16);
+    for (size_t i = 0; i < rows.size(); i++) rows[i] = (int)i < s.out ? RowRef{0, (int)i} : RowRef{-1, 0};
+    return upload_packed(c, {s}, {prefix + ".weight"}, rows, pl);
+}
+
+int upload_raw(ming_ctx* c, const std::string& name, int dtype, int64_t count, void** out) {
+    const HostTensor* t = find(c, name);
+    if (!t) return fail(MING_ERR_MISSING, "missing weight " + name);
+    const size_t esz = dtype == MING_DTYPE_BF16 ? 2 : 4;
+    if (t->dtype != dtype || t->data.size() != (size_t)count * esz)
+        return fail(MING_ERR_INVALID, name + ": unexpected dtype or size");
+    int rc = MING_OK;
+    uint8_t* d = c->mem.alloc<uint8_t>(t->data.size(), &rc);
+    if (!d) return rc;
+    CK(cudaMemcpy(d, t->data.data(), t->data.size(), cudaMemcpyHostToDevice));
+    *out = d;
+    return MING_OK;
+}
+
+// DiT q|k|v with neighbour-interleaved rows (rotary pairs in one thread).
+int pack_dit_qkv(ming_ctx* c, const std::string& pre, PackedLin& pl, int H) {
+    LinearSrc s[3];
+    const char* nm[3] = {".attn.to_q", ".attn.to_k", ".attn.to_v"};
+    for (int i = 0; i < 3; i++) {
+        int rc = lin_src(c, pre + nm[i], s[i], true);
+        if (rc) return rc;
+        if (s[i].out != H) return fail(MING_ERR_INVALID, pre + nm[i] + ": wrong out dim");
+    }
+    std::vector<RowRef> rows;
+    for (int b = 0; b < 3; b++)
+        for (int lt = 0; lt < H / 16; lt++)
+            for (int r = 0; r < 16; r++) rows.push_back({b, r < 8 ? lt * 16 + 2 * r : lt * 16 + 2 * (r - 8) + 1});
+    return upload_packed(c, {s[0], s[1], s[2]}, {pre + nm[0] + ".weight", pre + nm[1] + ".weight", pre + nm[2] + ".weight"},
+                         rows, pl);
+}
+
+int load_dit_blocks(ming_ctx* c, const std::string& prefix, int nblocks, int H, bool adaln, std::vector<DitBlockW>& out) {
+    out.resize(nblocks);
+    for (int i = 0; i < nblocks; i++) {
+        const std::string pre = prefix + ".blocks." + std::to_string(i);
+        DitBlockW& b = out[i];
+        int rc;
+        if (adaln) {
+            if ((rc = pack_plain(c, pre + ".adaLN_modulation.1", true, b.ada))) return rc;
+        } else {
+            if ((rc = upload_raw(c, pre + ".norm1.weight", MING_DTYPE_BF16, H, (void**)&b.norm1))) return rc;
+            if ((rc = upload_raw(c, pre + ".norm2.weight", MING_DTYPE_BF16, H, (void**)&b.norm2))) return rc;
+        }
+        if ((rc = pack_dit_qkv(c, pre, b.qkv, H))) return rc;
+        if ((rc = pack_plain(c, pre + ".attn.to_out.0", true, b.o))) return rc;
+        if ((rc = pack_plain(c, pre + ".mlp.ff.0.0", true, b.ff1))) return rc;
+        if ((rc = pack_plain(c, pre + ".mlp.ff.2", true, b.ff2))) return rc;
+    }
+    return MING_OK;
+}
+
+// EPSS + sway flow schedule in bf16 (flowSchedule, src/ming_model.zig:1205-1215).
+float h_rb(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    u &= 0xffff0000u;
+    std::memcpy(&f, &u, 4);
+    return f;
+}
+uint16_t h_f2bf(float f) {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+void flow_schedule(float* t, float* dt, float* sq) {
+    static const float sched[11] = {0, 2, 4, 6, 8, 12, 16, 20, 24, 28, 32};
+    const float hh = h_rb(1.0f / 32.0f), hp = h_rb(3.14159265358979f / 2.0f);
+    for (int i = 0; i <= 10; i++) {
+        const float tt = h_rb(hh * h_rb(sched[i]));
+        const float ct = h_rb(cosf(h_rb(hp * tt)));
+        const float sw = h_rb(h_rb(ct - 1.0f) + tt);
+        t[i] = h_rb(tt + h_rb(-1.0f * sw));
+    }
+    for (int i = 0; i < 10; i++) {
+        dt[i] = h_rb(t[i + 1] - t[i]);
+        sq[i] = h_rb(powf(fabsf(dt[i]), 0.5f));
+    }
+}
+
+// Timestep embeddings of the 10 Euler steps (TimestepEmbedder,
+// src/ming_model.zig:1064-1076; t_freq :966-975): sinusoid table on the
+// host, the two linears + SiLU on the device.
+int build_temb(ming_ctx* c, int freq_dim, int H) {
+    float t[11];
+    flow_schedule(t, c->flow_dt, c->flow_sq);
+    const int half = freq_dim / 2;
+    const float e = (float)(std::log(10000.0) / (double)(half - 1));
+    std::vector<uint16_t> sc((size_t)10 * freq_dim);
+    for (int r = 0; r < 10; r++) {
+        const float ts = h_rb(h_rb(1000.0f) * t[r]);
+        for (int j = 0; j < half; j++) {
+            const float a = ts * std::exp((float)j * -e);
+            sc[(size_t)r * freq_dim + j] = h_f2bf(std::sin(a));
+            sc[(size_t)r * freq_dim + half + j] = h_f2bf(std::cos(a));
+        }
+    }
+    int rc = MING_OK;
+    uint16_t* d_sc = c->mem.alloc<uint16_t>(sc.size(), &rc);
+    uint16_t* d_h0 = c->mem.alloc<uint16_t>((size_t)10 * H, &rc);
+    c->temb = c->mem.alloc<uint16_t>((size_t)10 * H, &rc);
+    if (rc) return rc;
+    CK(cudaMemcpy(d_sc, sc.data(), sc.size() * 2, cudaMemcpyHostToDevice));
+    run_linear(c->t_mlp0.w, ProPlain{d_sc, freq_dim, 0}, EpiAct{d_h0, nullptr, c->t_mlp0.w.bias, H, 2, H}, 10, c->stream);
+    run_linear(c->t_mlp2.w, ProPlain{d_h0, H, 0}, EpiAct{c->temb, nullptr, c->t_mlp2.w.bias, H, 0, H}, 10, c->stream);
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaGetLastError());
+    return MING_OK;
+}
+
+int check_seq(ming_ctx* c, int s) {
+    if (s < 0 || s >= (int)c->seqs.size() || !c->seqs[s].live) return fail(MING_ERR_INVALID, "invalid sequence id");
+    return MING_OK;
+}
+
+// Makes sure positions [from, to) of sequence s have pages; uploads new
+// block-table entries.
+int ensure_pages(ming_ctx* c, int s, int from, int to) {
+    if (to > c->cfg.max_ctx) return fail(MING_ERR_NOMEM, "sequence would exceed max_ctx positions");
+    for (int p = from / PAGE; p < (to + PAGE - 1) / PAGE; p++) {
+        int& e = c->bt_host[(size_t)s * c->bt_ld + p];
+        if (e >= 0) continue;
+        if (c->free_pages.empty()) return fail(MING_ERR_NOMEM, "KV page pool exhausted");
+        e = c->free_pages.back();
+        c->free_pages.pop_back();
+        CK(cudaMemcpyAsync(c->bt + (size_t)s * c->bt_ld + p, &e, 4, cudaMemcpyHostToDevice, c->stream));
+    }
+    return MING_OK;
+}
+
+int copy_in(ming_ctx* c, void* dst, const void* src, size_t bytes, int kind) {
+    if (bytes == 0) return MING_OK;
+    CK(cudaMemcpyAsync(dst, src, bytes, kind == MING_PTR_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                       c->stream));
+    return MING_OK;
+}
+int copy_out(ming_ctx* c, void* dst, const void* src, size_t bytes, int kind) {
+    if (bytes == 0 || !dst) return MING_OK;
+    CK(cudaMemcpyAsync(dst, src, bytes, kind == MING_PTR_DEVICE ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                       c->stream));
+    return MING_OK;
+}
+
+// The 24-layer step over `rows` rows whose row_seq/row_pos are on the device.
+void enqueue_layers(ming_ctx* c, int rows) {
+    const ming_cfg& f = c->cfg;
+    RowsDev rd{c->row_seq, c->row_pos};
+    KvDev kv{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
+    for (int l = 0; l < f.layers; l++) {
+        auto& L = c->layers[l];
+        run_linear(L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
+                   EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, rows, c->stream);
+        launch_attn(AttnArgs{c->q, c->part, kv, rd, l, f.heads, f.kv_heads, c->nsplit}, rows, c->stream);
+        run_linear(L.o.w, ProAttn{c->part, rd, c->nsplit, f.heads, 0, nullptr},
+                   EpiResidual{c->x, c->x1, nullptr, f.hidden}, rows, c->stream);
+        run_linear(L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr}, EpiSwiGLU{c->h, f.ff}, rows,
+                   c->stream);
+        run_linear(L.down.w, ProPlain{c->h, f.ff, 0}, EpiResidual{c->x1, c->x, nullptr, f.hidden}, rows, c->stream);
+    }
+}
+
+StepDev step_dev(ming_ctx* c) {
+    return StepDev{c->seq_len, c->row_seq, c->row_pos, c->step_counter, c->out_cell, c->stop_cell};
+}
+
+// Decode graph for B rows: step_begin, layers, final (+ feedback into x).
+int decode_graph(ming_ctx* c, int B, cudaGraphExec_t* out) {
+    auto it = c->decode_graphs.find(B);
+    if (it != c->decode_graphs.end()) {
+        *out = it->second;
+        return MING_OK;
+    }
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    launch_step_begin(step_dev(c), B, c->stream);
+    enqueue_layers(c, B);
+    launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, c->x, step_dev(c), c->cfg.hidden, 0, 1,
+                           c->cfg.rms_eps},
+                 B, c->stream);
+    cudaError_t ce = cudaStreamEndCapture(c->stream, &g);
+    if (ce != cudaSuccess) return fail(MING_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+    cudaGraphExec_t ge;
+    ce = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess) return fail(MING_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+    c->decode_graphs[B] = ge;
+    *out = ge;
+    return MING_OK;
+}
+
+int prepare_rows(ming_ctx* c, int B, const int* seq_ids, int steps) {
+    if (B < 1 || B > c->cfg.max_batch) return fail(MING_ERR_INVALID, "batch size out of range");
+    std::vector<int> ids(seq_ids, seq_ids + B);
+    for (int i = 0; i < B; i++) {
+        int rc = check_seq(c, ids[i]);
+        if (rc) return rc;
+        for (int j = 0; j < i; j++)
+            if (ids[j] == ids[i]) return fail(MING_ERR_INVALID, "a sequence appears twice in one batch");
+    }
+    for (int i = 0; i < B; i++) {
+        const int s = ids[i], len = c->seqs[s].len;
+        if (len < 1) return fail(MING_ERR_INVALID, "decode needs a prefilled sequence");
+        int rc = ensure_pages(c, s, len, len + steps);
+        if (rc) return rc;
+    }
+    if ((int)c->row_seq_host.size() != B || !std::equal(ids.begin(), ids.end(), c->row_seq_host.begin())) {
+        c->row_seq_host = ids;
+        CK(cudaMemcpyAsync(c->row_seq, ids.data(), B * 4, cudaMemcpyHostToDevice, c->stream));
+    }
+    return MING_OK;
+}
+
+// ---- flow head ----
+
+int cfm_token_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift) {
+    const ming_cfg& f = c->cfg;
+    const int H = f.dit_hidden, LAT = f.dit_latent, R = 6 * B;
+    cudaStream_t s = c->stream;
+    run_linear(c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, 2 * B,
+               s);
+    run_linear(c->x_emb.w, ProPlain{c->f_hist, LAT, 0}, EpiAct{c->f_xh, nullptr, c->x_emb.w.bias, H, 0, H}, B, s);
+    for (int st = 0; st < 10; st++) {
+        run_linear(c->x_emb.w, ProPlain{c->f_y, LAT, 0}, EpiAct{c->f_xy, nullptr, c->x_emb.w.bias, H, 0, H}, B, s);
+        launch_tok_rows(c->temb + (size_t)st * H, c->f_ce, c->f_xh, c->f_xy, c->f_rows, B, H, s);
+        for (auto& b : c->dit) {
+            run_linear(b.qkv.w, ProRms{c->f_rows, b.norm1, H, H, 1e-6f, 0, nullptr},
+                       EpiDitQKV{b.qkv.w.bias, c->f_qkv, c->inv_freq, H, 3, R}, R, s);
+            launch_dit_attention(c->f_qkv, c->f_att, R, 3, H, f.dit_heads, s);
+            run_linear(b.o.w, ProPlain{c->f_att, H, 0}, EpiResidual{c->f_rows, c->f_x1, b.o.w.bias, H}, R, s);
+            run_linear(b.ff1.w, ProRms{c->f_x1, b.norm2, H, H, 1e-6f, 0, nullptr},
+                       EpiAct{c->f_hh, nullptr, b.ff1.w.bias, f.dit_ff, 1, f.dit_ff}, R, s);
+            run_linear(b.ff2.w, ProPlain{c->f_hh, f.dit_ff, 0}, EpiResidual{c->f_x1, c->f_rows, b.ff2.w.bias, H}, R, s);
+        }
+        launch_tok_final(c->f_rows, c->final_norm, c->final_w, c->final_b, c->f_y, with_sde ? c->f_sde : nullptr, st,
+                         c->flow_dt[st], c->flow_sq[st], cfg, shift, B, H, LAT, s);
+    }
+    return MING_OK;
+}
+
+int cfm_ada_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift) {
+    const ming_cfg& f = c->cfg;
+    const int H = f.dit_hidden, LAT = f.dit_latent, F = f.dit_frames, NC = 2 * B, R = NC * F;
+    cudaStream_t s = c->stream;
+    run_linear(c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, NC, s);
+    for (int st = 0; st < 10; st++) {
+        launch_ada_cond(c->temb + (size_t)st * H, c->f_ce, c->f_sc, NC, H, s);
+        run_linear(c->x_emb.w, ProLatent{c->f_y, B, F, LAT, 0}, EpiAct{c->f_rows, nullptr, c->x_emb.w.bias, H, 0, H}, R, s);
+        for (auto& b : c->dit) {
+            const int MS = 6 * H;
+            run_linear(b.ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{c->f_mod, nullptr, b.ada.w.bias, MS, 0, MS}, NC, s);
+            run_linear(b.qkv.w, ProLnMod{c->f_rows, c->f_mod, c->f_mod + H, H, MS, H, F, 0, nullptr},
+                       EpiDitQKV{b.qkv.w.bias, c->f_qkv, c->inv_freq, H, F, R}, R, s);
+            launch_dit_attention(c->f_qkv, c->f_att, R, F, H, f.dit_heads, s);
+            run_linear(b.o.w, ProPlain{c->f_att, H, 0}, EpiGatedRes{c->f_rows, c->f_rows, b.o.w.bias, c->f_mod + 2 * H, H, MS, F},
+                       R, s);
+            run_linear(b.ff1.w, ProLnMod{c->f_rows, c->f_mod + 3 * H, c->f_mod + 4 * H, H, MS, H, F, 0, nullptr},
+                       EpiAct{c->f_hh, nullptr, b.ff1.w.bias, f.dit_ff, 1, f.dit_ff}, R, s);
+            run_linear(b.ff2.w, ProPlain{c->f_hh, f.dit_ff, 0},
+                       EpiGatedRes{c->f_rows, c->f_rows, b.ff2.w.bias, c->f_mod + 5 * H, H, MS, F}, R, s);
+        }
+        run_linear(c->final_ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{c->f_mod, nullptr, c->final_ada.w.bias, 2 * H, 0, 2 * H},
+                   NC, s);
+        run_linear(c->final_lin.w, ProLnMod{c->f_rows, c->f_mod, c->f_mod + H, H, 2 * H, H, F, 0, nullptr},
+                   EpiAct{nullptr, c->f_vel, c->final_lin.w.bias, LAT, 3, LAT}, R, s);
+        launch_ada_euler(c->f_vel, c->f_y, with_sde ? c->f_sde : nullptr, st, c->flow_dt[st], c->flow_sq[st], cfg, shift, B,
+                         F, LAT, s);
+    }
+    return MING_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------
+
+extern "C" {
+
+const char* ming_cuda_last_error(void) { return g_err.c_str(); }
+
+void ming_cuda_default_cfg(ming_cfg* c) {
+    std::memset(c, 0, sizeof(*c));
+    c->hidden = 896;
+    c->layers = 24;
+    c->heads = 14;
+    c->kv_heads = 2;
+    c->head_dim = 64;
+    c->ff = 4864;
+    c->rope_theta = 1e6f;
+    c->rms_eps = 1e-6f;
+    c->weight_bits = 16;
+    c->group_size = 64;
+    c->page_size = 16;
+    c->max_seqs = 64;
+    c->max_ctx = 4096;
+    c->max_pages = 4096;
+    c->max_batch = 64;
+    c->max_prefill = 256;
+    c->dit_mode = MING_DIT_TOKEN;
+    c->dit_hidden = 1024;
+    c->dit_blocks = 8;
+    c->dit_heads = 16;
+    c->dit_ff = 4096;
+    c->dit_latent = 64;
+    c->dit_frames = 1;
+    c->dit_cond_dim = 896;
+    c->dit_freq_dim = 256;
+    c->dit_max_batch = 32;
+    c->agg_blocks = 8;
+}
+
+int ming_cuda_create(int device, const ming_cfg* cfg, ming_ctx** out) {
+    if (!cfg || !out) return fail(MING_ERR_INVALID, "null argument");
+    const ming_cfg& f = *cfg;
+    if (f.head_dim != 64) return fail(MING_ERR_INVALID, "head_dim must be 64");
+    if (f.page_size != PAGE) return fail(MING_ERR_INVALID, "page_size must be 16");
+    if (f.hidden % 64 || f.ff % 64 || f.hidden != f.heads * 64)
+        return fail(MING_ERR_INVALID, "hidden and ff must be multiples of 64, hidden = heads*64");
+    if (f.kv_heads < 1 || f.heads % f.kv_heads || f.heads / f.kv_heads > 8)
+        return fail(MING_ERR_INVALID, "heads must be a multiple of kv_heads with at most 8 per group");
+    if (f.group_size != 64) return fail(MING_ERR_INVALID, "group_size must be 64");
+    if (f.max_ctx < PAGE || f.max_ctx % ATT_SPLIT) return fail(MING_ERR_INVALID, "max_ctx must be a multiple of 256");
+    if (f.max_batch < 1 || f.max_batch > 256 || f.max_prefill < 1 || f.max_seqs < 1 || f.max_pages < 1)
+        return fail(MING_ERR_INVALID, "bad batch/prefill/sequence/page limits");
+    if (f.dit_mode != MING_DIT_NONE) {
+        if (f.dit_hidden % 64 || f.dit_ff % 64 || f.dit_hidden != f.dit_heads * 64 || f.dit_latent % 16 ||
+            f.dit_cond_dim % 64 || f.dit_freq_dim % 64 || f.dit_max_batch < 1)
+            return fail(MING_ERR_INVALID, "bad flow-head shape");
+        if (f.dit_mode == MING_DIT_TOKEN && f.dit_frames != 1) return fail(MING_ERR_INVALID, "token mode has one frame");
+        if (f.dit_mode == MING_DIT_ADALN && (f.dit_frames < 1 || f.dit_frames > 16))
+            return fail(MING_ERR_INVALID, "adaLN frames must be 1..16");
+    }
+    int ndev = 0;
+    CK(cudaGetDeviceCount(&ndev));
+    if (device < 0 || device >= ndev) return fail(MING_ERR_INVALID, "no such CUDA device");
+    CK(cudaSetDevice(device));
+    std::unique_ptr<ming_ctx> c(new ming_ctx());
+    c->device = device;
+    c->cfg = f;
+    CK(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    *out = c.release();
+    return MING_OK;
+}
+
+int ming_cuda_load_tensor(ming_ctx* c, const char* name, int dtype, const int64_t* shape, int ndim, const void* host) {
+    if (!c || !name || (!shape && ndim) || !host || ndim < 0 || ndim > 4) return fail(MING_ERR_INVALID, "bad argument");
+    if (c->finalized) return fail(MING_ERR_INVALID, "context already finalized");
+    if (dtype != MING_DTYPE_BF16 && dtype != MING_DTYPE_F32 && dtype != MING_DTYPE_U32)
+        return fail(MING_ERR_INVALID, "unsupported dtype");
+    HostTensor t;
+    t.dtype = dtype;
+    int64_t n = 1;
+    for (int i = 0; i < ndim; i++) {
+        if (shape[i] < 0) return fail(MING_ERR_INVALID, "negative dimension");
+        t.shape.push_back(shape[i]);
+        n *= shape[i];
+    }
+    const size_t bytes = (size_t)n * (dtype == MING_DTYPE_BF16 ? 2 : 4);
+    t.data.resize(bytes);
+    std::memcpy(t.data.data(), host, bytes);
+    c->staged[name] = std::move(t);
+    return MING_OK;
+}
+
+int ming_cuda_finalize(ming_ctx* c) {
+    if (!c) return fail(MING_ERR_INVALID, "null context");
+    if (c->finalized) return MING_OK;
+    CK(cudaSetDevice(c->device));
+    const ming_cfg& f = c->cfg;
+    int rc;
+    // ---- LM (layers == 0: a flow-head-only context) ----
+    c->layers.resize(f.layers);
+    const int H = f.hidden, QD = f.heads * 64, KD = f.kv_heads * 64;
+    for (int l = 0; l < f.layers; l++) {
+        const std::string p = "model.model.layers." + std::to_string(l);
+        auto& L = c->layers[l];
+        LinearSrc q, k, v, o, g, u, d;
+        if ((rc = lin_src(c, p + ".self_attn.q_proj", q, true))) return rc;
+        if ((rc = lin_src(c, p + ".self_attn.k_proj", k, true))) return rc;
+        if ((rc = lin_src(c, p + ".self_attn.v_proj", v, true))) return rc;
+        if ((rc = lin_src(c, p + ".self_attn.o_proj", o, false))) return rc;
+        if ((rc = lin_src(c, p + ".mlp.gate_proj", g, false))) return rc;
+        if ((rc = lin_src(c, p + ".mlp.up_proj", u, false))) return rc;
+        if ((rc = lin_src(c, p + ".mlp.down_proj", d, false))) return rc;
+        if (q.out != QD || k.out != KD || v.out != KD || q.in != H || o.out != H || o.in != QD || g.out != f.ff ||
+            u.out != f.ff || d.out != H || d.in != f.ff)
+            return fail(MING_ERR_INVALID, p + ": linear shapes do not match the config");
+        if (q.fmt != f.weight_bits || o.fmt != f.weight_bits || g.fmt != f.weight_bits || d.fmt != f.weight_bits)
+            return fail(MING_ERR_INVALID, p + ": weight format differs from cfg.weight_bits");
+        // q|k|v: tile t of a block covers head t/4, dims d0 = 8(t%4)..+7 and d0+32..+39
+        std::vector<RowRef> rows;
+        const int nh[3] = {f.heads, f.kv_heads, f.kv_heads};
+        for (int b = 0; b < 3; b++)
+            for (int t = 0; t < nh[b] * 4; t++)
+                for (int r = 0; r < 16; r++) {
+                    const int h = t / 4, d0 = (t % 4) * 8;
+                    rows.push_back({b, h * 64 + (r < 8 ? d0 + r : 32 + d0 + r - 8)});
+                }
+        if ((rc = upload_packed(c, {q, k, v},
+                                {p + ".self_attn.q_proj.weight", p + ".self_attn.k_proj.weight", p + ".self_attn.v_proj.weight"},
+                                rows, L.qkv)))
+            return rc;
+        rows.clear();
+        for (int i = 0; i < H; i++) rows.push_back({0, i});
+        if ((rc = upload_packed(c, {o}, {p + ".self_attn.o_proj.weight"}, rows, L.o))) return rc;
+        if ((rc = upload_packed(c, {d}, {p + ".mlp.down_proj.weight"}, rows, L.down))) return rc;
+        rows.clear();
+        for (int t = 0; t < f.ff / 8; t++)
+            for (int r = 0; r < 16; r++) rows.push_back({r < 8 ? 0 : 1, t * 8 + (r & 7)});
+        if ((rc = upload_packed(c, {g, u}, {p + ".mlp.gate_proj.weight", p + ".mlp.up_proj.weight"}, rows, L.gu))) return rc;
+        if ((rc = upload_raw(c, p + ".input_layernorm.weight", MING_DTYPE_BF16, H, (void**)&L.ln1))) return rc;
+        if ((rc = upload_raw(c, p + ".post_attention_layernorm.weight", MING_DTYPE_BF16, H, (void**)&L.ln2))) return rc;
+    }
+    if (f.layers > 0) {
+        if ((rc = upload_raw(c, "model.model.norm.weight", MING_DTYPE_BF16, H, (void**)&c->norm))) return rc;
+        if ((rc = upload_raw(c, "stop_head.weight", MING_DTYPE_BF16, 2 * H, (void**)&c->stop_w))) return rc;
+        if ((rc = upload_raw(c, "stop_head.bias", MING_DTYPE_BF16, 2, (void**)&c->stop_b))) return rc;
+    }
+    c->log2_theta = log2f(f.rope_theta);
+
+    // ---- KV pool, step state, activations ----
+    c->bt_ld = f.max_ctx / PAGE;
+    c->nsplit = f.max_ctx / ATT_SPLIT;
+    c->maxr = std::max(f.max_batch, f.max_prefill);
+    const size_t page_elems = (size_t)f.layers * 2 * f.kv_heads * PAGE * 64;
+    rc = MING_OK;
+    c->pool = c->mem.alloc<uint16_t>((size_t)f.max_pages * page_elems, &rc);
+    c->bt = c->mem.alloc<int>((size_t)f.max_seqs * c->bt_ld, &rc);
+    c->x = c->mem.alloc<uint16_t>((size_t)c->maxr * H, &rc);
+    c->x1 = c->mem.alloc<uint16_t>((size_t)c->maxr * H, &rc);
+    c->q = c->mem.alloc<uint16_t>((size_t)c->maxr * QD, &rc);
+    c->h = c->mem.alloc<uint16_t>((size_t)c->maxr * f.ff, &rc);
+    c->z = c->mem.alloc<uint16_t>((size_t)c->maxr * H, &rc);
+    c->stop = c->mem.alloc<float>(c->maxr, &rc);
+    c->part = c->mem.alloc<float>((size_t)c->maxr * c->nsplit * f.heads * PART_STRIDE, &rc);
+    c->seq_len = c->mem.alloc<int>(f.max_seqs, &rc);
+    c->row_seq = c->mem.alloc<int>(c->maxr, &rc);
+    c->row_pos = c->mem.alloc<int>(c->maxr, &rc);
+    c->step_counter = c->mem.alloc<int>(2, &rc);
+    c->out_cell = c->mem.alloc<uint16_t*>(1, &rc);
+    c->stop_cell = c->mem.alloc<float*>(1, &rc);
+    if (rc) return rc;
+    c->bt_host.assign((size_t)f.max_seqs * c->bt_ld, -1);
+    CK(cudaMemcpy(c->bt, c->bt_host.data(), c->bt_host.size() * 4, cudaMemcpyHostToDevice));
+    for (int p = f.max_pages - 1; p >= 0; p--) c->free_pages.push_back(p);
+    c->seqs.assign(f.max_seqs, SeqInfo{});
+
+    // ---- flow head ----
+    if (f.dit_mode != MING_DIT_NONE) {
+        const int DH = f.dit_hidden, LAT = f.dit_latent, MB = f.dit_max_batch;
+        const bool ada = f.dit_mode == MING_DIT_ADALN;
+        const std::string F = ada ? "adaln_head" : "flowloss.cfm.model";
+        if ((rc = load_dit_blocks(c, F, f.dit_blocks, DH, ada, c->dit))) return rc;
+        if ((rc = pack_plain(c, F + ".t_embedder.time_mlp.0", true, c->t_mlp0))) return rc;
+        if ((rc = pack_plain(c, F + ".t_embedder.time_mlp.2", true, c->t_mlp2))) return rc;
+        if ((rc = pack_plain(c, F + ".x_embedder", true, c->x_emb))) return rc;
+        if ((rc = pack_plain(c, F + ".c_embedder.cond_embedder", true, c->c_emb))) return rc;
+        if ((rc = upload_raw(c, F + ".rotary_embed.inv_freq", MING_DTYPE_F32, 32, (void**)&c->inv_freq))) return rc;
+        if (ada) {
+            if ((rc = pack_plain(c, F + ".final_layer.adaLN_modulation.1", true, c->final_ada))) return rc;
+            if ((rc = pack_plain(c, F + ".final_layer.linear", true, c->final_lin))) return rc;
+        } else {
+            if ((rc = upload_raw(c, F + ".final_layer.norm_final.weight", MING_DTYPE_BF16, DH, (void**)&c->final_norm))) return rc;
+            if ((rc = upload_raw(c, F + ".final_layer.linear.weight", MING_DTYPE_BF16, (int64_t)LAT * DH, (void**)&c->final_w)))
+                return rc;
+            if ((rc = upload_raw(c, F + ".final_layer.linear.bias", MING_DTYPE_BF16, LAT, (void**)&c->final_b))) return rc;
+        }
+        if (c->c_emb.w.K != f.dit_cond_dim || c->x_emb.w.K != LAT || c->t_mlp0.w.K != f.dit_freq_dim)
+            return fail(MING_ERR_INVALID, "flow head input dims do not match the config");
+        const int F_ = f.dit_frames, rows = ada ? 2 * MB * F_ : 6 * MB;
+        rc = MING_OK;
+        c->f_zc = c->mem.alloc<uint16_t>((size_t)2 * MB * f.dit_cond_dim, &rc);
+        c->f_hist = c->mem.alloc<uint16_t>((size_t)MB * LAT, &rc);
+        c->f_y = c->mem.alloc<uint16_t>((size_t)MB * F_ * LAT, &rc);
+        c->f_sde = c->mem.alloc<uint16_t>((size_t)10 * MB * F_ * LAT, &rc);
+        c->f_ce = c->mem.alloc<uint16_t>((size_t)2 * MB * DH, &rc);
+        c->f_xh = c->mem.alloc<uint16_t>((size_t)MB * DH, &rc);
+        c->f_xy = c->mem.alloc<uint16_t>((size_t)MB * DH, &rc);
+        c->f_rows = c->mem.alloc<uint16_t>((size_t)rows * DH, &rc);
+        c->f_x1 = c->mem.alloc<uint16_t>((size_t)rows * DH, &rc);
+        c->f_qkv = c->mem.alloc<uint16_t>((size_t)3 * rows * DH, &rc);
+        c->f_att = c->mem.alloc<uint16_t>((size_t)rows * DH, &rc);
+        c->f_hh = c->mem.alloc<uint16_t>((size_t)rows * f.dit_ff, &rc);
+        c->f_sc = c->mem.alloc<uint16_t>((size_t)2 * MB * DH, &rc);
+        c->f_mod = c->mem.alloc<uint16_t>((size_t)2 * MB * 6 * DH, &rc);
+        c->f_vel = c->mem.alloc<float>((size_t)rows * LAT, &rc);
+        if (rc) return rc;
+        if ((rc = build_temb(c, f.dit_freq_dim, DH))) return rc;
+    }
+    // ---- aggregator ----
+    if (f.agg_blocks > 0 && f.dit_mode == MING_DIT_TOKEN) {
+        const int DH = f.dit_hidden, MB = f.dit_max_batch;
+        const std::string A = "linear_proj_audio";
+        if ((rc = load_dit_blocks(c, A, f.agg_blocks, DH, false, c->agg))) return rc;
+        if ((rc = pack_plain(c, A + ".x_embedder", true, c->agg_x_emb))) return rc;
+        if ((rc = pack_plain(c, A + ".final_layer.linear", true, c->agg_final))) return rc;
+        if ((rc = upload_raw(c, A + ".word_embedder.weight", MING_DTYPE_BF16, DH, (void**)&c->agg_cls))) return rc;
+        if ((rc = upload_raw(c, A + ".final_layer.norm_final.weight", MING_DTYPE_BF16, DH, (void**)&c->agg_norm))) return rc;
+        if ((rc = upload_raw(c, A + ".rotary_embed.inv_freq", MING_DTYPE_F32, 32, (void**)&c->agg_inv_freq))) return rc;
+        rc = MING_OK;
+        c->a_lat = c->mem.alloc<uint16_t>((size_t)MB * f.dit_latent, &rc);
+        c->a_xe = c->mem.alloc<uint16_t>((size_t)MB * DH, &rc);
+        c->a_rows = c->mem.alloc<uint16_t>((size_t)2 * MB * DH, &rc);
+        c->a_x1 = c->mem.alloc<uint16_t>((size_t)2 * MB * DH, &rc);
+        c->a_qkv = c->mem.alloc<uint16_t>((size_t)6 * MB * DH, &rc);
+        c->a_att = c->mem.alloc<uint16_t>((size_t)2 * MB * DH, &rc);
+        c->a_hh = c->mem.alloc<uint16_t>((size_t)2 * MB * f.dit_ff, &rc);
+        c->a_out = c->mem.alloc<uint16_t>((size_t)MB * f.hidden, &rc);
+        if (rc) return rc;
+    }
+    CK(cudaDeviceSynchronize());
+    c->staged.clear();
+    c->finalized = true;
+    return MING_OK;
+}
+
+int ming_cuda_seq_alloc(ming_ctx* c, int* id) {
+    if (!c || !id || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
+    for (int i = 0; i < (int)c->seqs.size(); i++)
+        if (!c->seqs[i].live) {
+            c->seqs[i] = SeqInfo{true, 0};
+            const int zero = 0;
+            CK(cudaMemcpyAsync(c->seq_len + i, &zero, 4, cudaMemcpyHostToDevice, c->stream));
+            *id = i;
+            return MING_OK;
+        }
+    return fail(MING_ERR_NOMEM, "all sequence slots are in use");
+}
+
+int ming_cuda_seq_free(ming_ctx* c, int id) {
+    if (!c) return fail(MING_ERR_INVALID, "null context");
+    int rc = check_seq(c, id);
+    if (rc) return rc;
+    CK(cudaStreamSynchronize(c->stream));  // no kernel may still read its pages
+    for (int p = 0; p < c->bt_ld; p++) {
+        int& e = c->bt_host[(size_t)id * c->bt_ld + p];
+        if (e >= 0) c->free_pages.push_back(e);
+        e = -1;
+    }
+    CK(cudaMemcpy(c->bt + (size_t)id * c->bt_ld, c->bt_host.data() + (size_t)id * c->bt_ld, c->bt_ld * 4,
+                  cudaMemcpyHostToDevice));
+    c->seqs[id] = SeqInfo{};
+    return MING_OK;
+}
+
+int ming_cuda_seq_len(ming_ctx* c, int id, int* len) {
+    if (!c || !len) return fail(MING_ERR_INVALID, "null argument");
+    int rc = check_seq(c, id);
+    if (rc) return rc;
+    *len = c->seqs[id].len;
+    return MING_OK;
+}
+
+int ming_cuda_seq_truncate(ming_ctx* c, int id, int len) {
+    if (!c) return fail(MING_ERR_INVALID, "null context");
+    int rc = check_seq(c, id);
+    if (rc) return rc;
+    if (len < 0 || len > c->seqs[id].len) return fail(MING_ERR_INVALID, "truncate length out of range");
+    c->seqs[id].len = len;
+    CK(cudaMemcpyAsync(c->seq_len + id, &c->seqs[id].len, 4, cudaMemcpyHostToDevice, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    return MING_OK;
+}
+
+int ming_cuda_lm_prefill(ming_ctx* c, int s, const uint16_t* x, int L, uint16_t* out, float* stop, int kind) {
+    if (!c || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
+    if (c->cfg.layers < 1) return fail(MING_ERR_INVALID, "no LM configured");
+    if (!x || L < 1) return fail(MING_ERR_INVALID, "empty prompt");
+    int rc = check_seq(c, s);
+    if (rc) return rc;
+    CK(cudaSetDevice(c->device));
+    const int H = c->cfg.hidden, start = c->seqs[s].len;
+    if ((rc = ensure_pages(c, s, start, start + L))) return rc;
+    c->row_seq_host.clear();  // row_seq is overwritten below
+    std::vector<int> seqv(c->cfg.max_prefill, s), posv(c->cfg.max_prefill);
+    for (int c0 = 0; c0 < L; c0 += c->cfg.max_prefill) {
+        const int n = std::min(c->cfg.max_prefill, L - c0);
+        for (int r = 0; r < n; r++) posv[r] = start + c0 + r;
+        CK(cudaMemcpyAsync(c->row_seq, seqv.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(c->row_pos, posv.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+        if ((rc = copy_in(c, c->x, x + (size_t)c0 * H, (size_t)n * H * 2, kind))) return rc;
+        enqueue_layers(c, n);
+        if (out || stop) {
+            launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, nullptr, step_dev(c), H, 0, 0,
+                                   c->cfg.rms_eps},
+                         n, c->stream);
+            if ((rc = copy_out(c, out ? out + (size_t)c0 * H : nullptr, c->z, (size_t)n * H * 2, kind))) return rc;
+            if ((rc = copy_out(c, stop ? stop + c0 : nullptr, c->stop, (size_t)n * 4, kind))) return rc;
+        }
+        if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(c->stream));
+    }
+    CK(cudaGetLastError());
+    c->seqs[s].len = start + L;
+    CK(cudaMemcpyAsync(c->seq_len + s, &c->seqs[s].len, 4, cudaMemcpyHostToDevice, c->stream));
+    if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(c->stream));
+    return MING_OK;
+}
+
+int ming_cuda_lm_decode(ming_ctx* c, int B, const int* ids, const uint16_t* x, uint16_t* out, float* stop, int kind) {
+    if (!c || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
+    if (c->cfg.layers < 1) return fail(MING_ERR_INVALID, "no LM configured");
+    if (!ids || !x) return fail(MING_ERR_INVALID, "null argument");
+    CK(cudaSetDevice(c->device));
+    int rc = prepare_rows(c, B, ids, 1);
+    if (rc) return rc;
+    const int H = c->cfg.hidden;
+    cudaGraphExec_t g;
+    if ((rc = decode_graph(c, B, &g))) return rc;
+    uint16_t* null_out = nullptr;
+    float* null_stop = nullptr;
+    CK(cudaMemcpyAsync(c->out_cell, &null_out, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->stop_cell, &null_stop, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
+    if ((rc = copy_in(c, c->x, x, (size_t)B * H * 2, kind))) return rc;
+    CK(cudaGraphLaunch(g, c->stream));
+    for (int i = 0; i < B; i++) c->seqs[ids[i]].len += 1;
+    if ((rc = copy_out(c, out, c->z, (size_t)B * H * 2, kind))) return rc;
+    if ((rc = copy_out(c, stop, c->stop, (size_t)B * 4, kind))) return rc;
+    if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(c->stream));
+    return MING_OK;
+}
+
+int ming_cuda_lm_generate(ming_ctx* c, int B, const int* ids, const uint16_t* x0, int steps, uint16_t* out, float* stop,
+                          int kind) {
+    if (!c || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
+    if (c->cfg.layers < 1) return fail(MING_ERR_INVALID, "no LM configured");
+    if (!ids || !x0 || steps < 1) return fail(MING_ERR_INVALID, "bad argument");
+    CK(cudaSetDevice(c->device));
+    int rc = prepare_rows(c, B, ids, steps);
+    if (rc) return rc;
+    const int H = c->cfg.hidden;
+    cudaGraphExec_t g;
+    if ((rc = decode_graph(c, B, &g))) return rc;
+    uint16_t* o = nullptr;
+    float* sp = nullptr;
+    if (out) {
+        if (kind == MING_PTR_DEVICE) o = out;
+        else {
+            const size_t need = (size_t)steps * B * H;
+            if (c->gen_out_elems < need) {
+                if (c->gen_out) cudaFree(c->gen_out);
+                c->gen_out = nullptr;
+                c->gen_out_elems = 0;
+                CK(cudaMalloc(&c->gen_out, need * 2));
+                c->gen_out_elems = need;
+            }
+            o = c->gen_out;
+        }
+    }
+    if (stop) {
+        if (kind == MING_PTR_DEVICE) sp = stop;
+        else {
+            const size_t need = (size_t)steps * B;
+            if (c->gen_stop_elems < need) {
+                if (c->gen_stop) cudaFree(c->gen_stop);
+                c->gen_stop = nullptr;
+                c->gen_stop_elems = 0;
+                CK(cudaMalloc(&c->gen_stop, need * 4));
+                c->gen_stop_elems = need;
+            }
+            sp = c->gen_stop;
+        }
+    }
+    CK(cudaMemcpyAsync(c->out_cell, &o, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemcpyAsync(c->stop_cell, &sp, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
+    CK(cudaMemsetAsync(c->step_counter, 0, 8, c->stream));
+    if ((rc = copy_in(c, c->x, x0, (size_t)B * H * 2, kind))) return rc;
+    for (int i = 0; i < steps; i++) CK(cudaGraphLaunch(g, c->stream));
+    for (int i = 0; i < B; i++) c->seqs[ids[i]].len += steps;
+    if (kind == MING_PTR_HOST) {
+        if (out) CK(cudaMemcpyAsync(out, o, (size_t)steps * B * H * 2, cudaMemcpyDeviceToHost, c->stream));
+        if (stop) CK(cudaMemcpyAsync(stop, sp, (size_t)steps * B * 4, cudaMemcpyDeviceToHost, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+    }
+    return MING_OK;
+}
+
+int ming_cuda_cfm_sample(ming_ctx* c, int B, const uint16_t* z, const uint16_t* hist, const uint16_t* noise,
+                         const uint16_t* sde, float cfg, float shift, uint16_t* y, int kind) {
+    if (!c || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
+    const ming_cfg& f = c->cfg;
+    if (f.dit_mode == MING_DIT_NONE) return fail(MING_ERR_INVALID, "no flow head configured");
+    if (B < 1 || B > f.dit_max_batch) return fail(MING_ERR_INVALID, "flow batch out of range");
+    const bool ada = f.dit_mode == MING_DIT_ADALN;
+    if (!z || !noise || !y || (!ada && !hist)) return fail(MING_ERR_INVALID, "null argument");
+    CK(cudaSetDevice(c->device));
+    const int LAT = f.dit_latent, F = f.dit_frames, CD = f.dit_cond_dim;
+    int rc;
+    // inputs: z rows then zeros (the unconditional half), hist, noise, sde
+    CK(cudaMemsetAsync(c->f_zc + (size_t)B * CD, 0, (size_t)B * CD * 2, c->stream));
+    if ((rc = copy_in(c, c->f_zc, z, (size_t)B * CD * 2, kind))) return rc;
+    if (!ada && (rc = copy_in(c, c->f_hist, hist, (size_t)B * LAT * 2, kind))) return rc;
+    if ((rc = copy_in(c, c->f_y, noise, (size_t)B * F * LAT * 2, kind))) return rc;
+    if (sde && (rc = copy_in(c, c->f_sde, sde, (size_t)10 * B * F * LAT * 2, kind))) return rc;
+    if (cfg != c->cfm_cfg || shift != c->cfm_shift) {  // scalars are baked into the graphs
+        for (auto& kv : c->cfm_graphs) cudaGraphExecDestroy(kv.second);
+        c->cfm_graphs.clear();
+        c->cfm_cfg = cfg;
+        c->cfm_shift = shift;
+    }
+    const auto key = std::make_pair(B, sde ? 1 : 0);
+    auto it = c->cfm_graphs.find(key);
+    if (it == c->cfm_graphs.end()) {
+        cudaGraph_t g;
+        CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        if (ada) cfm_ada_enqueue(c, B, sde != nullptr, cfg, shift);
+        else cfm_token_enqueue(c, B, sde != nullptr, cfg, shift);
+        cudaError_t ce = cudaStreamEndCapture(c->stream, &g);
+        if (ce != cudaSuccess) return fail(MING_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+        cudaGraphExec_t ge;
+        ce = cudaGraphInstantiate(&ge, g, 0);
+        cudaGraphDestroy(g);
+        if (ce != cudaSuccess) return fail(MING_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+        it = c->cfm_graphs.emplace(key, ge).first;
+    }
+    CK(cudaGraphLaunch(it->second, c->stream));
+    if ((rc = copy_out(c, y, c->f_y, (size_t)B * F * LAT * 2, kind))) return rc;
+    if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(c->stream));
+    return MING_OK;
+}
+
+int ming_cuda_aggregate(ming_ctx* c, int B, const uint16_t* latent, uint16_t* out, int kind) {
+    if (!c || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
+    const ming_cfg& f = c->cfg;
+    if (c->agg.empty()) return fail(MING_ERR_INVALID, "no aggregator configured");
+    if (B < 1 || B > f.dit_max_batch || !latent || !out) return fail(MING_ERR_INVALID, "bad argument");
+    CK(cudaSetDevice(c->device));
+    const int H = f.dit_hidden, R = 2 * B;
+    cudaStream_t s = c->stream;
+    int rc;
+    if ((rc = copy_in(c, c->a_lat, latent, (size_t)B * f.dit_latent * 2, kind))) return rc;
+    run_linear(c->agg_x_emb.w, ProPlain{c->a_lat, f.dit_latent, 0}, EpiAct{c->a_xe, nullptr, c->agg_x_emb.w.bias, H, 0, H}, B,
+               s);
+    // rows [cls, x_emb(latent)] per sequence
+    for (int b = 0; b < B; b++) {
+        CK(cudaMemcpyAsync(c->a_rows + (size_t)(2 * b) * H, c->agg_cls, (size_t)H * 2, cudaMemcpyDeviceToDevice, s));
+        CK(cudaMemcpyAsync(c->a_rows + (size_t)(2 * b + 1) * H, c->a_xe + (size_t)b * H, (size_t)H * 2,
+                           cudaMemcpyDeviceToDevice, s));
+    }
+    for (auto& b : c->agg) {
+        run_linear(b.qkv.w, ProRms{c->a_rows, b.norm1, H, H, 1e-6f, 0, nullptr},
+                   EpiDitQKV{b.qkv.w.bias, c->a_qkv, c->agg_inv_freq, H, 2, R}, R, s);
+        launch_dit_attention(c->a_qkv, c->a_att, R, 2, H, f.dit_heads, s);
+        run_linear(b.o.w, ProPlain{c->a_att, H, 0}, EpiResidual{c->a_rows, c->a_x1, b.o.w.bias, H}, R, s);
+        run_linear(b.ff1.w, ProRms{c->a_x1, b.norm2, H, H, 1e-6f, 0, nullptr},
+                   EpiAct{c->a_hh, nullptr, b.ff1.w.bias, f.dit_ff, 1, f.dit_ff}, R, s);
+        run_linear(b.ff2.w, ProPlain{c->a_hh, f.dit_ff, 0}, EpiResidual{c->a_x1, c->a_rows, b.ff2.w.bias, H}, R, s);
+    }
+    // final RMSNorm + linear on each CLS row (row stride 2H selects them)
+    run_linear(c->agg_final.w, ProRms{c->a_rows, c->agg_norm, 2 * H, H, 1e-6f, 0, nullptr},
+               EpiAct{c->a_out, nullptr, c->agg_final.w.bias, f.hidden, 0, f.hidden}, B, s);
+    CK(cudaGetLastError());
+    if ((rc = copy_out(c, out, c->a_out, (size_t)B * f.hidden * 2, kind))) return rc;
+    if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(s));
+    return MING_OK;
+}
+
+int ming_cuda_get_stream(ming_ctx* c, void** s) {
+    if (!c || !s) return fail(MING_ERR_INVALID, "null argument");
+    *s = c->stream;
+    return MING_OK;
+}
+
+int ming_cuda_sync(ming_ctx* c) {
+    if (!c) return fail(MING_ERR_INVALID, "null context");
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaGetLastError());
+    return MING_OK;
+}
+
+int ming_cuda_destroy(ming_ctx* c) {
+    if (!c) return MING_OK;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    if (c->gen_out) cudaFree(c->gen_out);
+    if (c->gen_stop) cudaFree(c->gen_stop);
+    delete c;
+    return MING_OK;
+}
+
+int ming_cuda_kv_read(ming_ctx* c, int s, int layer, int pos0, int n, uint16_t* k, uint16_t* v) {
+    if (!c || !c->finalized || !k || !v) return fail(MING_ERR_INVALID, "bad argument");
+    int rc = check_seq(c, s);
+    if (rc) return rc;
+    if (layer < 0 || layer >= c->cfg.layers || pos0 < 0 || n < 0 || pos0 + n > c->seqs[s].len)
+        return fail(MING_ERR_INVALID, "range out of bounds");
+    CK(cudaStreamSynchronize(c->stream));
+    const int KH = c->cfg.kv_heads;
+    for (int p = pos0; p < pos0 + n; p++) {
+        const int page = c->bt_host[(size_t)s * c->bt_ld + p / PAGE];
+        for (int h = 0; h < KH; h++)
+            for (int w = 0; w < 2; w++) {
+                const size_t off = ((((size_t)page * c->cfg.layers + layer) * 2 + w) * KH + h) * (PAGE * 64) + (p % PAGE) * 64;
+                uint16_t* dst = (w == 0 ? k : v) + ((size_t)h * n + (p - pos0)) * 64;
+                CK(cudaMemcpy(dst, c->pool + off, 128, cudaMemcpyDeviceToHost));
+            }
+    }
+    return MING_OK;
+}
+
+int ming_cuda_unpack_linear(ming_ctx* c, const char* name, float* out) {
+    if (!c || !c->finalized || !name || !out) return fail(MING_ERR_INVALID, "bad argument");
+    for (PackedLin* pl : c->all_lins) {
+        for (size_t si = 0; si < pl->src_names.size(); si++) {
+            if (pl->src_names[si] != name) continue;
+            const int K = pl->w.K, nrow = pl->w.ntiles * 16;
+            float* d = nullptr;
+            CK(cudaMalloc(&d, (size_t)nrow * K * 4));
+            unpack_tiles_kernel<<<dim3(pl->w.ntiles, K / 64), 32, 0, c->stream>>>(pl->w, d);
+            std::vector<float> h((size_t)nrow * K);
+            cudaError_t e = cudaMemcpyAsync(h.data(), d, h.size() * 4, cudaMemcpyDeviceToHost, c->stream);
+            if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+            cudaFree(d);
+            if (e != cudaSuccess) return fail(MING_ERR_CUDA, std::string("unpack: ") + cudaGetErrorString(e));
+            for (int i = 0; i < nrow; i++)
+                if (pl->rows[i].src == (int)si)
+                    std::memcpy(out + (size_t)pl->rows[i].row * K, h.data() + (size_t)i * K, (size_t)K * 4);
+            return MING_OK;
+        }
+    }
+    return fail(MING_ERR_INVALID, std::string("no packed linear holds ") + name);
+}
+
+int ming_cuda_flow_temb(ming_ctx* c, uint16_t* te) {
+    if (!c || !c->finalized || !te) return fail(MING_ERR_INVALID, "bad argument");
+    if (!c->temb) return fail(MING_ERR_INVALID, "no flow head configured");
+    CK(cudaMemcpy(te, c->temb, (size_t)10 * c->cfg.dit_hidden * 2, cudaMemcpyDeviceToHost));
+    return MING_OK;
+}
+
+}  // extern "C"

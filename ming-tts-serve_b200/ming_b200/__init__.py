@@ -1,0 +1,249 @@
+"""Python binding of libming_cuda.so (include/ming_cuda.h) — the B200 hot path
+of ming-tts-serve: the Qwen2 LM decode step and the DiT flow head.
+
+This is a thin ctypes mirror of the C ABI, the same calls a Zig host makes
+through `extern` declarations. The library must have been built
+(ming-tts-serve_b200/build.py); there is no CPU fallback: every compute call
+raises if the CUDA library is missing or fails.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+from . import synth  # noqa: F401
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(HERE), "libming_cuda.so")
+
+MING_OK = 0
+DTYPE_BF16, DTYPE_F32, DTYPE_U32 = 0, 1, 2
+PTR_HOST, PTR_DEVICE = 0, 1
+DIT_NONE, DIT_TOKEN, DIT_ADALN = 0, 1, 2
+
+# Exported symbols, in header order (tests check the library exports each).
+SYMBOLS = [
+    "ming_cuda_default_cfg", "ming_cuda_create", "ming_cuda_load_tensor", "ming_cuda_finalize",
+    "ming_cuda_seq_alloc", "ming_cuda_seq_free", "ming_cuda_seq_len", "ming_cuda_seq_truncate",
+    "ming_cuda_lm_prefill", "ming_cuda_lm_decode", "ming_cuda_lm_generate", "ming_cuda_cfm_sample",
+    "ming_cuda_aggregate", "ming_cuda_get_stream", "ming_cuda_sync", "ming_cuda_destroy",
+    "ming_cuda_last_error", "ming_cuda_kv_read", "ming_cuda_unpack_linear", "ming_cuda_flow_temb",
+]
+
+
+class Cfg(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("hidden", "layers", "heads", "kv_heads", "head_dim", "ff")] + [
+        ("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float)] + [
+        (n, ctypes.c_int) for n in (
+            "weight_bits", "group_size", "page_size", "max_seqs", "max_pages", "max_ctx", "max_batch", "max_prefill",
+            "dit_mode", "dit_hidden", "dit_blocks", "dit_heads", "dit_ff", "dit_latent", "dit_frames",
+            "dit_cond_dim", "dit_freq_dim", "dit_max_batch", "agg_blocks")]
+
+
+class MingError(RuntimeError):
+    pass
+
+
+_lib = None
+
+
+def lib():
+    """Loads libming_cuda.so (raises if it has not been built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise MingError(f"{LIB_PATH} is missing: build it with ming-tts-serve_b200/build.py")
+    L = ctypes.CDLL(LIB_PATH)
+    P, I, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+    IP = ctypes.POINTER(ctypes.c_int)
+    sig = {
+        "ming_cuda_default_cfg": (None, [ctypes.POINTER(Cfg)]),
+        "ming_cuda_create": (I, [I, ctypes.POINTER(Cfg), ctypes.POINTER(P)]),
+        "ming_cuda_load_tensor": (I, [P, ctypes.c_char_p, I, ctypes.POINTER(ctypes.c_int64), I, P]),
+        "ming_cuda_finalize": (I, [P]),
+        "ming_cuda_seq_alloc": (I, [P, IP]),
+        "ming_cuda_seq_free": (I, [P, I]),
+        "ming_cuda_seq_len": (I, [P, I, IP]),
+        "ming_cuda_seq_truncate": (I, [P, I, I]),
+        "ming_cuda_lm_prefill": (I, [P, I, P, I, P, P, I]),
+        "ming_cuda_lm_decode": (I, [P, I, IP, P, P, P, I]),
+        "ming_cuda_lm_generate": (I, [P, I, IP, P, I, P, P, I]),
+        "ming_cuda_cfm_sample": (I, [P, I, P, P, P, P, F, F, P, I]),
+        "ming_cuda_aggregate": (I, [P, I, P, P, I]),
+        "ming_cuda_get_stream": (I, [P, ctypes.POINTER(P)]),
+        "ming_cuda_sync": (I, [P]),
+        "ming_cuda_destroy": (I, [P]),
+        "ming_cuda_last_error": (ctypes.c_char_p, []),
+        "ming_cuda_kv_read": (I, [P, I, I, I, I, P, P]),
+        "ming_cuda_unpack_linear": (I, [P, ctypes.c_char_p, P]),
+        "ming_cuda_flow_temb": (I, [P, P]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+def _check(rc):
+    if rc != MING_OK:
+        msg = lib().ming_cuda_last_error().decode(errors="replace")
+        raise MingError(f"ming_cuda error {rc}: {msg}")
+
+
+def default_cfg(**kw):
+    c = Cfg()
+    lib().ming_cuda_default_cfg(ctypes.byref(c))
+    for k, v in kw.items():
+        if not hasattr(c, k):
+            raise KeyError(k)
+        setattr(c, k, v)
+    return c
+
+
+def _ptr(a):
+    """Host numpy array -> void*; device tensor (has data_ptr) -> its address."""
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        return ctypes.c_void_p(a.data_ptr())
+    assert a.flags["C_CONTIGUOUS"], "arrays must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _dtype_code(a):
+    if a.dtype == np.uint16:
+        return DTYPE_BF16
+    if a.dtype == np.float32:
+        return DTYPE_F32
+    if a.dtype == np.uint32:
+        return DTYPE_U32
+    raise TypeError(f"unsupported dtype {a.dtype}")
+
+
+class Context:
+    """One device context (ming_ctx). Mirrors the reference Model's hot-path
+    surface: load, lm_prefill/lm_decode (lmForward), generate (the token loop),
+    cfm_sample (cfmSample), aggregate."""
+
+    def __init__(self, cfg=None, device=0, weights=None):
+        self.cfg = cfg if cfg is not None else default_cfg()
+        self._h = ctypes.c_void_p()
+        _check(lib().ming_cuda_create(device, ctypes.byref(self.cfg), ctypes.byref(self._h)))
+        if weights is not None:
+            self.load(weights)
+            self.finalize()
+
+    def load(self, weights):
+        for name, arr in weights.items():
+            arr = np.ascontiguousarray(arr)
+            shape = (ctypes.c_int64 * arr.ndim)(*arr.shape)
+            _check(lib().ming_cuda_load_tensor(self._h, name.encode(), _dtype_code(arr), shape, arr.ndim, _ptr(arr)))
+
+    def finalize(self):
+        _check(lib().ming_cuda_finalize(self._h))
+
+    def seq_alloc(self):
+        s = ctypes.c_int()
+        _check(lib().ming_cuda_seq_alloc(self._h, ctypes.byref(s)))
+        return s.value
+
+    def seq_free(self, s):
+        _check(lib().ming_cuda_seq_free(self._h, s))
+
+    def seq_len(self, s):
+        n = ctypes.c_int()
+        _check(lib().ming_cuda_seq_len(self._h, s, ctypes.byref(n)))
+        return n.value
+
+    def seq_truncate(self, s, n):
+        _check(lib().ming_cuda_seq_truncate(self._h, s, n))
+
+    def prefill(self, s, x, want_out=True):
+        """x: uint16 [L, hidden] host array -> (out [L, hidden] uint16, stop [L] f32)."""
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        L = x.shape[0]
+        out = np.empty_like(x) if want_out else None
+        stop = np.empty(L, dtype=np.float32) if want_out else None
+        _check(lib().ming_cuda_lm_prefill(self._h, s, _ptr(x), L, _ptr(out), _ptr(stop), PTR_HOST))
+        return out, stop
+
+    def decode(self, seqs, x):
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        B = len(seqs)
+        ids = (ctypes.c_int * B)(*seqs)
+        out = np.empty_like(x)
+        stop = np.empty(B, dtype=np.float32)
+        _check(lib().ming_cuda_lm_decode(self._h, B, ids, _ptr(x), _ptr(out), _ptr(stop), PTR_HOST))
+        return out, stop
+
+    def generate(self, seqs, x0, steps, kind=PTR_HOST, out=None, stop=None):
+        """steps decode steps feeding each output back. Host mode returns
+        (out [steps, B, hidden], stop [steps, B]); device mode takes device
+        tensors (anything with data_ptr()) and returns them."""
+        B = len(seqs)
+        ids = (ctypes.c_int * B)(*seqs)
+        if kind == PTR_HOST:
+            x0 = np.ascontiguousarray(x0, dtype=np.uint16)
+            if out is None:
+                out = np.empty((steps, B, x0.shape[-1]), dtype=np.uint16)
+            if stop is None:
+                stop = np.empty((steps, B), dtype=np.float32)
+        _check(lib().ming_cuda_lm_generate(self._h, B, ids, _ptr(x0), steps, _ptr(out), _ptr(stop), kind))
+        return out, stop
+
+    def cfm_sample(self, z, hist, noise, sde=None, cfg=2.0, shift=0.0):
+        z = np.ascontiguousarray(z, dtype=np.uint16)
+        B = z.shape[0]
+        noise = np.ascontiguousarray(noise, dtype=np.uint16)
+        y = np.empty_like(noise)
+        _check(lib().ming_cuda_cfm_sample(self._h, B, _ptr(z), _ptr(None if hist is None else np.ascontiguousarray(hist)),
+                                          _ptr(noise), _ptr(None if sde is None else np.ascontiguousarray(sde)),
+                                          float(cfg), float(shift), _ptr(y), PTR_HOST))
+        return y
+
+    def aggregate(self, latent):
+        latent = np.ascontiguousarray(latent, dtype=np.uint16)
+        B = latent.shape[0]
+        out = np.empty((B, self.cfg.hidden), dtype=np.uint16)
+        _check(lib().ming_cuda_aggregate(self._h, B, _ptr(latent), _ptr(out), PTR_HOST))
+        return out
+
+    def kv_read(self, s, layer, pos0, n):
+        kh = self.cfg.kv_heads
+        k = np.empty((kh, n, 64), dtype=np.uint16)
+        v = np.empty((kh, n, 64), dtype=np.uint16)
+        _check(lib().ming_cuda_kv_read(self._h, s, layer, pos0, n, _ptr(k), _ptr(v)))
+        return k, v
+
+    def unpack_linear(self, weight_name, out_dim, in_dim):
+        out = np.empty((out_dim, in_dim), dtype=np.float32)
+        _check(lib().ming_cuda_unpack_linear(self._h, weight_name.encode(), _ptr(out)))
+        return out
+
+    def flow_temb(self):
+        te = np.empty((10, self.cfg.dit_hidden), dtype=np.uint16)
+        _check(lib().ming_cuda_flow_temb(self._h, _ptr(te)))
+        return te
+
+    @property
+    def stream(self):
+        s = ctypes.c_void_p()
+        _check(lib().ming_cuda_get_stream(self._h, ctypes.byref(s)))
+        return s.value
+
+    def sync(self):
+        _check(lib().ming_cuda_sync(self._h))
+
+    def close(self):
+        if self._h:
+            lib().ming_cuda_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
