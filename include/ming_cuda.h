@@ -115,6 +115,13 @@ int ming_cuda_lm_generate(ming_ctx* ctx, int B, const int* seq_ids, const uint16
 int ming_cuda_cfm_sample(ming_ctx* ctx, int B, const uint16_t* z, const uint16_t* hist, const uint16_t* noise,
                          const uint16_t* sde, float cfg, float shift, uint16_t* y, int ptr_kind);
 
+/* The same Euler update restricted to steps [step0, step0+nsteps) starting
+ * from latent y_in (layout of `noise`); cfm_sample is steps [0, 10) from the
+ * noise. Lets a caller replay the sampler one step at a time (the reference's
+ * teacher-forced parity method, src/ming_parity.zig:6-8). */
+int ming_cuda_cfm_steps(ming_ctx* ctx, int B, const uint16_t* z, const uint16_t* hist, const uint16_t* y_in,
+                        const uint16_t* sde, float cfg, float shift, int step0, int nsteps, uint16_t* y, int ptr_kind);
+
 /* Model.aggregate (src/ming_model.zig:1040-1053,1153-1157): latent [B][latent]
  * -> next LM input rows [B][hidden]. */
 int ming_cuda_aggregate(ming_ctx* ctx, int B, const uint16_t* latent, uint16_t* out, int ptr_kind);

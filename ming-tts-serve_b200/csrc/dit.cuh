@@ -69,6 +69,7 @@ struct ProLatent {
         return bf2f(lat[((size_t)b * F + f) * latent + k]);
     }
     MING_DEV float y(int row, int k) const { return y_at(r0 + row, k); }
+    MING_DEV float post(int) const { return 1.f; }
 };
 
 // Launchers (dit.cu)

@@ -147,6 +147,7 @@ MING_DEV void group_mma(const uint8_t* chunk, const uint2* sB /*at group's first
 // Prologue API:
 //   MING_DEV void init(int r0, int nrows, float* aux) const;   // per-row stats into aux
 //   MING_DEV float y(int row, int k) const;                    // after init
+//   MING_DEV float post(int row) const;                        // scale of the row's f32 sums
 // Epilogue API:
 //   MING_DEV void operator()(int tile, int r8, int row /*absolute*/, float lo, float hi) const;
 template <int FMT, int NT, class Pro, class Epi>
@@ -203,7 +204,8 @@ __global__ void __launch_bounds__(LIN_THREADS) linear_kernel(PackedW W, Pro pro,
             lo += sRed[(w * 16 + r8) * 8 * NT + col];
             hi += sRed[(w * 16 + r8 + 8) * 8 * NT + col];
         }
-        epi(tile, r8, r0 + col, lo, hi);
+        const float ps = p.post(col);
+        epi(tile, r8, r0 + col, lo * ps, hi * ps);
     }
 }
 
@@ -218,12 +220,54 @@ struct ProPlain {
     int r0;
     MING_DEV void init(int r0_, int, float*) { r0 = r0_; }
     MING_DEV float y(int row, int k) const { return bf2f(x[(size_t)(r0 + row) * ld + k]); }
+    MING_DEV float post(int) const { return 1.f; }
 };
 
-// RMSNorm folded in: y = x * rsqrt(mean(x^2) + eps) * nw (the reference's
-// LA/LD/A/C prologue, src/ming_fused.zig:100-142; the tensor-core operand
-// needs 16-bit y, so 1/rms is applied before the product).
+// RMSNorm folded in as the reference's fused kernels do (LA/LD/A/C,
+// src/ming_fused.zig:100-142): the operand is x * nw, the row's
+// rsqrt(mean(x^2) + eps) scales the f32 sum. With unit gains x * nw is
+// exactly the bf16 input. For the fp16 operand of the quantized paths the
+// row is pre-scaled by a power of two (exact) so |x * nw| stays below 2^12.
 struct ProRms {
+    const uint16_t* x;
+    const uint16_t* nw;
+    int ld, K;
+    float eps;
+    int r0;
+    float* st;  // [row][2]: operand scale (power of two), post scale
+    MING_DEV void init(int r0_, int nrows, float* aux) {
+        r0 = r0_;
+        st = aux;
+        const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+        for (int r = warp; r < nrows; r += LIN_WARPS) {
+            const uint16_t* xr = x + (size_t)(r0 + r) * ld;
+            float s = 0.f, amax = 0.f;
+            for (int k = lane * 2; k < K; k += 64) {
+                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(xr + k));
+                const float2 w = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(nw + k));
+                s += v.x * v.x + v.y * v.y;
+                amax = fmaxf(amax, fmaxf(fabsf(v.x * w.x), fabsf(v.y * w.y)));
+            }
+            s = warp_sum(s);
+            amax = warp_max(amax);
+            if (lane == 0) {
+                int e = 0;
+                if (amax > 4096.f) frexpf(amax / 4096.f, &e);  // 2^e >= amax / 4096
+                aux[2 * r] = ldexpf(1.f, -e);
+                aux[2 * r + 1] = rsqrtf(s / (float)K + eps) * ldexpf(1.f, e);
+            }
+        }
+    }
+    MING_DEV float y(int row, int k) const {
+        return bf2f(x[(size_t)(r0 + row) * ld + k]) * bf2f(nw[k]) * st[2 * row];
+    }
+    MING_DEV float post(int row) const { return st[2 * row + 1]; }
+};
+
+// RMSNorm as MLX's fast_rms_norm: the normed row rounded, rb(nw * rb(x * inv))
+// (the reference's plain graph, used where it applies MLX ops, e.g. the
+// aggregator's final layer, src/ming_model.zig:1051).
+struct ProRmsGraph {
     const uint16_t* x;
     const uint16_t* nw;
     int ld, K;
@@ -237,17 +281,15 @@ struct ProRms {
         for (int r = warp; r < nrows; r += LIN_WARPS) {
             const uint16_t* xr = x + (size_t)(r0 + r) * ld;
             float s = 0.f;
-            for (int k = lane * 2; k < K; k += 64) {
-                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(xr + k));
-                s += v.x * v.x + v.y * v.y;
-            }
+            for (int k = lane; k < K; k += 32) { const float v = bf2f(xr[k]); s += v * v; }
             s = warp_sum(s);
             if (lane == 0) aux[r] = rsqrtf(s / (float)K + eps);
         }
     }
     MING_DEV float y(int row, int k) const {
-        return bf2f(x[(size_t)(r0 + row) * ld + k]) * inv[row] * bf2f(nw[k]);
+        return rb(bf2f(nw[k]) * rb(bf2f(x[(size_t)(r0 + row) * ld + k]) * inv[row]));
     }
+    MING_DEV float post(int) const { return 1.f; }
 };
 
 // LayerNorm (no affine, eps 1e-6) + adaLN modulation, evaluated in f32 and
@@ -280,6 +322,7 @@ struct ProLnMod {
         const float n = (bf2f(x[(size_t)ar * ld + k]) - st[2 * row]) * st[2 * row + 1];
         return rb(n * (1.0f + bf2f(scale[(size_t)c * mod_ld + k])) + bf2f(shift[(size_t)c * mod_ld + k]));
     }
+    MING_DEV float post(int) const { return 1.f; }
 };
 
 // ---------------------------------------------------------------------

@@ -117,6 +117,7 @@ struct ProAttn {
         }
         return rb(o * il);
     }
+    MING_DEV float post(int) const { return 1.f; }
 };
 
 // gate/up tiles: rows 0..7 gate features 8t.., rows 8..15 the same up features.

@@ -148,7 +148,7 @@ struct ming_ctx {
     uint16_t *f_ce = nullptr, *f_xh = nullptr, *f_xy = nullptr, *f_rows = nullptr, *f_x1 = nullptr, *f_qkv = nullptr;
     uint16_t *f_att = nullptr, *f_hh = nullptr, *f_sc = nullptr, *f_mod = nullptr;
     float* f_vel = nullptr;
-    std::map<std::pair<int, int>, cudaGraphExec_t> cfm_graphs;  // (B, sde?) -> graph
+    std::map<int, cudaGraphExec_t> cfm_graphs;  // (B, sde?, step0, nsteps) -> graph
     float cfm_cfg = NAN, cfm_shift = NAN;
 
     // aggregator
@@ -556,14 +556,14 @@ int prepare_rows(ming_ctx* c, int B, const int* seq_ids, int steps) {
 
 // ---- flow head ----
 
-int cfm_token_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift) {
+int cfm_token_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift, int step0, int nsteps) {
     const ming_cfg& f = c->cfg;
     const int H = f.dit_hidden, LAT = f.dit_latent, R = 6 * B;
     cudaStream_t s = c->stream;
     run_linear(c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, 2 * B,
                s);
     run_linear(c->x_emb.w, ProPlain{c->f_hist, LAT, 0}, EpiAct{c->f_xh, nullptr, c->x_emb.w.bias, H, 0, H}, B, s);
-    for (int st = 0; st < 10; st++) {
+    for (int st = step0; st < step0 + nsteps; st++) {
         run_linear(c->x_emb.w, ProPlain{c->f_y, LAT, 0}, EpiAct{c->f_xy, nullptr, c->x_emb.w.bias, H, 0, H}, B, s);
         launch_tok_rows(c->temb + (size_t)st * H, c->f_ce, c->f_xh, c->f_xy, c->f_rows, B, H, s);
         for (auto& b : c->dit) {
@@ -581,12 +581,12 @@ int cfm_token_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift)
     return MING_OK;
 }
 
-int cfm_ada_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift) {
+int cfm_ada_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift, int step0, int nsteps) {
     const ming_cfg& f = c->cfg;
     const int H = f.dit_hidden, LAT = f.dit_latent, F = f.dit_frames, NC = 2 * B, R = NC * F;
     cudaStream_t s = c->stream;
     run_linear(c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, NC, s);
-    for (int st = 0; st < 10; st++) {
+    for (int st = step0; st < step0 + nsteps; st++) {
         launch_ada_cond(c->temb + (size_t)st * H, c->f_ce, c->f_sc, NC, H, s);
         run_linear(c->x_emb.w, ProLatent{c->f_y, B, F, LAT, 0}, EpiAct{c->f_rows, nullptr, c->x_emb.w.bias, H, 0, H}, R, s);
         for (auto& b : c->dit) {
@@ -1018,22 +1018,23 @@ int ming_cuda_lm_generate(ming_ctx* c, int B, const int* ids, const uint16_t* x0
     return MING_OK;
 }
 
-int ming_cuda_cfm_sample(ming_ctx* c, int B, const uint16_t* z, const uint16_t* hist, const uint16_t* noise,
-                         const uint16_t* sde, float cfg, float shift, uint16_t* y, int kind) {
+int ming_cuda_cfm_steps(ming_ctx* c, int B, const uint16_t* z, const uint16_t* hist, const uint16_t* y_in,
+                        const uint16_t* sde, float cfg, float shift, int step0, int nsteps, uint16_t* y, int kind) {
     if (!c || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
     const ming_cfg& f = c->cfg;
     if (f.dit_mode == MING_DIT_NONE) return fail(MING_ERR_INVALID, "no flow head configured");
     if (B < 1 || B > f.dit_max_batch) return fail(MING_ERR_INVALID, "flow batch out of range");
+    if (step0 < 0 || nsteps < 1 || step0 + nsteps > 10) return fail(MING_ERR_INVALID, "Euler step range out of [0, 10)");
     const bool ada = f.dit_mode == MING_DIT_ADALN;
-    if (!z || !noise || !y || (!ada && !hist)) return fail(MING_ERR_INVALID, "null argument");
+    if (!z || !y_in || !y || (!ada && !hist)) return fail(MING_ERR_INVALID, "null argument");
     CK(cudaSetDevice(c->device));
     const int LAT = f.dit_latent, F = f.dit_frames, CD = f.dit_cond_dim;
     int rc;
-    // inputs: z rows then zeros (the unconditional half), hist, noise, sde
+    // inputs: z rows then zeros (the unconditional half), hist, y, sde
     CK(cudaMemsetAsync(c->f_zc + (size_t)B * CD, 0, (size_t)B * CD * 2, c->stream));
     if ((rc = copy_in(c, c->f_zc, z, (size_t)B * CD * 2, kind))) return rc;
     if (!ada && (rc = copy_in(c, c->f_hist, hist, (size_t)B * LAT * 2, kind))) return rc;
-    if ((rc = copy_in(c, c->f_y, noise, (size_t)B * F * LAT * 2, kind))) return rc;
+    if ((rc = copy_in(c, c->f_y, y_in, (size_t)B * F * LAT * 2, kind))) return rc;
     if (sde && (rc = copy_in(c, c->f_sde, sde, (size_t)10 * B * F * LAT * 2, kind))) return rc;
     if (cfg != c->cfm_cfg || shift != c->cfm_shift) {  // scalars are baked into the graphs
         for (auto& kv : c->cfm_graphs) cudaGraphExecDestroy(kv.second);
@@ -1041,13 +1042,13 @@ int ming_cuda_cfm_sample(ming_ctx* c, int B, const uint16_t* z, const uint16_t* 
         c->cfm_cfg = cfg;
         c->cfm_shift = shift;
     }
-    const auto key = std::make_pair(B, sde ? 1 : 0);
+    const int key = ((B * 2 + (sde ? 1 : 0)) * 16 + step0) * 16 + nsteps;
     auto it = c->cfm_graphs.find(key);
     if (it == c->cfm_graphs.end()) {
         cudaGraph_t g;
         CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-        if (ada) cfm_ada_enqueue(c, B, sde != nullptr, cfg, shift);
-        else cfm_token_enqueue(c, B, sde != nullptr, cfg, shift);
+        if (ada) cfm_ada_enqueue(c, B, sde != nullptr, cfg, shift, step0, nsteps);
+        else cfm_token_enqueue(c, B, sde != nullptr, cfg, shift, step0, nsteps);
         cudaError_t ce = cudaStreamEndCapture(c->stream, &g);
         if (ce != cudaSuccess) return fail(MING_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
         cudaGraphExec_t ge;
@@ -1060,6 +1061,11 @@ int ming_cuda_cfm_sample(ming_ctx* c, int B, const uint16_t* z, const uint16_t* 
     if ((rc = copy_out(c, y, c->f_y, (size_t)B * F * LAT * 2, kind))) return rc;
     if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(c->stream));
     return MING_OK;
+}
+
+int ming_cuda_cfm_sample(ming_ctx* c, int B, const uint16_t* z, const uint16_t* hist, const uint16_t* noise,
+                         const uint16_t* sde, float cfg, float shift, uint16_t* y, int kind) {
+    return ming_cuda_cfm_steps(c, B, z, hist, noise, sde, cfg, shift, 0, 10, y, kind);
 }
 
 int ming_cuda_aggregate(ming_ctx* c, int B, const uint16_t* latent, uint16_t* out, int kind) {
@@ -1090,7 +1096,7 @@ int ming_cuda_aggregate(ming_ctx* c, int B, const uint16_t* latent, uint16_t* ou
         run_linear(b.ff2.w, ProPlain{c->a_hh, f.dit_ff, 0}, EpiResidual{c->a_x1, c->a_rows, b.ff2.w.bias, H}, R, s);
     }
     // final RMSNorm + linear on each CLS row (row stride 2H selects them)
-    run_linear(c->agg_final.w, ProRms{c->a_rows, c->agg_norm, 2 * H, H, 1e-6f, 0, nullptr},
+    run_linear(c->agg_final.w, ProRmsGraph{c->a_rows, c->agg_norm, 2 * H, H, 1e-6f, 0, nullptr},
                EpiAct{c->a_out, nullptr, c->agg_final.w.bias, f.hidden, 0, f.hidden}, B, s);
     CK(cudaGetLastError());
     if ((rc = copy_out(c, out, c->a_out, (size_t)B * f.hidden * 2, kind))) return rc;

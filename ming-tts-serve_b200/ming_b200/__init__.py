@@ -26,6 +26,7 @@ SYMBOLS = [
     "ming_cuda_default_cfg", "ming_cuda_create", "ming_cuda_load_tensor", "ming_cuda_finalize",
     "ming_cuda_seq_alloc", "ming_cuda_seq_free", "ming_cuda_seq_len", "ming_cuda_seq_truncate",
     "ming_cuda_lm_prefill", "ming_cuda_lm_decode", "ming_cuda_lm_generate", "ming_cuda_cfm_sample",
+    "ming_cuda_cfm_steps",
     "ming_cuda_aggregate", "ming_cuda_get_stream", "ming_cuda_sync", "ming_cuda_destroy",
     "ming_cuda_last_error", "ming_cuda_kv_read", "ming_cuda_unpack_linear", "ming_cuda_flow_temb",
 ]
@@ -70,6 +71,7 @@ def lib():
         "ming_cuda_lm_decode": (I, [P, I, IP, P, P, P, I]),
         "ming_cuda_lm_generate": (I, [P, I, IP, P, I, P, P, I]),
         "ming_cuda_cfm_sample": (I, [P, I, P, P, P, P, F, F, P, I]),
+        "ming_cuda_cfm_steps": (I, [P, I, P, P, P, P, F, F, I, I, P, I]),
         "ming_cuda_aggregate": (I, [P, I, P, P, I]),
         "ming_cuda_get_stream": (I, [P, ctypes.POINTER(P)]),
         "ming_cuda_sync": (I, [P]),
@@ -203,6 +205,15 @@ class Context:
                                           _ptr(noise), _ptr(None if sde is None else np.ascontiguousarray(sde)),
                                           float(cfg), float(shift), _ptr(y), PTR_HOST))
         return y
+
+    def cfm_steps(self, z, hist, y, step0, nsteps, sde=None, cfg=2.0, shift=0.0):
+        z = np.ascontiguousarray(z, dtype=np.uint16)
+        y = np.ascontiguousarray(y, dtype=np.uint16)
+        out = np.empty_like(y)
+        _check(lib().ming_cuda_cfm_steps(self._h, z.shape[0], _ptr(z), _ptr(None if hist is None else np.ascontiguousarray(hist)),
+                                         _ptr(y), _ptr(None if sde is None else np.ascontiguousarray(sde)), float(cfg),
+                                         float(shift), step0, nsteps, _ptr(out), PTR_HOST))
+        return out
 
     def aggregate(self, latent):
         latent = np.ascontiguousarray(latent, dtype=np.uint16)

@@ -154,8 +154,10 @@ def unpack_codes(words, bits, cols):
 LM_SHAPE = dict(hidden=896, layers=24, heads=14, kv_heads=2, head_dim=64, ff=4864, theta=1e6, eps=1e-6)
 
 
-def lm_weights(seed=0, bits=16, layers=24, hidden=896, heads=14, kv_heads=2, ff=4864, std=0.02, group=64):
-    """Qwen2 LM weights under model.model.* plus the stop head."""
+def lm_weights(seed=0, bits=16, layers=24, hidden=896, heads=14, kv_heads=2, ff=4864, std=0.02, group=64,
+               qscale=(0.005, 0.02)):
+    """Qwen2 LM weights under model.model.* plus the stop head. qscale is the
+    U(lo, hi) range of the 4/8-bit group scales (BASELINE: 0.005..0.02)."""
     W = {}
     H, QD, KD = hidden, heads * 64, kv_heads * 64
 
@@ -163,7 +165,7 @@ def lm_weights(seed=0, bits=16, layers=24, hidden=896, heads=14, kv_heads=2, ff=
         if bits == 16:
             W[name + ".weight"] = normal_bf16(seed, name + ".weight", (o, i), std)
         else:
-            q, s, b = quantized(seed, name + ".weight", o, i, bits, group)
+            q, s, b = quantized(seed, name + ".weight", o, i, bits, group, qscale[0], qscale[1])
             W[name + ".weight"], W[name + ".scales"], W[name + ".biases"] = q, s, b
         if bias:
             W[name + ".bias"] = normal_bf16(seed, name + ".bias", (o,), std)

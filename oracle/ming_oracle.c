@@ -546,8 +546,8 @@ static inline float cfg_euler(float y, float pc, float pu, float cfg, float dtv,
     return yn;
 }
 
-void mo_cfm_sample(const mo_flow* f, const uint16_t* z, const uint16_t* hist, const uint16_t* noise,
-                   const uint16_t* sde, float cfg, float shift, uint16_t* y_out, int mode) {
+void mo_cfm_steps(const mo_flow* f, const uint16_t* z, const uint16_t* hist, const uint16_t* y_in,
+                  const uint16_t* sde, float cfg, float shift, int step0, int nsteps, uint16_t* y_out, int mode) {
     const int H = f->dit.hidden, LAT = f->latent, CD = f->cond_dim, L = 3;
     float t[FLOW_STEPS + 1], dt[FLOW_STEPS], sq[FLOW_STEPS];
     flow_schedule_mode(t, dt, sq, mode);
@@ -559,12 +559,12 @@ void mo_cfm_sample(const mo_flow* f, const uint16_t* z, const uint16_t* hist, co
     float* ce = (float*)malloc(sizeof(float) * (size_t)2 * H);
     lin_apply(&f->c_emb, zc, 2, NULL, ce);
     float hf[256], yv[256], xe[1 << 12];
-    for (int i = 0; i < LAT; i++) { hf[i] = bf(hist, i); yv[i] = bf(noise, i); }
+    for (int i = 0; i < LAT; i++) { hf[i] = bf(hist, i); yv[i] = bf(y_in, i); }
     float* xh = (float*)malloc(sizeof(float) * (size_t)H);
     lin_apply(&f->x_emb, hf, 1, NULL, xh);
     for (int i = 0; i < H; i++) { xh[i] = R(xh[i], mode); ce[i] = R(ce[i], mode); ce[H + i] = R(ce[H + i], mode); }
     float* rows = (float*)malloc(sizeof(float) * (size_t)2 * L * H);
-    for (int s = 0; s < FLOW_STEPS; s++) {
+    for (int s = step0; s < step0 + nsteps && s < FLOW_STEPS; s++) {
         lin_apply(&f->x_emb, yv, 1, NULL, xe);
         for (int b = 0; b < 2; b++)
             for (int i = 0; i < H; i++) {
@@ -583,6 +583,11 @@ void mo_cfm_sample(const mo_flow* f, const uint16_t* z, const uint16_t* hist, co
     }
     for (int o = 0; o < LAT; o++) y_out[o] = mo_f32_to_bf16(yv[o]);
     free(te); free(zc); free(ce); free(xh); free(rows);
+}
+
+void mo_cfm_sample(const mo_flow* f, const uint16_t* z, const uint16_t* hist, const uint16_t* noise,
+                   const uint16_t* sde, float cfg, float shift, uint16_t* y_out, int mode) {
+    mo_cfm_steps(f, z, hist, noise, sde, cfg, shift, 0, FLOW_STEPS, y_out, mode);
 }
 
 /* Aggregator (src/ming_model.zig:1040-1053): x_embedder, CLS row prepended,
@@ -651,8 +656,8 @@ void mo_ada_temb(const mo_ada* a, uint16_t* te, int mode) {
     free(o);
 }
 
-void mo_ada_sample(const mo_ada* a, int B, const uint16_t* z, const uint16_t* noise, const uint16_t* sde,
-                   float cfg, float shift, uint16_t* y_out, int mode) {
+void mo_ada_steps(const mo_ada* a, int B, const uint16_t* z, const uint16_t* y_in, const uint16_t* sde,
+                  float cfg, float shift, int step0, int nsteps, uint16_t* y_out, int mode) {
     const int H = a->hidden, F = a->frames, LAT = a->latent, CD = a->cond_dim, FF = a->ff;
     const int NC = 2 * B;        /* condition rows: cond halves then uncond halves */
     const int NR = NC * F;       /* token rows */
@@ -667,7 +672,7 @@ void mo_ada_sample(const mo_ada* a, int B, const uint16_t* z, const uint16_t* no
     lin_apply(&a->c_emb, zc, NC, NULL, ce);
     for (int64_t i = 0; i < (int64_t)NC * H; i++) ce[i] = R(ce[i], mode);
     float* y = (float*)malloc(sizeof(float) * (size_t)B * F * LAT);
-    for (int64_t i = 0; i < (int64_t)B * F * LAT; i++) y[i] = bf(noise, i);
+    for (int64_t i = 0; i < (int64_t)B * F * LAT; i++) y[i] = bf(y_in, i);
     float* sc = (float*)malloc(sizeof(float) * (size_t)NC * H);
     float* mod = (float*)malloc(sizeof(float) * (size_t)NC * 6 * H);
     float* x = (float*)malloc(sizeof(float) * (size_t)NR * H);
@@ -680,7 +685,7 @@ void mo_ada_sample(const mo_ada* a, int B, const uint16_t* z, const uint16_t* no
     float* f1 = (float*)malloc(sizeof(float) * (size_t)NR * FF);
     float* yin = (float*)malloc(sizeof(float) * (size_t)NR * LAT);
     float* vel = (float*)malloc(sizeof(float) * (size_t)NR * LAT);
-    for (int s = 0; s < FLOW_STEPS; s++) {
+    for (int s = step0; s < step0 + nsteps && s < FLOW_STEPS; s++) {
         /* c = rb(t_emb + c_emb); SiLU per op */
         for (int r = 0; r < NC; r++)
             for (int i = 0; i < H; i++) {
@@ -747,4 +752,9 @@ void mo_ada_sample(const mo_ada* a, int B, const uint16_t* z, const uint16_t* no
     for (int64_t i = 0; i < (int64_t)B * F * LAT; i++) y_out[i] = mo_f32_to_bf16(y[i]);
     free(te); free(zc); free(ce); free(y); free(sc); free(mod); free(x); free(hm);
     free(q); free(k); free(v); free(att); free(tmp); free(f1); free(yin); free(vel);
+}
+
+void mo_ada_sample(const mo_ada* a, int B, const uint16_t* z, const uint16_t* noise, const uint16_t* sde,
+                   float cfg, float shift, uint16_t* y_out, int mode) {
+    mo_ada_steps(a, B, z, noise, sde, cfg, shift, 0, FLOW_STEPS, y_out, mode);
 }

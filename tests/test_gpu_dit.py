@@ -1,6 +1,14 @@
 """GPU parity of the flow head (token mode = the reference's head; adaLN mode
 = BASELINE config 4) and the aggregator, through the C ABI, against the CPU
-oracle. Tolerance: latents within max-abs 2e-2 and cosine > 0.999 (bf16)."""
+oracle.
+
+Gate: each Euler step teacher-forced (both sides start the step from the
+oracle's latent) within max-abs 2e-2 and cosine > 0.999 — the north star's
+per-step bf16 tolerance. A whole 10-step sample drifts further: the
+reference's own fused and plain paths differ by ~1e-2 relative per CFM sample
+(README.md:225; the oracle's two rounding modes differ by 0.03-0.05 max-abs
+here), so whole samples are bounded at the oracle's bf16-vs-f32 drift
+(max-abs 0.2, cosine > 0.999)."""
 import numpy as np
 import pytest
 
@@ -48,11 +56,20 @@ def test_cfm_token_parity(token_head, B, shift):
     hist = synth.normal_bf16(10, f"cfm.h.{B}", (B, 64))
     noise = synth.normal_bf16(10, f"cfm.n.{B}", (B, 64))
     sde = synth.normal_bf16(10, f"cfm.sde.{B}", (10, B, 64)) if shift else None
+    sd = lambda b: None if sde is None else sde[:, b].copy()
+    # teacher-forced Euler steps
+    y = noise.copy()
+    for st in range(10):
+        got = ctx.cfm_steps(z, hist, y, st, 1, sde, 2.0, shift)
+        ref = np.stack([f.steps(z[b], hist[b], y[b], st, 1, sd(b), 2.0, shift) for b in range(B)])
+        d, c, ok = close(got, ref)
+        assert ok, (st, d, c)
+        y = ref
+    # whole sample
     got = ctx.cfm_sample(z, hist, noise, sde, 2.0, shift)
-    for b in range(B):
-        ref = f.sample(z[b], hist[b], noise[b], None if sde is None else sde[:, b].copy(), 2.0, shift)
-        d, c, ok = close(got[b:b + 1], ref[None])
-        assert ok, (b, d, c)
+    ref = np.stack([f.sample(z[b], hist[b], noise[b], sd(b), 2.0, shift) for b in range(B)])
+    d, c, ok = close(got, ref, tol=0.2)
+    assert ok, ("sample", d, c)
 
 
 def test_cfm_repeat_is_bit_identical(token_head):
@@ -80,7 +97,14 @@ def test_cfm_adaln_parity(ada_head, B):
     a = O.Ada(W)
     z = synth.normal_bf16(13, f"ada.z.{B}", (B, 896))
     noise = synth.normal_bf16(13, f"ada.n.{B}", (B, 4, 64))
+    y = noise.copy()
+    for st in (range(10) if B <= 2 else (0, 5, 9)):
+        got = ctx.cfm_steps(z, None, y, st, 1)
+        ref = a.steps(z, y, st, 1)
+        d, c, ok = close(got.reshape(B * 4, 64), ref.reshape(B * 4, 64))
+        assert ok, (st, d, c)
+        y = ref
     got = ctx.cfm_sample(z, None, noise)
     ref = a.sample(z, noise)
-    d, c, ok = close(got.reshape(B * 4, 64), ref.reshape(B * 4, 64))
-    assert ok, (d, c)
+    d, c, ok = close(got.reshape(B * 4, 64), ref.reshape(B * 4, 64), tol=0.2)
+    assert ok, ("sample", d, c)
