@@ -1,0 +1,1039 @@
+// mega.cu — persistent decode-step kernel (see mega.cuh for the design).
+#include <cuda_runtime.h>
+
+#include "mega.cuh"
+
+namespace ming {
+
+namespace {
+
+constexpr long long MG_TIMEOUT = 4000000000LL;  // cycles (~2 s) before a wait gives up
+constexpr int MG_SK = 32;                       // staged 64-groups of activations (max)
+
+// ---------------- PTX helpers ----------------
+MING_DEV uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+MING_DEV void mbar_init(uint64_t* b, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(su32(b)), "r"(count));
+}
+MING_DEV void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(su32(b)), "r"(bytes) : "memory");
+}
+MING_DEV void mbar_arrive(uint64_t* b) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(su32(b)) : "memory");
+}
+MING_DEV bool mbar_try(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait on an mbarrier phase; false on timeout.
+MING_DEV bool mbar_wait(uint64_t* b, uint32_t parity) {
+    if (mbar_try(b, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try(b, parity))
+        if (clock64() - t0 > MG_TIMEOUT) return false;
+    return true;
+}
+MING_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(su32(dst)),
+                 "l"(src), "r"(bytes), "r"(su32(bar))
+                 : "memory");
+}
+MING_DEV void cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(su32(dst)), "l"(src) : "memory");
+}
+MING_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+MING_DEV void cp_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
+MING_DEV void cbar() { asm volatile("bar.sync 1, 256;\n" ::: "memory"); }  // consumer warps only
+MING_DEV uint64_t ldr64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+MING_DEV uint32_t ldr32(const int* p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+MING_DEV void str64(uint64_t* p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+MING_DEV uint64_t tagged(uint32_t tag, float v) { return ((uint64_t)tag << 32) | __float_as_uint(v); }
+
+struct Ctx {
+    const MegaDev* a;
+    int* fail;       // shared: first failure code of this CTA (0 = none)
+    int* gerr;
+};
+
+// Polls one tagged f32 word until its tag is `tag`. On timeout or a failure
+// elsewhere, records it and returns 0 (the caller checks *fail at the next
+// barrier). Kept out of line: it is the rare path of every gather.
+__device__ __noinline__ float poll(const Ctx& x, const uint64_t* p, uint32_t tag) {
+    uint64_t v = ldr64(p);
+    if ((uint32_t)(v >> 32) == tag) return __uint_as_float((uint32_t)v);
+    const long long t0 = clock64();
+    int it = 0;
+    while (true) {
+        v = ldr64(p);
+        if ((uint32_t)(v >> 32) == tag) return __uint_as_float((uint32_t)v);
+        if (((++it) & 63) == 0) {
+            if (*(volatile int*)x.fail) return 0.f;
+            if (ldr32(x.gerr)) {
+                atomicCAS(x.fail, 0, 5);
+                return 0.f;
+            }
+            if (clock64() - t0 > MG_TIMEOUT) {
+                atomicCAS(x.fail, 0, 1);
+                return 0.f;
+            }
+        }
+    }
+}
+
+// ---------------- tensor-core groups on shared-memory chunks ----------------
+// Weights of one 64-group (this lane's words + the group scales).
+struct GroupW {
+    uint32_t w[8];
+    float s_lo, b_lo, s_hi, b_hi;
+};
+template <int FMT>
+MING_DEV void load_group(const uint8_t* chunk, int lane, GroupW& g) {
+    if constexpr (FMT == 16) {
+        // bf16 tiles: 4 k-steps x this lane's uint4, loaded at use
+    } else if constexpr (FMT == 4) {
+        const uint4 w = *reinterpret_cast<const uint4*>(chunk + (size_t)lane * 16);
+        g.w[0] = w.x; g.w[1] = w.y; g.w[2] = w.z; g.w[3] = w.w;
+    } else {
+        const uint4 w0 = *reinterpret_cast<const uint4*>(chunk + (size_t)lane * 16);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(chunk + (size_t)(32 + lane) * 16);
+        g.w[0] = w0.x; g.w[1] = w0.y; g.w[2] = w0.z; g.w[3] = w0.w;
+        g.w[4] = w1.x; g.w[5] = w1.y; g.w[6] = w1.z; g.w[7] = w1.w;
+    }
+    if constexpr (FMT != 16) {
+        const uint2 sc = *reinterpret_cast<const uint2*>(chunk + (FMT == 4 ? 512 : 1024) + (lane >> 2) * 8);
+        g.s_lo = __uint_as_float(sc.x << 16);
+        g.b_lo = __uint_as_float(sc.x & 0xffff0000u);
+        g.s_hi = __uint_as_float(sc.y << 16);
+        g.b_hi = __uint_as_float(sc.y & 0xffff0000u);
+    }
+}
+template <int FMT>
+MING_DEV void a_frag(const uint8_t* chunk, const GroupW& g, int ks, int lane, uint32_t (&a)[4]) {
+    if constexpr (FMT == 16) {
+        const uint4 w = *reinterpret_cast<const uint4*>(chunk + ((size_t)ks * 32 + lane) * 16);
+        a[0] = w.x; a[1] = w.y; a[2] = w.z; a[3] = w.w;
+    } else if constexpr (FMT == 4) {
+        dq4(g.w[ks], a);
+    } else {
+        dq8(g.w[(ks >> 1) * 4 + (ks & 1) * 2], g.w[(ks >> 1) * 4 + (ks & 1) * 2 + 1], a);
+    }
+}
+template <int FMT>
+MING_DEV void mma_k(float (&t)[4], const uint32_t (&a)[4], uint2 b) {
+    if constexpr (FMT == 16) mma_bf16(t, a, b.x, b.y);
+    else mma_f16(t, a, b.x, b.y);
+}
+// acc += W_group . y_group for one group (t: the group's own sums for the
+// quantized scale/bias, added to acc after the 4 k-steps).
+template <int FMT>
+MING_DEV void group_finish(const GroupW& g, const float (&t)[4], const float* ys, int lane, float (&acc)[4]) {
+    if constexpr (FMT == 16) {
+        acc[0] += t[0]; acc[1] += t[1]; acc[2] += t[2]; acc[3] += t[3];
+    } else {
+        const int c = 2 * (lane & 3);
+        const float y0 = ys[c], y1 = ys[c + 1];
+        acc[0] += g.s_lo * t[0] + g.b_lo * y0;
+        acc[1] += g.s_lo * t[1] + g.b_lo * y1;
+        acc[2] += g.s_hi * t[2] + g.b_hi * y0;
+        acc[3] += g.s_hi * t[3] + g.b_hi * y1;
+    }
+}
+
+// Shared-memory carve-up (byte offsets from the dynamic base). sB, sYs and sT
+// are contiguous: an attention item uses the three as one scratch area.
+constexpr int MG_T_BYTES = MG_SK * 64 * MG_MAXB * 2;  // bf16 [stage][64][row]
+constexpr int MG_META_INTS = 4096;                    // tile maps of the 4 phases + CTA ranges
+constexpr int MG_BT_INTS = 512;                       // block-table row per batch row
+struct SmemMap {
+    int ring, bars, sB, sYs, sT, sRed, sX, lp, meta, bt, misc, total;
+};
+__host__ __device__ inline SmemMap smem_map(int nslots, int slot_bytes, int H, int lp_bytes) {
+    SmemMap m;
+    m.ring = 0;
+    m.bars = nslots * slot_bytes;
+    m.sB = (m.bars + (2 * nslots + 4) * 8 + 127) / 128 * 128;
+    m.sYs = m.sB + MG_SK * 4 * 32 * 8;
+    m.sT = m.sYs + MG_SK * 8 * 4;
+    m.sRed = m.sT + MG_T_BYTES;
+    m.sX = m.sRed + MG_CWARPS * 2 * 16 * 8 * 4;
+    m.lp = m.sX + (MG_MAXB * H * 2 + 127) / 128 * 128;
+    m.meta = m.lp + 2 * ((lp_bytes + 127) / 128 * 128);
+    m.bt = m.meta + MG_META_INTS * 4;
+    m.misc = m.bt + MG_MAXB * MG_BT_INTS * 4;
+    m.total = m.misc + 4096;
+    return m;
+}
+constexpr int MG_ATT_SCRATCH = MG_SK * 4 * 32 * 8 + MG_SK * 8 * 4 + MG_T_BYTES;
+// attention item scratch: K, V rows (padded to 72) + q + new k/v + scores
+static_assert(2 * MG_ATT_CH * (HD + 8) * 2 + 8 * HD * 4 + 2 * HD * 4 + 8 * MG_ATT_CH * 4 <= MG_ATT_SCRATCH,
+              "attention scratch does not fit");
+
+struct Misc {          // small per-CTA state in shared memory
+    float inv[MG_MAXB];    // 1/rms of each row (current norm)
+    float scl[MG_MAXB];    // operand pre-scale (power of two) of each row
+    float post[MG_MAXB];   // scale applied to the f32 partial sums
+    int pos[MG_MAXB];      // row positions (cache length before this step)
+    int seq[MG_MAXB];      // row sequences
+    float ml[2 * 16 * MG_MAXB];  // per (stage, row): attention split max, 1/sum
+    float red[MG_CWARPS * 2 * MG_MAXB];  // block reductions
+    int g0[MG_NPH], g1[MG_NPH];  // this CTA's group range per phase
+    int toff[MG_NPH];            // offset of each phase's tile map in meta
+    int wtile[MG_NPH][MG_CWARPS];  // first tile of each warp's group range (-1: none)
+    float rc[MG_MAXB][HD / 2];   // RoPE cos/sin of each row's position, per frequency
+    float rs[MG_MAXB][HD / 2];
+    int fail;
+    int prod_done;
+    int issued;
+    uint32_t epoch;
+    int step;
+};
+static_assert(sizeof(Misc) <= 4096, "Misc must fit its shared-memory slot");
+
+struct Sm {            // shared-memory views used by the phases
+    uint2* sB;
+    float* sYs;
+    uint16_t* sT;
+    float* sRed;
+    uint16_t* sX;
+    const uint8_t* lp;   // current layer's parameter block
+    const int* meta;
+    const int* bt;       // [MG_MAXB][MG_BT_INTS]
+    Misc* ms;
+    long long* st;       // optional per-layer stamp row (diagnostics)
+};
+#define MG_SUB(k) \
+    if (sm.st && threadIdx.x == 0) sm.st[(k)] = clock64();
+
+// tile map entry of phase p: first CTA covering tile t, and how many do
+MING_DEV int tile_first(const Sm& sm, int p, int t) { return sm.meta[sm.ms->toff[p] + 2 * t]; }
+MING_DEV int tile_count(const Sm& sm, int p, int t) { return sm.meta[sm.ms->toff[p] + 2 * t + 1]; }
+
+// ---------------- batched tagged gathers ----------------
+// Sum of n (<= 4) tagged partials p[0], p[stride], ...: issue() starts the
+// loads, finish() checks the tags (polling only the stragglers) and sums in
+// slot order, so a thread pays one L2 round trip per batch.
+struct Pend {
+    uint64_t v[4];
+    const uint64_t* p;
+    int n, stride;
+    MING_DEV void issue(const uint64_t* p_, int n_, int stride_) {
+        p = p_;
+        n = n_;
+        stride = stride_;
+#pragma unroll
+        for (int k = 0; k < 4; k++) v[k] = k < n ? ldr64(p + (size_t)k * stride) : 0ull;
+    }
+    MING_DEV float finish(const Ctx& cx, uint32_t tag) const {
+        float s = 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; k++)
+            if (k < n) s += ((uint32_t)(v[k] >> 32) == tag) ? __uint_as_float((uint32_t)v[k]) : poll(cx, p + (size_t)k * stride, tag);
+        return s;
+    }
+};
+
+MING_DEV uint64_t* part_ptr(const MegaPhase& ph, int l, int B, int t, int r, int b) {
+    return ph.part + ((((size_t)l * ph.tiles + t) * ph.slots) * 16 + r) * B + b;
+}
+
+// ---------------- staging of the mma B operand ----------------
+// Fragment entry (stage si, kstep ks, lane) holds rows b = lane/4 at
+// k = si*64 + 16ks + 2t, +1, +8, +9 (t = lane%4). Entries of rows >= B are
+// zero. The 16 entries of one (stage, row) are computed by 16 consecutive
+// threads, which also reduce the row's group sum (the quantized formats'
+// bias term) with shuffles. Sources: mode 0, sX times the norm weight nw and
+// the row pre-scale; mode 1, the bf16 values sT [stage][64][row].
+template <bool F16>
+MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint16_t* nw, bool ysum) {
+    const int tid = threadIdx.x;
+    // zero the fragment entries of the unused rows (all entries, then overwrite)
+    uint4* z = reinterpret_cast<uint4*>(sm.sB);
+    for (int e = tid; e < nstage * 4 * 32 / 2; e += 256) z[e] = make_uint4(0u, 0u, 0u, 0u);
+    for (int e = tid; e < nstage * 8; e += 256) sm.sYs[e] = 0.f;
+    cbar();
+    const int tot = nstage * B * 16;
+    // warp-uniform trip count (a multiple of 32): every lane reaches the shuffles
+    const int totr = (tot + 31) & ~31;
+    for (int e = tid; e < totr; e += 256) {
+        const bool act = e < tot;
+        const int q16 = e & 15, sb = e >> 4, si = act ? sb / B : 0, b = act ? sb - si * B : 0;
+        const int ks = q16 >> 2, tq = q16 & 3, kk = ks * 16 + 2 * tq;
+        float sum = 0.f;
+        if (act) {
+            const int ko[4] = {kk, kk + 1, kk + 8, kk + 9};
+            float y[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                if (mode == 0) {
+                    const int f = si * 64 + ko[u];
+                    y[u] = bf2f(sm.sX[b * H + f]) * bf2f(nw[f]) * sm.ms->scl[b];
+                } else {
+                    y[u] = bf2f(sm.sT[(si * 64 + ko[u]) * B + b]);
+                }
+            }
+            const uint2 v = make_bfrag<F16>(y[0], y[1], y[2], y[3]);
+            sm.sB[(si * 4 + ks) * 32 + b * 4 + tq] = v;
+            float2 p, q;
+            if (F16) {
+                p = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+                q = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+            } else {
+                p = unpack_bf16x2(v.x);
+                q = unpack_bf16x2(v.y);
+            }
+            sum = (p.x + p.y) + (q.x + q.y);
+        }
+        sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        if (ysum && act && q16 == 0) sm.sYs[si * 8 + b] = sum;
+    }
+}
+
+// Residual update from a GEMV phase's partials, fused with the RMSNorm
+// statistics of the updated rows: sX[b][f] = rb(sX + rb(sum of the partials
+// of feature f)) (plain row order: tile f/16, row f%16), then inv, pre-scale
+// and post-scale of each row for the norm weight nw. With p < 0 the rows are
+// left as they are (layer 0) and only the statistics are computed.
+MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, int p, int l, uint32_t tag, const uint16_t* nw, bool f16) {
+    const MegaDev& a = *cx.a;
+    const int H = a.H, B = a.B, tot = B * H, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float ss[MG_MAXB], am[MG_MAXB];
+#pragma unroll
+    for (int b = 0; b < MG_MAXB; b++) ss[b] = am[b] = 0.f;
+    for (int base = 0; base < tot; base += 256 * 4) {
+        Pend pd[4];
+        if (p >= 0) {
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int idx = base + tid + i * 256;
+                if (idx < tot) {
+                    const int b = idx / H, f = idx % H, t = f >> 4;
+                    pd[i].issue(part_ptr(a.ph[p], l, B, t, f & 15, b), tile_count(sm, p, t), 16 * B);
+                } else {
+                    pd[i].n = 0;
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int idx = base + tid + i * 256;
+            if (idx >= tot) continue;
+            const int b = idx / H, f = idx % H;
+            float x = bf2f(sm.sX[idx]);
+            if (p >= 0) {
+                x = rb(x + rb(pd[i].finish(cx, tag)));
+                sm.sX[idx] = f2bf(x);
+            }
+#pragma unroll
+            for (int bb = 0; bb < MG_MAXB; bb++)
+                if (bb == b) {
+                    ss[bb] += x * x;
+                    am[bb] = fmaxf(am[bb], fabsf(x * bf2f(nw[f])));
+                }
+        }
+    }
+    if (p == 1) MG_SUB(20)
+#pragma unroll
+    for (int b = 0; b < MG_MAXB; b++) {
+        const float s1 = warp_sum(ss[b]), a1 = warp_max(am[b]);
+        if (lane == 0) {
+            sm.ms->red[(warp * MG_MAXB + b) * 2] = s1;
+            sm.ms->red[(warp * MG_MAXB + b) * 2 + 1] = a1;
+        }
+    }
+    cbar();
+    if (tid < B) {
+        float s1 = 0.f, a1 = 0.f;
+        for (int w = 0; w < MG_CWARPS; w++) {
+            s1 += sm.ms->red[(w * MG_MAXB + tid) * 2];
+            a1 = fmaxf(a1, sm.ms->red[(w * MG_MAXB + tid) * 2 + 1]);
+        }
+        int e = 0;
+        if (f16 && a1 > 4096.f) frexpf(a1 / 4096.f, &e);
+        sm.ms->inv[tid] = rsqrtf(s1 / (float)H + a.eps);
+        sm.ms->scl[tid] = ldexpf(1.f, -e);
+        sm.ms->post[tid] = sm.ms->inv[tid] * ldexpf(1.f, e);
+    }
+    cbar();
+}
+
+// One GEMV phase on the CTA's ring chunks: partial sums of the CTA's group
+// range, reduced over warps in fixed order and published per (tile, CTA).
+template <int FMT>
+MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int l, uint32_t tag, uint8_t* ring, uint64_t* full,
+                                        uint64_t* empty, int stage_base, bool use_post, int& cons) {
+    const MegaDev& a = *cx.a;
+    const MegaPhase& ph = a.ph[p];
+    Misc* ms = sm.ms;
+    const int c = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g0 = ms->g0[p], g1 = ms->g1[p], n = g1 - g0, gpt = ph.gpt;
+    const int nsc = (n + a.gps - 1) / a.gps;
+    for (int j = 0; j < nsc; j++) {
+        const int sc = cons + j;
+        if (!mbar_wait(&full[sc % a.nslots], (sc / a.nslots) & 1)) atomicCAS(cx.fail, 0, 2);
+    }
+    if (p == 2) MG_SUB(16)
+    const int i0 = warp * n / MG_CWARPS, i1 = (warp + 1) * n / MG_CWARPS;
+    const int tb = ms->wtile[p][warp];
+    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (!*(volatile int*)cx.fail) {
+        // two groups per iteration: independent mma chains
+        for (int i = i0; i < i1; i += 2) {
+            const bool two = i + 1 < i1;
+            const uint8_t* ch[2];
+            int si[2], slot_u[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int ii = (u == 1 && !two) ? i : i + u;
+                const int g = g0 + ii, t = g / gpt, kg = g - t * gpt;
+                const int sc = cons + ii / a.gps;
+                ch[u] = ring + (size_t)(sc % a.nslots) * a.slot_bytes + (size_t)(ii - (ii / a.gps) * a.gps) * a.cb;
+                int s_ = kg - stage_base;
+                if (s_ < 0) s_ += gpt;
+                si[u] = s_;
+                slot_u[u] = t == tb ? 0 : 1;
+            }
+            GroupW gw[2];
+            load_group<FMT>(ch[0], lane, gw[0]);
+            load_group<FMT>(ch[1], lane, gw[1]);
+            float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++) {
+                uint32_t a0[4], a1[4];
+                a_frag<FMT>(ch[0], gw[0], ks, lane, a0);
+                a_frag<FMT>(ch[1], gw[1], ks, lane, a1);
+                const uint2 b0 = sm.sB[(si[0] * 4 + ks) * 32 + lane];
+                const uint2 b1 = sm.sB[(si[1] * 4 + ks) * 32 + lane];
+                mma_k<FMT>(t0, a0, b0);
+                mma_k<FMT>(t1, a1, b1);
+            }
+            if (slot_u[0] == 0) group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc[0]);
+            else group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc[1]);
+            if (two) {
+                if (slot_u[1] == 0) group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc[0]);
+                else group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc[1]);
+            }
+        }
+    }
+    {
+        const int gr = lane >> 2, cc = 2 * (lane & 3);
+        float* r = sm.sRed + warp * 2 * 128;
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            r[u * 128 + gr * 8 + cc] = acc[u][0];
+            r[u * 128 + gr * 8 + cc + 1] = acc[u][1];
+            r[u * 128 + (gr + 8) * 8 + cc] = acc[u][2];
+            r[u * 128 + (gr + 8) * 8 + cc + 1] = acc[u][3];
+        }
+    }
+    if (p == 2) MG_SUB(17)
+    cbar();
+    if (p == 2) MG_SUB(18)
+    if (lane == 0)
+        for (int j = 0; j < nsc; j++) mbar_arrive(&empty[(cons + j) % a.nslots]);
+    cons += nsc;
+    // fixed-order reduction over warps, one partial per (tile, CTA)
+    const int t0 = g0 / gpt, t1 = (g1 - 1) / gpt;
+    const int B = a.B;
+    for (int e = threadIdx.x; e < (t1 - t0 + 1) * 16 * B; e += 256) {
+        const int t = t0 + e / (16 * B), r = (e / B) % 16, b = e % B;
+        float s = 0.f;
+#pragma unroll
+        for (int w = 0; w < MG_CWARPS; w++) {
+            const int wt = ms->wtile[p][w];
+            if (wt == t) s += sm.sRed[(w * 2 + 0) * 128 + r * 8 + b];
+            else if (wt >= 0 && wt + 1 == t) s += sm.sRed[(w * 2 + 1) * 128 + r * 8 + b];
+        }
+        if (use_post) s *= ms->post[b];
+        const int slot = c - tile_first(sm, p, t);
+        str64(part_ptr(ph, l, B, t, r, b) + (size_t)slot * 16 * B, tagged(tag, s));
+    }
+    cbar();
+}
+
+// Attention of one (row, kv head, 128-position chunk) item. q/k/v come from
+// the P0 partials (+ bias, bf16, RoPE on q and k as MLX fast_rope); cached K/V
+// rows are prefetched with cp.async before the wait.
+MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, int b, int g, int s) {
+    const MegaDev& a = *cx.a;
+    Misc* ms = sm.ms;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int grp = a.heads / a.kvh, pos = ms->pos[b], B = a.B;
+    const int p0 = s * MG_ATT_CH, p1 = min(pos + 1, p0 + MG_ATT_CH), pc = min(p1, pos);
+    // K/V rows padded to 72 elements (144 B): 16-byte loads of 8 consecutive
+    // rows fall on distinct bank groups
+    constexpr int KS = HD + 8;
+    uint16_t* sK = reinterpret_cast<uint16_t*>(sm.sB);              // [128][72]
+    uint16_t* sV = sK + MG_ATT_CH * KS;                               // [128][72]
+    float* sq = reinterpret_cast<float*>(sV + MG_ATT_CH * KS);       // [8][64]
+    float* skn = sq + 8 * HD;                                         // [64]
+    float* svn = skn + HD;                                            // [64]
+    float* sS = svn + HD;                                             // [8][128]
+    const int* bt = sm.bt + b * MG_BT_INTS;
+    // 1. prefetch cached K/V rows [p0, pc)
+    for (int e = tid; e < (pc - p0) * 8; e += 256) {
+        const int j = e >> 3, piece = e & 7, p = p0 + j;
+        const int page = bt[p / PAGE];
+        cp16(sK + j * KS + piece * 8, a.kv.pool + kv_index(a.kv, page, l, 0, g, p % PAGE) + piece * 8);
+        cp16(sV + j * KS + piece * 8, a.kv.pool + kv_index(a.kv, page, l, 1, g, p % PAGE) + piece * 8);
+    }
+    cp_commit();
+    MG_SUB(10)
+    // 2. q (the group's heads), k, v of the new position from the P0 partials:
+    //    item (tile, r8) holds the RoPE pair (d, d+32); all loads issued first
+    const MegaPhase& ph = a.ph[0];
+    const float* bias = reinterpret_cast<const float*>(sm.lp + 4 * a.H);
+    const int nt = grp * 4 + 8;
+    {
+        Pend lo[2], hi[2];
+        int tl_[2], t_[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int e = tid + u * 256;
+            lo[u].n = hi[u].n = 0;
+            tl_[u] = -1;
+            if (e < nt * 8) {
+                const int tl = e >> 3, r8 = e & 7;
+                int t;
+                if (tl < grp * 4) t = (g * grp + tl / 4) * 4 + (tl & 3);
+                else if (tl < grp * 4 + 4) t = a.heads * 4 + g * 4 + (tl - grp * 4);
+                else t = a.heads * 4 + a.kvh * 4 + g * 4 + (tl - grp * 4 - 4);
+                const int cn = tile_count(sm, 0, t);
+                lo[u].issue(part_ptr(ph, l, B, t, r8, b), cn, 16 * B);
+                hi[u].issue(part_ptr(ph, l, B, t, r8 + 8, b), cn, 16 * B);
+                tl_[u] = tl;
+                t_[u] = t;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            if (tl_[u] < 0) continue;
+            const int tl = tl_[u], t = t_[u], r8 = (tid + u * 256) & 7;
+            const int kind = tl < grp * 4 ? 0 : (tl < grp * 4 + 4 ? 1 : 2);
+            const int d = (t & 3) * 8 + r8;
+            float x1 = rb(lo[u].finish(cx, tag) + bias[t * 16 + r8]);
+            float x2 = rb(hi[u].finish(cx, tag) + bias[t * 16 + r8 + 8]);
+            if (kind < 2) {
+                const float cs = ms->rc[b][d], sn = ms->rs[b][d];
+                const float p_ = x1 * cs - x2 * sn, q_ = x1 * sn + x2 * cs;
+                x1 = rb(p_);
+                x2 = rb(q_);
+            }
+            if (kind == 0) {
+                const int h = tl / 4;
+                sq[h * HD + d] = 0.125f * x1;
+                sq[h * HD + d + 32] = 0.125f * x2;
+            } else if (kind == 1) {
+                skn[d] = x1;
+                skn[d + 32] = x2;
+            } else {
+                svn[d] = x1;
+                svn[d + 32] = x2;
+            }
+        }
+    }
+    MG_SUB(11)
+    cp_wait_all();
+    cbar();
+    MG_SUB(12)
+    // 3. the chunk holding the new position appends it to the cache
+    if (p1 == pos + 1 && tid < 2 * HD) {
+        const int which = tid / HD, d = tid % HD;
+        const int page = bt[pos / PAGE];
+        a.kv.pool[kv_index(a.kv, page, l, which, g, pos % PAGE) + d] = f2bf(which ? svn[d] : skn[d]);
+    }
+    // 4. scores: thread (position j, head quad hq) keeps the key row in
+    //    registers and accumulates 4 heads independently
+    const int len = p1 - p0;
+    {
+        const int j = tid & (MG_ATT_CH - 1), hq = tid >> 7;
+        if (j < len && hq * 4 < grp) {
+            uint32_t kr[HD / 2];
+            if (p0 + j < pos) {
+                const uint4* src = reinterpret_cast<const uint4*>(sK + j * KS);
+#pragma unroll
+                for (int q = 0; q < HD / 8; q++) {
+                    const uint4 v = src[q];
+                    kr[4 * q] = v.x; kr[4 * q + 1] = v.y; kr[4 * q + 2] = v.z; kr[4 * q + 3] = v.w;
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < HD / 2; q++) kr[q] = pack_bf16x2(skn[2 * q], skn[2 * q + 1]);
+            }
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+            for (int q = 0; q < HD / 2; q++) {
+                const float2 kv = unpack_bf16x2(kr[q]);
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const float2 qv = *reinterpret_cast<const float2*>(sq + (hq * 4 + u) * HD + 2 * q);
+                    acc[u] += qv.x * kv.x + qv.y * kv.y;
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                if (hq * 4 + u < grp) sS[(hq * 4 + u) * MG_ATT_CH + j] = acc[u];
+        }
+    }
+    cbar();
+    MG_SUB(13)
+    // 5. softmax inside the chunk (warp per head)
+    if (warp < grp) {
+        float m = -INFINITY;
+        for (int j = lane; j < len; j += 32) m = fmaxf(m, sS[warp * MG_ATT_CH + j]);
+        m = warp_max(m);
+        float sum = 0.f;
+        for (int j = lane; j < len; j += 32) {
+            const float p = expf(sS[warp * MG_ATT_CH + j] - m);
+            sS[warp * MG_ATT_CH + j] = p;
+            sum += p;
+        }
+        sum = warp_sum(sum);
+        if (lane == 0) {
+            uint64_t* o = a.attn + (((size_t)b * a.heads + g * grp + warp) * a.max_splits + s) * MG_PART;
+            str64(o, tagged(tag, m));
+            str64(o + 1, tagged(tag, sum));
+        }
+    }
+    cbar();
+    MG_SUB(14)
+    // 6. P.V: thread (head, dim pair), 4 independent accumulators
+    for (int e = tid; e < grp * (HD / 2); e += 256) {
+        const int h = e / (HD / 2), dp = e % (HD / 2);
+        float2 ac[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+        const float* ph_ = sS + h * MG_ATT_CH;
+        const int lc = min(len, pos - p0);  // cached positions of the chunk
+        int j = 0;
+        for (; j + 4 <= lc; j += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (j + u) * KS + 2 * dp));
+                const float pw = ph_[j + u];
+                ac[u].x += pw * v.x;
+                ac[u].y += pw * v.y;
+            }
+        }
+        for (; j < len; j++) {
+            float2 v;
+            if (p0 + j < pos) v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * KS + 2 * dp));
+            else v = make_float2(svn[2 * dp], svn[2 * dp + 1]);
+            const float pw = ph_[j];
+            ac[0].x += pw * v.x;
+            ac[0].y += pw * v.y;
+        }
+        const float ox = (ac[0].x + ac[1].x) + (ac[2].x + ac[3].x), oy = (ac[0].y + ac[1].y) + (ac[2].y + ac[3].y);
+        uint64_t* o = a.attn + (((size_t)b * a.heads + g * grp + h) * a.max_splits + s) * MG_PART;
+        str64(o + 2 + 2 * dp, tagged(tag, ox));
+        str64(o + 3 + 2 * dp, tagged(tag, oy));
+    }
+    cbar();
+    MG_SUB(15)
+}
+
+// o_proj input: the attention output of the heads this CTA's o_proj range
+// reads, combined over the chunks: o = sum_s acc_s e^(m_s - M) / L, rounded.
+// Weights e^(m_s - M) / L go to wt [(si * B + b) * max_splits + s].
+MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int gpt, uint32_t tag) {
+    const MegaDev& a = *cx.a;
+    Misc* ms = sm.ms;
+    float* wt = sm.sRed;
+    const int B = a.B, tid = threadIdx.x;
+    for (int e = tid; e < nst * B; e += 256) {
+        const int si = e / B, b = e % B, h = (si + base) % gpt;
+        const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
+        const uint64_t* o = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART;
+        float M = -INFINITY, L = 0.f;
+        for (int s0 = 0; s0 < ns; s0 += 8) {
+            uint64_t vm[8], vl[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                vm[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART) : 0ull;
+                vl[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART + 1) : 0ull;
+            }
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (s0 + k >= ns) continue;
+                const float m = (uint32_t)(vm[k] >> 32) == tag ? __uint_as_float((uint32_t)vm[k]) : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
+                const float l = (uint32_t)(vl[k] >> 32) == tag ? __uint_as_float((uint32_t)vl[k]) : poll(cx, o + (size_t)(s0 + k) * MG_PART + 1, tag);
+                wt[(size_t)e * a.max_splits + s0 + k] = m;  // m for now, weights below
+                const float nm = fmaxf(M, m);
+                L = L * expf(M - nm) + l * expf(m - nm);
+                M = nm;
+            }
+        }
+        const float il = 1.0f / L;
+        for (int s2 = 0; s2 < ns; s2++) wt[(size_t)e * a.max_splits + s2] = expf(wt[(size_t)e * a.max_splits + s2] - M) * il;
+    }
+    cbar();
+    const int tot = nst * 64 * B;
+    for (int e = tid; e < tot; e += 256) {
+        const int si = e / (64 * B), d = (e / B) % 64, b = e % B, h = (si + base) % gpt;
+        const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
+        const uint64_t* o = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART + 2 + d;
+        const float* w = wt + (size_t)(si * B + b) * a.max_splits;
+        float v = 0.f;
+        for (int s0 = 0; s0 < ns; s0 += 8) {
+            uint64_t va[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) va[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART) : 0ull;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (s0 + k >= ns) continue;
+                const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k]) : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
+                v += x * w[s0 + k];
+            }
+        }
+        sm.sT[e] = f2bf(v);  // [si][d][b]
+    }
+    cbar();
+}
+
+// down_proj input: h = SwiGLU of the gate/up partials for the features of the
+// CTA's down range: rb(rb(g * rb(sigmoid g)) * u) (src/ming_fused.zig:386-393).
+MING_DEV void swiglu_gather(const Ctx& cx, const Sm& sm, int nst, int base, int gpt, int l, uint32_t tag) {
+    const MegaDev& a = *cx.a;
+    const MegaPhase& gu = a.ph[2];
+    const int B = a.B, tot = nst * 64 * B;
+    for (int e0 = 0; e0 < tot; e0 += 256 * 4) {
+        Pend pg[4], pu[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int e = e0 + threadIdx.x + i * 256;
+            if (e < tot) {
+                const int si = e / (64 * B), d = (e / B) % 64, b = e % B;
+                int kg = si + base;
+                if (kg >= gpt) kg -= gpt;
+                const int f = kg * 64 + d, t = f >> 3;
+                const int cn = tile_count(sm, 2, t);
+                pg[i].issue(part_ptr(gu, l, B, t, f & 7, b), cn, 16 * B);
+                pu[i].issue(part_ptr(gu, l, B, t, 8 + (f & 7), b), cn, 16 * B);
+            } else {
+                pg[i].n = pu[i].n = 0;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int e = e0 + threadIdx.x + i * 256;
+            if (e >= tot) continue;
+            const float gv = rb(pg[i].finish(cx, tag)), uv = rb(pu[i].finish(cx, tag));
+            const float sg = rb(1.0f / (1.0f + expf(-gv)));
+            sm.sT[e] = f2bf(rb(rb(gv * sg) * uv));
+        }
+    }
+    cbar();
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    const SmemMap mp = smem_map(a.nslots, a.slot_bytes, a.H, a.lp_bytes);
+    uint8_t* ring = smem + mp.ring;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + mp.bars);
+    uint64_t* empty = full + a.nslots;
+    uint64_t* lp_full = empty + a.nslots;  // [2]
+    uint64_t* lp_empty = lp_full + 2;      // [2]
+    uint8_t* lpbuf = smem + mp.lp;
+    const int lp_stride = (a.lp_bytes + 127) / 128 * 128;
+    int* meta = reinterpret_cast<int*>(smem + mp.meta);
+    int* btab = reinterpret_cast<int*>(smem + mp.bt);
+    Misc* ms = reinterpret_cast<Misc*>(smem + mp.misc);
+    Sm sm{reinterpret_cast<uint2*>(smem + mp.sB), reinterpret_cast<float*>(smem + mp.sYs),
+          reinterpret_cast<uint16_t*>(smem + mp.sT), reinterpret_cast<float*>(smem + mp.sRed),
+          reinterpret_cast<uint16_t*>(smem + mp.sX), lpbuf, meta, btab, ms, nullptr};
+    const int tid = threadIdx.x, c = blockIdx.x, H = a.H, B = a.B;
+    constexpr bool F16 = FMT != 16;
+    // ---- set-up: barriers, this CTA's ranges, tile maps, block-table rows ----
+    if (tid == 0) {
+        for (int i = 0; i < a.nslots; i++) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], MG_CWARPS);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&lp_full[i], 1);
+            mbar_init(&lp_empty[i], 1);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        ms->fail = 0;
+        ms->prod_done = 0;
+        ms->issued = 0;
+        ms->epoch = (uint32_t)a.counter[0] + 1u;
+        ms->step = a.counter[1];
+        int off = 0;
+        for (int p = 0; p < MG_NPH; p++) {
+            ms->toff[p] = off;
+            off += 2 * a.ph[p].tiles;
+        }
+    }
+    if (tid < MG_NPH) {
+        ms->g0[tid] = a.ph[tid].cta_g0[c];
+        ms->g1[tid] = a.ph[tid].cta_g0[c + 1];
+    }
+    if (tid < B) {
+        const int sq = a.row_seq[tid];
+        ms->seq[tid] = sq;
+        ms->pos[tid] = a.seq_len[sq];
+    }
+    __syncthreads();
+    {
+        int off = 0;
+        for (int p = 0; p < MG_NPH; p++) {
+            for (int i = tid; i < 2 * a.ph[p].tiles; i += MG_THREADS) meta[off + i] = a.ph[p].tile_c0[i];
+            off += 2 * a.ph[p].tiles;
+        }
+        for (int b = 0; b < B; b++) {
+            const int np = ms->pos[b] / PAGE + 1;
+            for (int i = tid; i < np; i += MG_THREADS) btab[b * MG_BT_INTS + i] = a.kv.bt[(size_t)ms->seq[b] * a.kv.bt_ld + i];
+        }
+        if (tid < B * (HD / 2)) {
+            // MLX fast_rope angles: pos * 2^(-(d/32) log2 theta), f32
+            const int b = tid / (HD / 2), d = tid % (HD / 2);
+            const float th = (float)ms->pos[b] * exp2f(-((float)d / 32.0f) * a.log2_theta);
+            float sn, cs;
+            sincosf(th, &sn, &cs);
+            ms->rc[b][d] = cs;
+            ms->rs[b][d] = sn;
+        }
+        if (tid < MG_NPH * MG_CWARPS) {
+            const int p = tid / MG_CWARPS, w = tid % MG_CWARPS, n = ms->g1[p] - ms->g0[p];
+            const int i0 = w * n / MG_CWARPS, i1 = (w + 1) * n / MG_CWARPS;
+            ms->wtile[p][w] = i1 > i0 ? (ms->g0[p] + i0) / a.ph[p].gpt : -1;
+        }
+    }
+    __syncthreads();
+    const uint32_t epoch = ms->epoch;
+
+    // ---------------- producer warp: stream this CTA's weight ranges ----------------
+    if (tid >= 256) {
+        if (tid == 256) {
+            int sc = 0;
+            bool ok = true;
+            for (int l = 0; l < a.layers && ok; l++) {
+                // the layer's parameter block (double-buffered)
+                const int lb = l & 1;
+                if (l >= 2 && !mbar_wait(&lp_empty[lb], ((l >> 1) - 1) & 1)) {
+                    atomicCAS(&ms->fail, 0, 3);
+                    break;
+                }
+                mbar_expect_tx(&lp_full[lb], (uint32_t)a.lp_bytes);
+                bulk_g2s(lpbuf + lb * lp_stride, a.lparams + (size_t)l * a.lp_bytes, (uint32_t)a.lp_bytes, &lp_full[lb]);
+                for (int p = 0; p < MG_NPH && ok; p++) {
+                    const int g0 = ms->g0[p], n = ms->g1[p] - g0;
+                    const uint8_t* src = a.wbase[l * MG_NPH + p] + (size_t)g0 * a.cb;
+                    for (int j = 0; j * a.gps < n; j++, sc++) {
+                        const int slot = sc % a.nslots;
+                        if (sc >= a.nslots && !mbar_wait(&empty[slot], ((sc / a.nslots) - 1) & 1)) {
+                            atomicCAS(&ms->fail, 0, 3);
+                            ok = false;
+                            break;
+                        }
+                        if (*(volatile int*)&ms->fail) { ok = false; break; }
+                        const int ng = min(a.gps, n - j * a.gps);
+                        const uint32_t bytes = (uint32_t)(ng * a.cb);
+                        mbar_expect_tx(&full[slot], bytes);
+                        bulk_g2s(ring + (size_t)slot * a.slot_bytes, src + (size_t)j * a.gps * a.cb, bytes, &full[slot]);
+                        *(volatile int*)&ms->issued = sc + 1;
+                    }
+                }
+            }
+            *(volatile int*)&ms->prod_done = 1;
+        }
+        return;
+    }
+
+    // ---------------- consumer warps ----------------
+    Ctx cx{&a, &ms->fail, a.err};
+    int cons = 0, lp_used = 0;
+    bool dead = false;
+    auto check = [&]() -> bool {
+        cbar();  // every consumer thread sees the same answer
+        if (*(volatile int*)&ms->fail) dead = true;
+        return dead;
+    };
+    for (int idx = tid; idx < B * H; idx += 256) sm.sX[idx] = a.x_in[idx];
+    long long* tr = a.trace ? a.trace + (size_t)c * a.layers * 32 : nullptr;
+#define MG_STAMP(k) \
+    if (tr && tid == 0) tr[l * 32 + (k)] = clock64();
+    for (int l = 0; l < a.layers && !dead; l++) {
+        const uint32_t tag = epoch * 32u + (uint32_t)l;
+        MG_STAMP(0)
+        if (!mbar_wait(&lp_full[l & 1], (l >> 1) & 1)) atomicCAS(cx.fail, 0, 2);
+        lp_used = l + 1;
+        sm.lp = lpbuf + (l & 1) * lp_stride;
+        sm.st = tr ? tr + l * 32 : nullptr;
+        const uint16_t* ln1 = reinterpret_cast<const uint16_t*>(sm.lp);
+        const uint16_t* ln2 = ln1 + H;
+        // ---- P0 prologue: x_l = x1_{l-1} + down partials; RMSNorm folded ----
+        residual_stats(cx, sm, l > 0 ? 3 : -1, l - 1, tag - 1u, ln1, F16);
+        if (check()) break;
+        MG_STAMP(22)
+        stage<F16>(sm, H / 64, B, H, 0, ln1, F16);
+        cbar();
+        MG_STAMP(1)
+        gemv_phase<FMT>(cx, sm, 0, l, tag, ring, full, empty, 0, true, cons);
+        MG_STAMP(2)
+        if (check()) break;
+        // ---- P1 attention ----
+        {
+            int tot = 0;
+            for (int b = 0; b < B; b++) tot += a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
+            for (int it = c; it < tot; it += a.C) {
+                int rem = it, b = 0;
+                while (rem >= a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH)) {
+                    rem -= a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
+                    b++;
+                }
+                const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
+                attention_item(cx, sm, l, tag, b, rem / ns, rem % ns);
+                if (check()) break;
+            }
+        }
+        if (check()) break;
+        MG_STAMP(3)
+        // ---- P2 prologue: combine the attention chunks of the heads this CTA needs ----
+        {
+            const int gpt = a.ph[1].gpt, n = ms->g1[1] - ms->g0[1];
+            const int base = ms->g0[1] % gpt, nst = min(n, gpt);
+            combine_heads(cx, sm, nst, base, gpt, tag);
+            MG_STAMP(25)
+            stage<F16>(sm, nst, B, H, 1, nullptr, F16);
+            cbar();
+            if (check()) break;
+            MG_STAMP(4)
+            gemv_phase<FMT>(cx, sm, 1, l, tag, ring, full, empty, base, false, cons);
+            MG_STAMP(5)
+            if (check()) break;
+        }
+        // ---- P3 prologue: x1 = x + o_proj partials; RMSNorm folded ----
+        residual_stats(cx, sm, 1, l, tag, ln2, F16);
+        if (check()) break;
+        MG_STAMP(26)
+        stage<F16>(sm, H / 64, B, H, 0, ln2, F16);
+        cbar();
+        MG_STAMP(6)
+        gemv_phase<FMT>(cx, sm, 2, l, tag, ring, full, empty, 0, true, cons);
+        MG_STAMP(7)
+        if (check()) break;
+        // ---- P4 prologue: h = SwiGLU of the gate/up partials this CTA's range needs ----
+        {
+            const int gpt = a.ph[3].gpt, n = ms->g1[3] - ms->g0[3];
+            const int base = ms->g0[3] % gpt, nst = min(n, gpt);
+            swiglu_gather(cx, sm, nst, base, gpt, l, tag);
+            MG_STAMP(24)
+            stage<F16>(sm, nst, B, H, 1, nullptr, F16);
+            cbar();
+            if (check()) break;
+            MG_STAMP(8)
+            gemv_phase<FMT>(cx, sm, 3, l, tag, ring, full, empty, base, false, cons);
+            MG_STAMP(9)
+            if (check()) break;
+        }
+        // release the layer's parameter block to the producer
+        if (tid == 0) mbar_arrive(&lp_empty[l & 1]);
+    }
+#undef MG_STAMP
+    // ---------------- final norm + stop head (CTA b handles row b) ----------------
+    if (!dead && c < B) {
+        const uint32_t tag = epoch * 32u + (uint32_t)(a.layers - 1);
+        residual_stats(cx, sm, 3, a.layers - 1, tag, a.norm, false);
+        check();
+        if (!dead) {
+            const int b = c, warp = tid >> 5, lane = tid & 31;
+            const float inv = ms->inv[b];
+            uint16_t* ob = a.out_cell ? *a.out_cell : nullptr;
+            uint16_t* oo = ob ? ob + ((size_t)ms->step * B + b) * H : nullptr;
+            float l0 = 0.f, l1 = 0.f;
+            for (int f = tid; f < H; f += 256) {
+                const float zf = rb(bf2f(a.norm[f]) * rb(bf2f(sm.sX[b * H + f]) * inv));
+                const uint16_t zb = f2bf(zf);
+                a.z[(size_t)b * H + f] = zb;
+                a.feed[(size_t)b * H + f] = zb;
+                if (oo) oo[f] = zb;
+                l0 += bf2f(a.stop_w[f]) * zf;
+                l1 += bf2f(a.stop_w[H + f]) * zf;
+            }
+            l0 = warp_sum(l0);
+            l1 = warp_sum(l1);
+            if (lane == 0) { ms->red[warp] = l0; ms->red[8 + warp] = l1; }
+            cbar();
+            if (tid == 0) {
+                float s0 = 0.f, s1 = 0.f;
+                for (int w = 0; w < MG_CWARPS; w++) { s0 += ms->red[w]; s1 += ms->red[8 + w]; }
+                s0 = rb(s0 + bf2f(a.stop_b[0]));
+                s1 = rb(s1 + bf2f(a.stop_b[1]));
+                const float m = fmaxf(s0, s1), e0 = expf(s0 - m), e1 = expf(s1 - m);
+                const float pr = e1 / (e0 + e1);
+                a.stop[b] = pr;
+                float* sb = a.stop_cell ? *a.stop_cell : nullptr;
+                if (sb) sb[(size_t)ms->step * B + b] = pr;
+            }
+        }
+    }
+    // ---------------- wind-down ----------------
+    if (dead || *(volatile int*)&ms->fail) {
+        // record the failure, then wait (bounded) for this CTA's copies in flight
+        if (tid == 0) {
+            atomicCAS(a.err, 0, ms->fail ? ms->fail : 4);
+            const long long t0 = clock64();
+            while (!*(volatile int*)&ms->prod_done && clock64() - t0 < MG_TIMEOUT) {}
+            const int issued = *(volatile int*)&ms->issued;
+            for (int sc = cons; sc < issued; sc++) mbar_wait(&full[sc % a.nslots], (sc / a.nslots) & 1);
+            for (int l = lp_used; l < a.layers && l < lp_used + 2; l++) mbar_wait(&lp_full[l & 1], (l >> 1) & 1);
+        }
+        return;
+    }
+    if (c == 0 && tid == 0) {
+        // every CTA read the epoch and positions before contributing to layer 0,
+        // which this CTA needed to reach here
+        a.counter[0] = (int)epoch;
+        a.counter[1] = ms->step + 1;
+        for (int b = 0; b < B; b++) a.seq_len[ms->seq[b]] += 1;
+    }
+}
+
+}  // namespace
+
+int mega_smem_bytes(int nslots, int slot_bytes, int H, int lp_bytes) { return smem_map(nslots, slot_bytes, H, lp_bytes).total; }
+
+cudaError_t launch_mega(const MegaDev& a, int smem, cudaStream_t s) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.C);
+    cfg.blockDim = dim3(MG_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeCooperative;
+    at[0].val.cooperative = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaError_t e;
+    if (a.fmt == 4) {
+        e = cudaFuncSetAttribute(mega_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, mega_kernel<4>, a);
+    } else if (a.fmt == 8) {
+        e = cudaFuncSetAttribute(mega_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, mega_kernel<8>, a);
+    } else {
+        e = cudaFuncSetAttribute(mega_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, mega_kernel<16>, a);
+    }
+    return e;
+}
+
+}  // namespace ming

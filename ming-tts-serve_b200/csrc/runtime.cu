@@ -14,6 +14,7 @@
 #include "../../include/ming_cuda.h"
 #include "dit.cuh"
 #include "lm.cuh"
+#include "mega.cuh"
 #include "pack.h"
 
 using namespace ming;
@@ -130,6 +131,12 @@ struct ming_ctx {
     float** stop_cell = nullptr;
     std::vector<int> row_seq_host;
     std::map<int, cudaGraphExec_t> decode_graphs;
+    // persistent decode kernel (batches of up to MG_MAXB rows)
+    bool mega_on = false;
+    MegaDev mega{};
+    int mega_smem = 0;
+    int* dev_err = nullptr;
+    int* mega_counter = nullptr;  // [2]: epoch (monotonic), generate step index
     uint16_t* gen_out = nullptr;
     size_t gen_out_elems = 0;
     float* gen_stop = nullptr;
@@ -516,12 +523,30 @@ int decode_graph(ming_ctx* c, int B, cudaGraphExec_t* out) {
     }
     cudaGraph_t g;
     CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    launch_step_begin(step_dev(c), B, c->stream);
-    enqueue_layers(c, B);
-    launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, c->x, step_dev(c), c->cfg.hidden, 0, 1,
-                           c->cfg.rms_eps},
-                 B, c->stream);
+    cudaError_t le = cudaSuccess;
+    if (c->mega_on && B <= MG_MAXB) {
+        // one persistent launch per step: it reads the positions, bumps them,
+        // and writes z, the fed-back input and the stop probabilities
+        MegaDev a = c->mega;
+        a.B = B;
+        a.row_seq = c->row_seq;
+        a.x_in = c->x;
+        a.z = c->z;
+        a.feed = c->x;
+        a.stop = c->stop;
+        le = launch_mega(a, c->mega_smem, c->stream);
+    } else {
+        launch_step_begin(step_dev(c), B, c->stream);
+        enqueue_layers(c, B);
+        launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, c->x, step_dev(c), c->cfg.hidden, 0, 1,
+                               c->cfg.rms_eps},
+                     B, c->stream);
+    }
     cudaError_t ce = cudaStreamEndCapture(c->stream, &g);
+    if (le != cudaSuccess) {
+        if (ce == cudaSuccess) cudaGraphDestroy(g);
+        return fail(MING_ERR_CUDA, std::string("persistent kernel launch: ") + cudaGetErrorString(le));
+    }
     if (ce != cudaSuccess) return fail(MING_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
     cudaGraphExec_t ge;
     ce = cudaGraphInstantiate(&ge, g, 0);
@@ -529,6 +554,143 @@ int decode_graph(ming_ctx* c, int B, cudaGraphExec_t* out) {
     if (ce != cudaSuccess) return fail(MING_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
     c->decode_graphs[B] = ge;
     *out = ge;
+    return MING_OK;
+}
+
+// Plans the persistent decode kernel: per-phase group ranges of every CTA,
+// partial-sum slots, buffers. Leaves it off when the device cannot co-schedule
+// one CTA per SM (no cooperative launch) or MING_MEGA=0.
+int setup_mega(ming_ctx* c) {
+    const ming_cfg& f = c->cfg;
+    const char* env = getenv("MING_MEGA");
+    if (env && std::string(env) == "0") return MING_OK;
+    int nsm = 0, coop = 0, optin = 0;
+    CK(cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, c->device));
+    CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, c->device));
+    CK(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
+    if (!coop) return MING_OK;
+    const int H = f.hidden, fmt = f.weight_bits, cb = chunk_bytes(fmt);
+    const int gps = fmt == 4 ? 14 : (fmt == 8 ? 7 : 4);
+    const int slot = (gps * cb + 127) / 128 * 128;
+    // per-layer parameter block: ln1 | ln2 (bf16) | q|k|v bias (f32), 16-byte multiple
+    const int qkv_rows = (f.heads + 2 * f.kv_heads) * 64;
+    const int lp_bytes = (4 * H + 4 * qkv_rows + 15) / 16 * 16;
+    int nslots = 0;
+    while (mega_smem_bytes(nslots + 1, slot, H, lp_bytes) <= optin) nslots++;
+    MegaDev& a = c->mega;
+    a = MegaDev{};
+    const int tiles[MG_NPH] = {(f.heads + 2 * f.kv_heads) * 4, H / 16, f.ff / 8, H / 16};
+    const int gpt[MG_NPH] = {H / 64, H / 64, H / 64, f.ff / 64};
+    const int C = nsm;
+    int rc = MING_OK;
+    int max_nsc = 0;
+    for (int p = 0; p < MG_NPH; p++) {
+        const int G = tiles[p] * gpt[p];
+        if (G < C) return MING_OK;  // too small to give every CTA work: stay on the per-kernel path
+        std::vector<int> g0(C + 1), tc(2 * tiles[p]);
+        for (int i = 0; i <= C; i++) g0[i] = (int)((long long)i * G / C);
+        int slots = 1, maxn = 0;
+        for (int i = 0; i < C; i++) {
+            maxn = std::max(maxn, g0[i + 1] - g0[i]);
+            max_nsc = std::max(max_nsc, (g0[i + 1] - g0[i] + gps - 1) / gps);
+        }
+        if ((p == 3 && maxn > MG_MAX_STAGE)) return MING_OK;  // staged groups of h
+        for (int t = 0; t < tiles[p]; t++) {
+            int first = -1, last = -1;
+            for (int i = 0; i < C; i++)
+                if (g0[i] < (t + 1) * gpt[p] && g0[i + 1] > t * gpt[p]) {
+                    if (first < 0) first = i;
+                    last = i;
+                }
+            tc[2 * t] = first;
+            tc[2 * t + 1] = last - first + 1;
+            slots = std::max(slots, last - first + 1);
+        }
+        if (slots > 4) return MING_OK;  // the gathers sum at most 4 partials per value
+        int* dg0 = c->mem.alloc<int>(C + 1, &rc);
+        int* dtc = c->mem.alloc<int>(2 * tiles[p], &rc);
+        uint64_t* part = c->mem.alloc<uint64_t>((size_t)f.layers * tiles[p] * slots * 16 * MG_MAXB, &rc);
+        if (rc) return rc;
+        CK(cudaMemcpy(dg0, g0.data(), (C + 1) * 4, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(dtc, tc.data(), 2 * tiles[p] * 4, cudaMemcpyHostToDevice));
+        a.ph[p] = MegaPhase{dg0, dtc, part, tiles[p], gpt[p], slots};
+    }
+    if (nslots < max_nsc + 2) return MING_OK;
+    {
+        int meta = 0;
+        for (int p = 0; p < MG_NPH; p++) meta += 2 * tiles[p];
+        if (meta > 4096 || f.max_ctx / PAGE + 1 > 512) return MING_OK;  // shared-memory tables of the kernel
+    }
+    // per-layer tables gathered into contiguous device arrays
+    std::vector<const uint8_t*> wb((size_t)f.layers * MG_NPH);
+    for (int l = 0; l < f.layers; l++) {
+        wb[l * MG_NPH + 0] = c->layers[l].qkv.w.tiles;
+        wb[l * MG_NPH + 1] = c->layers[l].o.w.tiles;
+        wb[l * MG_NPH + 2] = c->layers[l].gu.w.tiles;
+        wb[l * MG_NPH + 3] = c->layers[l].down.w.tiles;
+    }
+    const uint8_t** dwb = c->mem.alloc<const uint8_t*>(wb.size(), &rc);
+    uint8_t* lpar = c->mem.alloc<uint8_t>((size_t)f.layers * lp_bytes, &rc);
+    const int max_splits = (f.max_ctx + MG_ATT_CH - 1) / MG_ATT_CH;
+    if ((H / 64) * MG_MAXB * max_splits > 2048) return MING_OK;  // split weights live in the 8 KB reduction area
+    uint64_t* attn = c->mem.alloc<uint64_t>((size_t)MG_MAXB * f.heads * max_splits * MG_PART, &rc);
+    c->dev_err = c->mem.alloc<int>(1, &rc);
+    c->mega_counter = c->mem.alloc<int>(2, &rc);
+    if (rc) return rc;
+    CK(cudaMemcpy(dwb, wb.data(), wb.size() * sizeof(void*), cudaMemcpyHostToDevice));
+    for (int l = 0; l < f.layers; l++) {
+        uint8_t* blk = lpar + (size_t)l * lp_bytes;
+        CK(cudaMemcpy(blk, c->layers[l].ln1, H * 2, cudaMemcpyDeviceToDevice));
+        CK(cudaMemcpy(blk + 2 * H, c->layers[l].ln2, H * 2, cudaMemcpyDeviceToDevice));
+        CK(cudaMemcpy(blk + 4 * H, c->layers[l].qkv.w.bias, qkv_rows * 4, cudaMemcpyDeviceToDevice));
+    }
+    a.wbase = dwb;
+    a.lparams = lpar;
+    a.lp_bytes = lp_bytes;
+    a.norm = c->norm;
+    a.stop_w = c->stop_w;
+    a.stop_b = c->stop_b;
+    a.kv = KvDev{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
+    a.seq_len = c->seq_len;
+    a.attn = attn;
+    a.counter = c->mega_counter;
+    a.err = c->dev_err;
+    a.out_cell = c->out_cell;
+    a.stop_cell = c->stop_cell;
+    a.layers = f.layers;
+    a.H = H;
+    a.FF = f.ff;
+    a.heads = f.heads;
+    a.kvh = f.kv_heads;
+    a.fmt = fmt;
+    a.C = C;
+    a.max_splits = max_splits;
+    a.gps = gps;
+    a.cb = cb;
+    a.nslots = nslots;
+    a.slot_bytes = slot;
+    a.log2_theta = c->log2_theta;
+    a.eps = f.rms_eps;
+    const char* tr = getenv("MING_MEGA_TRACE");
+    if (tr && std::string(tr) == "1") {
+        a.trace = c->mem.alloc<long long>((size_t)C * f.layers * 32, &rc);
+        if (rc) return rc;
+    }
+    c->mega_smem = mega_smem_bytes(nslots, slot, H, lp_bytes);
+    c->mega_on = true;
+    return MING_OK;
+}
+
+// Reads (and clears) the persistent kernel's device error flag.
+int check_dev_err(ming_ctx* c) {
+    if (!c->dev_err) return MING_OK;
+    int e = 0;
+    CK(cudaMemcpy(&e, c->dev_err, 4, cudaMemcpyDeviceToHost));
+    if (e) {
+        const int zero = 0;
+        cudaMemcpy(c->dev_err, &zero, 4, cudaMemcpyHostToDevice);
+        return fail(MING_ERR_CUDA, "persistent decode kernel: a bounded device wait expired (code " + std::to_string(e) + ")");
+    }
     return MING_OK;
 }
 
@@ -788,6 +950,7 @@ int ming_cuda_finalize(ming_ctx* c) {
     CK(cudaMemcpy(c->bt, c->bt_host.data(), c->bt_host.size() * 4, cudaMemcpyHostToDevice));
     for (int p = f.max_pages - 1; p >= 0; p--) c->free_pages.push_back(p);
     c->seqs.assign(f.max_seqs, SeqInfo{});
+    if (f.layers > 0 && (rc = setup_mega(c))) return rc;
 
     // ---- flow head ----
     if (f.dit_mode != MING_DIT_NONE) {
@@ -959,7 +1122,10 @@ int ming_cuda_lm_decode(ming_ctx* c, int B, const int* ids, const uint16_t* x, u
     for (int i = 0; i < B; i++) c->seqs[ids[i]].len += 1;
     if ((rc = copy_out(c, out, c->z, (size_t)B * H * 2, kind))) return rc;
     if ((rc = copy_out(c, stop, c->stop, (size_t)B * 4, kind))) return rc;
-    if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(c->stream));
+    if (kind == MING_PTR_HOST) {
+        CK(cudaStreamSynchronize(c->stream));
+        if ((rc = check_dev_err(c))) return rc;
+    }
     return MING_OK;
 }
 
@@ -1007,6 +1173,7 @@ int ming_cuda_lm_generate(ming_ctx* c, int B, const int* ids, const uint16_t* x0
     CK(cudaMemcpyAsync(c->out_cell, &o, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(c->stop_cell, &sp, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemsetAsync(c->step_counter, 0, 8, c->stream));
+    if (c->mega_counter) CK(cudaMemsetAsync(c->mega_counter + 1, 0, 4, c->stream));  // the epoch is never reset
     if ((rc = copy_in(c, c->x, x0, (size_t)B * H * 2, kind))) return rc;
     for (int i = 0; i < steps; i++) CK(cudaGraphLaunch(g, c->stream));
     for (int i = 0; i < B; i++) c->seqs[ids[i]].len += steps;
@@ -1014,6 +1181,7 @@ int ming_cuda_lm_generate(ming_ctx* c, int B, const int* ids, const uint16_t* x0
         if (out) CK(cudaMemcpyAsync(out, o, (size_t)steps * B * H * 2, cudaMemcpyDeviceToHost, c->stream));
         if (stop) CK(cudaMemcpyAsync(stop, sp, (size_t)steps * B * 4, cudaMemcpyDeviceToHost, c->stream));
         CK(cudaStreamSynchronize(c->stream));
+        if ((rc = check_dev_err(c))) return rc;
     }
     return MING_OK;
 }
@@ -1114,7 +1282,7 @@ int ming_cuda_sync(ming_ctx* c) {
     if (!c) return fail(MING_ERR_INVALID, "null context");
     CK(cudaStreamSynchronize(c->stream));
     CK(cudaGetLastError());
-    return MING_OK;
+    return check_dev_err(c);
 }
 
 int ming_cuda_destroy(ming_ctx* c) {
@@ -1168,6 +1336,20 @@ int ming_cuda_unpack_linear(ming_ctx* c, const char* name, float* out) {
         }
     }
     return fail(MING_ERR_INVALID, std::string("no packed linear holds ") + name);
+}
+
+// Diagnostics: copies the persistent kernel's phase trace (MING_MEGA_TRACE=1):
+// [C][layers][32] clock64 stamps of the last step. Returns the CTA count in *n.
+extern "C" int ming_cuda_debug_trace(ming_ctx* c, long long* out, int cap, int* n) {
+    if (!c || !n) return fail(MING_ERR_INVALID, "null argument");
+    *n = 0;
+    if (!c->mega_on || !c->mega.trace) return MING_OK;
+    const size_t cnt = (size_t)c->mega.C * c->cfg.layers * 32;
+    if ((size_t)cap < cnt) return fail(MING_ERR_INVALID, "trace buffer too small");
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaMemcpy(out, c->mega.trace, cnt * 8, cudaMemcpyDeviceToHost));
+    *n = c->mega.C;
+    return MING_OK;
 }
 
 int ming_cuda_flow_temb(ming_ctx* c, uint16_t* te) {
