@@ -263,8 +263,10 @@ def run_ours(args, ws, rank, local):
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(cfgid, W, lens, x_last, args.cpu_seconds)
+    launches_per_step = ctx.step_kernels(B)
+    kname = ("mega_kernel (persistent decode step, one launch)" if launches_per_step == 1 else
+             "decode step (captured graph: %d kernels)" % launches_per_step)
     ctx.close()
-    launches_per_step = 1 + 24 * 5 + 1
     res = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
@@ -273,7 +275,7 @@ def run_ours(args, ws, rank, local):
         "config": {"workload": c["name"], "batch_per_gpu": B, "prompt_lens": lens if len(lens) <= 4 else f"U[32,512] x{len(lens)}",
                    "kv_positions_at_start": lens_start, "parallelism": f"replicas x{ws} (no collective)",
                    "l2": "inputs larger than L2: every step streams all weights (%.0f MB) from HBM" % (wbytes / 1e6)},
-        "roofline": {"bound": "hbm", "kernel": "decode step (captured graph: %d kernels)" % launches_per_step,
+        "roofline": {"bound": "hbm", "kernel": kname,
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_step": step_bytes, "traffic": traffic},
         "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": ck, "cpu_baseline": cpu,

@@ -129,6 +129,11 @@ int ming_cuda_aggregate(ming_ctx* ctx, int B, const uint16_t* latent, uint16_t* 
 /* The context's CUDA stream (a cudaStream_t), for event timing by callers. */
 int ming_cuda_get_stream(ming_ctx* ctx, void** stream);
 int ming_cuda_sync(ming_ctx* ctx);
+/* Kernels one decode step of B rows launches: 1 when the persistent decode
+ * kernel serves B (B <= 4 and a device that co-schedules one block per SM),
+ * else the per-kernel path's count. No reference counterpart: the reference
+ * dispatches its Metal kernels itself and exposes no such count. */
+int ming_cuda_step_kernels(ming_ctx* ctx, int B, int* n);
 int ming_cuda_destroy(ming_ctx* ctx);
 const char* ming_cuda_last_error(void);
 

@@ -8,7 +8,7 @@ namespace ming {
 namespace {
 
 constexpr long long MG_TIMEOUT = 4000000000LL;  // cycles (~2 s) before a wait gives up
-constexpr int MG_SK = 32;                       // staged 64-groups of activations (max)
+constexpr int MG_SK = MG_MAX_STAGE;             // staged 64-groups of activations (max)
 
 // ---------------- PTX helpers ----------------
 MING_DEV uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -49,25 +49,50 @@ MING_DEV void cp16(void* dst, const void* src) {
 MING_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 MING_DEV void cp_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 MING_DEV void cbar() { asm volatile("bar.sync 1, 256;\n" ::: "memory"); }  // consumer warps only
-MING_DEV uint64_t ldr64(const uint64_t* p) {
+MING_DEV uint64_t ldr64(const void* p) {
     uint64_t v;
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-MING_DEV uint32_t ldr32(const int* p) {
+MING_DEV uint32_t ldr32(const void* p) {
     uint32_t v;
     asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
+MING_DEV uint32_t lda32(const unsigned int* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+MING_DEV uint4 ldcg16(const void* p) {  // 16 bytes from L2 (never a stale L1 line)
+    uint4 r;
+    asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p)
+                 : "memory");
+    return r;
+}
 MING_DEV void str64(uint64_t* p, uint64_t v) {
     asm volatile("st.relaxed.gpu.global.b64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
+MING_DEV void red_add64(unsigned long long* p, long long v) {
+    asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
+}
+MING_DEV void red_release_add32(unsigned int* p, unsigned int v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+}
 MING_DEV uint64_t tagged(uint32_t tag, float v) { return ((uint64_t)tag << 32) | __float_as_uint(v); }
+// fixed point with MG_FIX fraction bits (|v| < 2^31)
+MING_DEV long long to_fix(float v) { return __float2ll_rn(v * (float)(1ull << MG_FIX)); }
+MING_DEV float from_fix(unsigned long long u) { return __ll2float_rn((long long)u) * (1.0f / (float)(1ull << MG_FIX)); }
+MING_DEV float from_fix2(uint32_t lo, uint32_t hi) { return from_fix(((unsigned long long)hi << 32) | lo); }
+
+// x / B for the step's row count B <= 4 (bm = ceil(2^32 / B)), exact for x < 2^30
+MING_DEV int divB(int x, unsigned long long bm) { return (int)(((unsigned long long)(uint32_t)x * bm) >> 32); }
 
 struct Ctx {
     const MegaDev* a;
-    int* fail;       // shared: first failure code of this CTA (0 = none)
-    int* gerr;
+    int* fail;  // shared: first failure code of this CTA (0 = none)
 };
 
 // Polls one tagged f32 word until its tag is `tag`. On timeout or a failure
@@ -83,13 +108,32 @@ __device__ __noinline__ float poll(const Ctx& x, const uint64_t* p, uint32_t tag
         if ((uint32_t)(v >> 32) == tag) return __uint_as_float((uint32_t)v);
         if (((++it) & 63) == 0) {
             if (*(volatile int*)x.fail) return 0.f;
-            if (ldr32(x.gerr)) {
+            if (ldr32(x.a->err)) {
                 atomicCAS(x.fail, 0, 5);
                 return 0.f;
             }
             if (clock64() - t0 > MG_TIMEOUT) {
                 atomicCAS(x.fail, 0, 1);
                 return 0.f;
+            }
+        }
+    }
+}
+
+// One thread waits until the counter reaches target (acquire); bounded.
+__device__ __noinline__ void wait_count(const Ctx& x, const unsigned int* cnt, unsigned int target) {
+    const long long t0 = clock64();
+    int it = 0;
+    while ((int)(lda32(cnt) - target) < 0) {
+        if (((++it) & 15) == 0) {
+            if (*(volatile int*)x.fail) return;
+            if (ldr32(x.a->err)) {
+                atomicCAS(x.fail, 0, 5);
+                return;
+            }
+            if (clock64() - t0 > MG_TIMEOUT) {
+                atomicCAS(x.fail, 0, 1);
+                return;
             }
         }
     }
@@ -138,8 +182,8 @@ MING_DEV void mma_k(float (&t)[4], const uint32_t (&a)[4], uint2 b) {
     if constexpr (FMT == 16) mma_bf16(t, a, b.x, b.y);
     else mma_f16(t, a, b.x, b.y);
 }
-// acc += W_group . y_group for one group (t: the group's own sums for the
-// quantized scale/bias, added to acc after the 4 k-steps).
+// acc += W_group . y_group (t: the group's own sums; the quantized scale and
+// bias apply per group: s * sum(q y) + b * sum(y)).
 template <int FMT>
 MING_DEV void group_finish(const GroupW& g, const float (&t)[4], const float* ys, int lane, float (&acc)[4]) {
     if constexpr (FMT == 16) {
@@ -154,101 +198,71 @@ MING_DEV void group_finish(const GroupW& g, const float (&t)[4], const float* ys
     }
 }
 
-// Shared-memory carve-up (byte offsets from the dynamic base). sB, sYs and sT
-// are contiguous: an attention item uses the three as one scratch area.
+// ---------------- shared memory ----------------
 constexpr int MG_T_BYTES = MG_SK * 64 * MG_MAXB * 2;  // bf16 [stage][64][row]
-constexpr int MG_META_INTS = 4096;                    // tile maps of the 4 phases + CTA ranges
 constexpr int MG_BT_INTS = 512;                       // block-table row per batch row
+constexpr int MG_B_BYTES = MG_SK * 4 * 32 * 8;        // mma B fragments
 struct SmemMap {
-    int ring, bars, sB, sYs, sT, sRed, sX, lp, meta, bt, misc, total;
+    int ring, bars, sB, sYs, sT, sRed, sX, lp, bt, misc, total;
 };
 __host__ __device__ inline SmemMap smem_map(int nslots, int slot_bytes, int H, int lp_bytes) {
     SmemMap m;
     m.ring = 0;
     m.bars = nslots * slot_bytes;
     m.sB = (m.bars + (2 * nslots + 4) * 8 + 127) / 128 * 128;
-    m.sYs = m.sB + MG_SK * 4 * 32 * 8;
+    m.sYs = m.sB + MG_B_BYTES;
     m.sT = m.sYs + MG_SK * 8 * 4;
     m.sRed = m.sT + MG_T_BYTES;
     m.sX = m.sRed + MG_CWARPS * 2 * 16 * 8 * 4;
     m.lp = m.sX + (MG_MAXB * H * 2 + 127) / 128 * 128;
-    m.meta = m.lp + 2 * ((lp_bytes + 127) / 128 * 128);
-    m.bt = m.meta + MG_META_INTS * 4;
+    m.bt = m.lp + 2 * ((lp_bytes + 127) / 128 * 128);
     m.misc = m.bt + MG_MAXB * MG_BT_INTS * 4;
     m.total = m.misc + 4096;
     return m;
 }
-constexpr int MG_ATT_SCRATCH = MG_SK * 4 * 32 * 8 + MG_SK * 8 * 4 + MG_T_BYTES;
+constexpr int MG_ATT_SCRATCH = MG_B_BYTES + MG_SK * 8 * 4 + MG_T_BYTES;
 // attention item scratch: K, V rows (padded to 72) + q + new k/v + scores
 static_assert(2 * MG_ATT_CH * (HD + 8) * 2 + 8 * HD * 4 + 2 * HD * 4 + 8 * MG_ATT_CH * 4 <= MG_ATT_SCRATCH,
               "attention scratch does not fit");
 
-struct Misc {          // small per-CTA state in shared memory
+struct Misc {              // small per-CTA state in shared memory
     float inv[MG_MAXB];    // 1/rms of each row (current norm)
     float scl[MG_MAXB];    // operand pre-scale (power of two) of each row
-    float post[MG_MAXB];   // scale applied to the f32 partial sums
+    float post[MG_MAXB];   // scale applied to the f32 sums
     int pos[MG_MAXB];      // row positions (cache length before this step)
     int seq[MG_MAXB];      // row sequences
-    float ml[2 * 16 * MG_MAXB];  // per (stage, row): attention split max, 1/sum
     float red[MG_CWARPS * 2 * MG_MAXB];  // block reductions
-    int g0[MG_NPH], g1[MG_NPH];  // this CTA's group range per phase
-    int toff[MG_NPH];            // offset of each phase's tile map in meta
-    int wtile[MG_NPH][MG_CWARPS];  // first tile of each warp's group range (-1: none)
-    float rc[MG_MAXB][HD / 2];   // RoPE cos/sin of each row's position, per frequency
+    int g0[MG_NPH], g1[MG_NPH];          // this CTA's group range per phase
+    int wtile[MG_NPH][MG_CWARPS];        // first tile of each warp's group range (-1: none)
+    float rc[MG_MAXB][HD / 2];           // RoPE cos/sin of each row's position, per frequency
     float rs[MG_MAXB][HD / 2];
     int fail;
     int prod_done;
     int issued;
     uint32_t epoch;
     int step;
+    unsigned long long bm;  // divB multiplier of the step's row count
 };
 static_assert(sizeof(Misc) <= 4096, "Misc must fit its shared-memory slot");
 
-struct Sm {            // shared-memory views used by the phases
+struct Sm {  // shared-memory views used by the phases
     uint2* sB;
     float* sYs;
     uint16_t* sT;
     float* sRed;
     uint16_t* sX;
-    const uint8_t* lp;   // current layer's parameter block
-    const int* meta;
-    const int* bt;       // [MG_MAXB][MG_BT_INTS]
+    const uint8_t* lp;  // current layer's parameter block
+    const int* bt;      // [MG_MAXB][MG_BT_INTS]
     Misc* ms;
-    long long* st;       // optional per-layer stamp row (diagnostics)
+    long long* st;      // optional stamp row of the current layer (diagnostics)
+    int so;             // stamp slot of the current phase's sub-steps
 };
 #define MG_SUB(k) \
-    if (sm.st && threadIdx.x == 0) sm.st[(k)] = clock64();
+    if (sm.st && threadIdx.x == 0) sm.st[sm.so + (k)] = clock64();
 
-// tile map entry of phase p: first CTA covering tile t, and how many do
-MING_DEV int tile_first(const Sm& sm, int p, int t) { return sm.meta[sm.ms->toff[p] + 2 * t]; }
-MING_DEV int tile_count(const Sm& sm, int p, int t) { return sm.meta[sm.ms->toff[p] + 2 * t + 1]; }
-
-// ---------------- batched tagged gathers ----------------
-// Sum of n (<= 4) tagged partials p[0], p[stride], ...: issue() starts the
-// loads, finish() checks the tags (polling only the stragglers) and sums in
-// slot order, so a thread pays one L2 round trip per batch.
-struct Pend {
-    uint64_t v[4];
-    const uint64_t* p;
-    int n, stride;
-    MING_DEV void issue(const uint64_t* p_, int n_, int stride_) {
-        p = p_;
-        n = n_;
-        stride = stride_;
-#pragma unroll
-        for (int k = 0; k < 4; k++) v[k] = k < n ? ldr64(p + (size_t)k * stride) : 0ull;
-    }
-    MING_DEV float finish(const Ctx& cx, uint32_t tag) const {
-        float s = 0.f;
-#pragma unroll
-        for (int k = 0; k < 4; k++)
-            if (k < n) s += ((uint32_t)(v[k] >> 32) == tag) ? __uint_as_float((uint32_t)v[k]) : poll(cx, p + (size_t)k * stride, tag);
-        return s;
-    }
-};
-
-MING_DEV uint64_t* part_ptr(const MegaPhase& ph, int l, int B, int t, int r, int b) {
-    return ph.part + ((((size_t)l * ph.tiles + t) * ph.slots) * 16 + r) * B + b;
+// accumulator rows of (step parity, layer, kind); row b at + b * acc_w
+MING_DEV unsigned long long* acc_ptr(const MegaDev& a, uint32_t epoch, int l, int which) {
+    return a.acc + (((size_t)(epoch & 1) * a.layers + l) * MG_NACC + which) * MG_MAXB * a.acc_w;
 }
 
 // ---------------- staging of the mma B operand ----------------
@@ -259,19 +273,16 @@ MING_DEV uint64_t* part_ptr(const MegaPhase& ph, int l, int B, int t, int r, int
 // bias term) with shuffles. Sources: mode 0, sX times the norm weight nw and
 // the row pre-scale; mode 1, the bf16 values sT [stage][64][row].
 template <bool F16>
-MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint16_t* nw, bool ysum) {
+MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint16_t* nw) {
     const int tid = threadIdx.x;
-    // zero the fragment entries of the unused rows (all entries, then overwrite)
     uint4* z = reinterpret_cast<uint4*>(sm.sB);
     for (int e = tid; e < nstage * 4 * 32 / 2; e += 256) z[e] = make_uint4(0u, 0u, 0u, 0u);
-    for (int e = tid; e < nstage * 8; e += 256) sm.sYs[e] = 0.f;
     cbar();
     const int tot = nstage * B * 16;
-    // warp-uniform trip count (a multiple of 32): every lane reaches the shuffles
-    const int totr = (tot + 31) & ~31;
+    const int totr = (tot + 31) & ~31;  // warp-uniform trip count: every lane reaches the shuffles
     for (int e = tid; e < totr; e += 256) {
         const bool act = e < tot;
-        const int q16 = e & 15, sb = e >> 4, si = act ? sb / B : 0, b = act ? sb - si * B : 0;
+        const int q16 = e & 15, sb = e >> 4, si = act ? divB(sb, sm.ms->bm) : 0, b = act ? sb - si * B : 0;
         const int ks = q16 >> 2, tq = q16 & 3, kk = ks * 16 + 2 * tq;
         float sum = 0.f;
         if (act) {
@@ -302,54 +313,38 @@ MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint
         sum += __shfl_xor_sync(0xffffffffu, sum, 4);
         sum += __shfl_xor_sync(0xffffffffu, sum, 2);
         sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        if (ysum && act && q16 == 0) sm.sYs[si * 8 + b] = sum;
+        if (act && q16 == 0) sm.sYs[si * 8 + b] = sum;
     }
+    cbar();
+    MG_SUB(0)
 }
 
-// Residual update from a GEMV phase's partials, fused with the RMSNorm
-// statistics of the updated rows: sX[b][f] = rb(sX + rb(sum of the partials
-// of feature f)) (plain row order: tile f/16, row f%16), then inv, pre-scale
-// and post-scale of each row for the norm weight nw. With p < 0 the rows are
-// left as they are (layer 0) and only the statistics are computed.
-MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, int p, int l, uint32_t tag, const uint16_t* nw, bool f16) {
-    const MegaDev& a = *cx.a;
-    const int H = a.H, B = a.B, tot = B * H, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+// Residual update from a fixed-point accumulator, fused with the RMSNorm
+// statistics of the updated rows: sX[b][f] = rb(sX + rb(acc[b][f])), then
+// inv, pre-scale and post-scale of each row for the norm weight nw. With acc
+// null the rows stay as they are (the layer-0 input).
+MING_DEV void residual_stats(const Sm& sm, const MegaDev& a, const unsigned long long* acc, const uint16_t* nw, bool f16) {
+    const int H = a.H, B = a.B, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float ss[MG_MAXB], am[MG_MAXB];
 #pragma unroll
     for (int b = 0; b < MG_MAXB; b++) ss[b] = am[b] = 0.f;
-    for (int base = 0; base < tot; base += 256 * 4) {
-        Pend pd[4];
-        if (p >= 0) {
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int idx = base + tid + i * 256;
-                if (idx < tot) {
-                    const int b = idx / H, f = idx % H, t = f >> 4;
-                    pd[i].issue(part_ptr(a.ph[p], l, B, t, f & 15, b), tile_count(sm, p, t), 16 * B);
-                } else {
-                    pd[i].n = 0;
-                }
-            }
+    for (int idx = tid * 2; idx < B * H; idx += 512) {  // two features per thread per pass
+        const int b = idx / H, f = idx - b * H;
+        float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sm.sX + idx));
+        if (acc) {
+            const uint4 v = ldcg16(acc + (size_t)b * a.acc_w + f);
+            x.x = rb(x.x + rb(from_fix2(v.x, v.y)));
+            x.y = rb(x.y + rb(from_fix2(v.z, v.w)));
+            *reinterpret_cast<uint32_t*>(sm.sX + idx) = pack_bf16x2(x.x, x.y);
         }
+        const float2 w = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(nw + f));
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int idx = base + tid + i * 256;
-            if (idx >= tot) continue;
-            const int b = idx / H, f = idx % H;
-            float x = bf2f(sm.sX[idx]);
-            if (p >= 0) {
-                x = rb(x + rb(pd[i].finish(cx, tag)));
-                sm.sX[idx] = f2bf(x);
+        for (int bb = 0; bb < MG_MAXB; bb++)
+            if (bb == b) {
+                ss[bb] += x.x * x.x + x.y * x.y;
+                am[bb] = fmaxf(am[bb], fmaxf(fabsf(x.x * w.x), fabsf(x.y * w.y)));
             }
-#pragma unroll
-            for (int bb = 0; bb < MG_MAXB; bb++)
-                if (bb == b) {
-                    ss[bb] += x * x;
-                    am[bb] = fmaxf(am[bb], fabsf(x * bf2f(nw[f])));
-                }
-        }
     }
-    if (p == 1) MG_SUB(20)
 #pragma unroll
     for (int b = 0; b < MG_MAXB; b++) {
         const float s1 = warp_sum(ss[b]), a1 = warp_max(am[b]);
@@ -374,41 +369,82 @@ MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, int p, int l, uint32_t
     cbar();
 }
 
-// One GEMV phase on the CTA's ring chunks: partial sums of the CTA's group
-// range, reduced over warps in fixed order and published per (tile, CTA).
+// Publishes a phase's completion. The CTA barrier orders every thread's
+// contributions before thread 0 (release/acquire at CTA scope); thread 0's
+// gpu-scope release increment is cumulative over them, so a reader that
+// acquires the counter sees all of them. No per-thread fence is needed (a
+// sequentially consistent fence from every warp drains the SM's memory pipe).
+MING_DEV void publish(const Sm& sm, unsigned int* cnt) {
+    MG_SUB(5)
+    cbar();
+    if (threadIdx.x == 0) red_release_add32(cnt, 1u);
+    MG_SUB(6)
+}
+
+// One thread waits until every CTA published, then releases the CTA.
+MING_DEV void await(const Ctx& cx, const unsigned int* cnt, unsigned int target) {
+    if (threadIdx.x == 0 && (int)(lda32(cnt) - target) < 0) wait_count(cx, cnt, target);
+    cbar();
+}
+
+enum { OUT_ACC = 0, OUT_GLU = 1 };
+
+// One GEMV phase on the CTA's ring chunks. Warps take contiguous runs of the
+// CTA's groups (two groups per iteration: independent mma chains; a run spans
+// at most two tiles), meet in shared memory, and the CTA emits per (tile,
+// row, batch row) either a fixed-point contribution to acc (row index
+// tile*16 + r) or, for whole gate|up tiles, the SwiGLU outputs into hb.
 template <int FMT>
-MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int l, uint32_t tag, uint8_t* ring, uint64_t* full,
-                                        uint64_t* empty, int stage_base, bool use_post, int& cons) {
+MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint8_t* ring, uint64_t* full, uint64_t* empty,
+                         int stage_base, bool use_post, int out, unsigned long long* acc, uint16_t* hb) {
     const MegaDev& a = *cx.a;
-    const MegaPhase& ph = a.ph[p];
     Misc* ms = sm.ms;
-    const int c = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int g0 = ms->g0[p], g1 = ms->g1[p], n = g1 - g0, gpt = ph.gpt;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g0 = ms->g0[p], g1 = ms->g1[p], n = g1 - g0, gpt = a.ph[p].gpt;
+    if (n <= 0) return;  // CTA-uniform
     const int nsc = (n + a.gps - 1) / a.gps;
     for (int j = 0; j < nsc; j++) {
-        const int sc = cons + j;
+        const int sc = cons_base + j;
         if (!mbar_wait(&full[sc % a.nslots], (sc / a.nslots) & 1)) atomicCAS(cx.fail, 0, 2);
     }
-    if (p == 2) MG_SUB(16)
+    MG_SUB(1)
     const int i0 = warp * n / MG_CWARPS, i1 = (warp + 1) * n / MG_CWARPS;
     const int tb = ms->wtile[p][warp];
-    float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    if (!*(volatile int*)cx.fail) {
-        // two groups per iteration: independent mma chains
+    float acc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    if (i0 < i1 && !*(volatile int*)cx.fail) {
+        // walk the warp's run incrementally: tile t, group kg in the tile,
+        // ring slot and group wi in the slot
+        int t, kg, wi, slot;
+        {
+            const int g = g0 + i0;
+            t = g / gpt;
+            kg = g - t * gpt;
+            const int jj = i0 / a.gps;
+            wi = i0 - jj * a.gps;
+            slot = (cons_base + jj) % a.nslots;
+        }
         for (int i = i0; i < i1; i += 2) {
             const bool two = i + 1 < i1;
             const uint8_t* ch[2];
-            int si[2], slot_u[2];
+            int si[2], tu[2];
 #pragma unroll
             for (int u = 0; u < 2; u++) {
-                const int ii = (u == 1 && !two) ? i : i + u;
-                const int g = g0 + ii, t = g / gpt, kg = g - t * gpt;
-                const int sc = cons + ii / a.gps;
-                ch[u] = ring + (size_t)(sc % a.nslots) * a.slot_bytes + (size_t)(ii - (ii / a.gps) * a.gps) * a.cb;
-                int s_ = kg - stage_base;
-                if (s_ < 0) s_ += gpt;
-                si[u] = s_;
-                slot_u[u] = t == tb ? 0 : 1;
+                ch[u] = ring + (size_t)slot * a.slot_bytes + (size_t)wi * a.cb;
+                const int s_ = kg - stage_base;
+                si[u] = s_ < 0 ? s_ + gpt : s_;
+                tu[u] = t == tb ? 0 : 1;
+                if (++kg == gpt) {
+                    kg = 0;
+                    t++;
+                }
+                if (++wi == a.gps) {
+                    wi = 0;
+                    if (++slot == a.nslots) slot = 0;
+                }
+            }
+            if (!two) {
+                ch[1] = ch[0];
+                si[1] = si[0];
             }
             GroupW gw[2];
             load_group<FMT>(ch[0], lane, gw[0]);
@@ -424,68 +460,89 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int l, uint32_t tag
                 mma_k<FMT>(t0, a0, b0);
                 mma_k<FMT>(t1, a1, b1);
             }
-            if (slot_u[0] == 0) group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc[0]);
-            else group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc[1]);
+            if (tu[0] == 0) group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc2[0]);
+            else group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc2[1]);
             if (two) {
-                if (slot_u[1] == 0) group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc[0]);
-                else group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc[1]);
+                if (tu[1] == 0) group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc2[0]);
+                else group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc2[1]);
             }
         }
     }
+    MG_SUB(2)
     {
         const int gr = lane >> 2, cc = 2 * (lane & 3);
         float* r = sm.sRed + warp * 2 * 128;
 #pragma unroll
         for (int u = 0; u < 2; u++) {
-            r[u * 128 + gr * 8 + cc] = acc[u][0];
-            r[u * 128 + gr * 8 + cc + 1] = acc[u][1];
-            r[u * 128 + (gr + 8) * 8 + cc] = acc[u][2];
-            r[u * 128 + (gr + 8) * 8 + cc + 1] = acc[u][3];
+            r[u * 128 + gr * 8 + cc] = acc2[u][0];
+            r[u * 128 + gr * 8 + cc + 1] = acc2[u][1];
+            r[u * 128 + (gr + 8) * 8 + cc] = acc2[u][2];
+            r[u * 128 + (gr + 8) * 8 + cc + 1] = acc2[u][3];
         }
     }
-    if (p == 2) MG_SUB(17)
     cbar();
-    if (p == 2) MG_SUB(18)
+    // every warp is done with the phase's ring slots: hand them back before
+    // any global write of this phase (an arrive orders this thread's earlier
+    // memory operations before it)
     if (lane == 0)
-        for (int j = 0; j < nsc; j++) mbar_arrive(&empty[(cons + j) % a.nslots]);
-    cons += nsc;
-    // fixed-order reduction over warps, one partial per (tile, CTA)
-    const int t0 = g0 / gpt, t1 = (g1 - 1) / gpt;
-    const int B = a.B;
-    for (int e = threadIdx.x; e < (t1 - t0 + 1) * 16 * B; e += 256) {
-        const int t = t0 + e / (16 * B), r = (e / B) % 16, b = e % B;
-        float s = 0.f;
+        for (int j = 0; j < nsc; j++) mbar_arrive(&empty[(cons_base + j) % a.nslots]);
+    MG_SUB(3)
+    const int t0 = g0 / gpt, nt = (g1 - 1) / gpt - t0 + 1, B = a.B;
+    if (out == OUT_ACC) {
+        // entries (tile, row r, batch row b) with b padded to 4
+        for (int e = threadIdx.x; e < nt * 64; e += 256) {
+            const int b = e & 3, r = (e >> 2) & 15, t = t0 + (e >> 6);
+            if (b >= B) continue;
+            float s = 0.f;
 #pragma unroll
-        for (int w = 0; w < MG_CWARPS; w++) {
-            const int wt = ms->wtile[p][w];
-            if (wt == t) s += sm.sRed[(w * 2 + 0) * 128 + r * 8 + b];
-            else if (wt >= 0 && wt + 1 == t) s += sm.sRed[(w * 2 + 1) * 128 + r * 8 + b];
+            for (int w = 0; w < MG_CWARPS; w++) {  // fixed warp order
+                const int wt = ms->wtile[p][w];
+                if (wt == t) s += sm.sRed[(w * 2 + 0) * 128 + r * 8 + b];
+                else if (wt >= 0 && wt + 1 == t) s += sm.sRed[(w * 2 + 1) * 128 + r * 8 + b];
+            }
+            if (use_post) s *= ms->post[b];
+            red_add64(acc + (size_t)b * a.acc_w + t * 16 + r, to_fix(s));
         }
-        if (use_post) s *= ms->post[b];
-        const int slot = c - tile_first(sm, p, t);
-        str64(part_ptr(ph, l, B, t, r, b) + (size_t)slot * 16 * B, tagged(tag, s));
+    } else {
+        // whole gate|up tiles: rows 0..7 gate, 8..15 up of features 8t..8t+7
+        for (int e = threadIdx.x; e < nt * 32; e += 256) {
+            const int b = e & 3, r = (e >> 2) & 7, t = t0 + (e >> 5);
+            if (b >= B) continue;
+            float gs = 0.f, us = 0.f;
+#pragma unroll
+            for (int w = 0; w < MG_CWARPS; w++) {
+                const int wt = ms->wtile[p][w];
+                const int u = wt == t ? 0 : ((wt >= 0 && wt + 1 == t) ? 1 : -1);
+                if (u < 0) continue;
+                gs += sm.sRed[(w * 2 + u) * 128 + r * 8 + b];
+                us += sm.sRed[(w * 2 + u) * 128 + (r + 8) * 8 + b];
+            }
+            const float gv = rb(gs * ms->post[b]), uv = rb(us * ms->post[b]);
+            const float sg = rb(1.0f / (1.0f + expf(-gv)));
+            hb[(size_t)b * a.FF + t * 8 + r] = f2bf(rb(rb(gv * sg) * uv));
+        }
     }
-    cbar();
+    MG_SUB(4)
 }
 
 // Attention of one (row, kv head, 128-position chunk) item. q/k/v come from
-// the P0 partials (+ bias, bf16, RoPE on q and k as MLX fast_rope); cached K/V
-// rows are prefetched with cp.async before the wait.
-MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, int b, int g, int s) {
+// the q|k|v accumulator (+ bias, bf16, RoPE on q and k as MLX fast_rope);
+// cached K/V rows are prefetched with cp.async before the wait for q|k|v.
+MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, int b, int g, int s, bool waited) {
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int grp = a.heads / a.kvh, pos = ms->pos[b], B = a.B;
+    const int grp = a.heads / a.kvh, pos = ms->pos[b];
     const int p0 = s * MG_ATT_CH, p1 = min(pos + 1, p0 + MG_ATT_CH), pc = min(p1, pos);
     // K/V rows padded to 72 elements (144 B): 16-byte loads of 8 consecutive
     // rows fall on distinct bank groups
     constexpr int KS = HD + 8;
-    uint16_t* sK = reinterpret_cast<uint16_t*>(sm.sB);              // [128][72]
-    uint16_t* sV = sK + MG_ATT_CH * KS;                               // [128][72]
-    float* sq = reinterpret_cast<float*>(sV + MG_ATT_CH * KS);       // [8][64]
-    float* skn = sq + 8 * HD;                                         // [64]
-    float* svn = skn + HD;                                            // [64]
-    float* sS = svn + HD;                                             // [8][128]
+    uint16_t* sK = reinterpret_cast<uint16_t*>(sm.sB);         // [128][72]
+    uint16_t* sV = sK + MG_ATT_CH * KS;                          // [128][72]
+    float* sq = reinterpret_cast<float*>(sV + MG_ATT_CH * KS);  // [8][64]
+    float* skn = sq + 8 * HD;                                    // [64]
+    float* svn = skn + HD;                                       // [64]
+    float* sS = svn + HD;                                        // [8][128]
     const int* bt = sm.bt + b * MG_BT_INTS;
     // 1. prefetch cached K/V rows [p0, pc)
     for (int e = tid; e < (pc - p0) * 8; e += 256) {
@@ -495,64 +552,49 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         cp16(sV + j * KS + piece * 8, a.kv.pool + kv_index(a.kv, page, l, 1, g, p % PAGE) + piece * 8);
     }
     cp_commit();
-    MG_SUB(10)
-    // 2. q (the group's heads), k, v of the new position from the P0 partials:
-    //    item (tile, r8) holds the RoPE pair (d, d+32); all loads issued first
-    const MegaPhase& ph = a.ph[0];
+    // 2. q (the group's heads), k, v of the new position; item (tile, r8)
+    //    holds the RoPE pair (d, d+32) = tile rows r8, r8 + 8
+    if (!waited) await(cx, a.cnt + (size_t)l * MG_NCNT + MG_CNT_QKV, ms->epoch * (unsigned)a.C);
+    const unsigned long long* qacc = acc_ptr(a, ms->epoch, l, MG_ACC_QKV) + (size_t)b * a.acc_w;
     const float* bias = reinterpret_cast<const float*>(sm.lp + 4 * a.H);
     const int nt = grp * 4 + 8;
-    {
-        Pend lo[2], hi[2];
-        int tl_[2], t_[2];
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int e = tid + u * 256;
-            lo[u].n = hi[u].n = 0;
-            tl_[u] = -1;
-            if (e < nt * 8) {
-                const int tl = e >> 3, r8 = e & 7;
-                int t;
-                if (tl < grp * 4) t = (g * grp + tl / 4) * 4 + (tl & 3);
-                else if (tl < grp * 4 + 4) t = a.heads * 4 + g * 4 + (tl - grp * 4);
-                else t = a.heads * 4 + a.kvh * 4 + g * 4 + (tl - grp * 4 - 4);
-                const int cn = tile_count(sm, 0, t);
-                lo[u].issue(part_ptr(ph, l, B, t, r8, b), cn, 16 * B);
-                hi[u].issue(part_ptr(ph, l, B, t, r8 + 8, b), cn, 16 * B);
-                tl_[u] = tl;
-                t_[u] = t;
-            }
+    for (int e = tid; e < nt * 8; e += 256) {
+        const int tl = e >> 3, r8 = e & 7;
+        int t, kind;
+        if (tl < grp * 4) {
+            t = (g * grp + tl / 4) * 4 + (tl & 3);
+            kind = 0;
+        } else if (tl < grp * 4 + 4) {
+            t = a.heads * 4 + g * 4 + (tl - grp * 4);
+            kind = 1;
+        } else {
+            t = a.heads * 4 + a.kvh * 4 + g * 4 + (tl - grp * 4 - 4);
+            kind = 2;
         }
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            if (tl_[u] < 0) continue;
-            const int tl = tl_[u], t = t_[u], r8 = (tid + u * 256) & 7;
-            const int kind = tl < grp * 4 ? 0 : (tl < grp * 4 + 4 ? 1 : 2);
-            const int d = (t & 3) * 8 + r8;
-            float x1 = rb(lo[u].finish(cx, tag) + bias[t * 16 + r8]);
-            float x2 = rb(hi[u].finish(cx, tag) + bias[t * 16 + r8 + 8]);
-            if (kind < 2) {
-                const float cs = ms->rc[b][d], sn = ms->rs[b][d];
-                const float p_ = x1 * cs - x2 * sn, q_ = x1 * sn + x2 * cs;
-                x1 = rb(p_);
-                x2 = rb(q_);
-            }
-            if (kind == 0) {
-                const int h = tl / 4;
-                sq[h * HD + d] = 0.125f * x1;
-                sq[h * HD + d + 32] = 0.125f * x2;
-            } else if (kind == 1) {
-                skn[d] = x1;
-                skn[d + 32] = x2;
-            } else {
-                svn[d] = x1;
-                svn[d + 32] = x2;
-            }
+        const uint64_t vlo = ldr64(qacc + t * 16 + r8), vhi = ldr64(qacc + t * 16 + r8 + 8);
+        const int d = (t & 3) * 8 + r8;
+        float x1 = rb(from_fix(vlo) + bias[t * 16 + r8]);
+        float x2 = rb(from_fix(vhi) + bias[t * 16 + r8 + 8]);
+        if (kind < 2) {
+            const float cs = ms->rc[b][d], sn = ms->rs[b][d];
+            const float p_ = x1 * cs - x2 * sn, q_ = x1 * sn + x2 * cs;
+            x1 = rb(p_);
+            x2 = rb(q_);
+        }
+        if (kind == 0) {
+            const int h = tl / 4;
+            sq[h * HD + d] = 0.125f * x1;
+            sq[h * HD + d + 32] = 0.125f * x2;
+        } else if (kind == 1) {
+            skn[d] = x1;
+            skn[d + 32] = x2;
+        } else {
+            svn[d] = x1;
+            svn[d + 32] = x2;
         }
     }
-    MG_SUB(11)
     cp_wait_all();
     cbar();
-    MG_SUB(12)
     // 3. the chunk holding the new position appends it to the cache
     if (p1 == pos + 1 && tid < 2 * HD) {
         const int which = tid / HD, d = tid % HD;
@@ -578,8 +620,8 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
                 for (int q = 0; q < HD / 2; q++) kr[q] = pack_bf16x2(skn[2 * q], skn[2 * q + 1]);
             }
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-            for (int q = 0; q < HD / 2; q++) {
+#pragma unroll
+            for (int q = 0; q < HD / 2; q++) {  // fully unrolled: kr stays in registers
                 const float2 kv = unpack_bf16x2(kr[q]);
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
@@ -593,7 +635,6 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         }
     }
     cbar();
-    MG_SUB(13)
     // 5. softmax inside the chunk (warp per head)
     if (warp < grp) {
         float m = -INFINITY;
@@ -613,7 +654,6 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         }
     }
     cbar();
-    MG_SUB(14)
     // 6. P.V: thread (head, dim pair), 4 independent accumulators
     for (int e = tid; e < grp * (HD / 2); e += 256) {
         const int h = e / (HD / 2), dp = e % (HD / 2);
@@ -644,19 +684,19 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         str64(o + 3 + 2 * dp, tagged(tag, oy));
     }
     cbar();
-    MG_SUB(15)
 }
 
 // o_proj input: the attention output of the heads this CTA's o_proj range
-// reads, combined over the chunks: o = sum_s acc_s e^(m_s - M) / L, rounded.
-// Weights e^(m_s - M) / L go to wt [(si * B + b) * max_splits + s].
+// reads, combined over the chunks: o = sum_s acc_s e^(m_s - M) / L, rounded,
+// into sT [si][d][b]. The split weights e^(m_s - M) / L live in the B-fragment
+// area (free until the staging that follows).
 MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int gpt, uint32_t tag) {
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
-    float* wt = sm.sRed;
+    float* wt = reinterpret_cast<float*>(sm.sB);  // [(si * B + b) * max_splits + s]
     const int B = a.B, tid = threadIdx.x;
     for (int e = tid; e < nst * B; e += 256) {
-        const int si = e / B, b = e % B, h = (si + base) % gpt;
+        const int si = divB(e, ms->bm), b = e - si * B, h = si + base < gpt ? si + base : si + base - gpt;
         const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
         const uint64_t* o = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART;
         float M = -INFINITY, L = 0.f;
@@ -670,9 +710,11 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 if (s0 + k >= ns) continue;
-                const float m = (uint32_t)(vm[k] >> 32) == tag ? __uint_as_float((uint32_t)vm[k]) : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
-                const float l = (uint32_t)(vl[k] >> 32) == tag ? __uint_as_float((uint32_t)vl[k]) : poll(cx, o + (size_t)(s0 + k) * MG_PART + 1, tag);
-                wt[(size_t)e * a.max_splits + s0 + k] = m;  // m for now, weights below
+                const float m = (uint32_t)(vm[k] >> 32) == tag ? __uint_as_float((uint32_t)vm[k])
+                                                                : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
+                const float l = (uint32_t)(vl[k] >> 32) == tag ? __uint_as_float((uint32_t)vl[k])
+                                                                : poll(cx, o + (size_t)(s0 + k) * MG_PART + 1, tag);
+                wt[(size_t)e * a.max_splits + s0 + k] = m;
                 const float nm = fmaxf(M, m);
                 L = L * expf(M - nm) + l * expf(m - nm);
                 M = nm;
@@ -684,7 +726,8 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
     cbar();
     const int tot = nst * 64 * B;
     for (int e = tid; e < tot; e += 256) {
-        const int si = e / (64 * B), d = (e / B) % 64, b = e % B, h = (si + base) % gpt;
+        const int qd = divB(e, ms->bm), b = e - qd * B, si = qd >> 6, d = qd & 63;
+        const int h = si + base < gpt ? si + base : si + base - gpt;
         const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
         const uint64_t* o = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART + 2 + d;
         const float* w = wt + (size_t)(si * B + b) * a.max_splits;
@@ -696,7 +739,8 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
 #pragma unroll
             for (int k = 0; k < 8; k++) {
                 if (s0 + k >= ns) continue;
-                const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k]) : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
+                const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k])
+                                                                : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
                 v += x * w[s0 + k];
             }
         }
@@ -705,43 +749,8 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
     cbar();
 }
 
-// down_proj input: h = SwiGLU of the gate/up partials for the features of the
-// CTA's down range: rb(rb(g * rb(sigmoid g)) * u) (src/ming_fused.zig:386-393).
-MING_DEV void swiglu_gather(const Ctx& cx, const Sm& sm, int nst, int base, int gpt, int l, uint32_t tag) {
-    const MegaDev& a = *cx.a;
-    const MegaPhase& gu = a.ph[2];
-    const int B = a.B, tot = nst * 64 * B;
-    for (int e0 = 0; e0 < tot; e0 += 256 * 4) {
-        Pend pg[4], pu[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int e = e0 + threadIdx.x + i * 256;
-            if (e < tot) {
-                const int si = e / (64 * B), d = (e / B) % 64, b = e % B;
-                int kg = si + base;
-                if (kg >= gpt) kg -= gpt;
-                const int f = kg * 64 + d, t = f >> 3;
-                const int cn = tile_count(sm, 2, t);
-                pg[i].issue(part_ptr(gu, l, B, t, f & 7, b), cn, 16 * B);
-                pu[i].issue(part_ptr(gu, l, B, t, 8 + (f & 7), b), cn, 16 * B);
-            } else {
-                pg[i].n = pu[i].n = 0;
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const int e = e0 + threadIdx.x + i * 256;
-            if (e >= tot) continue;
-            const float gv = rb(pg[i].finish(cx, tag)), uv = rb(pu[i].finish(cx, tag));
-            const float sg = rb(1.0f / (1.0f + expf(-gv)));
-            sm.sT[e] = f2bf(rb(rb(gv * sg) * uv));
-        }
-    }
-    cbar();
-}
-
 template <int FMT>
-__global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
+__global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_constant__ MegaDev a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const SmemMap mp = smem_map(a.nslots, a.slot_bytes, a.H, a.lp_bytes);
     uint8_t* ring = smem + mp.ring;
@@ -751,15 +760,14 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
     uint64_t* lp_empty = lp_full + 2;      // [2]
     uint8_t* lpbuf = smem + mp.lp;
     const int lp_stride = (a.lp_bytes + 127) / 128 * 128;
-    int* meta = reinterpret_cast<int*>(smem + mp.meta);
     int* btab = reinterpret_cast<int*>(smem + mp.bt);
     Misc* ms = reinterpret_cast<Misc*>(smem + mp.misc);
     Sm sm{reinterpret_cast<uint2*>(smem + mp.sB), reinterpret_cast<float*>(smem + mp.sYs),
           reinterpret_cast<uint16_t*>(smem + mp.sT), reinterpret_cast<float*>(smem + mp.sRed),
-          reinterpret_cast<uint16_t*>(smem + mp.sX), lpbuf, meta, btab, ms, nullptr};
+          reinterpret_cast<uint16_t*>(smem + mp.sX), lpbuf, btab, ms, nullptr, 0};
     const int tid = threadIdx.x, c = blockIdx.x, H = a.H, B = a.B;
     constexpr bool F16 = FMT != 16;
-    // ---- set-up: barriers, this CTA's ranges, tile maps, block-table rows ----
+    // ---- set-up: barriers, this CTA's ranges, block-table rows, RoPE table ----
     if (tid == 0) {
         for (int i = 0; i < a.nslots; i++) {
             mbar_init(&full[i], 1);
@@ -775,11 +783,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
         ms->issued = 0;
         ms->epoch = (uint32_t)a.counter[0] + 1u;
         ms->step = a.counter[1];
-        int off = 0;
-        for (int p = 0; p < MG_NPH; p++) {
-            ms->toff[p] = off;
-            off += 2 * a.ph[p].tiles;
-        }
+        ms->bm = ((1ull << 32) + (unsigned long long)B - 1ull) / (unsigned long long)B;
     }
     if (tid < MG_NPH) {
         ms->g0[tid] = a.ph[tid].cta_g0[c];
@@ -791,30 +795,23 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
         ms->pos[tid] = a.seq_len[sq];
     }
     __syncthreads();
-    {
-        int off = 0;
-        for (int p = 0; p < MG_NPH; p++) {
-            for (int i = tid; i < 2 * a.ph[p].tiles; i += MG_THREADS) meta[off + i] = a.ph[p].tile_c0[i];
-            off += 2 * a.ph[p].tiles;
-        }
-        for (int b = 0; b < B; b++) {
-            const int np = ms->pos[b] / PAGE + 1;
-            for (int i = tid; i < np; i += MG_THREADS) btab[b * MG_BT_INTS + i] = a.kv.bt[(size_t)ms->seq[b] * a.kv.bt_ld + i];
-        }
-        if (tid < B * (HD / 2)) {
-            // MLX fast_rope angles: pos * 2^(-(d/32) log2 theta), f32
-            const int b = tid / (HD / 2), d = tid % (HD / 2);
-            const float th = (float)ms->pos[b] * exp2f(-((float)d / 32.0f) * a.log2_theta);
-            float sn, cs;
-            sincosf(th, &sn, &cs);
-            ms->rc[b][d] = cs;
-            ms->rs[b][d] = sn;
-        }
-        if (tid < MG_NPH * MG_CWARPS) {
-            const int p = tid / MG_CWARPS, w = tid % MG_CWARPS, n = ms->g1[p] - ms->g0[p];
-            const int i0 = w * n / MG_CWARPS, i1 = (w + 1) * n / MG_CWARPS;
-            ms->wtile[p][w] = i1 > i0 ? (ms->g0[p] + i0) / a.ph[p].gpt : -1;
-        }
+    for (int b = 0; b < B; b++) {
+        const int np = ms->pos[b] / PAGE + 1;
+        for (int i = tid; i < np; i += MG_THREADS) btab[b * MG_BT_INTS + i] = a.kv.bt[(size_t)ms->seq[b] * a.kv.bt_ld + i];
+    }
+    if (tid < B * (HD / 2)) {
+        // MLX fast_rope angles: pos * 2^(-(d/32) log2 theta), f32
+        const int b = tid / (HD / 2), d = tid % (HD / 2);
+        const float th = (float)ms->pos[b] * exp2f(-((float)d / 32.0f) * a.log2_theta);
+        float sn, cs;
+        sincosf(th, &sn, &cs);
+        ms->rc[b][d] = cs;
+        ms->rs[b][d] = sn;
+    }
+    if (tid < MG_NPH * MG_CWARPS) {
+        const int p = tid / MG_CWARPS, w = tid % MG_CWARPS, n = ms->g1[p] - ms->g0[p];
+        const int i0 = w * n / MG_CWARPS, i1 = (w + 1) * n / MG_CWARPS;
+        ms->wtile[p][w] = i1 > i0 ? (ms->g0[p] + i0) / a.ph[p].gpt : -1;
     }
     __syncthreads();
     const uint32_t epoch = ms->epoch;
@@ -825,8 +822,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
             int sc = 0;
             bool ok = true;
             for (int l = 0; l < a.layers && ok; l++) {
-                // the layer's parameter block (double-buffered)
-                const int lb = l & 1;
+                const int lb = l & 1;  // the layer's parameter block, double-buffered
                 if (l >= 2 && !mbar_wait(&lp_empty[lb], ((l >> 1) - 1) & 1)) {
                     atomicCAS(&ms->fail, 0, 3);
                     break;
@@ -843,7 +839,10 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
                             ok = false;
                             break;
                         }
-                        if (*(volatile int*)&ms->fail) { ok = false; break; }
+                        if (*(volatile int*)&ms->fail) {
+                            ok = false;
+                            break;
+                        }
                         const int ng = min(a.gps, n - j * a.gps);
                         const uint32_t bytes = (uint32_t)(ng * a.cb);
                         mbar_expect_tx(&full[slot], bytes);
@@ -858,7 +857,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
     }
 
     // ---------------- consumer warps ----------------
-    Ctx cx{&a, &ms->fail, a.err};
+    Ctx cx{&a, &ms->fail};
     int cons = 0, lp_used = 0;
     bool dead = false;
     auto check = [&]() -> bool {
@@ -866,94 +865,107 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
         if (*(volatile int*)&ms->fail) dead = true;
         return dead;
     };
+    {
+        // zero this CTA's slice of the accumulators of the next step (the
+        // previous step used them; this step's were zeroed by it)
+        const size_t per = (size_t)a.layers * MG_NACC * MG_MAXB * a.acc_w;  // int64 per parity
+        uint4* z = reinterpret_cast<uint4*>(a.acc + (size_t)((epoch + 1) & 1) * per);
+        const size_t n2 = per / 2, lo = n2 * c / a.C, hi = n2 * (c + 1) / a.C;
+        for (size_t i = lo + tid; i < hi; i += 256) z[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
     for (int idx = tid; idx < B * H; idx += 256) sm.sX[idx] = a.x_in[idx];
-    long long* tr = a.trace ? a.trace + (size_t)c * a.layers * 32 : nullptr;
+    cbar();
+    long long* tr = a.trace ? a.trace + (size_t)c * a.layers * MG_TRACE : nullptr;
 #define MG_STAMP(k) \
-    if (tr && tid == 0) tr[l * 32 + (k)] = clock64();
+    if (tr && tid == 0) tr[l * MG_TRACE + (k)] = clock64();
+    const unsigned int target = epoch * (unsigned)a.C;
+#pragma unroll 1
     for (int l = 0; l < a.layers && !dead; l++) {
         const uint32_t tag = epoch * 32u + (uint32_t)l;
+        unsigned int* cnt = a.cnt + (size_t)l * MG_NCNT;
+        uint16_t* hb = a.hbuf + (size_t)l * MG_MAXB * a.FF;
+        sm.st = tr ? tr + l * MG_TRACE : nullptr;
         MG_STAMP(0)
         if (!mbar_wait(&lp_full[l & 1], (l >> 1) & 1)) atomicCAS(cx.fail, 0, 2);
         lp_used = l + 1;
         sm.lp = lpbuf + (l & 1) * lp_stride;
-        sm.st = tr ? tr + l * 32 : nullptr;
         const uint16_t* ln1 = reinterpret_cast<const uint16_t*>(sm.lp);
         const uint16_t* ln2 = ln1 + H;
-        // ---- P0 prologue: x_l = x1_{l-1} + down partials; RMSNorm folded ----
-        residual_stats(cx, sm, l > 0 ? 3 : -1, l - 1, tag - 1u, ln1, F16);
-        if (check()) break;
-        MG_STAMP(22)
-        stage<F16>(sm, H / 64, B, H, 0, ln1, F16);
-        cbar();
-        MG_STAMP(1)
-        gemv_phase<FMT>(cx, sm, 0, l, tag, ring, full, empty, 0, true, cons);
-        MG_STAMP(2)
-        if (check()) break;
-        // ---- P1 attention ----
-        {
-            int tot = 0;
-            for (int b = 0; b < B; b++) tot += a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
-            for (int it = c; it < tot; it += a.C) {
-                int rem = it, b = 0;
-                while (rem >= a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH)) {
-                    rem -= a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
-                    b++;
-                }
-                const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
-                attention_item(cx, sm, l, tag, b, rem / ns, rem % ns);
-                if (check()) break;
+        // The four GEMV phases share one copy of their code (the kernel's
+        // instruction footprint per layer decides its speed):
+        //   q 0: x = x1(l-1) + down(l-1), RMSNorm folded, q|k|v -> acc QKV
+        //   q 1: attention over the cache (P1), chunk combine, o_proj -> acc X1
+        //   q 2: x1 = x + o_proj, RMSNorm folded, gate|up tiles -> SwiGLU h
+        //   q 3: h of this CTA's down range, down -> acc X2
+#pragma unroll 1
+        for (int q = 0; q < MG_NPH && !dead; q++) {
+            const int gpt = a.ph[q].gpt, n = ms->g1[q] - ms->g0[q];
+            const bool rows = q == 0 || q == 2;  // input = the normed residual rows
+            int base = 0, nst = H / 64;
+            if (!rows) {
+                base = ms->g0[q] % gpt;
+                nst = min(n, gpt);
             }
-        }
-        if (check()) break;
-        MG_STAMP(3)
-        // ---- P2 prologue: combine the attention chunks of the heads this CTA needs ----
-        {
-            const int gpt = a.ph[1].gpt, n = ms->g1[1] - ms->g0[1];
-            const int base = ms->g0[1] % gpt, nst = min(n, gpt);
-            combine_heads(cx, sm, nst, base, gpt, tag);
-            MG_STAMP(25)
-            stage<F16>(sm, nst, B, H, 1, nullptr, F16);
-            cbar();
+            if (q == 1) {
+                // P1: attention items (row, kv head, chunk) strided over the CTAs
+                int tot = 0;
+                for (int b = 0; b < B; b++) tot += a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
+                bool waited = false;
+                for (int it = c; it < tot && !dead; it += a.C) {
+                    int rem = it, b = 0;
+                    while (rem >= a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH)) {
+                        rem -= a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
+                        b++;
+                    }
+                    const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
+                    attention_item(cx, sm, l, tag, b, rem / ns, rem % ns, waited);
+                    waited = true;
+                    check();
+                }
+                if (check()) break;
+                MG_STAMP(9)
+                combine_heads(cx, sm, nst, base, gpt, tag);
+            } else {
+                const unsigned int* wc = q == 0 ? (l > 0 ? cnt - MG_NCNT + MG_CNT_X2 : nullptr) : cnt + (q == 2 ? MG_CNT_X1 : MG_CNT_H);
+                if (wc) await(cx, wc, target);
+                if (check()) break;
+                if (rows) {
+                    const unsigned long long* src =
+                        q == 2 ? acc_ptr(a, epoch, l, MG_ACC_X1) : (l > 0 ? acc_ptr(a, epoch, l - 1, MG_ACC_X2) : nullptr);
+                    residual_stats(sm, a, src, q == 0 ? ln1 : ln2, F16);
+                } else {
+                    for (int e = tid; e < nst * 8 * B; e += 256) {  // h: 8 features (16 bytes) per load
+                        const int qq = divB(e, ms->bm), b = e - qq * B, si = qq >> 3, k8 = qq & 7;
+                        const int kg = si + base < gpt ? si + base : si + base - gpt;
+                        const uint4 v = ldcg16(hb + (size_t)b * a.FF + kg * 64 + k8 * 8);
+                        const uint16_t* hv = reinterpret_cast<const uint16_t*>(&v);
+#pragma unroll
+                        for (int u = 0; u < 8; u++) sm.sT[(si * 64 + k8 * 8 + u) * B + b] = hv[u];
+                    }
+                    cbar();
+                }
+            }
             if (check()) break;
-            MG_STAMP(4)
-            gemv_phase<FMT>(cx, sm, 1, l, tag, ring, full, empty, base, false, cons);
-            MG_STAMP(5)
+            MG_STAMP(1 + 2 * q)
+            sm.so = 10 + 7 * q;
+            stage<F16>(sm, nst, B, H, rows ? 0 : 1, q == 0 ? ln1 : ln2);
+            const int which = q == 0 ? MG_ACC_QKV : (q == 1 ? MG_ACC_X1 : MG_ACC_X2);
+            gemv_phase<FMT>(cx, sm, q, cons, ring, full, empty, base, rows, q == 2 ? OUT_GLU : OUT_ACC,
+                            q == 2 ? nullptr : acc_ptr(a, epoch, l, which), hb);
+            cons += (n + a.gps - 1) / a.gps;
+            publish(sm, cnt + (q == 0 ? MG_CNT_QKV : (q == 1 ? MG_CNT_X1 : (q == 2 ? MG_CNT_H : MG_CNT_X2))));
             if (check()) break;
-        }
-        // ---- P3 prologue: x1 = x + o_proj partials; RMSNorm folded ----
-        residual_stats(cx, sm, 1, l, tag, ln2, F16);
-        if (check()) break;
-        MG_STAMP(26)
-        stage<F16>(sm, H / 64, B, H, 0, ln2, F16);
-        cbar();
-        MG_STAMP(6)
-        gemv_phase<FMT>(cx, sm, 2, l, tag, ring, full, empty, 0, true, cons);
-        MG_STAMP(7)
-        if (check()) break;
-        // ---- P4 prologue: h = SwiGLU of the gate/up partials this CTA's range needs ----
-        {
-            const int gpt = a.ph[3].gpt, n = ms->g1[3] - ms->g0[3];
-            const int base = ms->g0[3] % gpt, nst = min(n, gpt);
-            swiglu_gather(cx, sm, nst, base, gpt, l, tag);
-            MG_STAMP(24)
-            stage<F16>(sm, nst, B, H, 1, nullptr, F16);
-            cbar();
-            if (check()) break;
-            MG_STAMP(8)
-            gemv_phase<FMT>(cx, sm, 3, l, tag, ring, full, empty, base, false, cons);
-            MG_STAMP(9)
-            if (check()) break;
+            MG_STAMP(2 + 2 * q)
         }
         // release the layer's parameter block to the producer
-        if (tid == 0) mbar_arrive(&lp_empty[l & 1]);
+        if (!dead && tid == 0) mbar_arrive(&lp_empty[l & 1]);
     }
 #undef MG_STAMP
     // ---------------- final norm + stop head (CTA b handles row b) ----------------
     if (!dead && c < B) {
-        const uint32_t tag = epoch * 32u + (uint32_t)(a.layers - 1);
-        residual_stats(cx, sm, 3, a.layers - 1, tag, a.norm, false);
-        check();
-        if (!dead) {
+        await(cx, a.cnt + (size_t)(a.layers - 1) * MG_NCNT + MG_CNT_X2, target);
+        if (!check()) {
+            residual_stats(sm, a, acc_ptr(a, epoch, a.layers - 1, MG_ACC_X2), a.norm, false);
             const int b = c, warp = tid >> 5, lane = tid & 31;
             const float inv = ms->inv[b];
             uint16_t* ob = a.out_cell ? *a.out_cell : nullptr;
@@ -970,11 +982,17 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
             }
             l0 = warp_sum(l0);
             l1 = warp_sum(l1);
-            if (lane == 0) { ms->red[warp] = l0; ms->red[8 + warp] = l1; }
+            if (lane == 0) {
+                ms->red[warp] = l0;
+                ms->red[8 + warp] = l1;
+            }
             cbar();
             if (tid == 0) {
                 float s0 = 0.f, s1 = 0.f;
-                for (int w = 0; w < MG_CWARPS; w++) { s0 += ms->red[w]; s1 += ms->red[8 + w]; }
+                for (int w = 0; w < MG_CWARPS; w++) {
+                    s0 += ms->red[w];
+                    s1 += ms->red[8 + w];
+                }
                 s0 = rb(s0 + bf2f(a.stop_b[0]));
                 s1 = rb(s1 + bf2f(a.stop_b[1]));
                 const float m = fmaxf(s0, s1), e0 = expf(s0 - m), e1 = expf(s1 - m);
@@ -991,7 +1009,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
         if (tid == 0) {
             atomicCAS(a.err, 0, ms->fail ? ms->fail : 4);
             const long long t0 = clock64();
-            while (!*(volatile int*)&ms->prod_done && clock64() - t0 < MG_TIMEOUT) {}
+            while (!*(volatile int*)&ms->prod_done && clock64() - t0 < MG_TIMEOUT) {
+            }
             const int issued = *(volatile int*)&ms->issued;
             for (int sc = cons; sc < issued; sc++) mbar_wait(&full[sc % a.nslots], (sc / a.nslots) & 1);
             for (int l = lp_used; l < a.layers && l < lp_used + 2; l++) mbar_wait(&lp_full[l & 1], (l >> 1) & 1);
@@ -999,8 +1018,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(MegaDev a) {
         return;
     }
     if (c == 0 && tid == 0) {
-        // every CTA read the epoch and positions before contributing to layer 0,
-        // which this CTA needed to reach here
+        // every CTA read the epoch and positions before contributing to the
+        // last layer, which this CTA waited for
         a.counter[0] = (int)epoch;
         a.counter[1] = ms->step + 1;
         for (int b = 0; b < B; b++) a.seq_len[ms->seq[b]] += 1;

@@ -7,28 +7,28 @@
 // launch, and weight streaming never waits on the chain.
 //
 // Layout of the work (C = number of CTAs, one per SM):
-//   * every GEMV phase (P0 q|k|v, P2 o_proj, P3 gate|up, P4 down) is split by
-//     64-wide groups of its reduction dimension: CTA c owns the contiguous
-//     range [c*G/C, (c+1)*G/C) of the phase's G = tiles x groups-per-tile
-//     chunks, i.e. a contiguous byte range of the packed tile buffer
-//     (pack.h), so bytes per CTA are balanced to one group;
+//   * each GEMV phase's packed tiles (pack.h) are cut into contiguous ranges of
+//     64-wide groups, one per CTA (P0 q|k|v, P2 o_proj and P4 down split K;
+//     P3 gate|up is cut at whole tiles so a CTA finishes its SwiGLU features
+//     itself), so the bytes each CTA streams are balanced;
 //   * a producer warp streams the CTA's ranges, layer after layer, with
-//     cp.async.bulk into a shared-memory ring guarded by mbarriers; it runs
-//     ahead by the ring's capacity (several layers at 4 bits);
-//   * 8 consumer warps run the mma.sync tiles on the ring and write one f32
-//     partial per (tile, CTA) — the split-K partial sums;
-//   * the consumers of a phase reduce the partials of the tiles they need in a
-//     fixed order (deterministic) and apply the epilogue math of the reference
-//     (bias, bf16 rounding, RoPE, residual, SwiGLU) in their prologue; every
-//     CTA keeps the whole residual stream of its rows in shared memory and
-//     updates it from the o_proj / down partials, so no residual is published;
-//   * attention (P1) is split by (row, kv head, 128-position chunk); the chunk's
-//     K/V pages are prefetched with cp.async before the CTA waits for q.
-// Hand-offs: every published value carries the step's epoch tag in the same
-// 64-bit word (single-copy atomic), so a consumer polls the data itself — no
-// flag, no fence. A consumer issues all loads of a batch before checking any
-// tag (one L2 round trip per batch, not per word). Every wait is bounded; on
-// timeout the kernel records an error code and returns.
+//     cp.async.bulk into a shared-memory ring guarded by mbarriers, running
+//     ahead by the ring's capacity (several layers at 4 bits), together with
+//     each layer's norm weights and q|k|v bias;
+//   * 8 consumer warps run mma.sync on the ring; split-K partial sums are
+//     reduced with red.global.add.u64 on int64 fixed-point accumulators
+//     (integer addition is associative: the result is bit-deterministic);
+//   * each phase completes through one monotonic counter per (layer, phase):
+//     a CTA increments it after its contributions, a consumer polls it from
+//     one thread while the others wait at the CTA barrier;
+//   * every CTA keeps the residual stream of its rows in shared memory and
+//     applies the reference's epilogue math (bias, bf16 rounding, RoPE,
+//     residual, SwiGLU) where the values are consumed;
+//   * attention is split by (row, kv head, 128-position chunk); a chunk's
+//     K/V rows are prefetched with cp.async before the CTA waits for q; its
+//     (max, sum, P.V) partials carry the step's epoch in each 64-bit word.
+// Every wait is bounded: on timeout the kernel records an error code, waits
+// (bounded) for its own copies in flight and returns.
 #pragma once
 
 #include "lm.cuh"
@@ -41,12 +41,15 @@ constexpr int MG_MAXB = 4;                        // rows per step (mma n-tile o
 constexpr int MG_ATT_CH = 128;                    // positions per attention item
 constexpr int MG_PART = 2 + HD;                   // m, l, acc[64] per attention partial
 constexpr int MG_NPH = 4;                         // GEMV phases: P0 qkv, P2 o, P3 gate/up, P4 down
+constexpr int MG_FIX = 32;                        // fraction bits of the fixed-point accumulators
+constexpr int MG_MAX_STAGE = 32;                  // most 64-groups of activations one CTA stages per phase
+constexpr int MG_TRACE = 64;                      // clock64 stamp slots per (CTA, layer) when tracing
+enum { MG_ACC_QKV = 0, MG_ACC_X1 = 1, MG_ACC_X2 = 2, MG_NACC = 3 };
+enum { MG_CNT_QKV = 0, MG_CNT_X1 = 1, MG_CNT_H = 2, MG_CNT_X2 = 3, MG_NCNT = 4 };
 
 struct MegaPhase {
-    const int* cta_g0;   // [C + 1]: CTA c owns flattened groups [cta_g0[c], cta_g0[c+1])
-    const int* tile_c0;  // [tiles]: first CTA covering the tile (partial slot = c - tile_c0[t])
-    uint64_t* part;      // [layers][tiles][slots][16][B] tagged f32 partials
-    int tiles, gpt, slots;
+    const int* cta_g0;  // [C + 1]: CTA c owns flattened groups [cta_g0[c], cta_g0[c+1])
+    int tiles, gpt;
 };
 
 struct MegaDev {
@@ -63,6 +66,10 @@ struct MegaDev {
     KvDev kv;
     int* seq_len;              // [max_seqs]
     const int* row_seq;        // [B]
+    unsigned long long* acc;   // [2 parity][layers][MG_NACC][MG_MAXB][acc_w] int64 fixed point
+    int acc_w;
+    uint16_t* hbuf;            // [layers][MG_MAXB][FF] bf16 SwiGLU outputs
+    unsigned int* cnt;         // [layers][MG_NCNT] monotonic completion counters
     uint64_t* attn;            // [B][heads][max_splits][MG_PART] tagged attention partials
     const uint16_t* x_in;      // [B][H] step input
     uint16_t* z;               // [B][H] post-norm hidden
@@ -72,15 +79,13 @@ struct MegaDev {
     float* const* stop_cell;
     int* counter;              // [2]: epoch, generate step index
     int* err;                  // error code (0 = ok)
-    long long* trace;          // optional [C][layers][32] clock64 stamps at phase ends (null = off)
+    long long* trace;          // optional [C][layers][MG_TRACE] clock64 stamps (null = off)
     int layers, H, FF, heads, kvh, fmt, C, B, max_splits, gps, cb, nslots, slot_bytes;
     float log2_theta, eps;
 };
 
 // Host side (mega.cu)
-// Shared memory the kernel needs (bytes) for a ring of nslots x slot_bytes.
 int mega_smem_bytes(int nslots, int slot_bytes, int H, int lp_bytes);
-constexpr int MG_MAX_STAGE = 32;  // most 64-groups of activations one CTA stages per phase
 cudaError_t launch_mega(const MegaDev& a, int smem, cudaStream_t s);
 
 }  // namespace ming

@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <memory>
 #include <string>
@@ -137,6 +138,7 @@ struct ming_ctx {
     int mega_smem = 0;
     int* dev_err = nullptr;
     int* mega_counter = nullptr;  // [2]: epoch (monotonic), generate step index
+    std::function<cudaError_t()> mega_reset;  // clean persistent-kernel state after a device error
     uint16_t* gen_out = nullptr;
     size_t gen_out_elems = 0;
     float* gen_stop = nullptr;
@@ -558,7 +560,7 @@ int decode_graph(ming_ctx* c, int B, cudaGraphExec_t* out) {
 }
 
 // Plans the persistent decode kernel: per-phase group ranges of every CTA,
-// partial-sum slots, buffers. Leaves it off when the device cannot co-schedule
+// fixed-point accumulators, completion counters, buffers. Leaves it off when the device cannot co-schedule
 // one CTA per SM (no cooperative launch) or MING_MEGA=0.
 int setup_mega(ming_ctx* c) {
     const ming_cfg& f = c->cfg;
@@ -587,40 +589,25 @@ int setup_mega(ming_ctx* c) {
     for (int p = 0; p < MG_NPH; p++) {
         const int G = tiles[p] * gpt[p];
         if (G < C) return MING_OK;  // too small to give every CTA work: stay on the per-kernel path
-        std::vector<int> g0(C + 1), tc(2 * tiles[p]);
-        for (int i = 0; i <= C; i++) g0[i] = (int)((long long)i * G / C);
-        int slots = 1, maxn = 0;
+        std::vector<int> g0(C + 1);
+        for (int i = 0; i <= C; i++) {
+            // gate|up (p 2) is cut at whole tiles: each CTA finishes its SwiGLU features
+            g0[i] = p == 2 ? (int)((long long)i * tiles[p] / C) * gpt[p] : (int)((long long)i * G / C);
+        }
+        int maxn = 0;
         for (int i = 0; i < C; i++) {
             maxn = std::max(maxn, g0[i + 1] - g0[i]);
             max_nsc = std::max(max_nsc, (g0[i + 1] - g0[i] + gps - 1) / gps);
         }
-        if ((p == 3 && maxn > MG_MAX_STAGE)) return MING_OK;  // staged groups of h
-        for (int t = 0; t < tiles[p]; t++) {
-            int first = -1, last = -1;
-            for (int i = 0; i < C; i++)
-                if (g0[i] < (t + 1) * gpt[p] && g0[i + 1] > t * gpt[p]) {
-                    if (first < 0) first = i;
-                    last = i;
-                }
-            tc[2 * t] = first;
-            tc[2 * t + 1] = last - first + 1;
-            slots = std::max(slots, last - first + 1);
-        }
-        if (slots > 4) return MING_OK;  // the gathers sum at most 4 partials per value
+        if (p == 3 && maxn > MG_MAX_STAGE) return MING_OK;                // staged groups of h
+        if ((maxn + MG_CWARPS - 1) / MG_CWARPS > gpt[p]) return MING_OK;  // a warp's run spans at most two tiles
         int* dg0 = c->mem.alloc<int>(C + 1, &rc);
-        int* dtc = c->mem.alloc<int>(2 * tiles[p], &rc);
-        uint64_t* part = c->mem.alloc<uint64_t>((size_t)f.layers * tiles[p] * slots * 16 * MG_MAXB, &rc);
         if (rc) return rc;
         CK(cudaMemcpy(dg0, g0.data(), (C + 1) * 4, cudaMemcpyHostToDevice));
-        CK(cudaMemcpy(dtc, tc.data(), 2 * tiles[p] * 4, cudaMemcpyHostToDevice));
-        a.ph[p] = MegaPhase{dg0, dtc, part, tiles[p], gpt[p], slots};
+        a.ph[p] = MegaPhase{dg0, tiles[p], gpt[p]};
     }
     if (nslots < max_nsc + 2) return MING_OK;
-    {
-        int meta = 0;
-        for (int p = 0; p < MG_NPH; p++) meta += 2 * tiles[p];
-        if (meta > 4096 || f.max_ctx / PAGE + 1 > 512) return MING_OK;  // shared-memory tables of the kernel
-    }
+    if (f.max_ctx / PAGE + 1 > 512) return MING_OK;  // block-table rows live in shared memory
     // per-layer tables gathered into contiguous device arrays
     std::vector<const uint8_t*> wb((size_t)f.layers * MG_NPH);
     for (int l = 0; l < f.layers; l++) {
@@ -632,11 +619,29 @@ int setup_mega(ming_ctx* c) {
     const uint8_t** dwb = c->mem.alloc<const uint8_t*>(wb.size(), &rc);
     uint8_t* lpar = c->mem.alloc<uint8_t>((size_t)f.layers * lp_bytes, &rc);
     const int max_splits = (f.max_ctx + MG_ATT_CH - 1) / MG_ATT_CH;
-    if ((H / 64) * MG_MAXB * max_splits > 2048) return MING_OK;  // split weights live in the 8 KB reduction area
-    uint64_t* attn = c->mem.alloc<uint64_t>((size_t)MG_MAXB * f.heads * max_splits * MG_PART, &rc);
+    if ((H / 64) * MG_MAXB * max_splits > 8192) return MING_OK;  // split weights live in the 32 KB fragment area
+    const size_t attn_n = (size_t)MG_MAXB * f.heads * max_splits * MG_PART;
+    uint64_t* attn = c->mem.alloc<uint64_t>(attn_n, &rc);
+    const int acc_w = (std::max(qkv_rows, H) + 1) / 2 * 2;
+    const size_t acc_n = (size_t)2 * f.layers * MG_NACC * MG_MAXB * acc_w;
+    unsigned long long* acc = c->mem.alloc<unsigned long long>(acc_n, &rc);
+    uint16_t* hbuf = c->mem.alloc<uint16_t>((size_t)f.layers * MG_MAXB * f.ff, &rc);
+    const size_t cnt_n = (size_t)f.layers * MG_NCNT;
+    unsigned int* cnt = c->mem.alloc<unsigned int>(cnt_n, &rc);
     c->dev_err = c->mem.alloc<int>(1, &rc);
     c->mega_counter = c->mem.alloc<int>(2, &rc);
     if (rc) return rc;
+    int* counter = c->mega_counter;
+    c->mega_reset = [=]() -> cudaError_t {
+        // a step that gave up leaves accumulators, counters and partials of an
+        // unfinished epoch: restart the epochs from zero on clean state
+        cudaError_t e = cudaMemset(acc, 0, acc_n * 8);
+        if (e == cudaSuccess) e = cudaMemset(cnt, 0, cnt_n * 4);
+        if (e == cudaSuccess) e = cudaMemset(attn, 0, attn_n * 8);
+        if (e == cudaSuccess) e = cudaMemset(counter, 0, 8);
+        return e;
+    };
+    CK(c->mega_reset());
     CK(cudaMemcpy(dwb, wb.data(), wb.size() * sizeof(void*), cudaMemcpyHostToDevice));
     for (int l = 0; l < f.layers; l++) {
         uint8_t* blk = lpar + (size_t)l * lp_bytes;
@@ -653,6 +658,10 @@ int setup_mega(ming_ctx* c) {
     a.kv = KvDev{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
     a.seq_len = c->seq_len;
     a.attn = attn;
+    a.acc = acc;
+    a.acc_w = acc_w;
+    a.hbuf = hbuf;
+    a.cnt = cnt;
     a.counter = c->mega_counter;
     a.err = c->dev_err;
     a.out_cell = c->out_cell;
@@ -673,7 +682,7 @@ int setup_mega(ming_ctx* c) {
     a.eps = f.rms_eps;
     const char* tr = getenv("MING_MEGA_TRACE");
     if (tr && std::string(tr) == "1") {
-        a.trace = c->mem.alloc<long long>((size_t)C * f.layers * 32, &rc);
+        a.trace = c->mem.alloc<long long>((size_t)C * f.layers * MG_TRACE, &rc);
         if (rc) return rc;
     }
     c->mega_smem = mega_smem_bytes(nslots, slot, H, lp_bytes);
@@ -689,6 +698,7 @@ int check_dev_err(ming_ctx* c) {
     if (e) {
         const int zero = 0;
         cudaMemcpy(c->dev_err, &zero, 4, cudaMemcpyHostToDevice);
+        if (c->mega_reset) c->mega_reset();
         return fail(MING_ERR_CUDA, "persistent decode kernel: a bounded device wait expired (code " + std::to_string(e) + ")");
     }
     return MING_OK;
@@ -1278,6 +1288,15 @@ int ming_cuda_get_stream(ming_ctx* c, void** s) {
     return MING_OK;
 }
 
+int ming_cuda_step_kernels(ming_ctx* c, int B, int* n) {
+    if (!c || !n) return fail(MING_ERR_INVALID, "null argument");
+    if (!c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
+    if (B < 1 || B > c->cfg.max_batch) return fail(MING_ERR_INVALID, "batch size out of range");
+    // persistent: one launch; per-kernel: step_begin + 5 per layer + final
+    *n = (c->mega_on && B <= MG_MAXB) ? 1 : 1 + 5 * c->cfg.layers + 1;
+    return MING_OK;
+}
+
 int ming_cuda_sync(ming_ctx* c) {
     if (!c) return fail(MING_ERR_INVALID, "null context");
     CK(cudaStreamSynchronize(c->stream));
@@ -1344,7 +1363,7 @@ extern "C" int ming_cuda_debug_trace(ming_ctx* c, long long* out, int cap, int* 
     if (!c || !n) return fail(MING_ERR_INVALID, "null argument");
     *n = 0;
     if (!c->mega_on || !c->mega.trace) return MING_OK;
-    const size_t cnt = (size_t)c->mega.C * c->cfg.layers * 32;
+    const size_t cnt = (size_t)c->mega.C * c->cfg.layers * MG_TRACE;
     if ((size_t)cap < cnt) return fail(MING_ERR_INVALID, "trace buffer too small");
     CK(cudaStreamSynchronize(c->stream));
     CK(cudaMemcpy(out, c->mega.trace, cnt * 8, cudaMemcpyDeviceToHost));

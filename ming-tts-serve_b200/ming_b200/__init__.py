@@ -29,6 +29,7 @@ SYMBOLS = [
     "ming_cuda_cfm_steps",
     "ming_cuda_aggregate", "ming_cuda_get_stream", "ming_cuda_sync", "ming_cuda_destroy",
     "ming_cuda_last_error", "ming_cuda_kv_read", "ming_cuda_unpack_linear", "ming_cuda_flow_temb",
+    "ming_cuda_step_kernels",
 ]
 
 
@@ -244,6 +245,12 @@ class Context:
         s = ctypes.c_void_p()
         _check(lib().ming_cuda_get_stream(self._h, ctypes.byref(s)))
         return s.value
+
+    def step_kernels(self, B):
+        """Kernels one decode step of B rows launches (1 = persistent kernel)."""
+        n = ctypes.c_int(0)
+        _check(lib().ming_cuda_step_kernels(self._h, B, ctypes.byref(n)))
+        return n.value
 
     def sync(self):
         _check(lib().ming_cuda_sync(self._h))

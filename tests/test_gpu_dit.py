@@ -84,11 +84,18 @@ def test_cfm_repeat_is_bit_identical(token_head):
 
 @pytest.mark.parametrize("B", [1, 4])
 def test_aggregate_parity(token_head, B):
+    """The aggregator's 8 blocks at hidden 1024 amplify bf16 rounding: on these
+    inputs the reference's own fused kernels and its plain graph (oracle FUSED
+    vs GRAPH) already differ by up to ~0.03. The gate is therefore the larger
+    of the 2e-2 / 2-ulp bf16 tolerance and that measured reference spread on
+    the same input, with cosine > 0.999 per row."""
     Wf, Wa, ctx = token_head
     a = O.Agg(Wa)
     lat = synth.normal_bf16(12, f"agg.{B}", (B, 64))
-    d, c, ok = close(ctx.aggregate(lat), a(lat))
-    assert ok, (d, c)
+    ref = a(lat)
+    spread = close(a(lat, O.MODE_GRAPH), ref)[0]
+    d, c, ok = close(ctx.aggregate(lat), ref, tol=max(2e-2, spread))
+    assert ok, (d, c, spread)
 
 
 @pytest.mark.parametrize("B", [1, 2, 32])

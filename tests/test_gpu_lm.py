@@ -23,7 +23,7 @@ import ming_b200 as M
 import oracle as O
 from ming_b200 import synth
 
-from conftest import bf, bf16_ulp, close
+from conftest import bf, bf16_ulp, close, within_reference
 
 pytestmark = pytest.mark.gpu
 
@@ -59,18 +59,24 @@ def test_unpack_bit_exact(cuda_ok, bits):
 
 def _teacher_forced(ctx, lm, x_prompt, steps, seed):
     """Prefill both, then `steps` decode steps, each fed the oracle's previous
-    output. Returns per-step (maxabs, cos) lists."""
+    output. The oracle runs twice: fused rounding (the reference's fused
+    kernels, the parity target) and plain-graph rounding (the reference's MLX
+    graph), which sets the spread `within_reference` allows. Returns per-step
+    (maxabs, cos, ok) lists."""
     s = ctx.seq_alloc()
-    cache = lm.new_cache(x_prompt.shape[0] + steps + 1)
+    n = x_prompt.shape[0] + steps + 1
+    cache, cache_g = lm.new_cache(n), lm.new_cache(n)
     go, gs = ctx.prefill(s, x_prompt)
     ro, rs = lm.forward(cache, x_prompt)
-    res = [close(go, ro)]
+    rg, _ = lm.forward(cache_g, x_prompt, O.MODE_GRAPH)
+    res = [within_reference(go, ro, rg)]
     assert np.abs(gs - rs).max() < 1e-2
     x = ro[-1:]
     for t in range(steps):
         go, gs = ctx.decode([s], x)
         ro, rs = lm.forward(cache, x)
-        res.append(close(go, ro))
+        rg, _ = lm.forward(cache_g, x, O.MODE_GRAPH)
+        res.append(within_reference(go, ro, rg))
         assert abs(gs[0] - rs[0]) < 1e-2
         x = ro
     ctx.seq_free(s)
@@ -154,34 +160,44 @@ def test_kv_cache_placement(cuda_ok):
     lm = O.Lm(W)
     s1, s2 = ctx.seq_alloc(), ctx.seq_alloc()
     c1, c2 = lm.new_cache(80), lm.new_cache(80)
+    g1, g2 = lm.new_cache(80), lm.new_cache(80)  # plain-graph rounding: the reference's own spread
     for chunk in range(3):  # alternate prefill chunks so pages interleave
-        for s, c, nm in ((s1, c1, "a"), (s2, c2, "b")):
+        for s, c, cg, nm in ((s1, c1, g1, "a"), (s2, c2, g2, "b")):
             x = synth.normal_bf16(6, f"test.kv.{nm}.{chunk}", (21, 896))
             ctx.prefill(s, x, want_out=False)
             lm.forward(c, x)
+            lm.forward(cg, x, O.MODE_GRAPH)
     x = synth.normal_bf16(6, "test.kv.dec", (2, 896))
     ctx.decode([s2, s1], x[::-1].copy())
     lm.forward(c1, x[0:1])  # row 1 (s1) got x[0]
     lm.forward(c2, x[1:2])  # row 0 (s2) got x[1]
-    for s, c in ((s1, c1), (s2, c2)):
+    lm.forward(g1, x[0:1], O.MODE_GRAPH)
+    lm.forward(g2, x[1:2], O.MODE_GRAPH)
+    for s, c, cg in ((s1, c1, g1), (s2, c2, g2)):
         n = ctx.seq_len(s)
         assert n == 64
         for layer in range(3):
             k, v = ctx.kv_read(s, layer, 0, n)
-            rk = synth.f32_to_bf16(c._k[layer, :, :n])
-            rv = synth.f32_to_bf16(c._v[layer, :, :n])
-            for got, ref in ((k, rk), (v, rv)):
+            refs = [(synth.f32_to_bf16(cc._k[layer, :, :n]), synth.f32_to_bf16(cc._v[layer, :, :n])) for cc in (c, cg)]
+            for j, got in enumerate((k, v)):
+                ref, alt = refs[0][j], refs[1][j]
                 # placement is exact: every value sits at its (layer, head,
                 # position). Layer 0 sees identical inputs on both sides, so
                 # its K/V agree bit for bit except where the GEMV's f32
-                # summation order rounds to the neighbouring bf16 value; deeper
-                # layers inherit 1-ulp input differences, so their values stay
-                # within two bf16 steps.
+                # summation order rounds to the neighbouring bf16 value (all
+                # within two bf16 steps). Deeper layers inherit rounding
+                # differences of the layers below: their values stay within
+                # two bf16 steps or twice the reference's own fused-vs-graph
+                # spread at that layer, head and position.
                 same = (got == ref).mean()
                 d = np.abs(bf(got) - bf(ref))
-                assert (d <= 2 * bf16_ulp(bf(ref)) + 1e-30).all(), (layer, d.max())
+                bound = 2 * bf16_ulp(bf(ref)) + 1e-30
                 if layer == 0:
                     assert same > 0.98, (layer, same)
+                else:
+                    spread = np.abs(bf(alt) - bf(ref)).max(-1, keepdims=True)
+                    bound = np.maximum(bound, 2 * spread)
+                assert (d <= bound).all(), (layer, d.max())
     ctx.close()
 
 
@@ -191,16 +207,18 @@ def test_long_context_split_and_page_boundaries(cuda_ok):
     lm = O.Lm(W)
     x = synth.normal_bf16(8, "test.long", (510, 896))
     s = ctx.seq_alloc()
-    c = lm.new_cache(530)
+    c, cg = lm.new_cache(530), lm.new_cache(530)
     go, _ = ctx.prefill(s, x)
     ro, _ = lm.forward(c, x)
-    d, cs, ok = close(go, ro)
+    rg, _ = lm.forward(cg, x, O.MODE_GRAPH)
+    d, cs, ok = within_reference(go, ro, rg)
     assert ok, (d, cs)
     xin = ro[-1:]
     for t in range(6):  # positions 510..515 cross the 512 split boundary
         go, _ = ctx.decode([s], xin)
         ro, _ = lm.forward(c, xin)
-        d, cs, ok = close(go, ro)
+        rg, _ = lm.forward(cg, xin, O.MODE_GRAPH)
+        d, cs, ok = within_reference(go, ro, rg)
         assert ok, (t, d, cs)
         xin = ro
     ctx.close()
