@@ -107,6 +107,24 @@ int ming_cuda_lm_decode(ming_ctx* ctx, int B, const int* seq_ids, const uint16_t
 int ming_cuda_lm_generate(ming_ctx* ctx, int B, const int* seq_ids, const uint16_t* x0, int steps, uint16_t* out,
                           float* stop, int ptr_kind);
 
+/* ming_cuda_lm_decode for callers that cannot allocate device memory during a
+ * step: a host real-time audio thread must not block in cudaMalloc, and a
+ * process whose device memory is budgeted by another runtime has cudaMalloc
+ * refused once the budget is spent. Same arguments and results as
+ * ming_cuda_lm_decode (within bf16 rounding); it instantiates no CUDA graph
+ * and keeps its one scratch buffer, the split-K attention partials, in a
+ * fixed 4 MiB array compiled into the library (held by every GPU that loads
+ * the library until the process exits). A step needing more than that
+ * (B x ceil(max_ctx / 256) x heads x 264 bytes) is rejected with
+ * MING_ERR_INVALID. The first call on a device looks up the array's device
+ * address; make that first call before any stream capture. All calls on a
+ * device share the array and its contents persist between calls; nothing in
+ * it needs to start at zero, but calls that overlap on the GPU (other
+ * streams, other contexts on the same device) race on it.
+ * No reference counterpart: the reference's MLX allocator owns all memory. */
+int ming_cuda_lm_decode_noalloc(ming_ctx* ctx, int B, const int* seq_ids, const uint16_t* x, uint16_t* out, float* stop,
+                                int ptr_kind);
+
 /* Model.cfmSample (src/ming_model.zig:1143-1215): 10 Euler steps with CFG.
  * Token mode: z [B][cond_dim], hist [B][latent], noise [B][latent],
  * sde [10][B][latent] or NULL. adaLN mode: hist unused, noise/y

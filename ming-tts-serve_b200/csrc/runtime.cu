@@ -8,6 +8,7 @@
 #include <cstring>
 #include <functional>
 #include <map>
+#include <mutex>
 #include <memory>
 #include <string>
 #include <vector>
@@ -1379,3 +1380,99 @@ int ming_cuda_flow_temb(ming_ctx* c, uint16_t* te) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------
+// Allocation-free decode step
+// ---------------------------------------------------------------------
+//
+// Some callers cannot allocate device memory while they decode: a host
+// real-time audio thread must not block in cudaMalloc (which can synchronize
+// the whole device), and a process whose device memory is budgeted by another
+// runtime gets its cudaMalloc calls refused once the budget is spent. For them
+// ming_cuda_lm_decode_noalloc runs one decode step without any device
+// allocation: it launches the per-kernel decode sequence directly (no CUDA
+// graph is instantiated, which allocates on first use for each batch size)
+// and keeps its only scratch, the split-K attention partials, in the
+// fixed-size array below instead of a context buffer.
+
+// Most scratch one call may use: the attention partials of B rows,
+// B x (max_ctx / 256) splits x heads x 66 f32. 4 MiB covers 32 rows at the
+// default 4096 positions (1.9 MB). Every GPU that loads this library holds the
+// array until the process exits.
+constexpr size_t NOALLOC_SCRATCH_BYTES = (size_t)4 << 20;
+static __device__ __align__(256) float g_noalloc_scratch[NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace {
+
+std::mutex g_noalloc_mu;
+constexpr int NOALLOC_MAX_DEVICES = 64;
+float* g_noalloc_addr[NOALLOC_MAX_DEVICES] = {};  // device address of the array, per device
+
+// The array's device address on `device` (which must be current). In host
+// code `g_noalloc_scratch` names a host-side stand-in, not device memory, so
+// the address comes from cudaGetSymbolAddress, once per device.
+int noalloc_scratch(int device, float** out) {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (device < 0 || device >= NOALLOC_MAX_DEVICES) return fail(MING_ERR_INVALID, "device index out of range");
+    if (!g_noalloc_addr[device]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return fail(MING_ERR_CUDA, std::string("scratch address: ") + cudaGetErrorString(e));
+        g_noalloc_addr[device] = static_cast<float*>(p);
+    }
+    *out = g_noalloc_addr[device];
+    return MING_OK;
+}
+
+}  // namespace
+
+extern "C" int ming_cuda_lm_decode_noalloc(ming_ctx* c, int B, const int* ids, const uint16_t* x, uint16_t* out,
+                                           float* stop, int kind) {
+    if (!c || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
+    if (c->cfg.layers < 1) return fail(MING_ERR_INVALID, "no LM configured");
+    if (!ids || !x) return fail(MING_ERR_INVALID, "null argument");
+    if (B < 1 || B > c->cfg.max_batch) return fail(MING_ERR_INVALID, "batch size out of range");
+    const ming_cfg& f = c->cfg;
+    const size_t need = (size_t)B * c->nsplit * f.heads * PART_STRIDE * sizeof(float);
+    if (need > NOALLOC_SCRATCH_BYTES)
+        return fail(MING_ERR_INVALID, "allocation-free decode: " + std::to_string(B) + " rows at max_ctx " +
+                                          std::to_string(f.max_ctx) + " need " + std::to_string(need) +
+                                          " bytes of attention scratch, more than its fixed " +
+                                          std::to_string(NOALLOC_SCRATCH_BYTES) + " bytes");
+    CK(cudaSetDevice(c->device));
+    float* part = nullptr;
+    int rc = noalloc_scratch(c->device, &part);
+    if (rc) return rc;
+    if ((rc = prepare_rows(c, B, ids, 1))) return rc;
+    const int H = f.hidden;
+    cudaStream_t s = c->stream;
+    uint16_t* null_out = nullptr;
+    float* null_stop = nullptr;
+    CK(cudaMemcpyAsync(c->out_cell, &null_out, sizeof(void*), cudaMemcpyHostToDevice, s));
+    CK(cudaMemcpyAsync(c->stop_cell, &null_stop, sizeof(void*), cudaMemcpyHostToDevice, s));
+    if ((rc = copy_in(c, c->x, x, (size_t)B * H * 2, kind))) return rc;
+    // the per-kernel step (the same launches as the captured decode graph),
+    // with the attention partials in the shared scratch array: every split a
+    // row reads is written earlier in the same layer, so nothing in it needs
+    // clearing between calls
+    launch_step_begin(step_dev(c), B, s);
+    RowsDev rd{c->row_seq, c->row_pos};
+    KvDev kv{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
+    for (int l = 0; l < f.layers; l++) {
+        auto& L = c->layers[l];
+        run_linear(L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
+                   EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, B, s);
+        launch_attn(AttnArgs{c->q, part, kv, rd, l, f.heads, f.kv_heads, c->nsplit}, B, s);
+        run_linear(L.o.w, ProAttn{part, rd, c->nsplit, f.heads, 0, nullptr}, EpiResidual{c->x, c->x1, nullptr, f.hidden}, B,
+                   s);
+        run_linear(L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr}, EpiSwiGLU{c->h, f.ff}, B, s);
+        run_linear(L.down.w, ProPlain{c->h, f.ff, 0}, EpiResidual{c->x1, c->x, nullptr, f.hidden}, B, s);
+    }
+    launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, c->x, step_dev(c), H, 0, 1, f.rms_eps}, B, s);
+    CK(cudaGetLastError());
+    for (int i = 0; i < B; i++) c->seqs[ids[i]].len += 1;
+    if ((rc = copy_out(c, out, c->z, (size_t)B * H * 2, kind))) return rc;
+    if ((rc = copy_out(c, stop, c->stop, (size_t)B * 4, kind))) return rc;
+    if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(s));
+    return MING_OK;
+}

@@ -29,7 +29,7 @@ SYMBOLS = [
     "ming_cuda_cfm_steps",
     "ming_cuda_aggregate", "ming_cuda_get_stream", "ming_cuda_sync", "ming_cuda_destroy",
     "ming_cuda_last_error", "ming_cuda_kv_read", "ming_cuda_unpack_linear", "ming_cuda_flow_temb",
-    "ming_cuda_step_kernels",
+    "ming_cuda_step_kernels", "ming_cuda_lm_decode_noalloc",
 ]
 
 
@@ -180,6 +180,17 @@ class Context:
         out = np.empty_like(x)
         stop = np.empty(B, dtype=np.float32)
         _check(lib().ming_cuda_lm_decode(self._h, B, ids, _ptr(x), _ptr(out), _ptr(stop), PTR_HOST))
+        return out, stop
+
+    def decode_noalloc(self, seqs, x):
+        """One decode step without any device allocation (the attention
+        scratch lives in a fixed array compiled into the library)."""
+        x = np.ascontiguousarray(x, dtype=np.uint16)
+        B = len(seqs)
+        ids = (ctypes.c_int * B)(*seqs)
+        out = np.empty_like(x)
+        stop = np.empty(B, dtype=np.float32)
+        _check(lib().ming_cuda_lm_decode_noalloc(self._h, B, ids, _ptr(x), _ptr(out), _ptr(stop), PTR_HOST))
         return out, stop
 
     def generate(self, seqs, x0, steps, kind=PTR_HOST, out=None, stop=None):
