@@ -210,6 +210,161 @@ __global__ void __launch_bounds__(LIN_THREADS) linear_kernel(PackedW W, Pro pro,
 }
 
 // ---------------------------------------------------------------------
+// Many rows: the prologue runs once, not once per tile
+// ---------------------------------------------------------------------
+//
+// With more than 8 activation rows, linear_kernel would run the prologue (and
+// its conversion to B fragments) again in every CTA, i.e. once per tile.
+// stage_frag_kernel runs it once into global memory — B fragments in the
+// exact shared-memory order stage_chunk builds, per-(group, row) sums of the
+// rounded operand, and each row's post scale — and linear_frag_kernel copies
+// them with cp.async, streaming T tiles per CTA over the same staged chunk.
+// Values and summation orders are those of linear_kernel.
+
+struct LinScratch {
+    uint2* frag = nullptr;  // [rows/8][K/16][32 lanes]
+    float* ysum = nullptr;  // [rows/8][K/64][8]
+    float* post = nullptr;  // [rows]
+    int rows = 0, K = 0;    // capacity
+    int sms = 148;          // SMs of the device (sizes the tiles-per-CTA choice)
+};
+
+constexpr int STAGE_KC = 512;  // K per stage_frag_kernel CTA
+
+template <bool F16, class Pro>
+__global__ void __launch_bounds__(LIN_THREADS) stage_frag_kernel(Pro pro, int rows, int K, LinScratch sc, bool need_ysum) {
+    __shared__ float aux[8 * 32];
+    __shared__ uint2 sB[(STAGE_KC / 16) * 32];
+    const int rb = blockIdx.x, r0 = rb * 8, nrows = min(8, rows - r0);
+    const int kc = blockIdx.y * STAGE_KC, kcl = min(STAGE_KC, K - kc);
+    Pro p = pro;
+    p.init(r0, nrows, aux);
+    __syncthreads();
+    for (int e = threadIdx.x; e < (kcl / 16) * 32; e += LIN_THREADS) {
+        const int lane = e & 31, ks = e >> 5;
+        const int row = lane >> 2, k0 = kc + ks * 16 + 2 * (lane & 3);
+        float y0 = 0.f, y1 = 0.f, y8 = 0.f, y9 = 0.f;
+        if (row < nrows) {
+            y0 = p.y(row, k0);
+            y1 = p.y(row, k0 + 1);
+            y8 = p.y(row, k0 + 8);
+            y9 = p.y(row, k0 + 9);
+        }
+        const uint2 v = make_bfrag<F16>(y0, y1, y8, y9);
+        sB[e] = v;
+        sc.frag[((size_t)rb * (K / 16) + kc / 16 + ks) * 32 + lane] = v;
+    }
+    if (need_ysum) {
+        __syncthreads();
+        for (int e = threadIdx.x; e < (kcl / 64) * 8; e += LIN_THREADS) {
+            const int gi = e / 8, gr = e % 8;
+            float s = 0.f;
+            for (int ks = 0; ks < 4; ks++)
+                for (int tq = 0; tq < 4; tq++) {
+                    const uint2 v = sB[(gi * 4 + ks) * 32 + gr * 4 + tq];
+                    if (F16) {
+                        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+                        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+                        s += (a.x + a.y) + (b.x + b.y);
+                    } else {
+                        const float2 a = unpack_bf16x2(v.x), b = unpack_bf16x2(v.y);
+                        s += (a.x + a.y) + (b.x + b.y);
+                    }
+                }
+            sc.ysum[((size_t)rb * (K / 64) + kc / 64 + gi) * 8 + gr] = s;
+        }
+    }
+    if (blockIdx.y == 0 && threadIdx.x < nrows) sc.post[r0 + threadIdx.x] = p.post(threadIdx.x);
+}
+
+MING_DEV void lin_cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+
+// Grid: x = block of T tiles, y = block of 8*NT rows.
+template <int FMT, int NT, int T, class Epi>
+__global__ void __launch_bounds__(LIN_THREADS) linear_frag_kernel(PackedW W, LinScratch sc, Epi epi, int rows) {
+    using S = LinSmem<NT>;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint2* sB = reinterpret_cast<uint2*>(smem);
+    float* sYs = reinterpret_cast<float*>(smem + S::B_BYTES);
+    float* sRed = reinterpret_cast<float*>(smem + S::B_BYTES + S::YS_BYTES);
+    const int tile0 = blockIdx.x * T, rb0 = blockIdx.y * NT, r0 = rb0 * 8;
+    const int nrows = min(8 * NT, rows - r0), nrb = (rows + 7) / 8;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ng_total = W.K / 64;
+    float acc[T][NT][4];
+#pragma unroll
+    for (int t = 0; t < T; t++)
+#pragma unroll
+        for (int j = 0; j < NT; j++) acc[t][j][0] = acc[t][j][1] = acc[t][j][2] = acc[t][j][3] = 0.f;
+    for (int kc = 0; kc < W.K; kc += LIN_KC) {
+        const int kcl = min(LIN_KC, W.K - kc);
+        __syncthreads();
+        // B fragments: entry (kstep, row block j, lane) at sB[(ks * NT + j) * 32 + lane]; 2 entries per copy
+        for (int e = threadIdx.x; e < (kcl / 16) * NT * 16; e += LIN_THREADS) {
+            const int pr = e & 15, j = (e >> 4) % NT, ks = (e >> 4) / NT;
+            uint2* dst = sB + (ks * NT + j) * 32 + 2 * pr;
+            if (rb0 + j < nrb) lin_cp16(dst, sc.frag + ((size_t)(rb0 + j) * (W.K / 16) + kc / 16 + ks) * 32 + 2 * pr);
+            else *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        if (FMT != 16) {
+            // group sums: sYs[gi * 8 * NT + j * 8 + r]; 4 per copy
+            for (int e = threadIdx.x; e < (kcl / 64) * NT * 2; e += LIN_THREADS) {
+                const int hf = e & 1, j = (e >> 1) % NT, gi = (e >> 1) / NT;
+                float* dst = sYs + gi * 8 * NT + j * 8 + hf * 4;
+                if (rb0 + j < nrb) lin_cp16(dst, sc.ysum + ((size_t)(rb0 + j) * (W.K / 64) + kc / 64 + gi) * 8 + hf * 4);
+                else *reinterpret_cast<float4*>(dst) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        asm volatile("cp.async.wait_all;\n" ::: "memory");
+        __syncthreads();
+        const int ng = kcl / 64;
+#pragma unroll
+        for (int t = 0; t < T; t++) {
+            if (tile0 + t >= W.ntiles) break;
+            const uint8_t* tbase = W.tiles + (size_t)(tile0 + t) * ng_total * chunk_b(FMT);
+#pragma unroll 2
+            for (int gi = warp; gi < ng; gi += LIN_WARPS) {
+                const uint8_t* ch = tbase + (size_t)(kc / 64 + gi) * chunk_b(FMT);
+                group_mma<FMT, NT>(ch, sB + (size_t)gi * 4 * NT * 32, sYs + gi * 8 * NT, acc[t], lane);
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < T; t++) {
+        const int tile = tile0 + t;
+        if (tile >= W.ntiles) break;  // uniform across the CTA
+        __syncthreads();
+        {
+            const int g = lane >> 2, c = 2 * (lane & 3);
+            float* r = sRed + warp * 16 * 8 * NT;
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                r[g * 8 * NT + j * 8 + c] = acc[t][j][0];
+                r[g * 8 * NT + j * 8 + c + 1] = acc[t][j][1];
+                r[(g + 8) * 8 * NT + j * 8 + c] = acc[t][j][2];
+                r[(g + 8) * 8 * NT + j * 8 + c + 1] = acc[t][j][3];
+            }
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < 8 * 8 * NT; e += LIN_THREADS) {
+            const int r8 = e / (8 * NT), col = e % (8 * NT);
+            if (col >= nrows) continue;
+            float lo = 0.f, hi = 0.f;
+#pragma unroll
+            for (int w = 0; w < LIN_WARPS; w++) {
+                lo += sRed[(w * 16 + r8) * 8 * NT + col];
+                hi += sRed[(w * 16 + r8 + 8) * 8 * NT + col];
+            }
+            const float ps = sc.post[r0 + col];
+            epi(tile, r8, r0 + col, lo * ps, hi * ps);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------
 // Prologues
 // ---------------------------------------------------------------------
 

@@ -10,98 +10,164 @@ namespace ming {
 // head against the split's positions (two-pass softmax inside the split, as
 // the reference's LB kernel, src/ming_fused.zig:326-374), then P.V.
 // Partial (m, l, acc) go to `part` for the O prologue to combine.
-__global__ void __launch_bounds__(128) attn_partial_kernel(AttnArgs a) {
-    constexpr int MAXG = 8;  // query heads per kv head (<= 8)
-    __shared__ float sq[MAXG][HD];
-    __shared__ uint32_t sk[PAGE][HD / 2 + 1];  // padded: 16 rows on distinct banks
-    __shared__ uint16_t sv[PAGE][HD];
-    __shared__ float sc[MAXG][ATT_SPLIT];
-    __shared__ float sm[MAXG], sl[MAXG];
+namespace {
+constexpr int ATT_MAXG = 8;     // query heads per kv head (<= 8)
+constexpr int ATT_KS = HD + 8;  // padded K/V row in shared memory (elements): 8 rows hit distinct bank groups
+constexpr int ATT_SMEM = 2 * ATT_SPLIT * ATT_KS * 2 + ATT_MAXG * HD * 4 + ATT_MAXG * ATT_SPLIT * 4;
+
+MING_DEV uint32_t att_su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+MING_DEV void att_cp16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(att_su32(dst)), "l"(src) : "memory");
+}
+}  // namespace
+
+// One (split, kv head, row): the row's causal positions [p0, p1) of one
+// 256-position split, every query head of the kv group. All K/V rows of the
+// split are prefetched with cp.async (one round trip), then scores (a thread
+// per position keeps its key row in registers), a per-head softmax inside
+// the split, and P.V (a thread per (head, dim pair), 4 independent sums).
+// Output: (max, sum, unnormalised P.V) per head, combined by
+// attn_combine_kernel.
+__global__ void __launch_bounds__(256) attn_partial_kernel(AttnArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint16_t* sK = reinterpret_cast<uint16_t*>(smem);              // [ATT_SPLIT][ATT_KS]
+    uint16_t* sV = sK + ATT_SPLIT * ATT_KS;                         // [ATT_SPLIT][ATT_KS]
+    float* sq = reinterpret_cast<float*>(sV + ATT_SPLIT * ATT_KS);  // [ATT_MAXG][HD]
+    float* sc = sq + ATT_MAXG * HD;                                 // [ATT_MAXG][ATT_SPLIT]
     const int split = blockIdx.x, kh = blockIdx.y, row = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int grp = a.heads / a.kv_heads;
     const int pos = a.rows.pos[row], seq = a.rows.seq[row];
-    const int n = pos + 1, p0 = split * ATT_SPLIT, p1 = min(n, p0 + ATT_SPLIT);
+    const int n = pos + 1, p0 = split * ATT_SPLIT, p1 = min(n, p0 + ATT_SPLIT), len = p1 - p0;
     float* out = a.part + ((size_t)row * a.nsplit_max + split) * a.heads * PART_STRIDE;
     if (p0 >= n) return;  // split unused for this row (never read by the combine)
-    for (int e = tid; e < grp * HD; e += 128) {
-        const int i = e / HD, d = e % HD;
-        sq[i][d] = 0.125f * bf2f(a.q[(size_t)row * a.heads * HD + (kh * grp + i) * HD + d]);
-    }
     const int* bt = a.kv.bt + (size_t)seq * a.kv.bt_ld;
-    // pass 1: scores
-    for (int pb = p0; pb < p1; pb += PAGE) {
-        const int page = bt[pb / PAGE];
-        const uint16_t* kp = a.kv.pool + kv_index(a.kv, page, a.layer, 0, kh, 0);
-        __syncthreads();
-        {
-            const int slot = tid >> 3, c = (tid & 7) * 8;  // 128 threads x 8 dims
-            const uint4 v = *reinterpret_cast<const uint4*>(kp + slot * HD + c);
-            sk[slot][c / 2] = v.x;
-            sk[slot][c / 2 + 1] = v.y;
-            sk[slot][c / 2 + 2] = v.z;
-            sk[slot][c / 2 + 3] = v.w;
+    for (int e = tid; e < len * 8; e += 256) {
+        const int j = e >> 3, piece = e & 7, p = p0 + j;
+        const int page = bt[p / PAGE];
+        att_cp16(sK + j * ATT_KS + piece * 8, a.kv.pool + kv_index(a.kv, page, a.layer, 0, kh, p % PAGE) + piece * 8);
+        att_cp16(sV + j * ATT_KS + piece * 8, a.kv.pool + kv_index(a.kv, page, a.layer, 1, kh, p % PAGE) + piece * 8);
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    for (int e = tid; e < grp * HD; e += 256) {
+        const int i = e / HD, d = e % HD;
+        sq[i * HD + d] = 0.125f * bf2f(a.q[(size_t)row * a.heads * HD + (kh * grp + i) * HD + d]);
+    }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
+    __syncthreads();
+    if (tid < len) {
+        uint32_t kr[HD / 2];
+        const uint4* src = reinterpret_cast<const uint4*>(sK + tid * ATT_KS);
+#pragma unroll
+        for (int q = 0; q < HD / 8; q++) {
+            const uint4 v = src[q];
+            kr[4 * q] = v.x;
+            kr[4 * q + 1] = v.y;
+            kr[4 * q + 2] = v.z;
+            kr[4 * q + 3] = v.w;
         }
-        __syncthreads();
-        if (tid < grp * PAGE) {
-            const int i = tid / PAGE, slot = tid % PAGE, p = pb + slot;
-            if (p < p1) {
-                float s = 0.f;
-#pragma unroll 8
-                for (int d2 = 0; d2 < HD / 2; d2++) {
-                    const float2 kv2 = unpack_bf16x2(sk[slot][d2]);
-                    s += sq[i][2 * d2] * kv2.x + sq[i][2 * d2 + 1] * kv2.y;
-                }
-                sc[i][p - p0] = s;
+        for (int i = 0; i < grp; i++) {
+            float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+            for (int q = 0; q < HD / 2; q += 2) {
+                const float2 k0 = unpack_bf16x2(kr[q]), k1 = unpack_bf16x2(kr[q + 1]);
+                const float4 qv = *reinterpret_cast<const float4*>(sq + i * HD + 2 * q);
+                s0 += qv.x * k0.x + qv.y * k0.y;
+                s1 += qv.z * k1.x + qv.w * k1.y;
             }
+            sc[i * ATT_SPLIT + tid] = s0 + s1;
         }
     }
     __syncthreads();
-    const int len = p1 - p0;
-    for (int i = warp; i < grp; i += 4) {
+    if (warp < grp) {
         float m = -INFINITY;
-        for (int j = lane; j < len; j += 32) m = fmaxf(m, sc[i][j]);
+        for (int j = lane; j < len; j += 32) m = fmaxf(m, sc[warp * ATT_SPLIT + j]);
         m = warp_max(m);
         float l = 0.f;
         for (int j = lane; j < len; j += 32) {
-            const float p = expf(sc[i][j] - m);
-            sc[i][j] = p;
+            const float p = expf(sc[warp * ATT_SPLIT + j] - m);
+            sc[warp * ATT_SPLIT + j] = p;
             l += p;
         }
         l = warp_sum(l);
-        if (lane == 0) { sm[i] = m; sl[i] = l; }
-    }
-    // pass 2: P.V; thread owns dim d for heads i0, i0+2, i0+4, i0+6
-    const int d = tid & 63, i0 = tid >> 6;
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int pb = p0; pb < p1; pb += PAGE) {
-        const int page = bt[pb / PAGE];
-        const uint16_t* vp = a.kv.pool + kv_index(a.kv, page, a.layer, 1, kh, 0);
-        __syncthreads();
-        reinterpret_cast<uint4*>(&sv[0][0])[tid] = reinterpret_cast<const uint4*>(vp)[tid];
-        __syncthreads();
-        const int cnt = min(PAGE, p1 - pb);
-        for (int j = 0; j < cnt; j++) {
-            const float v = bf2f(sv[j][d]);
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int i = i0 + 2 * u;
-                if (i < grp) acc[u] += sc[i][pb - p0 + j] * v;
-            }
+        if (lane == 0) {
+            float* o = out + (size_t)(kh * grp + warp) * PART_STRIDE;
+            o[0] = m;
+            o[1] = l;
         }
     }
-    for (int u = 0; u < 4; u++) {
-        const int i = i0 + 2 * u;
-        if (i >= grp) continue;
+    __syncthreads();
+    if (tid < grp * (HD / 2)) {
+        const int i = tid >> 5, dp = tid & 31;  // a warp per head
+        const float* pw = sc + i * ATT_SPLIT;
+        float2 ac[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+        int j = 0;
+        for (; j + 4 <= len; j += 4) {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (j + u) * ATT_KS + 2 * dp));
+                ac[u].x += pw[j + u] * v.x;
+                ac[u].y += pw[j + u] * v.y;
+            }
+        }
+        for (; j < len; j++) {
+            const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * ATT_KS + 2 * dp));
+            ac[0].x += pw[j] * v.x;
+            ac[0].y += pw[j] * v.y;
+        }
         float* o = out + (size_t)(kh * grp + i) * PART_STRIDE;
-        o[2 + d] = acc[u];
-        if (d == 0) { o[0] = sm[i]; o[1] = sl[i]; }
+        o[2 + 2 * dp] = (ac[0].x + ac[1].x) + (ac[2].x + ac[3].x);
+        o[3 + 2 * dp] = (ac[0].y + ac[1].y) + (ac[2].y + ac[3].y);
     }
 }
 
 void launch_attn(const AttnArgs& a, int rows, cudaStream_t s) {
+    static int attr_set[64] = {};  // per device: the dynamic shared memory opt-in
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+        cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM);
+        attr_set[dev] = 1;
+    }
     dim3 grid(a.nsplit_max, a.kv_heads, rows);
-    attn_partial_kernel<<<grid, 128, 0, s>>>(a);
+    attn_partial_kernel<<<grid, 256, ATT_SMEM, s>>>(a);
+}
+
+// Combines the splits of each (row, head) once into att [rows][heads * 64]
+// bf16, the o_proj input: o = rb(sum_s acc_s e^(m_s - M) * (1 / L)) with
+// L = sum_s l_s e^(m_s - M).
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float* part, RowsDev rows, int nsplit_max, int heads,
+                                                           uint16_t* att) {
+    extern __shared__ float sw[];  // [heads][nsplit_max] e^(m_s - M), then [heads] 1/L
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const int ns = (rows.pos[row] + 1 + ATT_SPLIT - 1) / ATT_SPLIT;
+    const float* pr = part + (size_t)row * nsplit_max * heads * PART_STRIDE;
+    float* il = sw + heads * nsplit_max;
+    for (int h = tid; h < heads; h += 256) {
+        float M = -INFINITY;
+        for (int s = 0; s < ns; s++) M = fmaxf(M, pr[((size_t)s * heads + h) * PART_STRIDE]);
+        float L = 0.f;
+        for (int s = 0; s < ns; s++) {
+            const float* p = pr + ((size_t)s * heads + h) * PART_STRIDE;
+            const float w = expf(p[0] - M);
+            sw[h * nsplit_max + s] = w;
+            L += p[1] * w;
+        }
+        il[h] = 1.0f / L;
+    }
+    __syncthreads();
+    for (int e = tid; e < heads * HD; e += 256) {
+        const int h = e / HD, d = e % HD;
+        float o = 0.f;
+        for (int s = 0; s < ns; s++) o += pr[((size_t)s * heads + h) * PART_STRIDE + 2 + d] * sw[h * nsplit_max + s];
+        att[(size_t)row * heads * HD + e] = f2bf(rb(o * il[h]));
+    }
+}
+
+void launch_attn_combine(const float* part, RowsDev rows, int nsplit_max, int heads, uint16_t* att, int nrows,
+                         cudaStream_t s) {
+    const int smem = (heads * nsplit_max + heads) * 4;
+    attn_combine_kernel<<<nrows, 256, smem, s>>>(part, rows, nsplit_max, heads, att);
 }
 
 // Final RMSNorm (MLX fast_rms_norm: rb(w * rb(x * inv))) and the stop head:

@@ -126,6 +126,8 @@ struct ming_ctx {
     // activations / step state
     int maxr = 0, nsplit = 0;
     uint16_t *x = nullptr, *x1 = nullptr, *q = nullptr, *h = nullptr, *z = nullptr;
+    uint16_t* att = nullptr;  // [maxr][heads * 64] combined attention output (o_proj input)
+    LinScratch lin;           // staged activations of linears over more than 8 rows
     float* stop = nullptr;
     float* part = nullptr;
     int *seq_len = nullptr, *row_seq = nullptr, *row_pos = nullptr, *step_counter = nullptr;
@@ -198,19 +200,51 @@ void launch_lin_t(const PackedW& W, const Pro& p, const Epi& e, int rows, cudaSt
     linear_kernel<FMT, NT, Pro, Epi><<<grid, LIN_THREADS, smem, s>>>(W, p, e, rows);
 }
 
+template <int FMT, int NT, int T, class Epi>
+void launch_lin_frag(const PackedW& W, const LinScratch& sc, const Epi& e, int rows, cudaStream_t s) {
+    static unsigned attr_devices = 0;  // bit d: attribute set on device d
+    constexpr int smem = LinSmem<NT>::B_BYTES + LinSmem<NT>::YS_BYTES + LinSmem<NT>::RED_BYTES;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_devices & (1u << (dev & 31)))) {
+        cudaFuncSetAttribute(linear_frag_kernel<FMT, NT, T, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        attr_devices |= 1u << (dev & 31);
+    }
+    dim3 grid((W.ntiles + T - 1) / T, (rows + 8 * NT - 1) / (8 * NT));
+    linear_frag_kernel<FMT, NT, T, Epi><<<grid, LIN_THREADS, smem, s>>>(W, sc, e, rows);
+}
+
+// More than 8 rows: the prologue runs once into the context's staging
+// scratch, then CTAs of up to 4 tiles consume it (4 when that still gives
+// every SM several CTAs).
+template <int FMT, int NT, class Pro, class Epi>
+void launch_lin_staged(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
+    dim3 sg((rows + 7) / 8, (W.K + STAGE_KC - 1) / STAGE_KC);
+    stage_frag_kernel<FMT != 16, Pro><<<sg, LIN_THREADS, 0, s>>>(p, rows, W.K, sc, FMT != 16);
+    const long ctas = (long)W.ntiles * ((rows + 8 * NT - 1) / (8 * NT));
+    if (ctas >= 4L * sc.sms) launch_lin_frag<FMT, NT, 4>(W, sc, e, rows, s);
+    else launch_lin_frag<FMT, NT, 1>(W, sc, e, rows, s);
+}
+
 template <int FMT, class Pro, class Epi>
-void launch_lin_f(const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
+void launch_lin_f(const LinScratch& sc, const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
+    const bool staged = sc.frag && rows <= sc.rows && W.K <= sc.K;
     if (rows <= 8) launch_lin_t<FMT, 1>(W, p, e, rows, s);
-    else if (rows <= 16) launch_lin_t<FMT, 2>(W, p, e, rows, s);
-    else launch_lin_t<FMT, 4>(W, p, e, rows, s);
+    else if (rows <= 16) {
+        if (staged) launch_lin_staged<FMT, 2>(W, sc, p, e, rows, s);
+        else launch_lin_t<FMT, 2>(W, p, e, rows, s);
+    } else {
+        if (staged) launch_lin_staged<FMT, 4>(W, sc, p, e, rows, s);
+        else launch_lin_t<FMT, 4>(W, p, e, rows, s);
+    }
 }
 
 template <class Pro, class Epi>
-void run_linear(const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
+void run_linear(ming_ctx* c, const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
     if (rows <= 0) return;
-    if (W.fmt == 4) launch_lin_f<4>(W, p, e, rows, s);
-    else if (W.fmt == 8) launch_lin_f<8>(W, p, e, rows, s);
-    else launch_lin_f<16>(W, p, e, rows, s);
+    if (W.fmt == 4) launch_lin_f<4>(c->lin, W, p, e, rows, s);
+    else if (W.fmt == 8) launch_lin_f<8>(c->lin, W, p, e, rows, s);
+    else launch_lin_f<16>(c->lin, W, p, e, rows, s);
 }
 
 // Dequantizes every tile of a packed linear to f32 [ntiles*16][K] (the
@@ -455,8 +489,8 @@ int build_temb(ming_ctx* c, int freq_dim, int H) {
     c->temb = c->mem.alloc<uint16_t>((size_t)10 * H, &rc);
     if (rc) return rc;
     CK(cudaMemcpy(d_sc, sc.data(), sc.size() * 2, cudaMemcpyHostToDevice));
-    run_linear(c->t_mlp0.w, ProPlain{d_sc, freq_dim, 0}, EpiAct{d_h0, nullptr, c->t_mlp0.w.bias, H, 2, H}, 10, c->stream);
-    run_linear(c->t_mlp2.w, ProPlain{d_h0, H, 0}, EpiAct{c->temb, nullptr, c->t_mlp2.w.bias, H, 0, H}, 10, c->stream);
+    run_linear(c, c->t_mlp0.w, ProPlain{d_sc, freq_dim, 0}, EpiAct{d_h0, nullptr, c->t_mlp0.w.bias, H, 2, H}, 10, c->stream);
+    run_linear(c, c->t_mlp2.w, ProPlain{d_h0, H, 0}, EpiAct{c->temb, nullptr, c->t_mlp2.w.bias, H, 0, H}, 10, c->stream);
     CK(cudaStreamSynchronize(c->stream));
     CK(cudaGetLastError());
     return MING_OK;
@@ -502,14 +536,15 @@ void enqueue_layers(ming_ctx* c, int rows) {
     KvDev kv{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
     for (int l = 0; l < f.layers; l++) {
         auto& L = c->layers[l];
-        run_linear(L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
+        run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, rows, c->stream);
         launch_attn(AttnArgs{c->q, c->part, kv, rd, l, f.heads, f.kv_heads, c->nsplit}, rows, c->stream);
-        run_linear(L.o.w, ProAttn{c->part, rd, c->nsplit, f.heads, 0, nullptr},
+        launch_attn_combine(c->part, rd, c->nsplit, f.heads, c->att, rows, c->stream);
+        run_linear(c, L.o.w, ProPlain{c->att, f.heads * HD, 0},
                    EpiResidual{c->x, c->x1, nullptr, f.hidden}, rows, c->stream);
-        run_linear(L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr}, EpiSwiGLU{c->h, f.ff}, rows,
+        run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr}, EpiSwiGLU{c->h, f.ff}, rows,
                    c->stream);
-        run_linear(L.down.w, ProPlain{c->h, f.ff, 0}, EpiResidual{c->x1, c->x, nullptr, f.hidden}, rows, c->stream);
+        run_linear(c, L.down.w, ProPlain{c->h, f.ff, 0}, EpiResidual{c->x1, c->x, nullptr, f.hidden}, rows, c->stream);
     }
 }
 
@@ -733,20 +768,20 @@ int cfm_token_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift,
     const ming_cfg& f = c->cfg;
     const int H = f.dit_hidden, LAT = f.dit_latent, R = 6 * B;
     cudaStream_t s = c->stream;
-    run_linear(c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, 2 * B,
+    run_linear(c, c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, 2 * B,
                s);
-    run_linear(c->x_emb.w, ProPlain{c->f_hist, LAT, 0}, EpiAct{c->f_xh, nullptr, c->x_emb.w.bias, H, 0, H}, B, s);
+    run_linear(c, c->x_emb.w, ProPlain{c->f_hist, LAT, 0}, EpiAct{c->f_xh, nullptr, c->x_emb.w.bias, H, 0, H}, B, s);
     for (int st = step0; st < step0 + nsteps; st++) {
-        run_linear(c->x_emb.w, ProPlain{c->f_y, LAT, 0}, EpiAct{c->f_xy, nullptr, c->x_emb.w.bias, H, 0, H}, B, s);
+        run_linear(c, c->x_emb.w, ProPlain{c->f_y, LAT, 0}, EpiAct{c->f_xy, nullptr, c->x_emb.w.bias, H, 0, H}, B, s);
         launch_tok_rows(c->temb + (size_t)st * H, c->f_ce, c->f_xh, c->f_xy, c->f_rows, B, H, s);
         for (auto& b : c->dit) {
-            run_linear(b.qkv.w, ProRms{c->f_rows, b.norm1, H, H, 1e-6f, 0, nullptr},
+            run_linear(c, b.qkv.w, ProRms{c->f_rows, b.norm1, H, H, 1e-6f, 0, nullptr},
                        EpiDitQKV{b.qkv.w.bias, c->f_qkv, c->inv_freq, H, 3, R}, R, s);
             launch_dit_attention(c->f_qkv, c->f_att, R, 3, H, f.dit_heads, s);
-            run_linear(b.o.w, ProPlain{c->f_att, H, 0}, EpiResidual{c->f_rows, c->f_x1, b.o.w.bias, H}, R, s);
-            run_linear(b.ff1.w, ProRms{c->f_x1, b.norm2, H, H, 1e-6f, 0, nullptr},
+            run_linear(c, b.o.w, ProPlain{c->f_att, H, 0}, EpiResidual{c->f_rows, c->f_x1, b.o.w.bias, H}, R, s);
+            run_linear(c, b.ff1.w, ProRms{c->f_x1, b.norm2, H, H, 1e-6f, 0, nullptr},
                        EpiAct{c->f_hh, nullptr, b.ff1.w.bias, f.dit_ff, 1, f.dit_ff}, R, s);
-            run_linear(b.ff2.w, ProPlain{c->f_hh, f.dit_ff, 0}, EpiResidual{c->f_x1, c->f_rows, b.ff2.w.bias, H}, R, s);
+            run_linear(c, b.ff2.w, ProPlain{c->f_hh, f.dit_ff, 0}, EpiResidual{c->f_x1, c->f_rows, b.ff2.w.bias, H}, R, s);
         }
         launch_tok_final(c->f_rows, c->final_norm, c->final_w, c->final_b, c->f_y, with_sde ? c->f_sde : nullptr, st,
                          c->flow_dt[st], c->flow_sq[st], cfg, shift, B, H, LAT, s);
@@ -758,26 +793,26 @@ int cfm_ada_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift, i
     const ming_cfg& f = c->cfg;
     const int H = f.dit_hidden, LAT = f.dit_latent, F = f.dit_frames, NC = 2 * B, R = NC * F;
     cudaStream_t s = c->stream;
-    run_linear(c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, NC, s);
+    run_linear(c, c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, NC, s);
     for (int st = step0; st < step0 + nsteps; st++) {
         launch_ada_cond(c->temb + (size_t)st * H, c->f_ce, c->f_sc, NC, H, s);
-        run_linear(c->x_emb.w, ProLatent{c->f_y, B, F, LAT, 0}, EpiAct{c->f_rows, nullptr, c->x_emb.w.bias, H, 0, H}, R, s);
+        run_linear(c, c->x_emb.w, ProLatent{c->f_y, B, F, LAT, 0}, EpiAct{c->f_rows, nullptr, c->x_emb.w.bias, H, 0, H}, R, s);
         for (auto& b : c->dit) {
             const int MS = 6 * H;
-            run_linear(b.ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{c->f_mod, nullptr, b.ada.w.bias, MS, 0, MS}, NC, s);
-            run_linear(b.qkv.w, ProLnMod{c->f_rows, c->f_mod, c->f_mod + H, H, MS, H, F, 0, nullptr},
+            run_linear(c, b.ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{c->f_mod, nullptr, b.ada.w.bias, MS, 0, MS}, NC, s);
+            run_linear(c, b.qkv.w, ProLnMod{c->f_rows, c->f_mod, c->f_mod + H, H, MS, H, F, 0, nullptr},
                        EpiDitQKV{b.qkv.w.bias, c->f_qkv, c->inv_freq, H, F, R}, R, s);
             launch_dit_attention(c->f_qkv, c->f_att, R, F, H, f.dit_heads, s);
-            run_linear(b.o.w, ProPlain{c->f_att, H, 0}, EpiGatedRes{c->f_rows, c->f_rows, b.o.w.bias, c->f_mod + 2 * H, H, MS, F},
+            run_linear(c, b.o.w, ProPlain{c->f_att, H, 0}, EpiGatedRes{c->f_rows, c->f_rows, b.o.w.bias, c->f_mod + 2 * H, H, MS, F},
                        R, s);
-            run_linear(b.ff1.w, ProLnMod{c->f_rows, c->f_mod + 3 * H, c->f_mod + 4 * H, H, MS, H, F, 0, nullptr},
+            run_linear(c, b.ff1.w, ProLnMod{c->f_rows, c->f_mod + 3 * H, c->f_mod + 4 * H, H, MS, H, F, 0, nullptr},
                        EpiAct{c->f_hh, nullptr, b.ff1.w.bias, f.dit_ff, 1, f.dit_ff}, R, s);
-            run_linear(b.ff2.w, ProPlain{c->f_hh, f.dit_ff, 0},
+            run_linear(c, b.ff2.w, ProPlain{c->f_hh, f.dit_ff, 0},
                        EpiGatedRes{c->f_rows, c->f_rows, b.ff2.w.bias, c->f_mod + 5 * H, H, MS, F}, R, s);
         }
-        run_linear(c->final_ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{c->f_mod, nullptr, c->final_ada.w.bias, 2 * H, 0, 2 * H},
+        run_linear(c, c->final_ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{c->f_mod, nullptr, c->final_ada.w.bias, 2 * H, 0, 2 * H},
                    NC, s);
-        run_linear(c->final_lin.w, ProLnMod{c->f_rows, c->f_mod, c->f_mod + H, H, 2 * H, H, F, 0, nullptr},
+        run_linear(c, c->final_lin.w, ProLnMod{c->f_rows, c->f_mod, c->f_mod + H, H, 2 * H, H, F, 0, nullptr},
                    EpiAct{nullptr, c->f_vel, c->final_lin.w.bias, LAT, 3, LAT}, R, s);
         launch_ada_euler(c->f_vel, c->f_y, with_sde ? c->f_sde : nullptr, st, c->flow_dt[st], c->flow_sq[st], cfg, shift, B,
                          F, LAT, s);
@@ -946,6 +981,7 @@ int ming_cuda_finalize(ming_ctx* c) {
     c->x = c->mem.alloc<uint16_t>((size_t)c->maxr * H, &rc);
     c->x1 = c->mem.alloc<uint16_t>((size_t)c->maxr * H, &rc);
     c->q = c->mem.alloc<uint16_t>((size_t)c->maxr * QD, &rc);
+    c->att = c->mem.alloc<uint16_t>((size_t)c->maxr * f.heads * HD, &rc);
     c->h = c->mem.alloc<uint16_t>((size_t)c->maxr * f.ff, &rc);
     c->z = c->mem.alloc<uint16_t>((size_t)c->maxr * H, &rc);
     c->stop = c->mem.alloc<float>(c->maxr, &rc);
@@ -1025,6 +1061,26 @@ int ming_cuda_finalize(ming_ctx* c) {
         c->a_hh = c->mem.alloc<uint16_t>((size_t)2 * MB * f.dit_ff, &rc);
         c->a_out = c->mem.alloc<uint16_t>((size_t)MB * f.hidden, &rc);
         if (rc) return rc;
+    }
+    {
+        // staging scratch of the many-row linears: every (rows, K) a linear of
+        // this context can see; larger calls fall back to in-kernel staging
+        int rows_cap = c->maxr, k_cap = std::max(std::max(f.hidden, f.ff), f.heads * HD);
+        if (f.dit_mode != MING_DIT_NONE) {
+            const int MB = f.dit_max_batch;
+            rows_cap = std::max(rows_cap, std::max(2 * MB * f.dit_frames, 6 * MB));
+            k_cap = std::max(k_cap, std::max(std::max(f.dit_hidden, f.dit_ff), std::max(f.dit_cond_dim, f.dit_freq_dim)));
+        }
+        rows_cap = (rows_cap + 7) / 8 * 8;
+        k_cap = (k_cap + 63) / 64 * 64;
+        rc = MING_OK;
+        c->lin.frag = c->mem.alloc<uint2>((size_t)rows_cap / 8 * (k_cap / 16) * 32, &rc);
+        c->lin.ysum = c->mem.alloc<float>((size_t)rows_cap / 8 * (k_cap / 64) * 8, &rc);
+        c->lin.post = c->mem.alloc<float>(rows_cap, &rc);
+        if (rc) return rc;
+        c->lin.rows = rows_cap;
+        c->lin.K = k_cap;
+        CK(cudaDeviceGetAttribute(&c->lin.sms, cudaDevAttrMultiProcessorCount, c->device));
     }
     CK(cudaDeviceSynchronize());
     c->staged.clear();
@@ -1257,7 +1313,7 @@ int ming_cuda_aggregate(ming_ctx* c, int B, const uint16_t* latent, uint16_t* ou
     cudaStream_t s = c->stream;
     int rc;
     if ((rc = copy_in(c, c->a_lat, latent, (size_t)B * f.dit_latent * 2, kind))) return rc;
-    run_linear(c->agg_x_emb.w, ProPlain{c->a_lat, f.dit_latent, 0}, EpiAct{c->a_xe, nullptr, c->agg_x_emb.w.bias, H, 0, H}, B,
+    run_linear(c, c->agg_x_emb.w, ProPlain{c->a_lat, f.dit_latent, 0}, EpiAct{c->a_xe, nullptr, c->agg_x_emb.w.bias, H, 0, H}, B,
                s);
     // rows [cls, x_emb(latent)] per sequence
     for (int b = 0; b < B; b++) {
@@ -1266,16 +1322,16 @@ int ming_cuda_aggregate(ming_ctx* c, int B, const uint16_t* latent, uint16_t* ou
                            cudaMemcpyDeviceToDevice, s));
     }
     for (auto& b : c->agg) {
-        run_linear(b.qkv.w, ProRms{c->a_rows, b.norm1, H, H, 1e-6f, 0, nullptr},
+        run_linear(c, b.qkv.w, ProRms{c->a_rows, b.norm1, H, H, 1e-6f, 0, nullptr},
                    EpiDitQKV{b.qkv.w.bias, c->a_qkv, c->agg_inv_freq, H, 2, R}, R, s);
         launch_dit_attention(c->a_qkv, c->a_att, R, 2, H, f.dit_heads, s);
-        run_linear(b.o.w, ProPlain{c->a_att, H, 0}, EpiResidual{c->a_rows, c->a_x1, b.o.w.bias, H}, R, s);
-        run_linear(b.ff1.w, ProRms{c->a_x1, b.norm2, H, H, 1e-6f, 0, nullptr},
+        run_linear(c, b.o.w, ProPlain{c->a_att, H, 0}, EpiResidual{c->a_rows, c->a_x1, b.o.w.bias, H}, R, s);
+        run_linear(c, b.ff1.w, ProRms{c->a_x1, b.norm2, H, H, 1e-6f, 0, nullptr},
                    EpiAct{c->a_hh, nullptr, b.ff1.w.bias, f.dit_ff, 1, f.dit_ff}, R, s);
-        run_linear(b.ff2.w, ProPlain{c->a_hh, f.dit_ff, 0}, EpiResidual{c->a_x1, c->a_rows, b.ff2.w.bias, H}, R, s);
+        run_linear(c, b.ff2.w, ProPlain{c->a_hh, f.dit_ff, 0}, EpiResidual{c->a_x1, c->a_rows, b.ff2.w.bias, H}, R, s);
     }
     // final RMSNorm + linear on each CLS row (row stride 2H selects them)
-    run_linear(c->agg_final.w, ProRmsGraph{c->a_rows, c->agg_norm, 2 * H, H, 1e-6f, 0, nullptr},
+    run_linear(c, c->agg_final.w, ProRmsGraph{c->a_rows, c->agg_norm, 2 * H, H, 1e-6f, 0, nullptr},
                EpiAct{c->a_out, nullptr, c->agg_final.w.bias, f.hidden, 0, f.hidden}, B, s);
     CK(cudaGetLastError());
     if ((rc = copy_out(c, out, c->a_out, (size_t)B * f.hidden * 2, kind))) return rc;
@@ -1460,13 +1516,13 @@ extern "C" int ming_cuda_lm_decode_noalloc(ming_ctx* c, int B, const int* ids, c
     KvDev kv{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
     for (int l = 0; l < f.layers; l++) {
         auto& L = c->layers[l];
-        run_linear(L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
+        run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, B, s);
         launch_attn(AttnArgs{c->q, part, kv, rd, l, f.heads, f.kv_heads, c->nsplit}, B, s);
-        run_linear(L.o.w, ProAttn{part, rd, c->nsplit, f.heads, 0, nullptr}, EpiResidual{c->x, c->x1, nullptr, f.hidden}, B,
+        run_linear(c, L.o.w, ProAttn{part, rd, c->nsplit, f.heads, 0, nullptr}, EpiResidual{c->x, c->x1, nullptr, f.hidden}, B,
                    s);
-        run_linear(L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr}, EpiSwiGLU{c->h, f.ff}, B, s);
-        run_linear(L.down.w, ProPlain{c->h, f.ff, 0}, EpiResidual{c->x1, c->x, nullptr, f.hidden}, B, s);
+        run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr}, EpiSwiGLU{c->h, f.ff}, B, s);
+        run_linear(c, L.down.w, ProPlain{c->h, f.ff, 0}, EpiResidual{c->x1, c->x, nullptr, f.hidden}, B, s);
     }
     launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, c->x, step_dev(c), H, 0, 1, f.rms_eps}, B, s);
     CK(cudaGetLastError());
