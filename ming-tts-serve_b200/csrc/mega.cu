@@ -221,8 +221,8 @@ __host__ __device__ inline SmemMap smem_map(int nslots, int slot_bytes, int H, i
     return m;
 }
 constexpr int MG_ATT_SCRATCH = MG_B_BYTES + MG_SK * 8 * 4 + MG_T_BYTES;
-// attention item scratch: K, V rows (padded to 72) + q + new k/v + scores
-static_assert(2 * MG_ATT_CH * (HD + 8) * 2 + 8 * HD * 4 + 2 * HD * 4 + 8 * MG_ATT_CH * 4 <= MG_ATT_SCRATCH,
+// attention item scratch: K, V rows (padded to 72) + q + new k/v + scores + P.V partials
+static_assert(2 * MG_ATT_CH * (HD + 8) * 2 + 3 * HD * 4 + MG_ATT_CH * 4 + MG_CWARPS * 32 * 8 <= MG_ATT_SCRATCH,
               "attention scratch does not fit");
 
 struct Misc {              // small per-CTA state in shared memory
@@ -403,70 +403,76 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
     const int g0 = ms->g0[p], g1 = ms->g1[p], n = g1 - g0, gpt = a.ph[p].gpt;
     if (n <= 0) return;  // CTA-uniform
     const int nsc = (n + a.gps - 1) / a.gps;
-    for (int j = 0; j < nsc; j++) {
-        const int sc = cons_base + j;
-        if (!mbar_wait(&full[sc % a.nslots], (sc / a.nslots) & 1)) atomicCAS(cx.fail, 0, 2);
-    }
     MG_SUB(1)
     const int i0 = warp * n / MG_CWARPS, i1 = (warp + 1) * n / MG_CWARPS;
     const int tb = ms->wtile[p][warp];
     float acc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    if (i0 < i1 && !*(volatile int*)cx.fail) {
-        // walk the warp's run incrementally: tile t, group kg in the tile,
-        // ring slot and group wi in the slot
-        int t, kg, wi, slot;
-        {
-            const int g = g0 + i0;
-            t = g / gpt;
-            kg = g - t * gpt;
-            const int jj = i0 / a.gps;
-            wi = i0 - jj * a.gps;
-            slot = (cons_base + jj) % a.nslots;
-        }
-        for (int i = i0; i < i1; i += 2) {
-            const bool two = i + 1 < i1;
-            const uint8_t* ch[2];
-            int si[2], tu[2];
+    // walk the warp's run incrementally: tile t, group kg in the tile, group
+    // wi in its ring slot
+    int t = 0, kg = 0, wi = 0;
+    if (i0 < i1) {
+        const int g = g0 + i0;
+        t = g / gpt;
+        kg = g - t * gpt;
+        wi = i0 % a.gps;
+    }
+    // The phase's ring slots one at a time: every warp waits for each slot,
+    // uses the groups of its run inside it, and releases it, so a phase may be
+    // longer than the ring (the producer refills released slots meanwhile).
+    // A warp releases use u+1 of a slot only after waiting for its fill, which
+    // needs every warp's release of use u: arrivals of two uses never mix.
+    for (int jj = 0; jj < nsc; jj++) {
+        const int use = cons_base + jj, sl = use % a.nslots;
+        if (!mbar_wait(&full[sl], (use / a.nslots) & 1)) atomicCAS(cx.fail, 0, 2);
+        const int w0 = max(i0, jj * a.gps), w1 = min(i1, (jj + 1) * a.gps);
+        if (w0 < w1 && !*(volatile int*)cx.fail) {
+            const uint8_t* sbase = ring + (size_t)sl * a.slot_bytes;
+            for (int i = w0; i < w1; i += 2) {
+                const bool two = i + 1 < w1;
+                const uint8_t* ch[2];
+                int si[2], tu[2];
 #pragma unroll
-            for (int u = 0; u < 2; u++) {
-                ch[u] = ring + (size_t)slot * a.slot_bytes + (size_t)wi * a.cb;
-                const int s_ = kg - stage_base;
-                si[u] = s_ < 0 ? s_ + gpt : s_;
-                tu[u] = t == tb ? 0 : 1;
-                if (++kg == gpt) {
-                    kg = 0;
-                    t++;
+                for (int u = 0; u < 2; u++) {
+                    if (u == 1 && !two) {
+                        ch[1] = ch[0];
+                        si[1] = si[0];
+                        tu[1] = tu[0];
+                        break;
+                    }
+                    ch[u] = sbase + (size_t)wi * a.cb;
+                    const int s_ = kg - stage_base;
+                    si[u] = s_ < 0 ? s_ + gpt : s_;
+                    tu[u] = t == tb ? 0 : 1;
+                    if (++kg == gpt) {
+                        kg = 0;
+                        t++;
+                    }
+                    if (++wi == a.gps) wi = 0;
                 }
-                if (++wi == a.gps) {
-                    wi = 0;
-                    if (++slot == a.nslots) slot = 0;
-                }
-            }
-            if (!two) {
-                ch[1] = ch[0];
-                si[1] = si[0];
-            }
-            GroupW gw[2];
-            load_group<FMT>(ch[0], lane, gw[0]);
-            load_group<FMT>(ch[1], lane, gw[1]);
-            float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
+                GroupW gw[2];
+                load_group<FMT>(ch[0], lane, gw[0]);
+                load_group<FMT>(ch[1], lane, gw[1]);
+                float t0[4] = {0.f, 0.f, 0.f, 0.f}, t1[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (int ks = 0; ks < 4; ks++) {
-                uint32_t a0[4], a1[4];
-                a_frag<FMT>(ch[0], gw[0], ks, lane, a0);
-                a_frag<FMT>(ch[1], gw[1], ks, lane, a1);
-                const uint2 b0 = sm.sB[(si[0] * 4 + ks) * 32 + lane];
-                const uint2 b1 = sm.sB[(si[1] * 4 + ks) * 32 + lane];
-                mma_k<FMT>(t0, a0, b0);
-                mma_k<FMT>(t1, a1, b1);
-            }
-            if (tu[0] == 0) group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc2[0]);
-            else group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc2[1]);
-            if (two) {
-                if (tu[1] == 0) group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc2[0]);
-                else group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc2[1]);
+                for (int ks = 0; ks < 4; ks++) {
+                    uint32_t a0[4], a1[4];
+                    a_frag<FMT>(ch[0], gw[0], ks, lane, a0);
+                    a_frag<FMT>(ch[1], gw[1], ks, lane, a1);
+                    const uint2 b0 = sm.sB[(si[0] * 4 + ks) * 32 + lane];
+                    const uint2 b1 = sm.sB[(si[1] * 4 + ks) * 32 + lane];
+                    mma_k<FMT>(t0, a0, b0);
+                    mma_k<FMT>(t1, a1, b1);
+                }
+                if (tu[0] == 0) group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc2[0]);
+                else group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc2[1]);
+                if (two) {
+                    if (tu[1] == 0) group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc2[0]);
+                    else group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc2[1]);
+                }
             }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[sl]);  // before any global write of this phase
     }
     MG_SUB(2)
     {
@@ -481,11 +487,6 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
         }
     }
     cbar();
-    // every warp is done with the phase's ring slots: hand them back before
-    // any global write of this phase (an arrive orders this thread's earlier
-    // memory operations before it)
-    if (lane == 0)
-        for (int j = 0; j < nsc; j++) mbar_arrive(&empty[(cons_base + j) % a.nslots]);
     MG_SUB(3)
     const int t0 = g0 / gpt, nt = (g1 - 1) / gpt - t0 + 1, B = a.B;
     if (out == OUT_ACC) {
@@ -525,24 +526,27 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
     MG_SUB(4)
 }
 
-// Attention of one (row, kv head, 128-position chunk) item. q/k/v come from
-// the q|k|v accumulator (+ bias, bf16, RoPE on q and k as MLX fast_rope);
-// cached K/V rows are prefetched with cp.async before the wait for q|k|v.
-MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, int b, int g, int s, bool waited) {
+// Attention of one (row, query head, 128-position chunk) item. q of the head
+// and the kv group's new k, v come from the q|k|v accumulator (+ bias, bf16,
+// RoPE on q and k as MLX fast_rope); the chunk's cached K/V rows are
+// prefetched with cp.async before the wait for q|k|v. The first head of the
+// group appends the new position to the cache (in the chunk holding it).
+MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, int b, int h, int s, bool waited) {
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int grp = a.heads / a.kvh, pos = ms->pos[b];
-    const int p0 = s * MG_ATT_CH, p1 = min(pos + 1, p0 + MG_ATT_CH), pc = min(p1, pos);
+    const int grp = a.heads / a.kvh, g = h / grp, pos = ms->pos[b];
+    const int p0 = s * MG_ATT_CH, p1 = min(pos + 1, p0 + MG_ATT_CH), pc = min(p1, pos), len = p1 - p0;
     // K/V rows padded to 72 elements (144 B): 16-byte loads of 8 consecutive
     // rows fall on distinct bank groups
     constexpr int KS = HD + 8;
     uint16_t* sK = reinterpret_cast<uint16_t*>(sm.sB);         // [128][72]
     uint16_t* sV = sK + MG_ATT_CH * KS;                          // [128][72]
-    float* sq = reinterpret_cast<float*>(sV + MG_ATT_CH * KS);  // [8][64]
-    float* skn = sq + 8 * HD;                                    // [64]
+    float* sq = reinterpret_cast<float*>(sV + MG_ATT_CH * KS);  // [64]
+    float* skn = sq + HD;                                        // [64]
     float* svn = skn + HD;                                       // [64]
-    float* sS = svn + HD;                                        // [8][128]
+    float* sS = svn + HD;                                        // [128]
+    float2* sP = reinterpret_cast<float2*>(sS + MG_ATT_CH);     // [8 warps][32]
     const int* bt = sm.bt + b * MG_BT_INTS;
     // 1. prefetch cached K/V rows [p0, pc)
     for (int e = tid; e < (pc - p0) * 8; e += 256) {
@@ -552,27 +556,16 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         cp16(sV + j * KS + piece * 8, a.kv.pool + kv_index(a.kv, page, l, 1, g, p % PAGE) + piece * 8);
     }
     cp_commit();
-    // 2. q (the group's heads), k, v of the new position; item (tile, r8)
-    //    holds the RoPE pair (d, d+32) = tile rows r8, r8 + 8
+    // 2. q of the head, k, v of the new position: entry (kind, tile, r8) holds
+    //    the RoPE pair (d, d+32) = tile rows r8, r8 + 8
     if (!waited) await(cx, a.cnt + (size_t)l * MG_NCNT + MG_CNT_QKV, ms->epoch * (unsigned)a.C);
     const unsigned long long* qacc = acc_ptr(a, ms->epoch, l, MG_ACC_QKV) + (size_t)b * a.acc_w;
     const float* bias = reinterpret_cast<const float*>(sm.lp + 4 * a.H);
-    const int nt = grp * 4 + 8;
-    for (int e = tid; e < nt * 8; e += 256) {
-        const int tl = e >> 3, r8 = e & 7;
-        int t, kind;
-        if (tl < grp * 4) {
-            t = (g * grp + tl / 4) * 4 + (tl & 3);
-            kind = 0;
-        } else if (tl < grp * 4 + 4) {
-            t = a.heads * 4 + g * 4 + (tl - grp * 4);
-            kind = 1;
-        } else {
-            t = a.heads * 4 + a.kvh * 4 + g * 4 + (tl - grp * 4 - 4);
-            kind = 2;
-        }
+    if (tid < 96) {
+        const int kind = tid >> 5, tl = (tid >> 3) & 3, r8 = tid & 7;
+        const int t = kind == 0 ? h * 4 + tl : (kind == 1 ? a.heads * 4 + g * 4 + tl : a.heads * 4 + a.kvh * 4 + g * 4 + tl);
         const uint64_t vlo = ldr64(qacc + t * 16 + r8), vhi = ldr64(qacc + t * 16 + r8 + 8);
-        const int d = (t & 3) * 8 + r8;
+        const int d = tl * 8 + r8;
         float x1 = rb(from_fix(vlo) + bias[t * 16 + r8]);
         float x2 = rb(from_fix(vhi) + bias[t * 16 + r8 + 8]);
         if (kind < 2) {
@@ -581,107 +574,103 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
             x1 = rb(p_);
             x2 = rb(q_);
         }
-        if (kind == 0) {
-            const int h = tl / 4;
-            sq[h * HD + d] = 0.125f * x1;
-            sq[h * HD + d + 32] = 0.125f * x2;
-        } else if (kind == 1) {
-            skn[d] = x1;
-            skn[d + 32] = x2;
-        } else {
-            svn[d] = x1;
-            svn[d + 32] = x2;
-        }
+        float* dst = kind == 0 ? sq : (kind == 1 ? skn : svn);
+        const float sc = kind == 0 ? 0.125f : 1.f;
+        dst[d] = sc * x1;
+        dst[d + 32] = sc * x2;
     }
     cp_wait_all();
     cbar();
-    // 3. the chunk holding the new position appends it to the cache
-    if (p1 == pos + 1 && tid < 2 * HD) {
+    // 3. the group's first head, in the chunk holding the new position, appends it
+    if (p1 == pos + 1 && h % grp == 0 && tid < 2 * HD) {
         const int which = tid / HD, d = tid % HD;
         const int page = bt[pos / PAGE];
         a.kv.pool[kv_index(a.kv, page, l, which, g, pos % PAGE) + d] = f2bf(which ? svn[d] : skn[d]);
     }
-    // 4. scores: thread (position j, head quad hq) keeps the key row in
-    //    registers and accumulates 4 heads independently
-    const int len = p1 - p0;
-    {
-        const int j = tid & (MG_ATT_CH - 1), hq = tid >> 7;
-        if (j < len && hq * 4 < grp) {
-            uint32_t kr[HD / 2];
-            if (p0 + j < pos) {
-                const uint4* src = reinterpret_cast<const uint4*>(sK + j * KS);
+    // 4. scores: a thread per position
+    if (tid < len) {
+        float s0 = 0.f, s1 = 0.f;
+        if (p0 + tid < pos) {
+            const uint4* src = reinterpret_cast<const uint4*>(sK + tid * KS);
 #pragma unroll
-                for (int q = 0; q < HD / 8; q++) {
-                    const uint4 v = src[q];
-                    kr[4 * q] = v.x; kr[4 * q + 1] = v.y; kr[4 * q + 2] = v.z; kr[4 * q + 3] = v.w;
-                }
-            } else {
-#pragma unroll
-                for (int q = 0; q < HD / 2; q++) kr[q] = pack_bf16x2(skn[2 * q], skn[2 * q + 1]);
+            for (int q = 0; q < HD / 8; q++) {
+                const uint4 v = src[q];
+                const float4 qa = *reinterpret_cast<const float4*>(sq + 8 * q);
+                const float4 qb = *reinterpret_cast<const float4*>(sq + 8 * q + 4);
+                const float2 k0 = unpack_bf16x2(v.x), k1 = unpack_bf16x2(v.y), k2 = unpack_bf16x2(v.z), k3 = unpack_bf16x2(v.w);
+                s0 += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y;
+                s1 += qb.x * k2.x + qb.y * k2.y + qb.z * k3.x + qb.w * k3.y;
             }
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int q = 0; q < HD / 2; q++) {  // fully unrolled: kr stays in registers
-                const float2 kv = unpack_bf16x2(kr[q]);
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const float2 qv = *reinterpret_cast<const float2*>(sq + (hq * 4 + u) * HD + 2 * q);
-                    acc[u] += qv.x * kv.x + qv.y * kv.y;
-                }
+        } else {
+#pragma unroll 8
+            for (int q = 0; q < HD / 2; q += 2) {
+                // the new key (already bf16-exact, as the cache holds it)
+                s0 += sq[2 * q] * skn[2 * q] + sq[2 * q + 1] * skn[2 * q + 1];
+                s1 += sq[2 * q + 2] * skn[2 * q + 2] + sq[2 * q + 3] * skn[2 * q + 3];
             }
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                if (hq * 4 + u < grp) sS[(hq * 4 + u) * MG_ATT_CH + j] = acc[u];
         }
+        sS[tid] = s0 + s1;
     }
     cbar();
-    // 5. softmax inside the chunk (warp per head)
-    if (warp < grp) {
+    // 5. softmax inside the chunk (warp 0)
+    if (warp == 0) {
         float m = -INFINITY;
-        for (int j = lane; j < len; j += 32) m = fmaxf(m, sS[warp * MG_ATT_CH + j]);
+        for (int j = lane; j < len; j += 32) m = fmaxf(m, sS[j]);
         m = warp_max(m);
         float sum = 0.f;
         for (int j = lane; j < len; j += 32) {
-            const float p = expf(sS[warp * MG_ATT_CH + j] - m);
-            sS[warp * MG_ATT_CH + j] = p;
+            const float p = expf(sS[j] - m);
+            sS[j] = p;
             sum += p;
         }
         sum = warp_sum(sum);
         if (lane == 0) {
-            uint64_t* o = a.attn + (((size_t)b * a.heads + g * grp + warp) * a.max_splits + s) * MG_PART;
+            uint64_t* o = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
             str64(o, tagged(tag, m));
             str64(o + 1, tagged(tag, sum));
         }
     }
     cbar();
-    // 6. P.V: thread (head, dim pair), 4 independent accumulators
-    for (int e = tid; e < grp * (HD / 2); e += 256) {
-        const int h = e / (HD / 2), dp = e % (HD / 2);
-        float2 ac[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
-        const float* ph_ = sS + h * MG_ATT_CH;
-        const int lc = min(len, pos - p0);  // cached positions of the chunk
-        int j = 0;
-        for (; j + 4 <= lc; j += 4) {
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (j + u) * KS + 2 * dp));
-                const float pw = ph_[j + u];
-                ac[u].x += pw * v.x;
-                ac[u].y += pw * v.y;
+    // 6. P.V: warp w sums positions [w*len/8, (w+1)*len/8) for dim pair = lane
+    {
+        const int j0 = warp * len / MG_CWARPS, j1 = (warp + 1) * len / MG_CWARPS;
+        float2 ac0 = make_float2(0.f, 0.f), ac1 = make_float2(0.f, 0.f);
+        int j = j0;
+        for (; j + 2 <= j1; j += 2) {
+            float2 v0, v1;
+            if (p0 + j + 1 < pos) {
+                v0 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * KS + 2 * lane));
+                v1 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (j + 1) * KS + 2 * lane));
+            } else {
+                v0 = p0 + j < pos ? unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * KS + 2 * lane))
+                                  : make_float2(svn[2 * lane], svn[2 * lane + 1]);
+                v1 = make_float2(svn[2 * lane], svn[2 * lane + 1]);
             }
+            ac0.x += sS[j] * v0.x;
+            ac0.y += sS[j] * v0.y;
+            ac1.x += sS[j + 1] * v1.x;
+            ac1.y += sS[j + 1] * v1.y;
         }
-        for (; j < len; j++) {
-            float2 v;
-            if (p0 + j < pos) v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * KS + 2 * dp));
-            else v = make_float2(svn[2 * dp], svn[2 * dp + 1]);
-            const float pw = ph_[j];
-            ac[0].x += pw * v.x;
-            ac[0].y += pw * v.y;
+        if (j < j1) {
+            const float2 v = p0 + j < pos ? unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * KS + 2 * lane))
+                                          : make_float2(svn[2 * lane], svn[2 * lane + 1]);
+            ac0.x += sS[j] * v.x;
+            ac0.y += sS[j] * v.y;
         }
-        const float ox = (ac[0].x + ac[1].x) + (ac[2].x + ac[3].x), oy = (ac[0].y + ac[1].y) + (ac[2].y + ac[3].y);
-        uint64_t* o = a.attn + (((size_t)b * a.heads + g * grp + h) * a.max_splits + s) * MG_PART;
-        str64(o + 2 + 2 * dp, tagged(tag, ox));
-        str64(o + 3 + 2 * dp, tagged(tag, oy));
+        sP[warp * 32 + lane] = make_float2(ac0.x + ac1.x, ac0.y + ac1.y);
+    }
+    cbar();
+    if (warp == 0) {
+        float ox = 0.f, oy = 0.f;
+#pragma unroll
+        for (int w = 0; w < MG_CWARPS; w++) {
+            const float2 v = sP[w * 32 + lane];
+            ox += v.x;
+            oy += v.y;
+        }
+        uint64_t* o = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
+        str64(o + 2 + 2 * lane, tagged(tag, ox));
+        str64(o + 3 + 2 * lane, tagged(tag, oy));
     }
     cbar();
 }
@@ -907,18 +896,18 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
                 nst = min(n, gpt);
             }
             if (q == 1) {
-                // P1: attention items (row, kv head, chunk) strided over the CTAs
+                // P1: attention items (row, chunk, query head) strided over the
+                // CTAs; neighbouring CTAs share a chunk's K/V lines in L2
                 int tot = 0;
-                for (int b = 0; b < B; b++) tot += a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
+                for (int b = 0; b < B; b++) tot += a.heads * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
                 bool waited = false;
                 for (int it = c; it < tot && !dead; it += a.C) {
                     int rem = it, b = 0;
-                    while (rem >= a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH)) {
-                        rem -= a.kvh * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
+                    while (rem >= a.heads * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH)) {
+                        rem -= a.heads * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
                         b++;
                     }
-                    const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
-                    attention_item(cx, sm, l, tag, b, rem / ns, rem % ns, waited);
+                    attention_item(cx, sm, l, tag, b, rem % a.heads, rem / a.heads, waited);
                     waited = true;
                     check();
                 }

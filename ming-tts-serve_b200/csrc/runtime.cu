@@ -621,7 +621,6 @@ int setup_mega(ming_ctx* c) {
     const int gpt[MG_NPH] = {H / 64, H / 64, H / 64, f.ff / 64};
     const int C = nsm;
     int rc = MING_OK;
-    int max_nsc = 0;
     for (int p = 0; p < MG_NPH; p++) {
         const int G = tiles[p] * gpt[p];
         if (G < C) return MING_OK;  // too small to give every CTA work: stay on the per-kernel path
@@ -633,7 +632,6 @@ int setup_mega(ming_ctx* c) {
         int maxn = 0;
         for (int i = 0; i < C; i++) {
             maxn = std::max(maxn, g0[i + 1] - g0[i]);
-            max_nsc = std::max(max_nsc, (g0[i + 1] - g0[i] + gps - 1) / gps);
         }
         if (p == 3 && maxn > MG_MAX_STAGE) return MING_OK;                // staged groups of h
         if ((maxn + MG_CWARPS - 1) / MG_CWARPS > gpt[p]) return MING_OK;  // a warp's run spans at most two tiles
@@ -642,7 +640,7 @@ int setup_mega(ming_ctx* c) {
         CK(cudaMemcpy(dg0, g0.data(), (C + 1) * 4, cudaMemcpyHostToDevice));
         a.ph[p] = MegaPhase{dg0, tiles[p], gpt[p]};
     }
-    if (nslots < max_nsc + 2) return MING_OK;
+    if (nslots < 4) return MING_OK;  // warps consume a phase slot by slot: any ring works, a deeper one streams ahead
     if (f.max_ctx / PAGE + 1 > 512) return MING_OK;  // block-table rows live in shared memory
     // per-layer tables gathered into contiguous device arrays
     std::vector<const uint8_t*> wb((size_t)f.layers * MG_NPH);
