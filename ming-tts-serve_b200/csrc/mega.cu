@@ -98,7 +98,9 @@ struct Ctx {
 // Polls one tagged f32 word until its tag is `tag`. On timeout or a failure
 // elsewhere, records it and returns 0 (the caller checks *fail at the next
 // barrier). Kept out of line: it is the rare path of every gather.
-__device__ __noinline__ float poll(const Ctx& x, const uint64_t* p, uint32_t tag) {
+// (Out of line and with scalar arguments: nothing of the caller's state has
+// to live in local memory, which the nearly full L1 would serve from L2.)
+__device__ __noinline__ float poll_word(const uint64_t* p, uint32_t tag, int* fail, const int* err) {
     uint64_t v = ldr64(p);
     if ((uint32_t)(v >> 32) == tag) return __uint_as_float((uint32_t)v);
     const long long t0 = clock64();
@@ -107,32 +109,33 @@ __device__ __noinline__ float poll(const Ctx& x, const uint64_t* p, uint32_t tag
         v = ldr64(p);
         if ((uint32_t)(v >> 32) == tag) return __uint_as_float((uint32_t)v);
         if (((++it) & 63) == 0) {
-            if (*(volatile int*)x.fail) return 0.f;
-            if (ldr32(x.a->err)) {
-                atomicCAS(x.fail, 0, 5);
+            if (*(volatile int*)fail) return 0.f;
+            if (ldr32(err)) {
+                atomicCAS(fail, 0, 5);
                 return 0.f;
             }
             if (clock64() - t0 > MG_TIMEOUT) {
-                atomicCAS(x.fail, 0, 1);
+                atomicCAS(fail, 0, 1);
                 return 0.f;
             }
         }
     }
 }
+MING_DEV float poll(const Ctx& x, const uint64_t* p, uint32_t tag) { return poll_word(p, tag, x.fail, x.a->err); }
 
 // One thread waits until the counter reaches target (acquire); bounded.
-__device__ __noinline__ void wait_count(const Ctx& x, const unsigned int* cnt, unsigned int target) {
+__device__ __noinline__ void wait_counter(const unsigned int* cnt, unsigned int target, int* fail, const int* err) {
     const long long t0 = clock64();
     int it = 0;
     while ((int)(lda32(cnt) - target) < 0) {
         if (((++it) & 15) == 0) {
-            if (*(volatile int*)x.fail) return;
-            if (ldr32(x.a->err)) {
-                atomicCAS(x.fail, 0, 5);
+            if (*(volatile int*)fail) return;
+            if (ldr32(err)) {
+                atomicCAS(fail, 0, 5);
                 return;
             }
             if (clock64() - t0 > MG_TIMEOUT) {
-                atomicCAS(x.fail, 0, 1);
+                atomicCAS(fail, 0, 1);
                 return;
             }
         }
@@ -383,7 +386,7 @@ MING_DEV void publish(const Sm& sm, unsigned int* cnt) {
 
 // One thread waits until every CTA published, then releases the CTA.
 MING_DEV void await(const Ctx& cx, const unsigned int* cnt, unsigned int target) {
-    if (threadIdx.x == 0 && (int)(lda32(cnt) - target) < 0) wait_count(cx, cnt, target);
+    if (threadIdx.x == 0 && (int)(lda32(cnt) - target) < 0) wait_counter(cnt, target, cx.fail, cx.a->err);
     cbar();
 }
 

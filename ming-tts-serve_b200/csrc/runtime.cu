@@ -17,6 +17,7 @@
 #include "dit.cuh"
 #include "lm.cuh"
 #include "mega.cuh"
+#include "tcgen05.cuh"
 #include "pack.h"
 
 using namespace ming;
@@ -226,9 +227,49 @@ void launch_lin_staged(const PackedW& W, const LinScratch& sc, const Pro& p, con
     else launch_lin_frag<FMT, NT, 1>(W, sc, e, rows, s);
 }
 
+template <int N, class Epi>
+void launch_tc_n(const PackedW& W, const uint16_t* xs, const float* post, const Epi& e, int rows, cudaStream_t s) {
+    static unsigned attr_devices = 0;  // bit d: attribute set on device d
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!(attr_devices & (1u << (dev & 31)))) {
+        cudaFuncSetAttribute(tc_linear_kernel<N, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem<N>::TOTAL);
+        attr_devices |= 1u << (dev & 31);
+    }
+    dim3 grid(W.ntiles / 8, (rows + N - 1) / N);
+    tc_linear_kernel<N, Epi><<<grid, TC_THREADS, TcSmem<N>::TOTAL, s>>>(W, xs, post, e, rows);
+}
+
+// bf16 weights, 64+ rows: the prologue once into row-major bf16, then the
+// tcgen05 linear with the widest row block that still gives ~96 CTAs.
+template <class Pro, class Epi>
+void launch_tc(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
+    uint16_t* xs = reinterpret_cast<uint16_t*>(sc.frag);
+    dim3 sg((rows + 7) / 8, (W.K + STAGE_KC - 1) / STAGE_KC);
+    stage_rows_kernel<Pro><<<sg, LIN_THREADS, 0, s>>>(p, rows, W.K, xs, sc.post);
+    const int mt = W.ntiles / 8;
+    if (mt * ((rows + 255) / 256) >= 96) launch_tc_n<256>(W, xs, sc.post, e, rows, s);
+    else if (mt * ((rows + 127) / 128) >= 96) launch_tc_n<128>(W, xs, sc.post, e, rows, s);
+    else launch_tc_n<64>(W, xs, sc.post, e, rows, s);
+}
+
+bool tc_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("MING_TC");
+        return !(v && std::string(v) == "0");
+    }();
+    return on;
+}
+
 template <int FMT, class Pro, class Epi>
 void launch_lin_f(const LinScratch& sc, const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
     const bool staged = sc.frag && rows <= sc.rows && W.K <= sc.K;
+    if constexpr (FMT == 16) {
+        if (staged && rows >= 64 && W.ntiles % 8 == 0 && W.K % 64 == 0 && tc_enabled()) {
+            launch_tc(W, sc, p, e, rows, s);
+            return;
+        }
+    }
     if (rows <= 8) launch_lin_t<FMT, 1>(W, p, e, rows, s);
     else if (rows <= 16) {
         if (staged) launch_lin_staged<FMT, 2>(W, sc, p, e, rows, s);

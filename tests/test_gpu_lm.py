@@ -102,6 +102,17 @@ def test_decode_parity_bf16_q8(cuda_ok, bits, layers):
     ctx.close()
 
 
+def test_prefill_bf16_many_rows(cuda_ok):
+    """bf16 weights with 96 prompt rows: the projections run on the tcgen05
+    linear (64+ rows), gated like the other multi-layer outputs."""
+    W = synth.lm_weights(seed=3, bits=16, layers=2)
+    ctx = make_ctx(W, 16, 2)
+    res = _teacher_forced(ctx, O.Lm(W), synth.normal_bf16(3, "test.prompt.bf16.96", (96, 896)), 2, 3)
+    for i, (d, c, ok) in enumerate(res):
+        assert ok, f"step {i}: maxabs {d:.4g} cos {c:.6f}"
+    ctx.close()
+
+
 def test_batched_decode_ragged_prompts(q4_24):
     W, ctx, lm = q4_24
     lens = [1, 17, 40, 64, 300]
