@@ -27,6 +27,7 @@ struct PackedW {
     const uint8_t* tiles = nullptr;
     const float* bias = nullptr;  // [ntiles*16] in packed row order, or null
     int ntiles = 0, K = 0, fmt = 16;
+    const uint8_t* tc = nullptr;  // bf16 only: swizzled weight blocks for the tcgen05 linear (tcgen05.cuh), or null
 };
 
 MING_DEV constexpr int chunk_b(int fmt) { return fmt == 4 ? 576 : (fmt == 8 ? 1088 : 2048); }
@@ -240,19 +241,29 @@ __global__ void __launch_bounds__(LIN_THREADS) stage_frag_kernel(Pro pro, int ro
     Pro p = pro;
     p.init(r0, nrows, aux);
     __syncthreads();
-    for (int e = threadIdx.x; e < (kcl / 16) * 32; e += LIN_THREADS) {
-        const int lane = e & 31, ks = e >> 5;
-        const int row = lane >> 2, k0 = kc + ks * 16 + 2 * (lane & 3);
-        float y0 = 0.f, y1 = 0.f, y8 = 0.f, y9 = 0.f;
-        if (row < nrows) {
-            y0 = p.y(row, k0);
-            y1 = p.y(row, k0 + 1);
-            y8 = p.y(row, k0 + 8);
-            y9 = p.y(row, k0 + 9);
+    // 4 fragment entries per pass: their 16 prologue values are independent
+    // loads, issued before any store
+    const int nent = (kcl / 16) * 32;
+    for (int e0 = threadIdx.x; e0 < nent; e0 += 4 * LIN_THREADS) {
+        float y[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int e = e0 + u * LIN_THREADS, lane = e & 31, ks = e >> 5;
+            const int row = lane >> 2, k0 = kc + ks * 16 + 2 * (lane & 3);
+            const bool live = e < nent && row < nrows;
+            y[u][0] = live ? p.y(row, k0) : 0.f;
+            y[u][1] = live ? p.y(row, k0 + 1) : 0.f;
+            y[u][2] = live ? p.y(row, k0 + 8) : 0.f;
+            y[u][3] = live ? p.y(row, k0 + 9) : 0.f;
         }
-        const uint2 v = make_bfrag<F16>(y0, y1, y8, y9);
-        sB[e] = v;
-        sc.frag[((size_t)rb * (K / 16) + kc / 16 + ks) * 32 + lane] = v;
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int e = e0 + u * LIN_THREADS;
+            if (e >= nent) break;
+            const uint2 v = make_bfrag<F16>(y[u][0], y[u][1], y[u][2], y[u][3]);
+            sB[e] = v;
+            sc.frag[((size_t)rb * (K / 16) + kc / 16 + (e >> 5)) * 32 + (e & 31)] = v;
+        }
     }
     if (need_ysum) {
         __syncthreads();

@@ -227,8 +227,8 @@ void launch_lin_staged(const PackedW& W, const LinScratch& sc, const Pro& p, con
     else launch_lin_frag<FMT, NT, 1>(W, sc, e, rows, s);
 }
 
-template <int N, class Epi>
-void launch_tc_n(const PackedW& W, const uint16_t* xs, const float* post, const Epi& e, int rows, cudaStream_t s) {
+template <int N, class Pro, class Epi>
+void launch_tc_n(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
     static unsigned attr_devices = 0;  // bit d: attribute set on device d
     int dev = 0;
     cudaGetDevice(&dev);
@@ -236,21 +236,21 @@ void launch_tc_n(const PackedW& W, const uint16_t* xs, const float* post, const 
         cudaFuncSetAttribute(tc_linear_kernel<N, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem<N>::TOTAL);
         attr_devices |= 1u << (dev & 31);
     }
-    dim3 grid(W.ntiles / 8, (rows + N - 1) / N);
-    tc_linear_kernel<N, Epi><<<grid, TC_THREADS, TcSmem<N>::TOTAL, s>>>(W, xs, post, e, rows);
+    uint8_t* xs = reinterpret_cast<uint8_t*>(sc.frag);
+    stage_rows_kernel<N, Pro><<<dim3((rows + 7) / 8, (W.K + STAGE_KC - 1) / STAGE_KC), LIN_THREADS, 0, s>>>(p, rows, W.K, xs,
+                                                                                                         sc.post);
+    tc_linear_kernel<N, Epi><<<dim3(W.ntiles / 8, (rows + N - 1) / N), TC_THREADS, TcSmem<N>::TOTAL, s>>>(W.tc, W.K, xs,
+                                                                                                        sc.post, e, rows);
 }
 
-// bf16 weights, 64+ rows: the prologue once into row-major bf16, then the
-// tcgen05 linear with the widest row block that still gives ~96 CTAs.
+// bf16 weights, 64+ rows: the tcgen05 linear with the widest row block that
+// still gives ~96 CTAs.
 template <class Pro, class Epi>
 void launch_tc(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
-    uint16_t* xs = reinterpret_cast<uint16_t*>(sc.frag);
-    dim3 sg((rows + 7) / 8, (W.K + STAGE_KC - 1) / STAGE_KC);
-    stage_rows_kernel<Pro><<<sg, LIN_THREADS, 0, s>>>(p, rows, W.K, xs, sc.post);
     const int mt = W.ntiles / 8;
-    if (mt * ((rows + 255) / 256) >= 96) launch_tc_n<256>(W, xs, sc.post, e, rows, s);
-    else if (mt * ((rows + 127) / 128) >= 96) launch_tc_n<128>(W, xs, sc.post, e, rows, s);
-    else launch_tc_n<64>(W, xs, sc.post, e, rows, s);
+    if (mt * ((rows + 255) / 256) >= 96) launch_tc_n<256>(W, sc, p, e, rows, s);
+    else if (mt * ((rows + 127) / 128) >= 96) launch_tc_n<128>(W, sc, p, e, rows, s);
+    else launch_tc_n<64>(W, sc, p, e, rows, s);
 }
 
 bool tc_enabled() {
@@ -265,7 +265,7 @@ template <int FMT, class Pro, class Epi>
 void launch_lin_f(const LinScratch& sc, const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
     const bool staged = sc.frag && rows <= sc.rows && W.K <= sc.K;
     if constexpr (FMT == 16) {
-        if (staged && rows >= 64 && W.ntiles % 8 == 0 && W.K % 64 == 0 && tc_enabled()) {
+        if (staged && rows >= 64 && W.tc && tc_enabled()) {
             launch_tc(W, sc, p, e, rows, s);
             return;
         }
@@ -404,6 +404,14 @@ int upload_packed(ming_ctx* c, const std::vector<LinearSrc>& srcs, const std::ve
     pl.w.ntiles = (int)rows.size() / 16;
     pl.w.K = K;
     pl.w.fmt = fmt;
+    if (fmt == 16 && pl.w.ntiles % 8 == 0 && K % 64 == 0) {
+        // the tcgen05 linear's weight blocks (same bytes, swizzled shared-memory order)
+        uint8_t* tc = c->mem.alloc<uint8_t>(tiles.size(), &rc);
+        if (!tc) return rc;
+        tc_swizzle_kernel<<<dim3(pl.w.ntiles / 8, K / 64), TC_THREADS>>>(dt, K / 64, tc);
+        CK(cudaGetLastError());
+        pl.w.tc = tc;
+    }
     pl.src_names = names;
     pl.rows = rows;
     for (auto& s : srcs) {
@@ -1110,7 +1118,7 @@ int ming_cuda_finalize(ming_ctx* c) {
             rows_cap = std::max(rows_cap, std::max(2 * MB * f.dit_frames, 6 * MB));
             k_cap = std::max(k_cap, std::max(std::max(f.dit_hidden, f.dit_ff), std::max(f.dit_cond_dim, f.dit_freq_dim)));
         }
-        rows_cap = (rows_cap + 7) / 8 * 8;
+        rows_cap = (rows_cap + 255) / 256 * 256;  // the tcgen05 linear reads whole 256-row blocks
         k_cap = (k_cap + 63) / 64 * 64;
         rc = MING_OK;
         c->lin.frag = c->mem.alloc<uint2>((size_t)rows_cap / 8 * (k_cap / 16) * 32, &rc);

@@ -5,16 +5,19 @@
 // rows >= 64 (the DiT head at batch 32, prefill of a bf16 LM):
 //   * a CTA owns 128 features (8 packed 16-row tiles, pack.h) and N rows
 //     (64, 128 or 256); the f32 accumulator D[128][N] lives in tensor memory;
-//   * per 64-wide K group the CTA's threads rewrite the 8 packed tile chunks
-//     (mma.sync fragment order) into a 128-byte-swizzled K-major shared tile
-//     and copy the N activation rows (the prologue's output, staged once,
-//     row-major bf16) with cp.async into the same swizzled layout;
-//   * one thread issues 4 tcgen05.mma (K = 16 each) and commits them to the
-//     stage's mbarrier; two stages let the copies of group g+1 overlap the
-//     MMAs of group g;
-//   * the epilogue reads D with tcgen05.ld (warp w: features 32w..32w+31)
-//     and hands (tile, r8, row, lo, hi) pairs to the same epilogue functors
-//     as the mma.sync kernels.
+//   * both operands sit in global memory as the exact shared-memory image
+//     the MMA reads — 128-byte-swizzled K-major blocks, one per 64-wide K
+//     group: the weights are rewritten into 16 KB blocks once at load
+//     (tc_swizzle_kernel), the activations by the stage kernel (prologue
+//     once per value, stage_rows_kernel);
+//   * a producer thread streams the two blocks of each K group with
+//     cp.async.bulk into a 4-stage shared ring (full/empty mbarriers); an MMA
+//     thread issues 4 tcgen05.mma (K = 16 each) per group and releases the
+//     stage with tcgen05.commit; a last commit signals the epilogue;
+//   * the epilogue reads D with tcgen05.ld (warp w: features 32 (w % 4) ..,
+//     a quarter of the N rows per warp w / 4) and hands (tile, r8, row, lo,
+//     hi) pairs to the same epilogue functors as the mma.sync kernels, every
+//     lane busy (lanes r8 and r8 + 8 swap the halves of even/odd rows).
 // Descriptor encodings follow the sm100 UMMA shared-memory and instruction
 // descriptor layouts (CUTLASS 4, cute/arch/mma_sm100_desc.hpp).
 #pragma once
@@ -24,18 +27,20 @@
 namespace ming {
 
 constexpr int TC_M = 128;  // features per CTA (tensor memory lanes)
-constexpr int TC_THREADS = 128;
+constexpr int TC_THREADS = 512;  // 16 warps: the epilogue work of 128 x N outputs is spread over all of them
+constexpr int TC_STAGES = 4;
+constexpr int TC_A_BLOCK = TC_M * 128;  // bytes of one weight block (128 features x 64 bf16)
 
 template <int N>
 struct TcSmem {
-    static constexpr int A_BYTES = TC_M * 128;  // 128 features x 64 bf16
-    static constexpr int B_BYTES = N * 128;     // N rows x 64 bf16
+    static constexpr int A_BYTES = TC_A_BLOCK;
+    static constexpr int B_BYTES = N * 128;  // N rows x 64 bf16
     static constexpr int STAGE = A_BYTES + B_BYTES;
-    static constexpr int TOTAL = 1024 + 2 * STAGE + 64;  // alignment slack, 2 stages, barriers + tmem slot
+    static constexpr int TOTAL = 1024 + TC_STAGES * STAGE + 128;  // alignment slack, stages, barriers + tmem slot
 };
 
 // Byte offset of 16-byte chunk c (0..7) of row r in a 128-byte-swizzled
-// K-major tile: 8-row atoms of 1024 bytes, chunk index XOR (row % 8).
+// K-major block: 8-row atoms of 1024 bytes, chunk index XOR (row % 8).
 MING_DEV uint32_t tc_sw128(int r, int c) { return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4)); }
 
 // Shared-memory matrix descriptor: start address >> 4 at [0,14), leading
@@ -56,9 +61,10 @@ MING_DEV constexpr uint32_t tc_idesc() {
 
 MING_DEV uint32_t tc_saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// Bounded wait on an mbarrier phase (the waits here end in microseconds).
 MING_DEV bool tc_mbar_wait(uint64_t* bar, uint32_t parity) {
     const uint32_t b = tc_saddr(bar);
-    for (long long it = 0; it < (1ll << 26); it++) {  // bounded: the tensor cores finish in microseconds
+    for (long long it = 0; it < (1ll << 26); it++) {
         uint32_t ok;
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
@@ -70,86 +76,113 @@ MING_DEV bool tc_mbar_wait(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
-// Rows -> row-major bf16 activations: the prologue once per (row, k), with
-// the operand rounding of the mma.sync kernels (pack_bf16x2), and each row's
-// post scale.
-template <class Pro>
-__global__ void __launch_bounds__(LIN_THREADS) stage_rows_kernel(Pro pro, int rows, int K, uint16_t* xs, float* post) {
+// Packed bf16 tiles -> swizzled weight blocks [ntiles / 8][K / 64][16 KB]:
+// block (mt, g) is the shared-memory image of features 128 mt.. and K group g.
+__global__ void __launch_bounds__(TC_THREADS) tc_swizzle_kernel(const uint8_t* tiles, int ng, uint8_t* out) {
+    const int mt = blockIdx.x, g = blockIdx.y;
+    uint8_t* dst = out + ((size_t)mt * ng + g) * TC_A_BLOCK;
+    for (int e = threadIdx.x; e < 8 * 4 * 32; e += TC_THREADS) {
+        const int i = e >> 7, ks = (e >> 5) & 3, L = e & 31;
+        const uint4 w = *reinterpret_cast<const uint4*>(tiles + ((size_t)(mt * 8 + i) * ng + g) * 2048 + ((size_t)ks * 32 + L) * 16);
+        // the lane's mma.sync A fragment: (row g, k), (row g+8, k), (row g, k+8), (row g+8, k+8), k = 16 ks + 2 (L % 4)
+        const int r0 = i * 16 + (L >> 2), k0 = ks * 16 + 2 * (L & 3);
+        const int c0 = k0 >> 3, b0 = (2 * k0) & 15;
+        *reinterpret_cast<uint32_t*>(dst + tc_sw128(r0, c0) + b0) = w.x;
+        *reinterpret_cast<uint32_t*>(dst + tc_sw128(r0 + 8, c0) + b0) = w.y;
+        *reinterpret_cast<uint32_t*>(dst + tc_sw128(r0, c0 + 1) + b0) = w.z;
+        *reinterpret_cast<uint32_t*>(dst + tc_sw128(r0 + 8, c0 + 1) + b0) = w.w;
+    }
+}
+
+// Rows -> swizzled activation blocks [rows / N][K / 64][N * 128 bytes]: the
+// prologue once per (row, k), with the operand rounding of the mma.sync
+// kernels (pack_bf16x2), and each row's post scale. Rows past `rows` in the
+// last block are left as they are (their outputs are never written).
+template <int N, class Pro>
+__global__ void __launch_bounds__(LIN_THREADS) stage_rows_kernel(Pro pro, int rows, int K, uint8_t* xs, float* post) {
     __shared__ float aux[8 * 32];
     const int r0 = blockIdx.x * 8, nrows = min(8, rows - r0);
-    const int kc = blockIdx.y * STAGE_KC, kcl = min(STAGE_KC, K - kc);
+    const int kc = blockIdx.y * STAGE_KC, kcl = min(STAGE_KC, K - kc), ng = K / 64;
     Pro p = pro;
     p.init(r0, nrows, aux);
     __syncthreads();
-    for (int e = threadIdx.x; e < nrows * (kcl / 2); e += LIN_THREADS) {
-        const int row = e / (kcl / 2), k = kc + 2 * (e % (kcl / 2));
-        *reinterpret_cast<uint32_t*>(xs + (size_t)(r0 + row) * K + k) = pack_bf16x2(p.y(row, k), p.y(row, k + 1));
+    // one 16-byte swizzled chunk (8 consecutive k of a row) per item: the 8
+    // prologue values are independent, then one store
+    for (int e = threadIdx.x; e < nrows * (kcl / 8); e += LIN_THREADS) {
+        const int row = e / (kcl / 8), k = kc + 8 * (e % (kcl / 8)), n = r0 + row;
+        float y[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) y[u] = p.y(row, k + u);
+        uint8_t* blk = xs + ((size_t)(n / N) * ng + k / 64) * (N * 128);
+        *reinterpret_cast<uint4*>(blk + tc_sw128(n % N, (k & 63) >> 3)) =
+            make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
     }
     if (blockIdx.y == 0 && threadIdx.x < nrows) post[r0 + threadIdx.x] = p.post(threadIdx.x);
 }
 
 // Grid: x = block of 8 packed tiles (128 features), y = block of N rows.
+// Thread 0 produces, thread 32 issues the MMAs, all 16 warps run the epilogue.
 template <int N, class Epi>
-__global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(PackedW W, const uint16_t* xs, const float* post, Epi epi,
-                                                               int rows) {
+__global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(const uint8_t* wtc, int K, const uint8_t* xs, const float* post,
+                                                               Epi epi, int rows) {
     using S = TcSmem<N>;
     extern __shared__ __align__(16) uint8_t tc_smem_raw[];
     // 1024-byte aligned base: the swizzle atoms are anchored at 1024 bytes
     const uint32_t raw = tc_saddr(tc_smem_raw);
     uint8_t* smem = tc_smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-    uint64_t* mbar = reinterpret_cast<uint64_t*>(smem + 2 * S::STAGE);  // [2]
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 2);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + TC_STAGES * S::STAGE);  // [TC_STAGES]
+    uint64_t* empty = full + TC_STAGES;                                          // [TC_STAGES]
+    uint64_t* done = empty + TC_STAGES;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int mt = blockIdx.x, n0 = blockIdx.y * N, ng = W.K / 64;
+    const int mt = blockIdx.x, nt = blockIdx.y, n0 = nt * N, ng = K / 64;
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(tc_saddr(tmem_slot)), "r"(N)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
     }
     if (tid == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_saddr(&mbar[0])));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_saddr(&mbar[1])));
+        for (int s = 0; s < TC_STAGES; s++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_saddr(&full[s])));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_saddr(&empty[s])));
+        }
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(tc_saddr(done)));
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
     }
     asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     const uint32_t tmem = *tmem_slot;
-    bool ok = true;
-    for (int g = 0; g < ng; g++) {
-        const int st = g & 1;
-        uint8_t* sA = smem + st * S::STAGE;
-        uint8_t* sB = sA + S::A_BYTES;
-        if (g >= 2) ok &= tc_mbar_wait(&mbar[st], ((g - 2) >> 1) & 1);  // the MMAs that read this stage are done
-        // weights: 8 tiles x 4 k-steps x 32 lanes of 16-byte fragment words
-        for (int e = tid; e < 8 * 4 * 32; e += TC_THREADS) {
-            const int i = e >> 7, ks = (e >> 5) & 3, L = e & 31;
-            const uint4 w = ldg_nc16(W.tiles + ((size_t)(mt * 8 + i) * ng + g) * 2048 + ((size_t)ks * 32 + L) * 16);
-            const int r0 = i * 16 + (L >> 2), k0 = ks * 16 + 2 * (L & 3);  // element (r0, k0..k0+1) and friends
-            const int c0 = k0 >> 3, b0 = (2 * k0) & 15;
-            *reinterpret_cast<uint32_t*>(sA + tc_sw128(r0, c0) + b0) = w.x;
-            *reinterpret_cast<uint32_t*>(sA + tc_sw128(r0 + 8, c0) + b0) = w.y;
-            *reinterpret_cast<uint32_t*>(sA + tc_sw128(r0, c0 + 1) + b0) = w.z;
-            *reinterpret_cast<uint32_t*>(sA + tc_sw128(r0 + 8, c0 + 1) + b0) = w.w;
+    // warp 0 lane 0 produces, warp 1 lane 0 issues the MMAs; the other lanes of
+    // those warps park at __syncwarp instead of spinning beside them
+    if (tid == 0) {
+        // producer: the weight block and the activation block of each K group
+        const uint8_t* wa = wtc + (size_t)mt * ng * S::A_BYTES;
+        const uint8_t* xb = xs + (size_t)nt * ng * S::B_BYTES;
+        for (int g = 0; g < ng; g++) {
+            const int s = g % TC_STAGES;
+            if (g >= TC_STAGES && !tc_mbar_wait(&empty[s], ((g / TC_STAGES) - 1) & 1)) break;
+            uint8_t* sA = smem + s * S::STAGE;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(tc_saddr(&full[s])),
+                         "r"((uint32_t)S::STAGE)
+                         : "memory");
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                             tc_saddr(sA)),
+                         "l"(wa + (size_t)g * S::A_BYTES), "r"((uint32_t)S::A_BYTES), "r"(tc_saddr(&full[s]))
+                         : "memory");
+            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                             tc_saddr(sA + S::A_BYTES)),
+                         "l"(xb + (size_t)g * S::B_BYTES), "r"((uint32_t)S::B_BYTES), "r"(tc_saddr(&full[s]))
+                         : "memory");
         }
-        // activations: N rows x 8 chunks of 16 bytes
-        for (int e = tid; e < N * 8; e += TC_THREADS) {
-            const int n = e >> 3, c = e & 7;
-            uint8_t* dst = sB + tc_sw128(n, c);
-            if (n0 + n < rows) {
-                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(tc_saddr(dst)),
-                             "l"(xs + (size_t)(n0 + n) * W.K + g * 64 + c * 8)
-                             : "memory");
-            } else {
-                *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
-            }
-        }
-        asm volatile("cp.async.wait_all;\n" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // generic-proxy writes -> tensor-core reads
-        __syncthreads();
-        if (tid == 0) {
+    } else if (tid == 32) {
+        // MMA issuer
+        int g = 0;
+        for (; g < ng; g++) {
+            const int s = g % TC_STAGES;
+            if (!tc_mbar_wait(&full[s], (g / TC_STAGES) & 1)) break;
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-            const uint32_t a0 = tc_saddr(sA), b0 = tc_saddr(sB);
+            const uint32_t a0 = tc_saddr(smem + s * S::STAGE), b0 = a0 + S::A_BYTES;
 #pragma unroll
             for (int ks = 0; ks < 4; ks++) {
                 const uint64_t da = tc_desc(a0 + 32 * ks), db = tc_desc(b0 + 32 * ks);
@@ -161,28 +194,38 @@ __global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(PackedW W, const 
                     : "memory");
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
-                             tc_saddr(&mbar[st]))
+                             tc_saddr(&empty[s]))
                          : "memory");
         }
+        // every MMA issued (all, unless a wait gave up) completes before this arrives
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(tc_saddr(done))
+                     : "memory");
     }
-    ok &= tc_mbar_wait(&mbar[(ng - 1) & 1], ((ng - 1) >> 1) & 1);  // every MMA of the CTA has completed
+    if (warp < 2) __syncwarp();
+    const bool ok = tc_mbar_wait(done, 0);
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-    // epilogue: warp w reads features 32w + lane; row pairs (r8, r8 + 8) of a tile are lanes 8 apart
-    const int m = warp * 32 + lane;
-    for (int c0 = 0; c0 < N; c0 += 16) {
+    // epilogue: warp w reads features m = 32 (w % 4) + lane (its tensor-memory
+    // lane quarter) for rows [q N / 4, (q + 1) N / 4), q = w / 4. Feature pairs
+    // (r8, r8 + 8) of a tile sit on lanes 8 apart: the lane holding r8 takes
+    // the even rows, its partner the odd ones, each getting the other half by
+    // one shuffle.
+    const int quarter = warp & 3, m = quarter * 32 + lane, hi_lane = lane & 8;
+    const int cbeg = (warp >> 2) * (N / 4), cend = cbeg + N / 4;
+    for (int c0 = cbeg; c0 < cend; c0 += 16) {
         uint32_t v[16];
         asm volatile(
             "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
               "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
-            : "r"(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c0));
+            : "r"(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0));
         asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
 #pragma unroll
-        for (int j = 0; j < 16; j++) {
-            const float lo = __uint_as_float(v[j]);
-            const float hi = __shfl_down_sync(0xffffffffu, lo, 8);
-            const int n = n0 + c0 + j;
-            if ((lane & 15) < 8 && n < rows && ok) {
+        for (int jj = 0; jj < 8; jj++) {
+            const float ev = __uint_as_float(v[2 * jj]), od = __uint_as_float(v[2 * jj + 1]);
+            const float other = __shfl_xor_sync(0xffffffffu, hi_lane ? ev : od, 8);
+            const float lo = hi_lane ? other : ev, hi = hi_lane ? od : other;
+            const int n = n0 + c0 + 2 * jj + (hi_lane ? 1 : 0);
+            if (n < rows && ok) {
                 const float ps = post[n];
                 epi(mt * 8 + (m >> 4), lane & 7, n, lo * ps, hi * ps);
             }
