@@ -331,8 +331,12 @@ MING_DEV void residual_stats(const Sm& sm, const MegaDev& a, const unsigned long
     float ss[MG_MAXB], am[MG_MAXB];
 #pragma unroll
     for (int b = 0; b < MG_MAXB; b++) ss[b] = am[b] = 0.f;
-    for (int idx = tid * 2; idx < B * H; idx += 512) {  // two features per thread per pass
-        const int b = idx / H, f = idx - b * H;
+    // two features per thread per pass, in increasing (row, feature) order;
+    // kept rolled (this code runs once per layer: its size is its cost)
+    int b = 0, f = tid * 2;
+    while (f >= H) f -= H, b++;
+#pragma unroll 1
+    for (int idx = tid * 2; idx < B * H; idx += 512) {
         float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sm.sX + idx));
         if (acc) {
             const uint4 v = ldcg16(acc + (size_t)b * a.acc_w + f);
@@ -341,19 +345,30 @@ MING_DEV void residual_stats(const Sm& sm, const MegaDev& a, const unsigned long
             *reinterpret_cast<uint32_t*>(sm.sX + idx) = pack_bf16x2(x.x, x.y);
         }
         const float2 w = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(nw + f));
+        const float dss = x.x * x.x + x.y * x.y, dam = fmaxf(fabsf(x.x * w.x), fabsf(x.y * w.y));
 #pragma unroll
         for (int bb = 0; bb < MG_MAXB; bb++)
             if (bb == b) {
-                ss[bb] += x.x * x.x + x.y * x.y;
-                am[bb] = fmaxf(am[bb], fmaxf(fabsf(x.x * w.x), fabsf(x.y * w.y)));
+                ss[bb] += dss;
+                am[bb] = fmaxf(am[bb], dam);
             }
+        f += 512;
+        while (f >= H) f -= H, b++;
     }
+#pragma unroll 1
+    for (int bb = 0; bb < B; bb++) {
+        // the row's values out of the register arrays without dynamic indexing
+        float s0 = 0.f, a0 = 0.f;
 #pragma unroll
-    for (int b = 0; b < MG_MAXB; b++) {
-        const float s1 = warp_sum(ss[b]), a1 = warp_max(am[b]);
+        for (int k = 0; k < MG_MAXB; k++)
+            if (k == bb) {
+                s0 = ss[k];
+                a0 = am[k];
+            }
+        const float s1 = warp_sum(s0), a1 = warp_max(a0);
         if (lane == 0) {
-            sm.ms->red[(warp * MG_MAXB + b) * 2] = s1;
-            sm.ms->red[(warp * MG_MAXB + b) * 2 + 1] = a1;
+            sm.ms->red[(warp * MG_MAXB + bb) * 2] = s1;
+            sm.ms->red[(warp * MG_MAXB + bb) * 2 + 1] = a1;
         }
     }
     cbar();
@@ -430,6 +445,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
         const int w0 = max(i0, jj * a.gps), w1 = min(i1, (jj + 1) * a.gps);
         if (w0 < w1 && !*(volatile int*)cx.fail) {
             const uint8_t* sbase = ring + (size_t)sl * a.slot_bytes;
+#pragma unroll 1
             for (int i = w0; i < w1; i += 2) {
                 const bool two = i + 1 < w1;
                 const uint8_t* ch[2];
@@ -499,10 +515,10 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
             if (b >= B) continue;
             float s = 0.f;
 #pragma unroll
-            for (int w = 0; w < MG_CWARPS; w++) {  // fixed warp order
+            for (int w = 0; w < MG_CWARPS; w++) {  // fixed warp order; loads independent of the test
                 const int wt = ms->wtile[p][w];
-                if (wt == t) s += sm.sRed[(w * 2 + 0) * 128 + r * 8 + b];
-                else if (wt >= 0 && wt + 1 == t) s += sm.sRed[(w * 2 + 1) * 128 + r * 8 + b];
+                const float x0 = sm.sRed[(w * 2 + 0) * 128 + r * 8 + b], x1 = sm.sRed[(w * 2 + 1) * 128 + r * 8 + b];
+                s += wt == t ? x0 : ((wt >= 0 && wt + 1 == t) ? x1 : 0.f);
             }
             if (use_post) s *= ms->post[b];
             red_add64(acc + (size_t)b * a.acc_w + t * 16 + r, to_fix(s));
@@ -516,10 +532,11 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
 #pragma unroll
             for (int w = 0; w < MG_CWARPS; w++) {
                 const int wt = ms->wtile[p][w];
-                const int u = wt == t ? 0 : ((wt >= 0 && wt + 1 == t) ? 1 : -1);
-                if (u < 0) continue;
-                gs += sm.sRed[(w * 2 + u) * 128 + r * 8 + b];
-                us += sm.sRed[(w * 2 + u) * 128 + (r + 8) * 8 + b];
+                const float g0 = sm.sRed[(w * 2 + 0) * 128 + r * 8 + b], g1 = sm.sRed[(w * 2 + 1) * 128 + r * 8 + b];
+                const float u0 = sm.sRed[(w * 2 + 0) * 128 + (r + 8) * 8 + b], u1 = sm.sRed[(w * 2 + 1) * 128 + (r + 8) * 8 + b];
+                const bool in0 = wt == t, in1 = wt >= 0 && wt + 1 == t;
+                gs += in0 ? g0 : (in1 ? g1 : 0.f);
+                us += in0 ? u0 : (in1 ? u1 : 0.f);
             }
             const float gv = rb(gs * ms->post[b]), uv = rb(us * ms->post[b]);
             const float sg = rb(1.0f / (1.0f + expf(-gv)));
@@ -639,6 +656,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         const int j0 = warp * len / MG_CWARPS, j1 = (warp + 1) * len / MG_CWARPS;
         float2 ac0 = make_float2(0.f, 0.f), ac1 = make_float2(0.f, 0.f);
         int j = j0;
+#pragma unroll 1
         for (; j + 2 <= j1; j += 2) {
             float2 v0, v1;
             if (p0 + j + 1 < pos) {
@@ -692,15 +710,16 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
         const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
         const uint64_t* o = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART;
         float M = -INFINITY, L = 0.f;
-        for (int s0 = 0; s0 < ns; s0 += 8) {
-            uint64_t vm[8], vl[8];
+#pragma unroll 1
+        for (int s0 = 0; s0 < ns; s0 += 4) {  // 4 chunks' loads in flight; kept rolled (code size)
+            uint64_t vm[4], vl[4];
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
+            for (int k = 0; k < 4; k++) {
                 vm[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART) : 0ull;
                 vl[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART + 1) : 0ull;
             }
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
+            for (int k = 0; k < 4; k++) {
                 if (s0 + k >= ns) continue;
                 const float m = (uint32_t)(vm[k] >> 32) == tag ? __uint_as_float((uint32_t)vm[k])
                                                                 : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
@@ -713,6 +732,7 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
             }
         }
         const float il = 1.0f / L;
+#pragma unroll 1
         for (int s2 = 0; s2 < ns; s2++) wt[(size_t)e * a.max_splits + s2] = expf(wt[(size_t)e * a.max_splits + s2] - M) * il;
     }
     cbar();
@@ -724,12 +744,13 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
         const uint64_t* o = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART + 2 + d;
         const float* w = wt + (size_t)(si * B + b) * a.max_splits;
         float v = 0.f;
-        for (int s0 = 0; s0 < ns; s0 += 8) {
-            uint64_t va[8];
+#pragma unroll 1
+        for (int s0 = 0; s0 < ns; s0 += 4) {
+            uint64_t va[4];
 #pragma unroll
-            for (int k = 0; k < 8; k++) va[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART) : 0ull;
+            for (int k = 0; k < 4; k++) va[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART) : 0ull;
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
+            for (int k = 0; k < 4; k++) {
                 if (s0 + k >= ns) continue;
                 const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k])
                                                                 : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
