@@ -59,11 +59,6 @@ MING_DEV uint32_t ldr32(const void* p) {
     asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
-MING_DEV uint32_t lda32(const unsigned int* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 MING_DEV uint4 ldcg16(const void* p) {  // 16 bytes from L2 (never a stale L1 line)
     uint4 r;
     asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];\n"
@@ -78,14 +73,16 @@ MING_DEV void str64(uint64_t* p, uint64_t v) {
 MING_DEV void red_add64(unsigned long long* p, long long v) {
     asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;\n" ::"l"(p), "l"(v) : "memory");
 }
-MING_DEV void red_release_add32(unsigned int* p, unsigned int v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
-}
 MING_DEV uint64_t tagged(uint32_t tag, float v) { return ((uint64_t)tag << 32) | __float_as_uint(v); }
-// fixed point with MG_FIX fraction bits (|v| < 2^31)
-MING_DEV long long to_fix(float v) { return __float2ll_rn(v * (float)(1ull << MG_FIX)); }
-MING_DEV float from_fix(unsigned long long u) { return __ll2float_rn((long long)u) * (1.0f / (float)(1ull << MG_FIX)); }
-MING_DEV float from_fix2(uint32_t lo, uint32_t hi) { return from_fix(((unsigned long long)hi << 32) | lo); }
+// A counted accumulator word is (contributors << 56) + sum of fixed-point
+// values (|sum| < 2^55): the count is the top byte after rounding.
+MING_DEV int acc_count(unsigned long long v) { return (int)((long long)(v + (1ull << 55)) >> 56); }
+MING_DEV float acc_value(unsigned long long v) {
+    const long long x = (long long)v - ((long long)acc_count(v) << 56);
+    return __ll2float_rn(x) * (1.0f / (float)(1ull << MG_FIX));
+}
+// fixed point with MG_FIX fraction bits (|v| < 2^23), plus one contributor count
+MING_DEV long long to_fix_counted(float v) { return __float2ll_rn(v * (float)(1ull << MG_FIX)) + (1ll << 56); }
 
 // x / B for the step's row count B <= 4 (bm = ceil(2^32 / B)), exact for x < 2^30
 MING_DEV int divB(int x, unsigned long long bm) { return (int)(((unsigned long long)(uint32_t)x * bm) >> 32); }
@@ -123,23 +120,39 @@ __device__ __noinline__ float poll_word(const uint64_t* p, uint32_t tag, int* fa
 }
 MING_DEV float poll(const Ctx& x, const uint64_t* p, uint32_t tag) { return poll_word(p, tag, x.fail, x.a->err); }
 
-// One thread waits until the counter reaches target (acquire); bounded.
-__device__ __noinline__ void wait_counter(const unsigned int* cnt, unsigned int target, int* fail, const int* err) {
+// Re-reads a counted accumulator word until `expect` CTAs have contributed
+// (bounded); returns the word (complete, or whatever it holds on failure).
+__device__ __noinline__ unsigned long long poll_acc(const unsigned long long* p, int expect, int* fail, const int* err) {
     const long long t0 = clock64();
     int it = 0;
-    while ((int)(lda32(cnt) - target) < 0) {
-        if (((++it) & 15) == 0) {
-            if (*(volatile int*)fail) return;
+    while (true) {
+        const unsigned long long v = ldr64(p);
+        if (acc_count(v) == expect) return v;
+        if (((++it) & 31) == 0) {
+            if (*(volatile int*)fail) return v;
             if (ldr32(err)) {
                 atomicCAS(fail, 0, 5);
-                return;
+                return v;
             }
             if (clock64() - t0 > MG_TIMEOUT) {
                 atomicCAS(fail, 0, 1);
-                return;
+                return v;
             }
         }
     }
+}
+MING_DEV float acc_get(const Ctx& x, const unsigned long long* p, unsigned long long v, int expect) {
+    if (acc_count(v) != expect) v = poll_acc(p, expect, x.fail, x.a->err);
+    return acc_value(v);
+}
+// One thread waits for one representative word of a hand-off (so thousands
+// of threads do not poll L2 while the writers work), then the CTA meets.
+MING_DEV void hint_acc(const Ctx& cx, const unsigned long long* p, int expect) {
+    if (threadIdx.x == 0) {
+        const unsigned long long v = ldr64(p);
+        if (acc_count(v) != expect) poll_acc(p, expect, cx.fail, cx.a->err);
+    }
+    cbar();
 }
 
 // ---------------- tensor-core groups on shared-memory chunks ----------------
@@ -245,6 +258,7 @@ struct Misc {              // small per-CTA state in shared memory
     uint32_t epoch;
     int step;
     unsigned long long bm;  // divB multiplier of the step's row count
+    uint8_t tcount[3][MG_MAX_TILES];  // contributors per tile of the split-K phases q 0, 1, 3
 };
 static_assert(sizeof(Misc) <= 4096, "Misc must fit its shared-memory slot");
 
@@ -326,7 +340,8 @@ MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint
 // statistics of the updated rows: sX[b][f] = rb(sX + rb(acc[b][f])), then
 // inv, pre-scale and post-scale of each row for the norm weight nw. With acc
 // null the rows stay as they are (the layer-0 input).
-MING_DEV void residual_stats(const Sm& sm, const MegaDev& a, const unsigned long long* acc, const uint16_t* nw, bool f16) {
+MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, const MegaDev& a, const unsigned long long* acc, const uint8_t* tcount,
+                               const uint16_t* nw, bool f16) {
     const int H = a.H, B = a.B, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     float ss[MG_MAXB], am[MG_MAXB];
 #pragma unroll
@@ -339,9 +354,13 @@ MING_DEV void residual_stats(const Sm& sm, const MegaDev& a, const unsigned long
     for (int idx = tid * 2; idx < B * H; idx += 512) {
         float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sm.sX + idx));
         if (acc) {
-            const uint4 v = ldcg16(acc + (size_t)b * a.acc_w + f);
-            x.x = rb(x.x + rb(from_fix2(v.x, v.y)));
-            x.y = rb(x.y + rb(from_fix2(v.z, v.w)));
+            const unsigned long long* pw = acc + (size_t)b * a.acc_w + f;
+            const uint4 v = ldcg16(pw);
+            const int expect = tcount[f >> 4];  // f, f + 1: same tile
+            const float d0 = acc_get(cx, pw, ((unsigned long long)v.y << 32) | v.x, expect);
+            const float d1 = acc_get(cx, pw + 1, ((unsigned long long)v.w << 32) | v.z, expect);
+            x.x = rb(x.x + rb(d0));
+            x.y = rb(x.y + rb(d1));
             *reinterpret_cast<uint32_t*>(sm.sX + idx) = pack_bf16x2(x.x, x.y);
         }
         const float2 w = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(nw + f));
@@ -387,24 +406,6 @@ MING_DEV void residual_stats(const Sm& sm, const MegaDev& a, const unsigned long
     cbar();
 }
 
-// Publishes a phase's completion. The CTA barrier orders every thread's
-// contributions before thread 0 (release/acquire at CTA scope); thread 0's
-// gpu-scope release increment is cumulative over them, so a reader that
-// acquires the counter sees all of them. No per-thread fence is needed (a
-// sequentially consistent fence from every warp drains the SM's memory pipe).
-MING_DEV void publish(const Sm& sm, unsigned int* cnt) {
-    MG_SUB(5)
-    cbar();
-    if (threadIdx.x == 0) red_release_add32(cnt, 1u);
-    MG_SUB(6)
-}
-
-// One thread waits until every CTA published, then releases the CTA.
-MING_DEV void await(const Ctx& cx, const unsigned int* cnt, unsigned int target) {
-    if (threadIdx.x == 0 && (int)(lda32(cnt) - target) < 0) wait_counter(cnt, target, cx.fail, cx.a->err);
-    cbar();
-}
-
 enum { OUT_ACC = 0, OUT_GLU = 1 };
 
 // One GEMV phase on the CTA's ring chunks. Warps take contiguous runs of the
@@ -414,7 +415,7 @@ enum { OUT_ACC = 0, OUT_GLU = 1 };
 // tile*16 + r) or, for whole gate|up tiles, the SwiGLU outputs into hb.
 template <int FMT>
 MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                         int stage_base, bool use_post, int out, unsigned long long* acc, uint16_t* hb) {
+                         int stage_base, bool use_post, int out, unsigned long long* acc, uint64_t* hb, uint32_t tag) {
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -521,7 +522,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
                 s += wt == t ? x0 : ((wt >= 0 && wt + 1 == t) ? x1 : 0.f);
             }
             if (use_post) s *= ms->post[b];
-            red_add64(acc + (size_t)b * a.acc_w + t * 16 + r, to_fix(s));
+            red_add64(acc + (size_t)b * a.acc_w + t * 16 + r, to_fix_counted(s));
         }
     } else {
         // whole gate|up tiles: rows 0..7 gate, 8..15 up of features 8t..8t+7
@@ -540,7 +541,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
             }
             const float gv = rb(gs * ms->post[b]), uv = rb(us * ms->post[b]);
             const float sg = rb(1.0f / (1.0f + expf(-gv)));
-            hb[(size_t)b * a.FF + t * 8 + r] = f2bf(rb(rb(gv * sg) * uv));
+            str64(hb + (size_t)b * a.FF + t * 8 + r, ((uint64_t)tag << 32) | f2bf(rb(rb(gv * sg) * uv)));
         }
     }
     MG_SUB(4)
@@ -578,16 +579,16 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     cp_commit();
     // 2. q of the head, k, v of the new position: entry (kind, tile, r8) holds
     //    the RoPE pair (d, d+32) = tile rows r8, r8 + 8
-    if (!waited) await(cx, a.cnt + (size_t)l * MG_NCNT + MG_CNT_QKV, ms->epoch * (unsigned)a.C);
     const unsigned long long* qacc = acc_ptr(a, ms->epoch, l, MG_ACC_QKV) + (size_t)b * a.acc_w;
+    if (!waited) hint_acc(cx, qacc + (size_t)(a.ph[0].tiles - 1) * 16 + 15, ms->tcount[0][a.ph[0].tiles - 1]);
     const float* bias = reinterpret_cast<const float*>(sm.lp + 4 * a.H);
     if (tid < 96) {
         const int kind = tid >> 5, tl = (tid >> 3) & 3, r8 = tid & 7;
         const int t = kind == 0 ? h * 4 + tl : (kind == 1 ? a.heads * 4 + g * 4 + tl : a.heads * 4 + a.kvh * 4 + g * 4 + tl);
         const uint64_t vlo = ldr64(qacc + t * 16 + r8), vhi = ldr64(qacc + t * 16 + r8 + 8);
-        const int d = tl * 8 + r8;
-        float x1 = rb(from_fix(vlo) + bias[t * 16 + r8]);
-        float x2 = rb(from_fix(vhi) + bias[t * 16 + r8 + 8]);
+        const int d = tl * 8 + r8, expect = ms->tcount[0][t];
+        float x1 = rb(acc_get(cx, qacc + t * 16 + r8, vlo, expect) + bias[t * 16 + r8]);
+        float x2 = rb(acc_get(cx, qacc + t * 16 + r8 + 8, vhi, expect) + bias[t * 16 + r8 + 8]);
         if (kind < 2) {
             const float cs = ms->rc[b][d], sn = ms->rs[b][d];
             const float p_ = x1 * cs - x2 * sn, q_ = x1 * sn + x2 * cs;
@@ -821,6 +822,10 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
         ms->rc[b][d] = cs;
         ms->rs[b][d] = sn;
     }
+    for (int i = tid; i < 3 * MG_MAX_TILES; i += MG_THREADS) {
+        const int q = i / MG_MAX_TILES, t = i % MG_MAX_TILES, p = q == 0 ? 0 : (q == 1 ? 1 : 3);
+        ms->tcount[q][t] = (uint8_t)(t < a.ph[p].tiles ? a.ph[p].tcount[t] : 0);
+    }
     if (tid < MG_NPH * MG_CWARPS) {
         const int p = tid / MG_CWARPS, w = tid % MG_CWARPS, n = ms->g1[p] - ms->g0[p];
         const int i0 = w * n / MG_CWARPS, i1 = (w + 1) * n / MG_CWARPS;
@@ -891,12 +896,10 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
     long long* tr = a.trace ? a.trace + (size_t)c * a.layers * MG_TRACE : nullptr;
 #define MG_STAMP(k) \
     if (tr && tid == 0) tr[l * MG_TRACE + (k)] = clock64();
-    const unsigned int target = epoch * (unsigned)a.C;
 #pragma unroll 1
     for (int l = 0; l < a.layers && !dead; l++) {
         const uint32_t tag = epoch * 32u + (uint32_t)l;
-        unsigned int* cnt = a.cnt + (size_t)l * MG_NCNT;
-        uint16_t* hb = a.hbuf + (size_t)l * MG_MAXB * a.FF;
+        uint64_t* hb = a.hbuf + (size_t)l * MG_MAXB * a.FF;
         sm.st = tr ? tr + l * MG_TRACE : nullptr;
         MG_STAMP(0)
         if (!mbar_wait(&lp_full[l & 1], (l >> 1) & 1)) atomicCAS(cx.fail, 0, 2);
@@ -938,25 +941,37 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
                 if (check()) break;
                 MG_STAMP(9)
                 combine_heads(cx, sm, nst, base, gpt, tag);
-            } else {
-                const unsigned int* wc = q == 0 ? (l > 0 ? cnt - MG_NCNT + MG_CNT_X2 : nullptr) : cnt + (q == 2 ? MG_CNT_X1 : MG_CNT_H);
-                if (wc) await(cx, wc, target);
+            } else if (rows) {
+                // q 0: x(l) = x1(l-1) + down(l-1); q 2: x1 = x + o_proj
+                const unsigned long long* src =
+                    q == 2 ? acc_ptr(a, epoch, l, MG_ACC_X1) : (l > 0 ? acc_ptr(a, epoch, l - 1, MG_ACC_X2) : nullptr);
+                const int sp = q == 2 ? 1 : 2;  // tile counts: o_proj / down
+                if (src) hint_acc(cx, src + (size_t)(a.ph[sp == 1 ? 1 : 3].tiles - 1) * 16 + 15,
+                                  ms->tcount[sp][a.ph[sp == 1 ? 1 : 3].tiles - 1]);
                 if (check()) break;
-                if (rows) {
-                    const unsigned long long* src =
-                        q == 2 ? acc_ptr(a, epoch, l, MG_ACC_X1) : (l > 0 ? acc_ptr(a, epoch, l - 1, MG_ACC_X2) : nullptr);
-                    residual_stats(sm, a, src, q == 0 ? ln1 : ln2, F16);
-                } else {
-                    for (int e = tid; e < nst * 8 * B; e += 256) {  // h: 8 features (16 bytes) per load
-                        const int qq = divB(e, ms->bm), b = e - qq * B, si = qq >> 3, k8 = qq & 7;
-                        const int kg = si + base < gpt ? si + base : si + base - gpt;
-                        const uint4 v = ldcg16(hb + (size_t)b * a.FF + kg * 64 + k8 * 8);
-                        const uint16_t* hv = reinterpret_cast<const uint16_t*>(&v);
-#pragma unroll
-                        for (int u = 0; u < 8; u++) sm.sT[(si * 64 + k8 * 8 + u) * B + b] = hv[u];
-                    }
-                    cbar();
+                residual_stats(cx, sm, a, src, ms->tcount[sp], q == 0 ? ln1 : ln2, F16);
+            } else {
+                // q 3: the SwiGLU outputs of this CTA's down range (tagged words, 4 per item)
+                if (tid == 0) {
+                    const uint64_t* hp = hb + (size_t)(B - 1) * a.FF + a.FF - 1;
+                    if ((uint32_t)(ldr64(hp) >> 32) != tag) poll(cx, hp, tag);
                 }
+                if (check()) break;
+                for (int e = tid; e < nst * 16 * B; e += 256) {
+                    const int qq = divB(e, ms->bm), b = e - qq * B, si = qq >> 4, k4 = qq & 15;
+                    const int kg = si + base < gpt ? si + base : si + base - gpt;
+                    const uint64_t* src = hb + (size_t)b * a.FF + kg * 64 + k4 * 4;
+                    const uint4 v0 = ldcg16(src), v1 = ldcg16(src + 2);
+                    const uint64_t w[4] = {((uint64_t)v0.y << 32) | v0.x, ((uint64_t)v0.w << 32) | v0.z,
+                                           ((uint64_t)v1.y << 32) | v1.x, ((uint64_t)v1.w << 32) | v1.z};
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        // the low half is a bf16 bit pattern; poll() returns it as the f32 bits
+                        const uint32_t x = (uint32_t)(w[u] >> 32) == tag ? (uint32_t)w[u] : __float_as_uint(poll(cx, src + u, tag));
+                        sm.sT[(si * 64 + k4 * 4 + u) * B + b] = (uint16_t)(x & 0xFFFFu);
+                    }
+                }
+                cbar();
             }
             if (check()) break;
             MG_STAMP(1 + 2 * q)
@@ -964,9 +979,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             stage<F16>(sm, nst, B, H, rows ? 0 : 1, q == 0 ? ln1 : ln2);
             const int which = q == 0 ? MG_ACC_QKV : (q == 1 ? MG_ACC_X1 : MG_ACC_X2);
             gemv_phase<FMT>(cx, sm, q, cons, ring, full, empty, base, rows, q == 2 ? OUT_GLU : OUT_ACC,
-                            q == 2 ? nullptr : acc_ptr(a, epoch, l, which), hb);
+                            q == 2 ? nullptr : acc_ptr(a, epoch, l, which), hb, tag);
             cons += (n + a.gps - 1) / a.gps;
-            publish(sm, cnt + (q == 0 ? MG_CNT_QKV : (q == 1 ? MG_CNT_X1 : (q == 2 ? MG_CNT_H : MG_CNT_X2))));
             if (check()) break;
             MG_STAMP(2 + 2 * q)
         }
@@ -976,9 +990,10 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
 #undef MG_STAMP
     // ---------------- final norm + stop head (CTA b handles row b) ----------------
     if (!dead && c < B) {
-        await(cx, a.cnt + (size_t)(a.layers - 1) * MG_NCNT + MG_CNT_X2, target);
+        const unsigned long long* src = acc_ptr(a, epoch, a.layers - 1, MG_ACC_X2);
+        hint_acc(cx, src + (size_t)(a.ph[3].tiles - 1) * 16 + 15, ms->tcount[2][a.ph[3].tiles - 1]);
         if (!check()) {
-            residual_stats(sm, a, acc_ptr(a, epoch, a.layers - 1, MG_ACC_X2), a.norm, false);
+            residual_stats(cx, sm, a, src, ms->tcount[2], a.norm, false);
             const int b = c, warp = tid >> 5, lane = tid & 31;
             const float inv = ms->inv[b];
             uint16_t* ob = a.out_cell ? *a.out_cell : nullptr;

@@ -18,9 +18,13 @@
 //   * 8 consumer warps run mma.sync on the ring; split-K partial sums are
 //     reduced with red.global.add.u64 on int64 fixed-point accumulators
 //     (integer addition is associative: the result is bit-deterministic);
-//   * each phase completes through one monotonic counter per (layer, phase):
-//     a CTA increments it after its contributions, a consumer polls it from
-//     one thread while the others wait at the CTA barrier;
+//   * every contribution also adds 2^56, so the top byte of an accumulator
+//     counts its contributors: a reader knows a value is complete when that
+//     count equals the tile's number of contributing CTAs (static). No writer
+//     fence and no completion counter; one thread per CTA first waits for a
+//     hint word, then every thread loads its values once and re-polls only
+//     the rare incomplete one. SwiGLU outputs are 64-bit words carrying the
+//     step's tag beside the bf16 value;
 //   * every CTA keeps the residual stream of its rows in shared memory and
 //     applies the reference's epilogue math (bias, bf16 rounding, RoPE,
 //     residual, SwiGLU) where the values are consumed;
@@ -45,10 +49,11 @@ constexpr int MG_FIX = 32;                        // fraction bits of the fixed-
 constexpr int MG_MAX_STAGE = 32;                  // most 64-groups of activations one CTA stages per phase
 constexpr int MG_TRACE = 64;                      // clock64 stamp slots per (CTA, layer) when tracing
 enum { MG_ACC_QKV = 0, MG_ACC_X1 = 1, MG_ACC_X2 = 2, MG_NACC = 3 };
-enum { MG_CNT_QKV = 0, MG_CNT_X1 = 1, MG_CNT_H = 2, MG_CNT_X2 = 3, MG_NCNT = 4 };
+constexpr int MG_MAX_TILES = 128;                 // most tiles of a split-K phase (q|k|v, o_proj, down)
 
 struct MegaPhase {
     const int* cta_g0;  // [C + 1]: CTA c owns flattened groups [cta_g0[c], cta_g0[c+1])
+    const int* tcount;  // [tiles]: CTAs contributing to each tile (split-K phases), or null
     int tiles, gpt;
 };
 
@@ -68,8 +73,7 @@ struct MegaDev {
     const int* row_seq;        // [B]
     unsigned long long* acc;   // [2 parity][layers][MG_NACC][MG_MAXB][acc_w] int64 fixed point
     int acc_w;
-    uint16_t* hbuf;            // [layers][MG_MAXB][FF] bf16 SwiGLU outputs
-    unsigned int* cnt;         // [layers][MG_NCNT] monotonic completion counters
+    uint64_t* hbuf;            // [layers][MG_MAXB][FF] SwiGLU outputs: step tag << 32 | bf16
     uint64_t* attn;            // [B][heads][max_splits][MG_PART] tagged attention partials
     const uint16_t* x_in;      // [B][H] step input
     uint16_t* z;               // [B][H] post-norm hidden

@@ -645,7 +645,7 @@ int decode_graph(ming_ctx* c, int B, cudaGraphExec_t* out) {
 }
 
 // Plans the persistent decode kernel: per-phase group ranges of every CTA,
-// fixed-point accumulators, completion counters, buffers. Leaves it off when the device cannot co-schedule
+// per-tile contributor counts, counted fixed-point accumulators, buffers. Leaves it off when the device cannot co-schedule
 // one CTA per SM (no cooperative launch) or MING_MEGA=0.
 int setup_mega(ming_ctx* c) {
     const ming_cfg& f = c->cfg;
@@ -687,7 +687,21 @@ int setup_mega(ming_ctx* c) {
         int* dg0 = c->mem.alloc<int>(C + 1, &rc);
         if (rc) return rc;
         CK(cudaMemcpy(dg0, g0.data(), (C + 1) * 4, cudaMemcpyHostToDevice));
-        a.ph[p] = MegaPhase{dg0, tiles[p], gpt[p]};
+        a.ph[p] = MegaPhase{dg0, nullptr, tiles[p], gpt[p]};
+        if (p == 2) continue;  // gate|up: whole tiles per CTA
+        // split-K phase: contributors per tile (the count every counted
+        // accumulator word of the tile reaches when complete)
+        if (tiles[p] > MG_MAX_TILES) return MING_OK;
+        std::vector<int> tc(tiles[p], 0);
+        for (int i = 0; i < C; i++)
+            for (int t = 0; t < tiles[p]; t++)
+                if (g0[i] < (t + 1) * gpt[p] && g0[i + 1] > t * gpt[p]) tc[t]++;
+        for (int t = 0; t < tiles[p]; t++)
+            if (tc[t] < 1 || tc[t] > 127) return MING_OK;  // the count lives in one byte of the word
+        int* dtc = c->mem.alloc<int>(tiles[p], &rc);
+        if (rc) return rc;
+        CK(cudaMemcpy(dtc, tc.data(), tiles[p] * 4, cudaMemcpyHostToDevice));
+        a.ph[p].tcount = dtc;
     }
     if (nslots < 4) return MING_OK;  // warps consume a phase slot by slot: any ring works, a deeper one streams ahead
     if (f.max_ctx / PAGE + 1 > 512) return MING_OK;  // block-table rows live in shared memory
@@ -708,18 +722,17 @@ int setup_mega(ming_ctx* c) {
     const int acc_w = (std::max(qkv_rows, H) + 1) / 2 * 2;
     const size_t acc_n = (size_t)2 * f.layers * MG_NACC * MG_MAXB * acc_w;
     unsigned long long* acc = c->mem.alloc<unsigned long long>(acc_n, &rc);
-    uint16_t* hbuf = c->mem.alloc<uint16_t>((size_t)f.layers * MG_MAXB * f.ff, &rc);
-    const size_t cnt_n = (size_t)f.layers * MG_NCNT;
-    unsigned int* cnt = c->mem.alloc<unsigned int>(cnt_n, &rc);
+    const size_t hbuf_n = (size_t)f.layers * MG_MAXB * f.ff;
+    uint64_t* hbuf = c->mem.alloc<uint64_t>(hbuf_n, &rc);
     c->dev_err = c->mem.alloc<int>(1, &rc);
     c->mega_counter = c->mem.alloc<int>(2, &rc);
     if (rc) return rc;
     int* counter = c->mega_counter;
     c->mega_reset = [=]() -> cudaError_t {
-        // a step that gave up leaves accumulators, counters and partials of an
-        // unfinished epoch: restart the epochs from zero on clean state
+        // a step that gave up leaves accumulators and tagged words of an
+        // unfinished epoch: restart the epochs from zero on cleared buffers
         cudaError_t e = cudaMemset(acc, 0, acc_n * 8);
-        if (e == cudaSuccess) e = cudaMemset(cnt, 0, cnt_n * 4);
+        if (e == cudaSuccess) e = cudaMemset(hbuf, 0, hbuf_n * 8);
         if (e == cudaSuccess) e = cudaMemset(attn, 0, attn_n * 8);
         if (e == cudaSuccess) e = cudaMemset(counter, 0, 8);
         return e;
@@ -744,7 +757,6 @@ int setup_mega(ming_ctx* c) {
     a.acc = acc;
     a.acc_w = acc_w;
     a.hbuf = hbuf;
-    a.cnt = cnt;
     a.counter = c->mega_counter;
     a.err = c->dev_err;
     a.out_cell = c->out_cell;
