@@ -289,6 +289,7 @@ def cpu_baseline(cfgid, W, lens, x_last, budget_s=20.0):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     from ming_b200 import synth
+    O.set_threads(len(os.sched_getaffinity(0)))
     c = CONFIGS[cfgid]
     lm = O.Lm(W)
     B = len(lens)
@@ -382,6 +383,8 @@ def run_reference(args, ws, rank, local):
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     from ming_b200 import synth
+    # every host thread this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    O.set_threads(len(os.sched_getaffinity(0)))
     cfgid = args.config
     c = CONFIGS[cfgid]
     if c.get("dit"):
