@@ -90,14 +90,27 @@ MING_DEV void stage_chunk(const Pro& pro, int nrows, int kc, int kcl, uint2* sB,
     }
 }
 
+// 16- and 8-byte weight loads: read-only global path, or shared memory (SM).
+template <bool SM>
+MING_DEV uint4 ldw16(const uint8_t* p) {
+    if constexpr (SM) return *reinterpret_cast<const uint4*>(p);
+    else return ldg_nc16(p);
+}
+template <bool SM>
+MING_DEV uint2 ldw8(const uint8_t* p) {
+    if constexpr (SM) return *reinterpret_cast<const uint2*>(p);
+    else return ldg_nc8(p);
+}
+
 // One 64-group of one tile for NT n-tiles: acc[j][4] += W_group . y_group.
-template <int FMT, int NT>
+// SM: the chunk sits in shared memory.
+template <int FMT, int NT, bool SM = false>
 MING_DEV void group_mma(const uint8_t* chunk, const uint2* sB /*at group's first kstep*/, const float* sYs /*group row sums*/,
                         float (&acc)[NT][4], int lane) {
     if constexpr (FMT == 16) {
 #pragma unroll
         for (int ks = 0; ks < 4; ks++) {
-            const uint4 w = ldg_nc16(chunk + ((size_t)ks * 32 + lane) * 16);
+            const uint4 w = ldw16<SM>(chunk + ((size_t)ks * 32 + lane) * 16);
             const uint32_t a[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int j = 0; j < NT; j++) {
@@ -108,15 +121,15 @@ MING_DEV void group_mma(const uint8_t* chunk, const uint2* sB /*at group's first
     } else {
         uint32_t words[8];
         if constexpr (FMT == 4) {
-            const uint4 w = ldg_nc16(chunk + (size_t)lane * 16);
+            const uint4 w = ldw16<SM>(chunk + (size_t)lane * 16);
             words[0] = w.x; words[1] = w.y; words[2] = w.z; words[3] = w.w;
         } else {
-            const uint4 w0 = ldg_nc16(chunk + (size_t)lane * 16);
-            const uint4 w1 = ldg_nc16(chunk + (size_t)(32 + lane) * 16);
+            const uint4 w0 = ldw16<SM>(chunk + (size_t)lane * 16);
+            const uint4 w1 = ldw16<SM>(chunk + (size_t)(32 + lane) * 16);
             words[0] = w0.x; words[1] = w0.y; words[2] = w0.z; words[3] = w0.w;
             words[4] = w1.x; words[5] = w1.y; words[6] = w1.z; words[7] = w1.w;
         }
-        const uint2 sc = ldg_nc8(chunk + (FMT == 4 ? 512 : 1024) + (lane >> 2) * 8);
+        const uint2 sc = ldw8<SM>(chunk + (FMT == 4 ? 512 : 1024) + (lane >> 2) * 8);
         const float s_lo = __uint_as_float(sc.x << 16), b_lo = __uint_as_float(sc.x & 0xffff0000u);
         const float s_hi = __uint_as_float(sc.y << 16), b_hi = __uint_as_float(sc.y & 0xffff0000u);
         float t[NT][4];
@@ -228,6 +241,7 @@ struct LinScratch {
     float* post = nullptr;  // [rows]
     int rows = 0, K = 0;    // capacity
     int sms = 148;          // SMs of the device (sizes the tiles-per-CTA choice)
+    int* err = nullptr;     // device error word (bounded waits that expire)
 };
 
 constexpr int STAGE_KC = 512;  // K per stage_frag_kernel CTA

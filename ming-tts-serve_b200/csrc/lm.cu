@@ -42,12 +42,22 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnArgs a) {
     float* out = a.part + ((size_t)row * a.nsplit_max + split) * a.heads * PART_STRIDE;
     if (p0 >= n) return;  // split unused for this row (never read by the combine)
     const int* bt = a.kv.bt + (size_t)seq * a.kv.bt_ld;
-    for (int e = tid; e < len * 8; e += 256) {
-        const int j = e >> 3, piece = e & 7, p = p0 + j;
-        const int page = bt[p / PAGE];
-        att_cp16(sK + j * ATT_KS + piece * 8, a.kv.pool + kv_index(a.kv, page, a.layer, 0, kh, p % PAGE) + piece * 8);
-        att_cp16(sV + j * ATT_KS + piece * 8, a.kv.pool + kv_index(a.kv, page, a.layer, 1, kh, p % PAGE) + piece * 8);
-    }
+    auto fetch = [&](int pa, int pb) {
+        for (int e = tid; e < (pb - pa) * 8; e += 256) {
+            const int p = pa + (e >> 3), j = p - p0, piece = e & 7;
+            const int page = bt[p / PAGE];
+            att_cp16(sK + j * ATT_KS + piece * 8, a.kv.pool + kv_index(a.kv, page, a.layer, 0, kh, p % PAGE) + piece * 8);
+            att_cp16(sV + j * ATT_KS + piece * 8, a.kv.pool + kv_index(a.kv, page, a.layer, 1, kh, p % PAGE) + piece * 8);
+        }
+    };
+    // Decode: positions before the row's own were cached by earlier steps and
+    // are fetched before the wait on the q|k|v kernel (launched with
+    // programmatic stream serialization); the rest after it.
+    const int pre = a.decode ? min(p1, pos) : p0;
+    fetch(p0, pre);
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+    fetch(pre, p1);
     asm volatile("cp.async.commit_group;\n" ::: "memory");
     for (int e = tid; e < grp * HD; e += 256) {
         const int i = e / HD, d = e % HD;
@@ -129,8 +139,17 @@ void launch_attn(const AttnArgs& a, int rows, cudaStream_t s) {
         cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM);
         attr_set[dev] = 1;
     }
-    dim3 grid(a.nsplit_max, a.kv_heads, rows);
-    attn_partial_kernel<<<grid, 256, ATT_SMEM, s>>>(a);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.nsplit_max, a.kv_heads, rows);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = ATT_SMEM;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, attn_partial_kernel, a);
 }
 
 // Combines the splits of each (row, head) once into att [rows][heads * 64]
@@ -140,25 +159,32 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* part, Ro
                                                            uint16_t* att) {
     extern __shared__ float sw[];  // [heads][nsplit_max] e^(m_s - M), then [heads] 1/L
     const int row = blockIdx.x, tid = threadIdx.x;
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int ns = (rows.pos[row] + 1 + ATT_SPLIT - 1) / ATT_SPLIT;
     const float* pr = part + (size_t)row * nsplit_max * heads * PART_STRIDE;
     float* il = sw + heads * nsplit_max;
-    for (int h = tid; h < heads; h += 256) {
+    // a warp per head, lanes over the splits (all (m, l) loads of a head at once)
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int h = warp; h < heads; h += 8) {
         float M = -INFINITY;
-        for (int s = 0; s < ns; s++) M = fmaxf(M, pr[((size_t)s * heads + h) * PART_STRIDE]);
+        for (int s = lane; s < ns; s += 32) M = fmaxf(M, pr[((size_t)s * heads + h) * PART_STRIDE]);
+        M = warp_max(M);
         float L = 0.f;
-        for (int s = 0; s < ns; s++) {
+        for (int s = lane; s < ns; s += 32) {
             const float* p = pr + ((size_t)s * heads + h) * PART_STRIDE;
             const float w = expf(p[0] - M);
             sw[h * nsplit_max + s] = w;
             L += p[1] * w;
         }
-        il[h] = 1.0f / L;
+        L = warp_sum(L);
+        if (lane == 0) il[h] = 1.0f / L;
     }
     __syncthreads();
     for (int e = tid; e < heads * HD; e += 256) {
         const int h = e / HD, d = e % HD;
         float o = 0.f;
+#pragma unroll 4
         for (int s = 0; s < ns; s++) o += pr[((size_t)s * heads + h) * PART_STRIDE + 2 + d] * sw[h * nsplit_max + s];
         att[(size_t)row * heads * HD + e] = f2bf(rb(o * il[h]));
     }
@@ -166,8 +192,17 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* part, Ro
 
 void launch_attn_combine(const float* part, RowsDev rows, int nsplit_max, int heads, uint16_t* att, int nrows,
                          cudaStream_t s) {
-    const int smem = (heads * nsplit_max + heads) * 4;
-    attn_combine_kernel<<<nrows, 256, smem, s>>>(part, rows, nsplit_max, heads, att);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nrows);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t)(heads * nsplit_max + heads) * 4;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, attn_combine_kernel, part, rows, nsplit_max, heads, att);
 }
 
 // Final RMSNorm (MLX fast_rms_norm: rb(w * rb(x * inv))) and the stop head:

@@ -138,6 +138,7 @@ struct AttnArgs {
     KvDev kv;
     RowsDev rows;
     int layer, heads, kv_heads, nsplit_max;
+    int decode = 0;  // 1: every row appends only its own position (positions before it are already cached)
 };
 
 // Step state kept on the device so one captured graph replays every decode step.

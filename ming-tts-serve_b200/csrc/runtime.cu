@@ -11,9 +11,11 @@
 #include <mutex>
 #include <memory>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/ming_cuda.h"
+#include "bulk.cuh"
 #include "dit.cuh"
 #include "lm.cuh"
 #include "mega.cuh"
@@ -253,6 +255,14 @@ void launch_tc(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& 
     else launch_tc_n<64>(W, sc, p, e, rows, s);
 }
 
+bool bulk_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("MING_BULK");
+        return !(v && std::string(v) == "0");
+    }();
+    return on;
+}
+
 bool tc_enabled() {
     static const bool on = [] {
         const char* v = getenv("MING_TC");
@@ -268,6 +278,22 @@ void launch_lin_f(const LinScratch& sc, const PackedW& W, const Pro& p, const Ep
         if (staged && rows >= 64 && W.tc && tc_enabled()) {
             launch_tc(W, sc, p, e, rows, s);
             return;
+        }
+    }
+    // decode batches (9..64 rows) of plain or RMS-normed inputs: bulk.cuh
+    if constexpr (std::is_same_v<Pro, ProRms> || std::is_same_v<Pro, ProPlain>) {
+        if (rows > 8 && rows <= 64 && sc.err && bulk_enabled()) {
+            if constexpr (std::is_same_v<Pro, ProRms>) {
+                if (p.K == W.K && p.ld % 8 == 0) {
+                    launch_bulk<FMT, true>(W, BulkIn{p.x, p.nw, p.ld, p.eps, sc.err}, e, rows, sc.sms, s);
+                    return;
+                }
+            } else {
+                if (p.ld % 8 == 0) {
+                    launch_bulk<FMT, false>(W, BulkIn{p.x, nullptr, p.ld, 0.f, sc.err}, e, rows, sc.sms, s);
+                    return;
+                }
+            }
         }
     }
     if (rows <= 8) launch_lin_t<FMT, 1>(W, p, e, rows, s);
@@ -579,7 +605,7 @@ int copy_out(ming_ctx* c, void* dst, const void* src, size_t bytes, int kind) {
 }
 
 // The 24-layer step over `rows` rows whose row_seq/row_pos are on the device.
-void enqueue_layers(ming_ctx* c, int rows) {
+void enqueue_layers(ming_ctx* c, int rows, bool decode) {
     const ming_cfg& f = c->cfg;
     RowsDev rd{c->row_seq, c->row_pos};
     KvDev kv{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
@@ -587,7 +613,7 @@ void enqueue_layers(ming_ctx* c, int rows) {
         auto& L = c->layers[l];
         run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, rows, c->stream);
-        launch_attn(AttnArgs{c->q, c->part, kv, rd, l, f.heads, f.kv_heads, c->nsplit}, rows, c->stream);
+        launch_attn(AttnArgs{c->q, c->part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, decode ? 1 : 0}, rows, c->stream);
         launch_attn_combine(c->part, rd, c->nsplit, f.heads, c->att, rows, c->stream);
         run_linear(c, L.o.w, ProPlain{c->att, f.heads * HD, 0},
                    EpiResidual{c->x, c->x1, nullptr, f.hidden}, rows, c->stream);
@@ -624,7 +650,7 @@ int decode_graph(ming_ctx* c, int B, cudaGraphExec_t* out) {
         le = launch_mega(a, c->mega_smem, c->stream);
     } else {
         launch_step_begin(step_dev(c), B, c->stream);
-        enqueue_layers(c, B);
+        enqueue_layers(c, B, true);
         launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, c->x, step_dev(c), c->cfg.hidden, 0, 1,
                                c->cfg.rms_eps},
                      B, c->stream);
@@ -794,7 +820,8 @@ int check_dev_err(ming_ctx* c) {
         const int zero = 0;
         cudaMemcpy(c->dev_err, &zero, 4, cudaMemcpyHostToDevice);
         if (c->mega_reset) c->mega_reset();
-        return fail(MING_ERR_CUDA, "persistent decode kernel: a bounded device wait expired (code " + std::to_string(e) + ")");
+        return fail(MING_ERR_CUDA, std::string(e == BK_ERR_WEIGHTS ? "decode-batch linear: weight copy" : "persistent decode kernel") +
+                                       ": a bounded device wait expired (code " + std::to_string(e) + ")");
     }
     return MING_OK;
 }
@@ -1140,6 +1167,9 @@ int ming_cuda_finalize(ming_ctx* c) {
         c->lin.rows = rows_cap;
         c->lin.K = k_cap;
         CK(cudaDeviceGetAttribute(&c->lin.sms, cudaDevAttrMultiProcessorCount, c->device));
+        if (!c->dev_err) c->dev_err = c->mem.alloc<int>(1, &rc);
+        if (rc) return rc;
+        c->lin.err = c->dev_err;
     }
     CK(cudaDeviceSynchronize());
     c->staged.clear();
@@ -1212,7 +1242,7 @@ int ming_cuda_lm_prefill(ming_ctx* c, int s, const uint16_t* x, int L, uint16_t*
         CK(cudaMemcpyAsync(c->row_seq, seqv.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
         CK(cudaMemcpyAsync(c->row_pos, posv.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
         if ((rc = copy_in(c, c->x, x + (size_t)c0 * H, (size_t)n * H * 2, kind))) return rc;
-        enqueue_layers(c, n);
+        enqueue_layers(c, n, false);
         if (out || stop) {
             launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, nullptr, step_dev(c), H, 0, 0,
                                    c->cfg.rms_eps},
@@ -1577,7 +1607,7 @@ extern "C" int ming_cuda_lm_decode_noalloc(ming_ctx* c, int B, const int* ids, c
         auto& L = c->layers[l];
         run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, B, s);
-        launch_attn(AttnArgs{c->q, part, kv, rd, l, f.heads, f.kv_heads, c->nsplit}, B, s);
+        launch_attn(AttnArgs{c->q, part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, 1}, B, s);
         run_linear(c, L.o.w, ProAttn{part, rd, c->nsplit, f.heads, 0, nullptr}, EpiResidual{c->x, c->x1, nullptr, f.hidden}, B,
                    s);
         run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr}, EpiSwiGLU{c->h, f.ff}, B, s);

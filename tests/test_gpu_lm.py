@@ -142,6 +142,58 @@ def test_batched_decode_ragged_prompts(q4_24):
         ctx.seq_free(s)
 
 
+@pytest.mark.parametrize("bits,B", [(4, 20), (4, 40), (8, 12), (16, 33)])
+def test_batched_decode_many_rows(cuda_ok, bits, B):
+    """Decode batches of 9..64 rows run on the decode-batch linear (bulk
+    weight copies, K split over thread-block clusters, 32-row blocks): B = 40
+    and 33 take two row blocks. Prompts of 1..30 rows also put the prefill
+    chunks above 8 rows on it. Teacher-forced against the oracle per row,
+    gated like the other multi-layer outputs (the oracle's fused rounding,
+    widened by its fused-vs-graph spread); replaying the same step gives the
+    same bits (the cluster reduction sums in a fixed order)."""
+    layers = 3
+    W = synth.lm_weights(seed=11, bits=bits, layers=layers, qscale=QS)
+    ctx = make_ctx(W, bits, layers, max_ctx=256, max_pages=1024, max_batch=64, max_seqs=64)
+    lm = O.Lm(W)
+    rng = np.random.default_rng(B)
+    lens = rng.integers(1, 31, size=B).tolist()
+    seqs, caches, gcaches, xs = [], [], [], []
+    for i, L in enumerate(lens):
+        s = ctx.seq_alloc()
+        x = synth.normal_bf16(7, f"test.many.{bits}.{B}.{i}", (L, 896))
+        c, cg = lm.new_cache(L + 4), lm.new_cache(L + 4)
+        got, _ = ctx.prefill(s, x)
+        ro, _ = lm.forward(c, x)
+        rg, _ = lm.forward(cg, x, O.MODE_GRAPH)
+        d, cs, ok = within_reference(got, ro, rg)
+        assert ok, f"prefill row {i} (L={L}): maxabs {d:.4g} cos {cs:.6f}"
+        seqs.append(s)
+        caches.append(c)
+        gcaches.append(cg)
+        xs.append(ro[-1])
+    x = np.stack(xs)
+    for t in range(2):
+        go, gs = ctx.decode(seqs, x)
+        ref, refg, rstop = [], [], []
+        for b in range(B):
+            ro, rs = lm.forward(caches[b], x[b:b + 1])
+            rg, _ = lm.forward(gcaches[b], x[b:b + 1], O.MODE_GRAPH)
+            ref.append(ro[0])
+            refg.append(rg[0])
+            rstop.append(rs[0])
+        ref = np.stack(ref)
+        d, cs, ok = within_reference(go, ref, np.stack(refg))
+        assert ok, f"step {t}: maxabs {d:.4g} cos {cs:.6f}"
+        assert np.abs(gs - np.array(rstop)).max() < 1e-2
+        if t == 0:  # the same step again, from the same cache state
+            for q, L in zip(seqs, lens):
+                ctx.seq_truncate(q, L)
+            go2, gs2 = ctx.decode(seqs, x)
+            assert np.array_equal(go, go2) and np.array_equal(gs, gs2)
+        x = ref
+    ctx.close()
+
+
 def test_generate_matches_decode_loop_bitwise(q4_24):
     W, ctx, lm = q4_24
     x = synth.normal_bf16(4, "test.gen", (20, 896))
