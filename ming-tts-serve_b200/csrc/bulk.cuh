@@ -1,55 +1,71 @@
 // bulk.cuh — the linear for decode batches (9..64 activation rows).
 //
 // A batched decode step moves every weight once and little else, but each
-// projection is small (0.45-4.9 MB at 4 bits), so what decides its time is
-// how many bytes are in flight while it starts. Here a CTA owns T tiles and a
-// K range of them; its first thread bulk-copies all of those weights into
-// shared memory (one cp.async.bulk per tile, the tile's K range being
-// contiguous) BEFORE it waits on the previous kernel — the launch carries the
-// programmatic-stream-serialization attribute, so the copies overlap the
-// previous kernel's tail. After `griddepcontrol.wait` the CTA stages its K
-// range of the activation rows (RMSNorm statistics over the whole row when
-// the input is normed) as mma B fragments and lets the next kernel launch.
-// The K ranges of one tile block form a thread-block cluster: partial sums
-// meet over distributed shared memory, summed in rank order (deterministic),
-// and the ranks split the epilogue.
+// projection is small (0.45-4.9 MB at 4 bits): its time is a chain of
+// latencies, so this kernel keeps the chain short.
 //
-// Numerics are those of linear_kernel / linear_frag_kernel (same operand
-// rounding, same per-group scale and bias terms); only the f32 summation
-// order of the K groups differs.
+//  * One CTA per SM (16 warps). A CTA owns a balanced range of tiles and a K
+//    range of them; the K ranges of one tile range form a thread-block
+//    cluster whose partial sums meet over distributed shared memory, summed
+//    in rank order (deterministic), the ranks splitting the epilogue.
+//  * The first thread bulk-copies the CTA's weights (one cp.async.bulk per
+//    tile: a tile's K range is contiguous) BEFORE `griddepcontrol.wait`: the
+//    launch is a programmatic dependent of the previous kernel, so the copies
+//    overlap its tail. After the wait it bulk-copies the K range of each
+//    activation row, raw bf16, into a row-major shared array whose row
+//    stride is 4 words mod 32 — the mma B fragments are read from it without
+//    bank conflicts and without any staging pass.
+//  * The tensor cores run bf16 x bf16 -> f32: 4- and 8-bit codes become exact
+//    bf16 integers in registers, the per-group scale and bias are applied in
+//    f32 (s * sum(q y) + b * sum(y)), and sum(y) of each 64-group and row
+//    comes once per CTA from an mma with an all-ones A operand.
+//  * RMSNorm inputs: each rank sums x^2 over its K range; the epilogue adds
+//    the ranks' sums (rank order) and applies rsqrt(mean + eps) to the f32
+//    dot products, as the reference's fused kernels fold the norm
+//    (src/ming_fused.zig:100-142). With non-unit gains the f32 product
+//    x * g enters the mma as two bf16 parts, hi + lo (~16 significant bits).
 #pragma once
 
+#include <cuda_bf16.h>
+
+#include <algorithm>
 #include <cooperative_groups.h>
 
 #include "linear.cuh"
 
 namespace ming {
 
-constexpr int BK_WARPS = 8;
+constexpr int BK_WARPS = 16;
 constexpr int BK_THREADS = BK_WARPS * 32;
-constexpr int BK_NT = 4;                     // 32 rows per CTA (zero rows are padding)
-constexpr long long BK_TIMEOUT = 2000000000LL;  // cycles (~1 s) before the weight wait gives up
-constexpr int BK_ERR_WEIGHTS = 7;            // device error code: weight copy never completed
+constexpr int BK_ROWS = 32;                     // activation rows per CTA (4 mma n-tiles)
+constexpr int BK_TMAX = 8;                      // tiles per CTA at most
+constexpr int BK_SMEM_MAX = 200 * 1024;
+constexpr long long BK_TIMEOUT = 2000000000LL;  // cycles (~1 s) before a copy wait gives up
+constexpr int BK_ERR_WEIGHTS = 7;               // device error code: a bulk copy never completed
 
 struct BulkIn {
     const uint16_t* x;   // [rows][ld] bf16 activations
-    const uint16_t* nw;  // RMSNorm gains [K] (normed input) or null (plain input)
+    const uint16_t* nw;  // RMSNorm gains [K] when not all 1, else null
     int ld;
     float eps;
     int* err;            // device error word
+    long long* trace = nullptr;  // launch trace: [CTA][4] globaltimer stamps (entry, wait done, rows in, exit) or null
 };
 
-// Shared-memory layout of one CTA (bytes), for T tiles and up to gmax groups.
+// Shared-memory layout of one CTA (bytes): barriers and per-row x^2 sums,
+// per-(group, row) operand sums [gmax][32], weights [tmax][gmax][chunk], staged rows [32][gmax * 64 + 8] bf16 (reused
+// for the warps' partial sums after the mma loop), per-tile sums.
 struct BulkSmem {
-    int w, frag, ysum, red, part, aux, total;
-    __host__ __device__ BulkSmem(int T, int gmax, int cb) {
-        w = 128;
-        frag = w + T * gmax * cb;
-        ysum = frag + gmax * 4 * BK_NT * 32 * 8;
-        red = ysum + gmax * 8 * BK_NT * 4;
-        part = red + BK_WARPS * 16 * 8 * BK_NT * 4;
-        aux = part + T * 16 * 8 * BK_NT * 4;
-        total = aux + 2 * 8 * BK_NT * 4;
+    int ss, ys, w, x, xstride, part, total;
+    __host__ __device__ BulkSmem(int tmax, int gmax, int cb, bool lo) {
+        ss = 16;
+        ys = 256;
+        w = ys + gmax * BK_ROWS * 4;
+        x = w + tmax * gmax * cb;
+        xstride = gmax * 128 + 16;
+        const int xb = (lo ? 2 : 1) * BK_ROWS * xstride, red = BK_WARPS * 16 * BK_ROWS * 4;
+        part = x + (xb > red ? xb : red);
+        total = part + tmax * 16 * BK_ROWS * 4;
     }
 };
 
@@ -70,288 +86,339 @@ MING_DEV bool bk_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
-template <bool F16>
-MING_DEV uint32_t bk_pack(float a, float b) {
-    return F16 ? pack_f16x2(a, b) : pack_bf16x2(a, b);
-}
-template <bool F16>
-MING_DEV float bk_sum2(uint32_t u) {
-    if (F16) {
-        const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&u));
-        return v.x + v.y;
-    }
-    const float2 v = unpack_bf16x2(u);
-    return v.x + v.y;
+MING_DEV void bk_bulk(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                     bk_saddr(dst)),
+                 "l"(src), "r"(bytes), "r"(bk_saddr(bar))
+                 : "memory");
 }
 
-// Grid: x = tile block * ks + rank (cluster (ks, 1, 1)), y = 32-row block.
-template <int FMT, int T, bool RMS, class Epi>
-__global__ void __launch_bounds__(BK_THREADS) linear_bulk_kernel(PackedW W, BulkIn in, Epi epi, int rows, int ks, int gmax) {
-    namespace cg = cooperative_groups;
-    extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int CB = chunk_b(FMT), NT = BK_NT;
-    constexpr bool F16 = FMT != 16;
-    const BulkSmem L(T, gmax, CB);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);
-    uint8_t* wbuf = smem + L.w;
-    uint2* sB = reinterpret_cast<uint2*>(smem + L.frag);
-    float* sYs = reinterpret_cast<float*>(smem + L.ysum);
-    float* sRed = reinterpret_cast<float*>(smem + L.red);
-    float* sPart = reinterpret_cast<float*>(smem + L.part);
-    float* sAux = reinterpret_cast<float*>(smem + L.aux);
+MING_DEV uint32_t bsub2_u(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hsub2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
 
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int rank = blockIdx.x % ks, tile0 = (blockIdx.x / ks) * T;
-    const int ng = W.K / 64;
-    const int g0 = rank * ng / ks, gc = (rank + 1) * ng / ks - g0;
-    const int r0 = blockIdx.y * 8 * NT, nrows = min(8 * NT, rows - r0);
-    const int nt = min(T, W.ntiles - tile0);
+// 4-bit codes of one m16k16 step (the word layout dq4 reads) as exact bf16
+// integers: (nibble | 0x4300) is 128 + nibble.
+MING_DEV void dq4_bf16(uint32_t u, uint32_t (&a)[4]) {
+    const uint32_t MAGIC = 0x43004300u;  // bf16x2(128, 128)
+    a[0] = bsub2_u(lop3<(0xF0 & 0xCC) | 0xAA>(u, 0x000F000Fu, MAGIC), MAGIC);
+    a[1] = bsub2_u(lop3<(0xF0 & 0xCC) | 0xAA>(u >> 4, 0x000F000Fu, MAGIC), MAGIC);
+    a[2] = bsub2_u(lop3<(0xF0 & 0xCC) | 0xAA>(u >> 8, 0x000F000Fu, MAGIC), MAGIC);
+    a[3] = bsub2_u(lop3<(0xF0 & 0xCC) | 0xAA>(u >> 12, 0x000F000Fu, MAGIC), MAGIC);
+}
 
-    // 1. this CTA's weights, before waiting on the previous kernel
-    if (tid == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(bar)) : "memory");
-        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bk_saddr(bar)),
-                     "r"((uint32_t)(nt * gc * CB))
-                     : "memory");
-        for (int t = 0; t < nt; t++)
-            asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
-                             bk_saddr(wbuf + (size_t)t * gmax * CB)),
-                         "l"(W.tiles + ((size_t)(tile0 + t) * ng + g0) * CB), "r"((uint32_t)(gc * CB)), "r"(bk_saddr(bar))
-                         : "memory");
-    }
-    // 2. the activations are the previous kernel's output
-    asm volatile("griddepcontrol.wait;\n" ::: "memory");
-    // 3. RMSNorm statistics over the whole row (ProRms::init's values): warp w
-    //    takes rows w, w + 8, w + 16, w + 24, 16-byte pieces, 16 loads in flight
-    if (RMS) {
-        const int npr = W.K / 8;
-        float s[4] = {0.f, 0.f, 0.f, 0.f}, amax[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int j0 = 0; j0 < npr; j0 += 128) {
-            uint4 v[4][4], w[4];
+// 8-bit codes (the word layout dq8 reads) as exact bf16 integers, through
+// f32: (byte | 0x4B000000) is 2^23 + byte.
+MING_DEV uint32_t b8pair(uint32_t w, uint32_t s0, uint32_t s1) {
+    const float f0 = __uint_as_float(__byte_perm(w, 0x4B000000u, s0)) - 8388608.f;
+    const float f1 = __uint_as_float(__byte_perm(w, 0x4B000000u, s1)) - 8388608.f;
+    return pack_bf16x2(f0, f1);
+}
+MING_DEV void dq8_bf16(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
+    a[0] = b8pair(w0, 0x7440u, 0x7441u);
+    a[1] = b8pair(w0, 0x7442u, 0x7443u);
+    a[2] = b8pair(w1, 0x7440u, 0x7441u);
+    a[3] = b8pair(w1, 0x7442u, 0x7443u);
+}
+
+constexpr uint32_t BK_ONE2 = 0x3F803F80u;  // bf16x2(1, 1)
+
+// One 64-group of one tile over the 32 staged rows: acc[j] += W_group . y
+// for n-tile j (rows 8j..8j+7). xs: the staged rows as 32-bit words, at the
+// group's first column; xw: words per staged row; ys: the group's operand
+// sums per row.
+template <int FMT>
+MING_DEV void bk_group(const uint8_t* chunk, const uint32_t* xs, int xw, bool lo, const float* ys, float (&acc)[4][4],
+                       int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    if constexpr (FMT == 16) {
 #pragma unroll
-            for (int jj = 0; jj < 4; jj++) {
-                const int p = j0 + lane + 32 * jj;
-                w[jj] = p < npr ? *reinterpret_cast<const uint4*>(in.nw + p * 8) : make_uint4(0u, 0u, 0u, 0u);
+        for (int ks = 0; ks < 4; ks++) {
+            const uint4 w = *reinterpret_cast<const uint4*>(chunk + ((size_t)ks * 32 + lane) * 16);
+            const uint32_t a[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const int r = warp + 8 * i;
-                    v[i][jj] = p < npr && r < nrows ? *reinterpret_cast<const uint4*>(in.x + (size_t)(r0 + r) * in.ld + p * 8)
-                                                    : make_uint4(0u, 0u, 0u, 0u);
-                }
+            for (int j = 0; j < 4; j++) {
+                const uint32_t* b = xs + (j * 8 + g) * xw + ks * 8 + t;
+                mma_bf16(acc[j], a, b[0], b[4]);
+                if (lo) mma_bf16(acc[j], a, b[BK_ROWS * xw], b[BK_ROWS * xw + 4]);
             }
+        }
+    } else {
+        uint32_t words[8];
+        if constexpr (FMT == 4) {
+            const uint4 w = *reinterpret_cast<const uint4*>(chunk + (size_t)lane * 16);
+            words[0] = w.x; words[1] = w.y; words[2] = w.z; words[3] = w.w;
+        } else {
+            const uint4 w0 = *reinterpret_cast<const uint4*>(chunk + (size_t)lane * 16);
+            const uint4 w1 = *reinterpret_cast<const uint4*>(chunk + (size_t)(32 + lane) * 16);
+            words[0] = w0.x; words[1] = w0.y; words[2] = w0.z; words[3] = w0.w;
+            words[4] = w1.x; words[5] = w1.y; words[6] = w1.z; words[7] = w1.w;
+        }
+        const uint2 sc = *reinterpret_cast<const uint2*>(chunk + (FMT == 4 ? 512 : 1024) + g * 8);
+        const float s_lo = __uint_as_float(sc.x << 16), b_lo = __uint_as_float(sc.x & 0xffff0000u);
+        const float s_hi = __uint_as_float(sc.y << 16), b_hi = __uint_as_float(sc.y & 0xffff0000u);
+        float tq[4][4];
 #pragma unroll
-            for (int jj = 0; jj < 4; jj++) {
-                const uint32_t ww[4] = {w[jj].x, w[jj].y, w[jj].z, w[jj].w};
+        for (int j = 0; j < 4; j++)
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const uint32_t xx[4] = {v[i][jj].x, v[i][jj].y, v[i][jj].z, v[i][jj].w};
+            for (int i = 0; i < 4; i++) tq[j][i] = 0.f;
 #pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const float2 a = unpack_bf16x2(xx[q]), b = unpack_bf16x2(ww[q]);
-                        s[i] += a.x * a.x + a.y * a.y;
-                        amax[i] = fmaxf(amax[i], fmaxf(fabsf(a.x * b.x), fabsf(a.y * b.y)));
-                    }
-                }
+        for (int ks = 0; ks < 4; ks++) {
+            uint32_t a[4];
+            if constexpr (FMT == 4) dq4_bf16(words[ks], a);
+            else dq8_bf16(words[(ks >> 1) * 4 + (ks & 1) * 2], words[(ks >> 1) * 4 + (ks & 1) * 2 + 1], a);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint32_t* b = xs + (j * 8 + g) * xw + ks * 8 + t;
+                mma_bf16(tq[j], a, b[0], b[4]);
+                if (lo) mma_bf16(tq[j], a, b[BK_ROWS * xw], b[BK_ROWS * xw + 4]);
             }
         }
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float ss = warp_sum(s[i]), am = warp_max(amax[i]);
-            const int r = warp + 8 * i;
-            if (lane == 0 && r < nrows) {
-                int e = 0;
-                if (F16 && am > 4096.f) frexpf(am / 4096.f, &e);  // 2^e >= amax / 4096
-                sAux[2 * r] = ldexpf(1.f, -e);
-                sAux[2 * r + 1] = rsqrtf(ss / (float)W.K + in.eps) * ldexpf(1.f, e);
+        for (int j = 0; j < 4; j++) {
+            const float2 y = *reinterpret_cast<const float2*>(ys + j * 8 + 2 * t);
+            acc[j][0] += s_lo * tq[j][0] + b_lo * y.x;
+            acc[j][1] += s_lo * tq[j][1] + b_lo * y.y;
+            acc[j][2] += s_hi * tq[j][2] + b_hi * y.x;
+            acc[j][3] += s_hi * tq[j][3] + b_hi * y.y;
+        }
+    }
+}
+
+// Grid: x = tile range * ks + rank (cluster (ks, 1, 1)), y = 32-row block.
+template <int FMT, bool RMS, class Epi>
+__global__ void __launch_bounds__(BK_THREADS, 1)
+    linear_bulk_kernel(PackedW W, BulkIn in, Epi epi, int rows, int ks, int nb, int tmax, int gmax) {
+    namespace cg = cooperative_groups;
+    extern __shared__ __align__(128) uint8_t smem[];
+    constexpr int CB = chunk_b(FMT);
+    const bool lo = RMS && in.nw;  // non-unit gains: the normed operand is hi + lo (two bf16 parts)
+    const BulkSmem L(tmax, gmax, CB, lo);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [0] weights, [1] rows
+    float* sSS = reinterpret_cast<float*>(smem + L.ss);  // [32] this rank's x^2 sums (RMS)
+    float* sYs = reinterpret_cast<float*>(smem + L.ys);  // [gmax][32] operand sums (quantized formats)
+    uint8_t* wbuf = smem + L.w;
+    uint16_t* sX = reinterpret_cast<uint16_t*>(smem + L.x);
+    float* sRed = reinterpret_cast<float*>(smem + L.x);  // after the mma loop
+    float* sPart = reinterpret_cast<float*>(smem + L.part);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rank = blockIdx.x % ks, blk = blockIdx.x / ks;
+    const int tile0 = blk * W.ntiles / nb, nt = (blk + 1) * W.ntiles / nb - tile0;
+    const int ng = W.K / 64;
+    const int g0 = rank * ng / ks, gc = (rank + 1) * ng / ks - g0;
+    const int r0 = blockIdx.y * BK_ROWS, nrows = min(BK_ROWS, rows - r0);
+    const int xs_b = L.xstride;
+
+    long long* tr = in.trace && tid == 0 ? in.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
+    if (tr) tr[0] = gtimer();
+    // 1. this CTA's weights, before the wait on the previous kernel
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(&bar[0])) : "memory");
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(&bar[1])) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bk_saddr(&bar[0])),
+                     "r"((uint32_t)(nt * gc * CB))
+                     : "memory");
+        for (int t = 0; t < nt; t++)
+            bk_bulk(wbuf + (size_t)t * gmax * CB, W.tiles + ((size_t)(tile0 + t) * ng + g0) * CB, (uint32_t)(gc * CB),
+                    &bar[0]);
+    }
+    __syncthreads();  // the barriers are initialised before anyone waits on them
+    // 2. the activation rows are the previous kernel's output
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    if (tr) tr[1] = gtimer();
+    if (tid == 0) {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bk_saddr(&bar[1])),
+                     "r"((uint32_t)(nrows * gc * 128))
+                     : "memory");
+        for (int r = 0; r < nrows; r++)
+            bk_bulk(reinterpret_cast<uint8_t*>(sX) + (size_t)r * xs_b, in.x + (size_t)(r0 + r) * in.ld + g0 * 64,
+                    (uint32_t)(gc * 128), &bar[1]);
+    }
+    // rows past the batch (and their low parts) are zero
+    for (int e = nrows * gc * 8 + tid; e < BK_ROWS * gc * 8; e += BK_THREADS) {
+        const int r = e / (gc * 8), c = e - r * gc * 8;
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sX) + (size_t)r * xs_b + c * 16) = make_uint4(0u, 0u, 0u, 0u);
+        if (lo)
+            *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sX) + (size_t)(BK_ROWS + r) * xs_b + c * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+    }
+    bool ok = bk_wait(&bar[1], 0);
+    if (tr) tr[2] = gtimer();
+    // 3. RMSNorm: this rank's x^2 sums (a warp per 2 rows); non-unit gains:
+    //    the f32 product x * g is kept as hi = bf16(x g) in place and
+    //    lo = bf16(x g - hi) in row 32 + r (both go through the mma)
+    if (RMS) {
+        for (int r = warp; r < nrows; r += BK_WARPS) {
+            uint8_t* xr = reinterpret_cast<uint8_t*>(sX) + (size_t)r * xs_b;
+            float s = 0.f;
+            for (int c = lane; c < gc * 8; c += 32) {
+                uint4 v = *reinterpret_cast<const uint4*>(xr + c * 16);
+                uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float2 f = unpack_bf16x2(vv[i]);
+                    s += f.x * f.x + f.y * f.y;
+                }
+                if (lo) {
+                    const uint4 wv = *reinterpret_cast<const uint4*>(in.nw + g0 * 64 + c * 8);
+                    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+                    uint32_t ll[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float2 f = unpack_bf16x2(vv[i]), w = unpack_bf16x2(ww[i]);
+                        const float px = f.x * w.x, py = f.y * w.y;
+                        vv[i] = pack_bf16x2(px, py);
+                        const float2 h = unpack_bf16x2(vv[i]);
+                        ll[i] = pack_bf16x2(px - h.x, py - h.y);
+                    }
+                    *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(vv[0], vv[1], vv[2], vv[3]);
+                    *reinterpret_cast<uint4*>(xr + (size_t)BK_ROWS * xs_b + c * 16) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+                }
+            }
+            s = warp_sum(s);
+            if (lane == 0) sSS[r] = s;
+        }
+    }
+    __syncthreads();
+    // per-(group, row) sums of the operand (the bias term of the quantized
+    // formats): one mma with an all-ones A per k-step, a warp per group
+    if (FMT != 16) {
+        const uint32_t ONES[4] = {BK_ONE2, BK_ONE2, BK_ONE2, BK_ONE2};
+        const uint32_t* xs = reinterpret_cast<const uint32_t*>(sX);
+        const int g = lane >> 2, t = lane & 3, xw = xs_b / 4;
+        for (int gi = warp; gi < gc; gi += BK_WARPS) {
+            float ty[4][4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) ty[j][0] = ty[j][1] = ty[j][2] = ty[j][3] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < 4; ks++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const uint32_t* b = xs + (j * 8 + g) * xw + gi * 32 + ks * 8 + t;
+                    mma_bf16(ty[j], ONES, b[0], b[4]);
+                    if (lo) mma_bf16(ty[j], ONES, b[BK_ROWS * xw], b[BK_ROWS * xw + 4]);
+                }
+            if (g == 0) {
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    *reinterpret_cast<float2*>(sYs + gi * BK_ROWS + j * 8 + 2 * t) = make_float2(ty[j][0], ty[j][1]);
             }
         }
         __syncthreads();
     }
-    // 4. B fragments of K range [64 g0, 64 (g0 + gc)) for 32 rows, 8 pieces of
-    //    8 values per thread in flight. Piece (row, k..k+7) fills the .x (k % 16
-    //    == 0) or .y half of entries lane 4 (row % 8) + t, t = 0..3. A warp
-    //    takes one 64-group of 4 rows (8 pieces per row in 8 consecutive
-    //    lanes: their shuffle sum is the group's operand sum; 128-byte row
-    //    segments from global memory; 4-way bank overlap on the stores).
-    {
-        const int tot = 8 * NT * gc * 8, kc0 = g0 * 64;  // 256 gc: e < tot is uniform over the CTA
-        for (int e0 = tid; e0 < tot; e0 += 8 * BK_THREADS) {
-            uint4 v[8];
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int e = e0 + u * BK_THREADS, b = e >> 5;
-                const int row = (b & 7) * 4 + ((e >> 3) & 3), k = ((b >> 3) * 8 + (e & 7)) * 8;
-                v[u] = e < tot && row < nrows ? *reinterpret_cast<const uint4*>(in.x + (size_t)(r0 + row) * in.ld + kc0 + k)
-                                              : make_uint4(0u, 0u, 0u, 0u);
-            }
-#pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int e = e0 + u * BK_THREADS, b = e >> 5;
-                if (e >= tot) break;
-                const int row = (b & 7) * 4 + ((e >> 3) & 3), k = ((b >> 3) * 8 + (e & 7)) * 8;
-                float y[8];
-                const uint32_t vv[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
-#pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float2 f = unpack_bf16x2(vv[i]);
-                    y[2 * i] = f.x;
-                    y[2 * i + 1] = f.y;
-                }
-                if (RMS && row < nrows) {
-                    const uint4 wv = *reinterpret_cast<const uint4*>(in.nw + kc0 + k);
-                    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-                    const float sc = sAux[2 * row];
-#pragma unroll
-                    for (int i = 0; i < 4; i++) {
-                        const float2 f = unpack_bf16x2(ww[i]);
-                        y[2 * i] = y[2 * i] * f.x * sc;
-                        y[2 * i + 1] = y[2 * i + 1] * f.y * sc;
-                    }
-                }
-                uint32_t* dst = reinterpret_cast<uint32_t*>(sB + ((size_t)(k >> 4) * NT + (row >> 3)) * 32 + 4 * (row & 7)) +
-                                ((k >> 3) & 1);
-                float s = 0.f;
-#pragma unroll
-                for (int t = 0; t < 4; t++) {
-                    const uint32_t pk = bk_pack<F16>(y[2 * t], y[2 * t + 1]);
-                    dst[2 * t] = pk;
-                    s += bk_sum2<F16>(pk);
-                }
-                if (F16) {
-                    s += __shfl_xor_sync(0xffffffffu, s, 1);
-                    s += __shfl_xor_sync(0xffffffffu, s, 2);
-                    s += __shfl_xor_sync(0xffffffffu, s, 4);
-                    if ((lane & 7) == 0) sYs[(k >> 6) * 8 * NT + row] = s;
-                }
-            }
-        }
-    }
-    __syncthreads();
     // the next kernel may launch and start its own weight copies
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-    // 5. weights landed?
-    if (!bk_wait(bar, 0) && tid == 0) atomicCAS(in.err, 0, BK_ERR_WEIGHTS);
-    // 6. warp w: tile w % T, groups w / T, + 8 / T, ...
-    float acc[NT][4];
+    ok = bk_wait(&bar[0], 0) && ok;
+    if (!ok && tid == 0) atomicCAS(in.err, 0, BK_ERR_WEIGHTS);
+    // 4. warp w: tile w / wpt, groups w % wpt, + wpt, ...
+    float acc[4][4];
 #pragma unroll
-    for (int j = 0; j < NT; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    {
-        const int t = warp % T;
-        if (t < nt) {
-#pragma unroll 2
-            for (int gi = warp / T; gi < gc; gi += BK_WARPS / T)
-                group_mma<FMT, NT, true>(wbuf + ((size_t)t * gmax + gi) * CB, sB + (size_t)gi * 4 * NT * 32,
-                                         sYs + gi * 8 * NT, acc, lane);
-        }
+    for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    const int wpt = BK_WARPS / nt, t = warp / wpt;
+    if (t < nt) {
+        const uint32_t* xs = reinterpret_cast<const uint32_t*>(sX);
+#pragma unroll 1
+        for (int gi = warp - t * wpt; gi < gc; gi += wpt)
+            bk_group<FMT>(wbuf + ((size_t)t * gmax + gi) * CB, xs + gi * 32, xs_b / 4, lo, sYs + gi * BK_ROWS, acc, lane);
     }
+    __syncthreads();  // the staged rows are dead: their space takes the partial sums
     {
         const int g = lane >> 2, c = 2 * (lane & 3);
-        float* r = sRed + warp * 16 * 8 * NT;
+        float* r = sRed + warp * 16 * BK_ROWS;
 #pragma unroll
-        for (int j = 0; j < NT; j++) {
-            r[g * 8 * NT + j * 8 + c] = acc[j][0];
-            r[g * 8 * NT + j * 8 + c + 1] = acc[j][1];
-            r[(g + 8) * 8 * NT + j * 8 + c] = acc[j][2];
-            r[(g + 8) * 8 * NT + j * 8 + c + 1] = acc[j][3];
+        for (int j = 0; j < 4; j++) {
+            r[g * BK_ROWS + j * 8 + c] = acc[j][0];
+            r[g * BK_ROWS + j * 8 + c + 1] = acc[j][1];
+            r[(g + 8) * BK_ROWS + j * 8 + c] = acc[j][2];
+            r[(g + 8) * BK_ROWS + j * 8 + c + 1] = acc[j][3];
         }
     }
     __syncthreads();
     // per tile: the sum of its warps, in warp order
-    for (int e = tid; e < T * 16 * 8 * NT; e += BK_THREADS) {
-        const int t = e / (16 * 8 * NT), rc = e - t * 16 * 8 * NT;
+    for (int e = tid; e < nt * 16 * BK_ROWS; e += BK_THREADS) {
+        const int tt = e / (16 * BK_ROWS), rc = e - tt * 16 * BK_ROWS;
         float s = 0.f;
-        for (int w = t; w < BK_WARPS; w += T) s += sRed[w * 16 * 8 * NT + rc];
+        for (int w = tt * wpt; w < (tt + 1) * wpt; w++) s += sRed[w * 16 * BK_ROWS + rc];
         sPart[e] = s;
     }
-    // 7. the ks ranks' partials, summed in rank order; rank r takes every
-    //    ks-th (tile, row pair, activation row)
+    // 5. the ks ranks' partials (and x^2 sums), summed in rank order; rank r
+    //    takes every ks-th (tile, row pair, activation row)
     cg::cluster_group cl = cg::this_cluster();
     if (ks > 1) cl.sync();
     else __syncthreads();
-    for (int e = rank * BK_THREADS + tid; e < T * 8 * 8 * NT; e += ks * BK_THREADS) {
-        const int t = e / (64 * NT), rem = e - t * 64 * NT, r8 = rem / (8 * NT), col = rem - r8 * 8 * NT;
-        if (t >= nt || col >= nrows) continue;
-        float lo = 0.f, hi = 0.f;
+    for (int e = rank * BK_THREADS + tid; e < nt * 8 * BK_ROWS; e += ks * BK_THREADS) {
+        const int tt = e / (8 * BK_ROWS), rem = e - tt * 8 * BK_ROWS, r8 = rem / BK_ROWS, col = rem - r8 * BK_ROWS;
+        if (col >= nrows) continue;
+        float lo = 0.f, hi = 0.f, ss = 0.f;
         for (int q = 0; q < ks; q++) {
             const float* pq = ks > 1 ? cl.map_shared_rank(sPart, q) : sPart;
-            lo += pq[(t * 16 + r8) * 8 * NT + col];
-            hi += pq[(t * 16 + r8 + 8) * 8 * NT + col];
+            lo += pq[(tt * 16 + r8) * BK_ROWS + col];
+            hi += pq[(tt * 16 + r8 + 8) * BK_ROWS + col];
+            if (RMS) ss += (ks > 1 ? cl.map_shared_rank(sSS, q) : sSS)[col];
         }
-        const float ps = RMS ? sAux[2 * col + 1] : 1.f;
-        epi(tile0 + t, r8, r0 + col, lo * ps, hi * ps);
+        const float ps = RMS ? rsqrtf(ss / (float)W.K + in.eps) : 1.f;
+        epi(tile0 + tt, r8, r0 + col, lo * ps, hi * ps);
     }
     // peers may still be reading this CTA's partials
     if (ks > 1) cl.sync();
+    if (tr) tr[3] = gtimer();
 }
 
 // ---------------- host side ----------------
 
 struct BulkPlan {
-    int T = 1, ks = 1, gmax = 0, smem = 0;
+    int ks = 1, nb = 1, tmax = 1, gmax = 1, smem = 0;
 };
 
-constexpr int BK_SMEM_MAX = 200 * 1024;
-
-// Picks T (4 or 1 tiles per CTA) and the K split (1..8 ranks): the fewest
-// waves of resident CTAs, then at least one CTA per SM, then the fewest
-// ranks, then the larger T. Residency from shared memory and the kernels'
-// register counts (regs[0]: T = 4, regs[1]: T = 1).
-inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, const int (&regs)[2]) {
+// One CTA per SM: for each K split (1..8 ranks, a cluster) the tile ranges
+// that fill the SMs, kept if a CTA holds at most 8 tiles and fits in shared
+// memory; the cheapest by a latency model (per-warp mma groups, cluster
+// rounds).
+inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, bool lo) {
     const int ng = K / 64, cb = fmt == 4 ? 576 : (fmt == 8 ? 1088 : 2048);
-    const long rb = (rows + 8 * BK_NT - 1) / (8 * BK_NT);
+    const int rb = (rows + BK_ROWS - 1) / BK_ROWS;
     BulkPlan best;
-    long bw = 0, bs = 0, bk = 0;
-    bool have = false;
-    for (int i = 0; i < 2; i++) {
-        const int T = i == 0 ? 4 : 1;
-        const int rg = (std::max(regs[i], 32) + 7) / 8 * 8;
-        for (int ks = 1; ks <= 8 && ks <= ng; ks++) {
-            BulkPlan p;
-            p.T = T;
-            p.ks = ks;
-            p.gmax = (ng + ks - 1) / ks;
-            p.smem = BulkSmem(T, p.gmax, cb).total;
-            if (p.smem > BK_SMEM_MAX) continue;
-            const long occ = std::max(1L, std::min({8L, 65536L / (rg * BK_THREADS), (long)(228 * 1024) / (p.smem + 1024)}));
-            const long ctas = (long)((ntiles + T - 1) / T) * ks * rb;
-            const long waves = (ctas + sms * occ - 1) / (sms * occ);
-            const long shortfall = ctas < sms ? 1 : 0;
-            if (!have || waves < bw || (waves == bw && (shortfall < bs || (shortfall == bs && ks < bk)))) {
-                best = p;
-                bw = waves;
-                bs = shortfall;
-                bk = ks;
-                have = true;
-            }
+    long best_cost = -1;
+    for (int ks = 1; ks <= 8 && ks <= ng; ks++) {
+        const int nb = std::min(ntiles, sms / (ks * rb));
+        if (nb < 1) break;
+        BulkPlan p;
+        p.ks = ks;
+        p.nb = nb;
+        p.tmax = (ntiles + nb - 1) / nb;
+        p.gmax = (ng + ks - 1) / ks;
+        if (p.tmax > BK_TMAX) continue;
+        p.smem = BulkSmem(p.tmax, p.gmax, cb, lo).total;
+        if (p.smem > BK_SMEM_MAX) continue;
+        const int wpt = BK_WARPS / p.tmax;
+        const long groups_per_warp = (p.gmax + wpt - 1) / wpt;
+        const long cost = 3000 + 400L * groups_per_warp + 40L * p.gmax + 600L * (ks - 1);
+        if (best_cost < 0 || cost < best_cost) {
+            best = p;
+            best_cost = cost;
         }
     }
     return best;
 }
 
-template <int FMT, int T, bool RMS, class Epi>
-int bulk_regs() {
-    static int r = 0;
-    if (!r) {
-        cudaFuncAttributes fa{};
-        if (cudaFuncGetAttributes(&fa, linear_bulk_kernel<FMT, T, RMS, Epi>) == cudaSuccess) r = fa.numRegs;
-        else r = 128;
-    }
-    return r;
-}
-
-template <int FMT, int T, bool RMS, class Epi>
-cudaError_t launch_bulk_t(const PackedW& W, const BulkIn& in, const Epi& e, int rows, const BulkPlan& p, cudaStream_t s) {
+// Launches the kernel; false when no plan fits (the caller takes another path).
+template <int FMT, bool RMS, class Epi>
+bool launch_bulk(const PackedW& W, const BulkIn& in, const Epi& e, int rows, int sms, cudaStream_t s) {
     static unsigned attr_devices = 0;  // bit d: attribute set on device d
-    auto kern = linear_bulk_kernel<FMT, T, RMS, Epi>;
+    auto kern = linear_bulk_kernel<FMT, RMS, Epi>;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_devices & (1u << (dev & 31)))) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BK_SMEM_MAX);
         attr_devices |= 1u << (dev & 31);
     }
+    const BulkPlan p = bulk_plan(W.ntiles, W.K, rows, FMT, sms, RMS && in.nw);
+    if (p.smem == 0) return false;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)(((W.ntiles + T - 1) / T) * p.ks), (unsigned)((rows + 8 * BK_NT - 1) / (8 * BK_NT)));
+    cfg.gridDim = dim3((unsigned)(p.nb * p.ks), (unsigned)((rows + BK_ROWS - 1) / BK_ROWS));
     cfg.blockDim = dim3(BK_THREADS);
     cfg.dynamicSmemBytes = (size_t)p.smem;
     cfg.stream = s;
@@ -364,15 +431,8 @@ cudaError_t launch_bulk_t(const PackedW& W, const BulkIn& in, const Epi& e, int 
     at[1].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = p.ks > 1 ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, kern, W, in, e, rows, p.ks, p.gmax);
-}
-
-template <int FMT, bool RMS, class Epi>
-cudaError_t launch_bulk(const PackedW& W, const BulkIn& in, const Epi& e, int rows, int sms, cudaStream_t s) {
-    const int regs[2] = {bulk_regs<FMT, 4, RMS, Epi>(), bulk_regs<FMT, 1, RMS, Epi>()};
-    const BulkPlan p = bulk_plan(W.ntiles, W.K, rows, FMT, sms, regs);
-    if (p.T == 4) return launch_bulk_t<FMT, 4, RMS>(W, in, e, rows, p, s);
-    return launch_bulk_t<FMT, 1, RMS>(W, in, e, rows, p, s);
+    cudaLaunchKernelEx(&cfg, kern, W, in, e, rows, p.ks, p.nb, p.tmax, p.gmax);  // errors surface at the caller's check
+    return true;
 }
 
 }  // namespace ming

@@ -106,6 +106,13 @@ MING_DEV uint2 ldg_nc8(const void* p) {
     return r;
 }
 
+// Global nanosecond timer (comparable across SMs; launch-trace stamps).
+MING_DEV long long gtimer() {
+    long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;\n" : "=l"(t));
+    return t;
+}
+
 MING_DEV float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

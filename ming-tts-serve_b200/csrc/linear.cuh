@@ -242,6 +242,7 @@ struct LinScratch {
     int rows = 0, K = 0;    // capacity
     int sms = 148;          // SMs of the device (sizes the tiles-per-CTA choice)
     int* err = nullptr;     // device error word (bounded waits that expire)
+    long long* trace = nullptr;  // launch-trace slot of this call (diagnostics) or null
 };
 
 constexpr int STAGE_KC = 512;  // K per stage_frag_kernel CTA
@@ -415,6 +416,7 @@ struct ProRms {
     float eps;
     int r0;
     float* st;  // [row][2]: operand scale (power of two), post scale
+    bool unit = false;  // every gain is 1 (lets the decode-batch linear skip the multiply)
     MING_DEV void init(int r0_, int nrows, float* aux) {
         r0 = r0_;
         st = aux;

@@ -2,6 +2,8 @@
 // bookkeeping kernels.
 #include <cuda_runtime.h>
 
+#include <cooperative_groups.h>
+
 #include "lm.cuh"
 
 namespace ming {
@@ -14,6 +16,7 @@ namespace {
 constexpr int ATT_MAXG = 8;     // query heads per kv head (<= 8)
 constexpr int ATT_KS = HD + 8;  // padded K/V row in shared memory (elements): 8 rows hit distinct bank groups
 constexpr int ATT_SMEM = 2 * ATT_SPLIT * ATT_KS * 2 + ATT_MAXG * HD * 4 + ATT_MAXG * ATT_SPLIT * 4;
+constexpr int ATT_SMEM_CL = ATT_SMEM + ATT_MAXG * PART_STRIDE * 4;
 
 MING_DEV uint32_t att_su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 MING_DEV void att_cp16(void* dst, const void* src) {
@@ -26,21 +29,30 @@ MING_DEV void att_cp16(void* dst, const void* src) {
 // split are prefetched with cp.async (one round trip), then scores (a thread
 // per position keeps its key row in registers), a per-head softmax inside
 // the split, and P.V (a thread per (head, dim pair), 4 independent sums).
-// Output: (max, sum, unnormalised P.V) per head, combined by
-// attn_combine_kernel.
+// CL = false: (max, sum, unnormalised P.V) per head go to `part`, combined by
+// attn_combine_kernel. CL = true: the splits of one (kv head, row) are one
+// thread-block cluster; each keeps its partials in shared memory and, after
+// a cluster barrier, rank r combines heads r, r + ns, ... over distributed
+// shared memory (the combine kernel's formula and split order) into `att`.
+template <bool CL>
 __global__ void __launch_bounds__(256) attn_partial_kernel(AttnArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint16_t* sK = reinterpret_cast<uint16_t*>(smem);              // [ATT_SPLIT][ATT_KS]
     uint16_t* sV = sK + ATT_SPLIT * ATT_KS;                         // [ATT_SPLIT][ATT_KS]
     float* sq = reinterpret_cast<float*>(sV + ATT_SPLIT * ATT_KS);  // [ATT_MAXG][HD]
     float* sc = sq + ATT_MAXG * HD;                                 // [ATT_MAXG][ATT_SPLIT]
+    float* sO = sc + ATT_MAXG * ATT_SPLIT;                          // CL: [ATT_MAXG][PART_STRIDE]
     const int split = blockIdx.x, kh = blockIdx.y, row = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int grp = a.heads / a.kv_heads;
     const int pos = a.rows.pos[row], seq = a.rows.seq[row];
     const int n = pos + 1, p0 = split * ATT_SPLIT, p1 = min(n, p0 + ATT_SPLIT), len = p1 - p0;
-    float* out = a.part + ((size_t)row * a.nsplit_max + split) * a.heads * PART_STRIDE;
-    if (p0 >= n) return;  // split unused for this row (never read by the combine)
+    const bool live = p0 < n;  // CTA-uniform
+    long long* tr =
+        a.trace && tid == 0 ? a.trace + (((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 4 : nullptr;
+    if (tr) tr[0] = gtimer();
+    float* out = CL ? sO : a.part + ((size_t)row * a.nsplit_max + split) * a.heads * PART_STRIDE + (size_t)kh * grp * PART_STRIDE;
+    if (!CL && !live) return;  // split unused for this row (never read by the combine)
     const int* bt = a.kv.bt + (size_t)seq * a.kv.bt_ld;
     auto fetch = [&](int pa, int pb) {
         for (int e = tid; e < (pb - pa) * 8; e += 256) {
@@ -53,104 +65,141 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnArgs a) {
     // Decode: positions before the row's own were cached by earlier steps and
     // are fetched before the wait on the q|k|v kernel (launched with
     // programmatic stream serialization); the rest after it.
-    const int pre = a.decode ? min(p1, pos) : p0;
-    fetch(p0, pre);
+    const int pre = live ? (a.decode ? min(p1, pos) : p0) : p0;
+    if (live) fetch(p0, pre);
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
-    fetch(pre, p1);
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-    for (int e = tid; e < grp * HD; e += 256) {
-        const int i = e / HD, d = e % HD;
-        sq[i * HD + d] = 0.125f * bf2f(a.q[(size_t)row * a.heads * HD + (kh * grp + i) * HD + d]);
-    }
-    asm volatile("cp.async.wait_all;\n" ::: "memory");
-    __syncthreads();
-    if (tid < len) {
-        uint32_t kr[HD / 2];
-        const uint4* src = reinterpret_cast<const uint4*>(sK + tid * ATT_KS);
-#pragma unroll
-        for (int q = 0; q < HD / 8; q++) {
-            const uint4 v = src[q];
-            kr[4 * q] = v.x;
-            kr[4 * q + 1] = v.y;
-            kr[4 * q + 2] = v.z;
-            kr[4 * q + 3] = v.w;
+    if (tr) tr[1] = gtimer();
+    if (live) {
+        fetch(pre, p1);
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        for (int e = tid; e < grp * HD; e += 256) {
+            const int i = e / HD, d = e % HD;
+            sq[i * HD + d] = 0.125f * bf2f(a.q[(size_t)row * a.heads * HD + (kh * grp + i) * HD + d]);
         }
-        for (int i = 0; i < grp; i++) {
-            float s0 = 0.f, s1 = 0.f;
+        asm volatile("cp.async.wait_all;\n" ::: "memory");
+        __syncthreads();
+        if (tr) tr[2] = gtimer();
+        if (tid < len) {
+            uint32_t kr[HD / 2];
+            const uint4* src = reinterpret_cast<const uint4*>(sK + tid * ATT_KS);
 #pragma unroll
-            for (int q = 0; q < HD / 2; q += 2) {
-                const float2 k0 = unpack_bf16x2(kr[q]), k1 = unpack_bf16x2(kr[q + 1]);
-                const float4 qv = *reinterpret_cast<const float4*>(sq + i * HD + 2 * q);
-                s0 += qv.x * k0.x + qv.y * k0.y;
-                s1 += qv.z * k1.x + qv.w * k1.y;
+            for (int q = 0; q < HD / 8; q++) {
+                const uint4 v = src[q];
+                kr[4 * q] = v.x;
+                kr[4 * q + 1] = v.y;
+                kr[4 * q + 2] = v.z;
+                kr[4 * q + 3] = v.w;
             }
-            sc[i * ATT_SPLIT + tid] = s0 + s1;
-        }
-    }
-    __syncthreads();
-    if (warp < grp) {
-        float m = -INFINITY;
-        for (int j = lane; j < len; j += 32) m = fmaxf(m, sc[warp * ATT_SPLIT + j]);
-        m = warp_max(m);
-        float l = 0.f;
-        for (int j = lane; j < len; j += 32) {
-            const float p = expf(sc[warp * ATT_SPLIT + j] - m);
-            sc[warp * ATT_SPLIT + j] = p;
-            l += p;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            float* o = out + (size_t)(kh * grp + warp) * PART_STRIDE;
-            o[0] = m;
-            o[1] = l;
-        }
-    }
-    __syncthreads();
-    if (tid < grp * (HD / 2)) {
-        const int i = tid >> 5, dp = tid & 31;  // a warp per head
-        const float* pw = sc + i * ATT_SPLIT;
-        float2 ac[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
-        int j = 0;
-        for (; j + 4 <= len; j += 4) {
+            for (int i = 0; i < grp; i++) {
+                float s0 = 0.f, s1 = 0.f;
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (j + u) * ATT_KS + 2 * dp));
-                ac[u].x += pw[j + u] * v.x;
-                ac[u].y += pw[j + u] * v.y;
+                for (int q = 0; q < HD / 2; q += 2) {
+                    const float2 k0 = unpack_bf16x2(kr[q]), k1 = unpack_bf16x2(kr[q + 1]);
+                    const float4 qv = *reinterpret_cast<const float4*>(sq + i * HD + 2 * q);
+                    s0 += qv.x * k0.x + qv.y * k0.y;
+                    s1 += qv.z * k1.x + qv.w * k1.y;
+                }
+                sc[i * ATT_SPLIT + tid] = s0 + s1;
             }
         }
-        for (; j < len; j++) {
-            const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * ATT_KS + 2 * dp));
-            ac[0].x += pw[j] * v.x;
-            ac[0].y += pw[j] * v.y;
+        __syncthreads();
+        if (warp < grp) {
+            float m = -INFINITY;
+            for (int j = lane; j < len; j += 32) m = fmaxf(m, sc[warp * ATT_SPLIT + j]);
+            m = warp_max(m);
+            float l = 0.f;
+            for (int j = lane; j < len; j += 32) {
+                const float p = expf(sc[warp * ATT_SPLIT + j] - m);
+                sc[warp * ATT_SPLIT + j] = p;
+                l += p;
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                float* o = out + (size_t)warp * PART_STRIDE;
+                o[0] = m;
+                o[1] = l;
+            }
         }
-        float* o = out + (size_t)(kh * grp + i) * PART_STRIDE;
-        o[2 + 2 * dp] = (ac[0].x + ac[1].x) + (ac[2].x + ac[3].x);
-        o[3 + 2 * dp] = (ac[0].y + ac[1].y) + (ac[2].y + ac[3].y);
+        __syncthreads();
+        if (tid < grp * (HD / 2)) {
+            const int i = tid >> 5, dp = tid & 31;  // a warp per head
+            const float* pw = sc + i * ATT_SPLIT;
+            float2 ac[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
+            int j = 0;
+            for (; j + 4 <= len; j += 4) {
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (j + u) * ATT_KS + 2 * dp));
+                    ac[u].x += pw[j + u] * v.x;
+                    ac[u].y += pw[j + u] * v.y;
+                }
+            }
+            for (; j < len; j++) {
+                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * ATT_KS + 2 * dp));
+                ac[0].x += pw[j] * v.x;
+                ac[0].y += pw[j] * v.y;
+            }
+            float* o = out + (size_t)i * PART_STRIDE;
+            o[2 + 2 * dp] = (ac[0].x + ac[1].x) + (ac[2].x + ac[3].x);
+            o[3 + 2 * dp] = (ac[0].y + ac[1].y) + (ac[2].y + ac[3].y);
+        }
+    } else if (CL) {
+        // an unused split contributes weight e^(-inf) = 0
+        for (int e = tid; e < grp * PART_STRIDE; e += 256) sO[e] = e % PART_STRIDE == 0 ? -INFINITY : 0.f;
     }
+    if constexpr (CL) {
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();
+        const int ns = (int)gridDim.x;
+        for (int e = tid; e < ((grp - split + ns - 1) / ns) * HD; e += 256) {
+            const int i = split + (e / HD) * ns, d = e % HD;
+            float M = -INFINITY;
+            for (int q = 0; q < ns; q++) M = fmaxf(M, cl.map_shared_rank(sO, q)[i * PART_STRIDE]);
+            float L = 0.f, o = 0.f;
+            for (int q = 0; q < ns; q++) {
+                const float* pq = cl.map_shared_rank(sO, q) + i * PART_STRIDE;
+                const float w = expf(pq[0] - M);
+                L += pq[1] * w;
+                o += pq[2 + d] * w;
+            }
+            a.att[(size_t)row * a.heads * HD + (kh * grp + i) * HD + d] = f2bf(rb(o * (1.0f / L)));
+        }
+        cl.sync();  // peers may still be reading this CTA's partials
+    }
+    if (tr) tr[3] = gtimer();
 }
 
 void launch_attn(const AttnArgs& a, int rows, cudaStream_t s) {
-    static int attr_set[64] = {};  // per device: the dynamic shared memory opt-in
+    static int attr_set[64] = {};  // per device: the dynamic shared memory opt-ins
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-        cudaFuncSetAttribute(attn_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM);
+        cudaFuncSetAttribute(attn_partial_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM);
+        cudaFuncSetAttribute(attn_partial_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM_CL);
         attr_set[dev] = 1;
     }
+    const bool cl = a.att && a.nsplit_max <= 8;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit_max, a.kv_heads, rows);
     cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = ATT_SMEM;
+    cfg.dynamicSmemBytes = cl ? ATT_SMEM_CL : ATT_SMEM;
     cfg.stream = s;
-    cudaLaunchAttribute at[1];
+    cudaLaunchAttribute at[2];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = 1;
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = (unsigned)a.nsplit_max;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
     cfg.attrs = at;
-    cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, attn_partial_kernel, a);
+    cfg.numAttrs = cl && a.nsplit_max > 1 ? 2 : 1;
+    if (cl) cudaLaunchKernelEx(&cfg, attn_partial_kernel<true>, a);
+    else cudaLaunchKernelEx(&cfg, attn_partial_kernel<false>, a);
 }
+
+bool attn_fused_combine(const AttnArgs& a) { return a.att && a.nsplit_max <= 8; }
 
 // Combines the splits of each (row, head) once into att [rows][heads * 64]
 // bf16, the o_proj input: o = rb(sum_s acc_s e^(m_s - M) * (1 / L)) with

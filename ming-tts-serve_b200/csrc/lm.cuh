@@ -139,6 +139,8 @@ struct AttnArgs {
     RowsDev rows;
     int layer, heads, kv_heads, nsplit_max;
     int decode = 0;  // 1: every row appends only its own position (positions before it are already cached)
+    uint16_t* att = nullptr;  // when set (and at most 8 splits): the splits combine in-kernel into att [rows][heads*64]
+    long long* trace = nullptr;  // launch trace: [CTA][4] globaltimer stamps (entry, wait done, keys in, exit) or null
 };
 
 // Step state kept on the device so one captured graph replays every decode step.
@@ -166,6 +168,7 @@ struct FinalArgs {
 
 // Launchers (lm.cu)
 void launch_attn(const AttnArgs& a, int rows, cudaStream_t s);
+bool attn_fused_combine(const AttnArgs& a);  // launch_attn wrote att itself (no combine launch needed)
 void launch_attn_combine(const float* part, RowsDev rows, int nsplit_max, int heads, uint16_t* att, int nrows,
                          cudaStream_t s);
 void launch_final(const FinalArgs& a, int rows, cudaStream_t s);

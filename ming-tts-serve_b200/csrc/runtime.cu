@@ -111,6 +111,7 @@ struct ming_ctx {
         PackedLin qkv, o, gu, down;
         uint16_t* ln1 = nullptr;
         uint16_t* ln2 = nullptr;
+        bool ln1_unit = false, ln2_unit = false;  // every gain is exactly 1
     };
     std::vector<Layer> layers;
     uint16_t* norm = nullptr;
@@ -143,6 +144,10 @@ struct ming_ctx {
     MegaDev mega{};
     int mega_smem = 0;
     int* dev_err = nullptr;
+    // launch trace of the per-kernel step (MING_KTRACE=1): KT_SLOTS launches x
+    // KT_CTAS CTAs x 4 globaltimer stamps, slot = launch order in the step
+    long long* ktrace = nullptr;
+    int ktrace_used = 0;
     int* mega_counter = nullptr;  // [2]: epoch (monotonic), generate step index
     std::function<cudaError_t()> mega_reset;  // clean persistent-kernel state after a device error
     uint16_t* gen_out = nullptr;
@@ -284,15 +289,12 @@ void launch_lin_f(const LinScratch& sc, const PackedW& W, const Pro& p, const Ep
     if constexpr (std::is_same_v<Pro, ProRms> || std::is_same_v<Pro, ProPlain>) {
         if (rows > 8 && rows <= 64 && sc.err && bulk_enabled()) {
             if constexpr (std::is_same_v<Pro, ProRms>) {
-                if (p.K == W.K && p.ld % 8 == 0) {
-                    launch_bulk<FMT, true>(W, BulkIn{p.x, p.nw, p.ld, p.eps, sc.err}, e, rows, sc.sms, s);
+                if (p.K == W.K && p.ld % 8 == 0 &&
+                    launch_bulk<FMT, true>(W, BulkIn{p.x, p.unit ? nullptr : p.nw, p.ld, p.eps, sc.err, sc.trace}, e, rows, sc.sms, s))
                     return;
-                }
             } else {
-                if (p.ld % 8 == 0) {
-                    launch_bulk<FMT, false>(W, BulkIn{p.x, nullptr, p.ld, 0.f, sc.err}, e, rows, sc.sms, s);
+                if (p.ld % 8 == 0 && launch_bulk<FMT, false>(W, BulkIn{p.x, nullptr, p.ld, 0.f, sc.err, sc.trace}, e, rows, sc.sms, s))
                     return;
-                }
             }
         }
     }
@@ -306,12 +308,16 @@ void launch_lin_f(const LinScratch& sc, const PackedW& W, const Pro& p, const Ep
     }
 }
 
+long long* ktrace_slot(ming_ctx* c);
+
 template <class Pro, class Epi>
 void run_linear(ming_ctx* c, const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
     if (rows <= 0) return;
-    if (W.fmt == 4) launch_lin_f<4>(c->lin, W, p, e, rows, s);
-    else if (W.fmt == 8) launch_lin_f<8>(c->lin, W, p, e, rows, s);
-    else launch_lin_f<16>(c->lin, W, p, e, rows, s);
+    LinScratch sc = c->lin;
+    sc.trace = ktrace_slot(c);
+    if (W.fmt == 4) launch_lin_f<4>(sc, W, p, e, rows, s);
+    else if (W.fmt == 8) launch_lin_f<8>(sc, W, p, e, rows, s);
+    else launch_lin_f<16>(sc, W, p, e, rows, s);
 }
 
 // Dequantizes every tile of a packed linear to f32 [ntiles*16][K] (the
@@ -446,6 +452,16 @@ int upload_packed(ming_ctx* c, const std::vector<LinearSrc>& srcs, const std::ve
     }
     c->all_lins.push_back(&pl);
     return MING_OK;
+}
+
+// True when a staged bf16 gain vector holds only 1.0.
+bool unit_gains(ming_ctx* c, const std::string& name) {
+    auto it = c->staged.find(name);
+    if (it == c->staged.end() || it->second.dtype != MING_DTYPE_BF16) return false;
+    const auto& d = it->second.data;
+    for (size_t i = 0; i + 1 < d.size(); i += 2)
+        if (d[i] != 0x80 || d[i + 1] != 0x3F) return false;
+    return !d.empty();
 }
 
 // Plain row order: tile row r -> source row 16t + r (zero rows past `out`).
@@ -604,20 +620,30 @@ int copy_out(ming_ctx* c, void* dst, const void* src, size_t bytes, int kind) {
     return MING_OK;
 }
 
+constexpr int KT_SLOTS = 160, KT_CTAS = 1024;
+
+long long* ktrace_slot(ming_ctx* c) {
+    if (!c->ktrace || c->ktrace_used >= KT_SLOTS) return nullptr;
+    return c->ktrace + (size_t)(c->ktrace_used++) * KT_CTAS * 4;
+}
+
 // The 24-layer step over `rows` rows whose row_seq/row_pos are on the device.
 void enqueue_layers(ming_ctx* c, int rows, bool decode) {
     const ming_cfg& f = c->cfg;
+    c->ktrace_used = 0;
     RowsDev rd{c->row_seq, c->row_pos};
     KvDev kv{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
     for (int l = 0; l < f.layers; l++) {
         auto& L = c->layers[l];
-        run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
+        run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln1_unit},
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, rows, c->stream);
-        launch_attn(AttnArgs{c->q, c->part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, decode ? 1 : 0}, rows, c->stream);
-        launch_attn_combine(c->part, rd, c->nsplit, f.heads, c->att, rows, c->stream);
+        AttnArgs aa{c->q, c->part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, decode ? 1 : 0, c->att};
+        aa.trace = (long)aa.nsplit_max * aa.kv_heads * rows <= KT_CTAS ? ktrace_slot(c) : nullptr;
+        launch_attn(aa, rows, c->stream);
+        if (!attn_fused_combine(aa)) launch_attn_combine(c->part, rd, c->nsplit, f.heads, c->att, rows, c->stream);
         run_linear(c, L.o.w, ProPlain{c->att, f.heads * HD, 0},
                    EpiResidual{c->x, c->x1, nullptr, f.hidden}, rows, c->stream);
-        run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr}, EpiSwiGLU{c->h, f.ff}, rows,
+        run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln2_unit}, EpiSwiGLU{c->h, f.ff}, rows,
                    c->stream);
         run_linear(c, L.down.w, ProPlain{c->h, f.ff, 0}, EpiResidual{c->x1, c->x, nullptr, f.hidden}, rows, c->stream);
     }
@@ -1046,6 +1072,8 @@ int ming_cuda_finalize(ming_ctx* c) {
         for (int t = 0; t < f.ff / 8; t++)
             for (int r = 0; r < 16; r++) rows.push_back({r < 8 ? 0 : 1, t * 8 + (r & 7)});
         if ((rc = upload_packed(c, {g, u}, {p + ".mlp.gate_proj.weight", p + ".mlp.up_proj.weight"}, rows, L.gu))) return rc;
+        L.ln1_unit = unit_gains(c, p + ".input_layernorm.weight");
+        L.ln2_unit = unit_gains(c, p + ".post_attention_layernorm.weight");
         if ((rc = upload_raw(c, p + ".input_layernorm.weight", MING_DTYPE_BF16, H, (void**)&L.ln1))) return rc;
         if ((rc = upload_raw(c, p + ".post_attention_layernorm.weight", MING_DTYPE_BF16, H, (void**)&L.ln2))) return rc;
     }
@@ -1170,6 +1198,11 @@ int ming_cuda_finalize(ming_ctx* c) {
         if (!c->dev_err) c->dev_err = c->mem.alloc<int>(1, &rc);
         if (rc) return rc;
         c->lin.err = c->dev_err;
+        const char* kt = getenv("MING_KTRACE");
+        if (kt && std::string(kt) == "1") {
+            c->ktrace = c->mem.alloc<long long>((size_t)KT_SLOTS * KT_CTAS * 4, &rc);
+            if (rc) return rc;
+        }
     }
     CK(cudaDeviceSynchronize());
     c->staged.clear();
@@ -1505,10 +1538,21 @@ int ming_cuda_unpack_linear(ming_ctx* c, const char* name, float* out) {
 
 // Diagnostics: copies the persistent kernel's phase trace (MING_MEGA_TRACE=1):
 // [C][layers][32] clock64 stamps of the last step. Returns the CTA count in *n.
+// Without it, the per-kernel step's launch trace (MING_KTRACE=1):
+// [160 slots][1024 CTAs][4] globaltimer stamps, *n = -(slots used).
 extern "C" int ming_cuda_debug_trace(ming_ctx* c, long long* out, int cap, int* n) {
     if (!c || !n) return fail(MING_ERR_INVALID, "null argument");
     *n = 0;
-    if (!c->mega_on || !c->mega.trace) return MING_OK;
+    if (!c->mega_on || !c->mega.trace) {
+        // the per-kernel step's launch trace (MING_KTRACE=1): [slot][CTA][4] globaltimer stamps
+        if (!c->ktrace) return MING_OK;
+        const size_t cnt = (size_t)KT_SLOTS * KT_CTAS * 4;
+        if ((size_t)cap < cnt) return fail(MING_ERR_INVALID, "trace buffer too small");
+        CK(cudaStreamSynchronize(c->stream));
+        CK(cudaMemcpy(out, c->ktrace, cnt * 8, cudaMemcpyDeviceToHost));
+        *n = -c->ktrace_used;  // negative: launch-trace slots
+        return MING_OK;
+    }
     const size_t cnt = (size_t)c->mega.C * c->cfg.layers * MG_TRACE;
     if ((size_t)cap < cnt) return fail(MING_ERR_INVALID, "trace buffer too small");
     CK(cudaStreamSynchronize(c->stream));
@@ -1605,12 +1649,12 @@ extern "C" int ming_cuda_lm_decode_noalloc(ming_ctx* c, int B, const int* ids, c
     KvDev kv{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
     for (int l = 0; l < f.layers; l++) {
         auto& L = c->layers[l];
-        run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr},
+        run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln1_unit},
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, B, s);
         launch_attn(AttnArgs{c->q, part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, 1}, B, s);
         run_linear(c, L.o.w, ProAttn{part, rd, c->nsplit, f.heads, 0, nullptr}, EpiResidual{c->x, c->x1, nullptr, f.hidden}, B,
                    s);
-        run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr}, EpiSwiGLU{c->h, f.ff}, B, s);
+        run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln2_unit}, EpiSwiGLU{c->h, f.ff}, B, s);
         run_linear(c, L.down.w, ProPlain{c->h, f.ff, 0}, EpiResidual{c->x1, c->x, nullptr, f.hidden}, B, s);
     }
     launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, c->x, step_dev(c), H, 0, 1, f.rms_eps}, B, s);

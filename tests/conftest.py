@@ -48,19 +48,26 @@ def close(got, ref, tol=2e-2, min_cos=0.999, ulps=2):
     return d, cos, bool((diff <= bound).all() and cos > min_cos)
 
 
-def within_reference(got, fused, graph, tol=2e-2, min_cos=0.999, ulps=2):
+def within_reference(got, fused, graph, tol=2e-2, min_cos=0.999, ulps=2, exact=None):
     """Parity gate for multi-layer LM outputs against the oracle's fused
     rounding (the reference's fused kernels), scaled by how far the
     reference's own plain graph (oracle GRAPH mode) lies from it on the same
     input. Per row: every element within `close`'s bound (max-abs `tol` or
     `ulps` bf16 steps) or, where the two reference paths already disagree,
     within twice that row's fused-vs-graph max-abs spread; and cosine above
-    `min_cos` or above the fused-vs-graph cosine of that row. Returns
-    (max-abs diff, min cosine, ok)."""
+    `min_cos` or above the fused-vs-graph cosine of that row. With `exact`
+    (the oracle without bf16 rounding, F32 mode), an element also passes when
+    it lies no further from the exact value than the farther of the two
+    reference paths plus one bf16 step: no less accurate than the reference
+    itself, rounded the other way. Returns (max-abs diff, min cosine, ok)."""
     g, f, r = (bf(a).reshape(-1, a.shape[-1]) for a in (got, fused, graph))
     diff = np.abs(g - f)
     spread = np.abs(r - f).max(1, keepdims=True)
     bound = np.maximum(np.maximum(tol, ulps * bf16_ulp(f)), 2 * spread)
+    if exact is not None:
+        e = np.asarray(exact, np.float64).reshape(g.shape)
+        as_good = np.abs(g - e) <= np.maximum(np.abs(f - e), np.abs(r - e)) + bf16_ulp(e)
+        bound = np.where(as_good, np.inf, bound)
 
     def cos(a, b):
         return (a * b).sum(1) / (np.linalg.norm(a, axis=1) * np.linalg.norm(b, axis=1) + 1e-30)
