@@ -17,8 +17,8 @@
 //    bank conflicts and without any staging pass.
 //  * The tensor cores run bf16 x bf16 -> f32: 4- and 8-bit codes become exact
 //    bf16 integers in registers, the per-group scale and bias are applied in
-//    f32 (s * sum(q y) + b * sum(y)), and sum(y) of each 64-group and row
-//    comes once per CTA from an mma with an all-ones A operand.
+//    f32 (s * sum(q y) + b * sum(y)), sum(y) of each 64-group and row
+//    computed once per CTA.
 //  * RMSNorm inputs: each rank sums x^2 over its K range; the epilogue adds
 //    the ranks' sums (rank order) and applies rsqrt(mean + eps) to the f32
 //    dot products, as the reference's fused kernels fold the norm
@@ -49,18 +49,21 @@ struct BulkIn {
     int ld;
     float eps;
     int* err;            // device error word
-    long long* trace = nullptr;  // launch trace: [CTA][4] globaltimer stamps (entry, wait done, rows in, exit) or null
+    long long* trace = nullptr;  // launch trace: [CTA][8] globaltimer stamps (entry, wait done, rows in, sums done,
+                                 // weights in, mma done, cluster met, exit) or null
 };
 
 // Shared-memory layout of one CTA (bytes): barriers and per-row x^2 sums,
-// per-(group, row) operand sums [gmax][32], weights [tmax][gmax][chunk], staged rows [32][gmax * 64 + 8] bf16 (reused
+// per-(group, row) operand sums and x^2 sums [gmax][32] each, weights
+// [tmax][gmax][chunk], staged rows [32][gmax * 64 + 8] bf16 (reused
 // for the warps' partial sums after the mma loop), per-tile sums.
 struct BulkSmem {
-    int ss, ys, w, x, xstride, part, total;
+    int ss, ys, xx, w, x, xstride, part, total;
     __host__ __device__ BulkSmem(int tmax, int gmax, int cb, bool lo) {
         ss = 16;
         ys = 256;
-        w = ys + gmax * BK_ROWS * 4;
+        xx = ys + gmax * BK_ROWS * 4;
+        w = xx + gmax * BK_ROWS * 4;
         x = w + tmax * gmax * cb;
         xstride = gmax * 128 + 16;
         const int xb = (lo ? 2 : 1) * BK_ROWS * xstride, red = BK_WARPS * 16 * BK_ROWS * 4;
@@ -121,8 +124,6 @@ MING_DEV void dq8_bf16(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
     a[2] = b8pair(w1, 0x7440u, 0x7441u);
     a[3] = b8pair(w1, 0x7442u, 0x7443u);
 }
-
-constexpr uint32_t BK_ONE2 = 0x3F803F80u;  // bf16x2(1, 1)
 
 // One 64-group of one tile over the 32 staged rows: acc[j] += W_group . y
 // for n-tile j (rows 8j..8j+7). xs: the staged rows as 32-bit words, at the
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
     const int r0 = blockIdx.y * BK_ROWS, nrows = min(BK_ROWS, rows - r0);
     const int xs_b = L.xstride;
 
-    long long* tr = in.trace && tid == 0 ? in.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 4 : nullptr;
+    long long* tr = in.trace && tid == 0 ? in.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 : nullptr;
     if (tr) tr[0] = gtimer();
     // 1. this CTA's weights, before the wait on the previous kernel
     if (tid == 0) {
@@ -229,12 +230,14 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
     // 2. the activation rows are the previous kernel's output
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     if (tr) tr[1] = gtimer();
-    if (tid == 0) {
-        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bk_saddr(&bar[1])),
-                     "r"((uint32_t)(nrows * gc * 128))
-                     : "memory");
-        for (int r = 0; r < nrows; r++)
-            bk_bulk(reinterpret_cast<uint8_t*>(sX) + (size_t)r * xs_b, in.x + (size_t)(r0 + r) * in.ld + g0 * 64,
+    if (warp == 0) {  // one row per lane: every copy in flight at once
+        if (lane == 0)
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bk_saddr(&bar[1])),
+                         "r"((uint32_t)(nrows * gc * 128))
+                         : "memory");
+        __syncwarp();
+        if (lane < nrows)
+            bk_bulk(reinterpret_cast<uint8_t*>(sX) + (size_t)lane * xs_b, in.x + (size_t)(r0 + lane) * in.ld + g0 * 64,
                     (uint32_t)(gc * 128), &bar[1]);
     }
     // rows past the batch (and their low parts) are zero
@@ -247,71 +250,67 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
     }
     bool ok = bk_wait(&bar[1], 0);
     if (tr) tr[2] = gtimer();
-    // 3. RMSNorm: this rank's x^2 sums (a warp per 2 rows); non-unit gains:
+    // 3. one pass over the staged rows, a thread per (64-group, row): the
+    //    operand sum of the group (the bias term of the quantized formats)
+    //    and, for RMSNorm inputs, the group's x^2 sum; with non-unit gains
     //    the f32 product x * g is kept as hi = bf16(x g) in place and
-    //    lo = bf16(x g - hi) in row 32 + r (both go through the mma)
-    if (RMS) {
-        for (int r = warp; r < nrows; r += BK_WARPS) {
-            uint8_t* xr = reinterpret_cast<uint8_t*>(sX) + (size_t)r * xs_b;
-            float s = 0.f;
-            for (int c = lane; c < gc * 8; c += 32) {
-                uint4 v = *reinterpret_cast<const uint4*>(xr + c * 16);
-                uint32_t vv[4] = {v.x, v.y, v.z, v.w};
+    //    lo = bf16(x g - hi) in row 32 + r (both go through the mma). Row
+    //    x^2 sums add the groups in order.
+    if (FMT != 16 || RMS) {
+        float* sXX = reinterpret_cast<float*>(smem + L.xx);  // [gmax][32] per-group x^2
+        for (int e = tid; e < gc * BK_ROWS; e += BK_THREADS) {
+            const int gi = e / BK_ROWS, r = e - gi * BK_ROWS;
+            uint8_t* xr = reinterpret_cast<uint8_t*>(sX) + (size_t)r * xs_b + gi * 128;
+            uint4 v[8];
 #pragma unroll
-                for (int i = 0; i < 4; i++) {
-                    const float2 f = unpack_bf16x2(vv[i]);
-                    s += f.x * f.x + f.y * f.y;
-                }
-                if (lo) {
-                    const uint4 wv = *reinterpret_cast<const uint4*>(in.nw + g0 * 64 + c * 8);
+            for (int c = 0; c < 8; c++) v[c] = reinterpret_cast<const uint4*>(xr)[c];
+            float sy[2] = {0.f, 0.f}, sx[2] = {0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                uint32_t vv[4] = {v[c].x, v[c].y, v[c].z, v[c].w};
+                if (lo && r < nrows) {
+                    const uint4 wv = *reinterpret_cast<const uint4*>(in.nw + (g0 + gi) * 64 + c * 8);
                     const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
                     uint32_t ll[4];
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
                         const float2 f = unpack_bf16x2(vv[i]), w = unpack_bf16x2(ww[i]);
+                        sx[i & 1] += f.x * f.x + f.y * f.y;
                         const float px = f.x * w.x, py = f.y * w.y;
-                        vv[i] = pack_bf16x2(px, py);
-                        const float2 h = unpack_bf16x2(vv[i]);
-                        ll[i] = pack_bf16x2(px - h.x, py - h.y);
+                        const uint32_t h = pack_bf16x2(px, py);
+                        const float2 hf = unpack_bf16x2(h);
+                        ll[i] = pack_bf16x2(px - hf.x, py - hf.y);
+                        const float2 lf = unpack_bf16x2(ll[i]);
+                        sy[i & 1] += (hf.x + hf.y) + (lf.x + lf.y);
+                        vv[i] = h;
                     }
-                    *reinterpret_cast<uint4*>(xr + c * 16) = make_uint4(vv[0], vv[1], vv[2], vv[3]);
-                    *reinterpret_cast<uint4*>(xr + (size_t)BK_ROWS * xs_b + c * 16) = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+                    reinterpret_cast<uint4*>(xr)[c] = make_uint4(vv[0], vv[1], vv[2], vv[3]);
+                    reinterpret_cast<uint4*>(xr + (size_t)BK_ROWS * xs_b)[c] = make_uint4(ll[0], ll[1], ll[2], ll[3]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float2 f = unpack_bf16x2(vv[i]);
+                        sy[i & 1] += f.x + f.y;
+                        sx[i & 1] += f.x * f.x + f.y * f.y;
+                    }
                 }
             }
-            s = warp_sum(s);
-            if (lane == 0) sSS[r] = s;
+            sYs[gi * BK_ROWS + r] = sy[0] + sy[1];
+            if (RMS) sXX[gi * BK_ROWS + r] = sx[0] + sx[1];
+        }
+        __syncthreads();
+        if (RMS && tid < nrows) {
+            float ss = 0.f;
+            for (int gi = 0; gi < gc; gi++) ss += sXX[gi * BK_ROWS + tid];
+            sSS[tid] = ss;
         }
     }
     __syncthreads();
-    // per-(group, row) sums of the operand (the bias term of the quantized
-    // formats): one mma with an all-ones A per k-step, a warp per group
-    if (FMT != 16) {
-        const uint32_t ONES[4] = {BK_ONE2, BK_ONE2, BK_ONE2, BK_ONE2};
-        const uint32_t* xs = reinterpret_cast<const uint32_t*>(sX);
-        const int g = lane >> 2, t = lane & 3, xw = xs_b / 4;
-        for (int gi = warp; gi < gc; gi += BK_WARPS) {
-            float ty[4][4];
-#pragma unroll
-            for (int j = 0; j < 4; j++) ty[j][0] = ty[j][1] = ty[j][2] = ty[j][3] = 0.f;
-#pragma unroll
-            for (int ks = 0; ks < 4; ks++)
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const uint32_t* b = xs + (j * 8 + g) * xw + gi * 32 + ks * 8 + t;
-                    mma_bf16(ty[j], ONES, b[0], b[4]);
-                    if (lo) mma_bf16(ty[j], ONES, b[BK_ROWS * xw], b[BK_ROWS * xw + 4]);
-                }
-            if (g == 0) {
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    *reinterpret_cast<float2*>(sYs + gi * BK_ROWS + j * 8 + 2 * t) = make_float2(ty[j][0], ty[j][1]);
-            }
-        }
-        __syncthreads();
-    }
+    if (tr) tr[3] = gtimer();
     // the next kernel may launch and start its own weight copies
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     ok = bk_wait(&bar[0], 0) && ok;
+    if (tr) tr[4] = gtimer();
     if (!ok && tid == 0) atomicCAS(in.err, 0, BK_ERR_WEIGHTS);
     // 4. warp w: tile w / wpt, groups w % wpt, + wpt, ...
     float acc[4][4];
@@ -325,6 +324,7 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
             bk_group<FMT>(wbuf + ((size_t)t * gmax + gi) * CB, xs + gi * 32, xs_b / 4, lo, sYs + gi * BK_ROWS, acc, lane);
     }
     __syncthreads();  // the staged rows are dead: their space takes the partial sums
+    if (tr) tr[5] = gtimer();
     {
         const int g = lane >> 2, c = 2 * (lane & 3);
         float* r = sRed + warp * 16 * BK_ROWS;
@@ -349,6 +349,7 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
     cg::cluster_group cl = cg::this_cluster();
     if (ks > 1) cl.sync();
     else __syncthreads();
+    if (tr) tr[6] = gtimer();
     for (int e = rank * BK_THREADS + tid; e < nt * 8 * BK_ROWS; e += ks * BK_THREADS) {
         const int tt = e / (8 * BK_ROWS), rem = e - tt * 8 * BK_ROWS, r8 = rem / BK_ROWS, col = rem - r8 * BK_ROWS;
         if (col >= nrows) continue;
@@ -364,7 +365,7 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
     }
     // peers may still be reading this CTA's partials
     if (ks > 1) cl.sync();
-    if (tr) tr[3] = gtimer();
+    if (tr) tr[7] = gtimer();
 }
 
 // ---------------- host side ----------------
@@ -376,8 +377,9 @@ struct BulkPlan {
 // One CTA per SM: for each K split (1..8 ranks, a cluster) the tile ranges
 // that fill the SMs, kept if a CTA holds at most 8 tiles and fits in shared
 // memory; the cheapest by a latency model (per-warp mma groups, cluster
-// rounds).
-inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, bool lo) {
+// rounds). (A 512-thread CTA holds most of an SM's registers, so the next
+// kernel's CTAs start on an SM only as this kernel's leave it.)
+inline BulkPlan bulk_plan_cap(int ntiles, int K, int rows, int fmt, int sms, bool lo, int cap) {
     const int ng = K / 64, cb = fmt == 4 ? 576 : (fmt == 8 ? 1088 : 2048);
     const int rb = (rows + BK_ROWS - 1) / BK_ROWS;
     BulkPlan best;
@@ -392,7 +394,7 @@ inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, bool lo
         p.gmax = (ng + ks - 1) / ks;
         if (p.tmax > BK_TMAX) continue;
         p.smem = BulkSmem(p.tmax, p.gmax, cb, lo).total;
-        if (p.smem > BK_SMEM_MAX) continue;
+        if (p.smem > cap) continue;
         const int wpt = BK_WARPS / p.tmax;
         const long groups_per_warp = (p.gmax + wpt - 1) / wpt;
         const long cost = 3000 + 400L * groups_per_warp + 40L * p.gmax + 600L * (ks - 1);
@@ -402,6 +404,10 @@ inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, bool lo
         }
     }
     return best;
+}
+
+inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, bool lo) {
+    return bulk_plan_cap(ntiles, K, rows, fmt, sms, lo, BK_SMEM_MAX);
 }
 
 // Launches the kernel; false when no plan fits (the caller takes another path).

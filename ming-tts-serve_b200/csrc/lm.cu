@@ -35,7 +35,7 @@ MING_DEV void att_cp16(void* dst, const void* src) {
 // a cluster barrier, rank r combines heads r, r + ns, ... over distributed
 // shared memory (the combine kernel's formula and split order) into `att`.
 template <bool CL>
-__global__ void __launch_bounds__(256) attn_partial_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint16_t* sK = reinterpret_cast<uint16_t*>(smem);              // [ATT_SPLIT][ATT_KS]
     uint16_t* sV = sK + ATT_SPLIT * ATT_KS;                         // [ATT_SPLIT][ATT_KS]
@@ -49,7 +49,7 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnArgs a) {
     const int n = pos + 1, p0 = split * ATT_SPLIT, p1 = min(n, p0 + ATT_SPLIT), len = p1 - p0;
     const bool live = p0 < n;  // CTA-uniform
     long long* tr =
-        a.trace && tid == 0 ? a.trace + (((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 4 : nullptr;
+        a.trace && tid == 0 ? a.trace + (((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 8 : nullptr;
     if (tr) tr[0] = gtimer();
     float* out = CL ? sO : a.part + ((size_t)row * a.nsplit_max + split) * a.heads * PART_STRIDE + (size_t)kh * grp * PART_STRIDE;
     if (!CL && !live) return;  // split unused for this row (never read by the combine)
@@ -81,24 +81,27 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnArgs a) {
         __syncthreads();
         if (tr) tr[2] = gtimer();
         if (tid < len) {
-            uint32_t kr[HD / 2];
+            // the key row, unpacked once for every head of the group
+            float kf[HD];
             const uint4* src = reinterpret_cast<const uint4*>(sK + tid * ATT_KS);
 #pragma unroll
             for (int q = 0; q < HD / 8; q++) {
                 const uint4 v = src[q];
-                kr[4 * q] = v.x;
-                kr[4 * q + 1] = v.y;
-                kr[4 * q + 2] = v.z;
-                kr[4 * q + 3] = v.w;
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const float2 f = unpack_bf16x2(w[u]);
+                    kf[8 * q + 2 * u] = f.x;
+                    kf[8 * q + 2 * u + 1] = f.y;
+                }
             }
             for (int i = 0; i < grp; i++) {
                 float s0 = 0.f, s1 = 0.f;
 #pragma unroll
                 for (int q = 0; q < HD / 2; q += 2) {
-                    const float2 k0 = unpack_bf16x2(kr[q]), k1 = unpack_bf16x2(kr[q + 1]);
                     const float4 qv = *reinterpret_cast<const float4*>(sq + i * HD + 2 * q);
-                    s0 += qv.x * k0.x + qv.y * k0.y;
-                    s1 += qv.z * k1.x + qv.w * k1.y;
+                    s0 += qv.x * kf[2 * q] + qv.y * kf[2 * q + 1];
+                    s1 += qv.z * kf[2 * q + 2] + qv.w * kf[2 * q + 3];
                 }
                 sc[i * ATT_SPLIT + tid] = s0 + s1;
             }
@@ -168,7 +171,7 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(AttnArgs a) {
         }
         cl.sync();  // peers may still be reading this CTA's partials
     }
-    if (tr) tr[3] = gtimer();
+    if (tr) tr[7] = gtimer();
 }
 
 void launch_attn(const AttnArgs& a, int rows, cudaStream_t s) {

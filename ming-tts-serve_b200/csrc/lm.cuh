@@ -140,7 +140,7 @@ struct AttnArgs {
     int layer, heads, kv_heads, nsplit_max;
     int decode = 0;  // 1: every row appends only its own position (positions before it are already cached)
     uint16_t* att = nullptr;  // when set (and at most 8 splits): the splits combine in-kernel into att [rows][heads*64]
-    long long* trace = nullptr;  // launch trace: [CTA][4] globaltimer stamps (entry, wait done, keys in, exit) or null
+    long long* trace = nullptr;  // launch trace: [CTA][8] globaltimer stamps (entry, wait done, keys in, .., exit at 7) or null
 };
 
 // Step state kept on the device so one captured graph replays every decode step.

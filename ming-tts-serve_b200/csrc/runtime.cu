@@ -145,7 +145,7 @@ struct ming_ctx {
     int mega_smem = 0;
     int* dev_err = nullptr;
     // launch trace of the per-kernel step (MING_KTRACE=1): KT_SLOTS launches x
-    // KT_CTAS CTAs x 4 globaltimer stamps, slot = launch order in the step
+    // KT_CTAS CTAs x 8 globaltimer stamps, slot = launch order in the step
     long long* ktrace = nullptr;
     int ktrace_used = 0;
     int* mega_counter = nullptr;  // [2]: epoch (monotonic), generate step index
@@ -624,7 +624,7 @@ constexpr int KT_SLOTS = 160, KT_CTAS = 1024;
 
 long long* ktrace_slot(ming_ctx* c) {
     if (!c->ktrace || c->ktrace_used >= KT_SLOTS) return nullptr;
-    return c->ktrace + (size_t)(c->ktrace_used++) * KT_CTAS * 4;
+    return c->ktrace + (size_t)(c->ktrace_used++) * KT_CTAS * 8;
 }
 
 // The 24-layer step over `rows` rows whose row_seq/row_pos are on the device.
@@ -1200,7 +1200,7 @@ int ming_cuda_finalize(ming_ctx* c) {
         c->lin.err = c->dev_err;
         const char* kt = getenv("MING_KTRACE");
         if (kt && std::string(kt) == "1") {
-            c->ktrace = c->mem.alloc<long long>((size_t)KT_SLOTS * KT_CTAS * 4, &rc);
+            c->ktrace = c->mem.alloc<long long>((size_t)KT_SLOTS * KT_CTAS * 8, &rc);
             if (rc) return rc;
         }
     }
@@ -1539,14 +1539,14 @@ int ming_cuda_unpack_linear(ming_ctx* c, const char* name, float* out) {
 // Diagnostics: copies the persistent kernel's phase trace (MING_MEGA_TRACE=1):
 // [C][layers][32] clock64 stamps of the last step. Returns the CTA count in *n.
 // Without it, the per-kernel step's launch trace (MING_KTRACE=1):
-// [160 slots][1024 CTAs][4] globaltimer stamps, *n = -(slots used).
+// [160 slots][1024 CTAs][8] globaltimer stamps, *n = -(slots used).
 extern "C" int ming_cuda_debug_trace(ming_ctx* c, long long* out, int cap, int* n) {
     if (!c || !n) return fail(MING_ERR_INVALID, "null argument");
     *n = 0;
     if (!c->mega_on || !c->mega.trace) {
         // the per-kernel step's launch trace (MING_KTRACE=1): [slot][CTA][4] globaltimer stamps
         if (!c->ktrace) return MING_OK;
-        const size_t cnt = (size_t)KT_SLOTS * KT_CTAS * 4;
+        const size_t cnt = (size_t)KT_SLOTS * KT_CTAS * 8;
         if ((size_t)cap < cnt) return fail(MING_ERR_INVALID, "trace buffer too small");
         CK(cudaStreamSynchronize(c->stream));
         CK(cudaMemcpy(out, c->ktrace, cnt * 8, cudaMemcpyDeviceToHost));
