@@ -17,6 +17,9 @@ constexpr int ATT_MAXG = 8;     // query heads per kv head (<= 8)
 constexpr int ATT_KS = HD + 8;  // padded K/V row in shared memory (elements): 8 rows hit distinct bank groups
 constexpr int ATT_SMEM = 2 * ATT_SPLIT * ATT_KS * 2 + ATT_MAXG * HD * 4 + ATT_MAXG * ATT_SPLIT * 4;
 constexpr int ATT_SMEM_CL = ATT_SMEM + ATT_MAXG * PART_STRIDE * 4;
+static_assert(8 * ATT_MAXG * 32 * 8 <= ATT_SPLIT * ATT_KS * 2, "P.V partial sums fit in the key area");
+static_assert(8 * ATT_MAXG * PART_STRIDE * 4 <= ATT_SPLIT * ATT_KS * 2 && (ATT_MAXG * PART_STRIDE) % 4 == 0,
+              "eight ranks' partials fit in the key area as float4");
 
 MING_DEV uint32_t att_su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 MING_DEV void att_cp16(void* dst, const void* src) {
@@ -28,12 +31,14 @@ MING_DEV void att_cp16(void* dst, const void* src) {
 // 256-position split, every query head of the kv group. All K/V rows of the
 // split are prefetched with cp.async (one round trip), then scores (a thread
 // per position keeps its key row in registers), a per-head softmax inside
-// the split, and P.V (a thread per (head, dim pair), 4 independent sums).
+// the split, and P.V (a warp per 32 positions, a lane per dim pair, all the
+// group's heads per V load).
 // CL = false: (max, sum, unnormalised P.V) per head go to `part`, combined by
 // attn_combine_kernel. CL = true: the splits of one (kv head, row) are one
-// thread-block cluster; each keeps its partials in shared memory and, after
-// a cluster barrier, rank r combines heads r, r + ns, ... over distributed
-// shared memory (the combine kernel's formula and split order) into `att`.
+// thread-block cluster; each keeps its partials in shared memory, copies
+// every rank's partials over distributed shared memory after a cluster
+// barrier, and rank r combines heads r, r + ns, ... (the combine kernel's
+// formula and split order) into `att`.
 template <bool CL>
 __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
@@ -107,6 +112,7 @@ __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
             }
         }
         __syncthreads();
+        if (tr) tr[3] = gtimer();
         if (warp < grp) {
             float m = -INFINITY;
             for (int j = lane; j < len; j += 32) m = fmaxf(m, sc[warp * ATT_SPLIT + j]);
@@ -125,28 +131,46 @@ __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
             }
         }
         __syncthreads();
-        if (tid < grp * (HD / 2)) {
-            const int i = tid >> 5, dp = tid & 31;  // a warp per head
-            const float* pw = sc + i * ATT_SPLIT;
-            float2 ac[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};
-            int j = 0;
-            for (; j + 4 <= len; j += 4) {
+        if (tr) tr[4] = gtimer();
+        // P.V: warp w takes positions [32 w, 32 w + 32), lane = dim pair, every
+        // head of the group at once (one V load feeds 7 heads); the 8 warps'
+        // sums meet in shared memory (the key area, unused since the scores),
+        // in warp order
+        {
+            float2 ac[ATT_MAXG];
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (j + u) * ATT_KS + 2 * dp));
-                    ac[u].x += pw[j + u] * v.x;
-                    ac[u].y += pw[j + u] * v.y;
+            for (int i = 0; i < ATT_MAXG; i++) ac[i] = make_float2(0.f, 0.f);
+            const int j0 = warp * 32, j1 = min(len, j0 + 32);
+            for (int j = j0; j < j1; j++) {
+                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * ATT_KS + 2 * lane));
+#pragma unroll
+                for (int i = 0; i < ATT_MAXG; i++) {
+                    if (i < grp) {
+                        const float pw = sc[i * ATT_SPLIT + j];
+                        ac[i].x += pw * v.x;
+                        ac[i].y += pw * v.y;
+                    }
                 }
             }
-            for (; j < len; j++) {
-                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * ATT_KS + 2 * dp));
-                ac[0].x += pw[j] * v.x;
-                ac[0].y += pw[j] * v.y;
+            float2* red = reinterpret_cast<float2*>(sK);  // [8 warps][ATT_MAXG][32 lanes]: 16 KB of the 36 KB
+#pragma unroll
+            for (int i = 0; i < ATT_MAXG; i++)
+                if (i < grp) red[(warp * ATT_MAXG + i) * 32 + lane] = ac[i];
+            __syncthreads();
+            for (int e = tid; e < grp * 32; e += 256) {
+                const int i = e >> 5, dp = e & 31;
+                float2 o = make_float2(0.f, 0.f);
+                for (int w = 0; w < 8; w++) {
+                    const float2 r = red[(w * ATT_MAXG + i) * 32 + dp];
+                    o.x += r.x;
+                    o.y += r.y;
+                }
+                float* ob = out + (size_t)i * PART_STRIDE;
+                ob[2 + 2 * dp] = o.x;
+                ob[3 + 2 * dp] = o.y;
             }
-            float* o = out + (size_t)i * PART_STRIDE;
-            o[2 + 2 * dp] = (ac[0].x + ac[1].x) + (ac[2].x + ac[3].x);
-            o[3 + 2 * dp] = (ac[0].y + ac[1].y) + (ac[2].y + ac[3].y);
         }
+        if (tr) tr[5] = gtimer();
     } else if (CL) {
         // an unused split contributes weight e^(-inf) = 0
         for (int e = tid; e < grp * PART_STRIDE; e += 256) sO[e] = e % PART_STRIDE == 0 ? -INFINITY : 0.f;
@@ -155,21 +179,31 @@ __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
         namespace cg = cooperative_groups;
         cg::cluster_group cl = cg::this_cluster();
         cl.sync();
+        if (tr) tr[6] = gtimer();
+        // every rank's partials into this CTA (all loads in flight at once, into
+        // the key area), then the cluster meets once more and the peers may exit
         const int ns = (int)gridDim.x;
+        float4* all = reinterpret_cast<float4*>(sK);  // [ns][ATT_MAXG * PART_STRIDE / 4]
+        constexpr int PQ = ATT_MAXG * PART_STRIDE / 4;
+        for (int e = tid; e < ns * PQ; e += 256) {
+            const int q = e / PQ, k = e - q * PQ;
+            all[e] = reinterpret_cast<const float4*>(cl.map_shared_rank(sO, q))[k];
+        }
+        cl.sync();
+        const float* pa = reinterpret_cast<const float*>(all);
         for (int e = tid; e < ((grp - split + ns - 1) / ns) * HD; e += 256) {
             const int i = split + (e / HD) * ns, d = e % HD;
             float M = -INFINITY;
-            for (int q = 0; q < ns; q++) M = fmaxf(M, cl.map_shared_rank(sO, q)[i * PART_STRIDE]);
+            for (int q = 0; q < ns; q++) M = fmaxf(M, pa[(q * ATT_MAXG + i) * PART_STRIDE]);
             float L = 0.f, o = 0.f;
             for (int q = 0; q < ns; q++) {
-                const float* pq = cl.map_shared_rank(sO, q) + i * PART_STRIDE;
+                const float* pq = pa + (q * ATT_MAXG + i) * PART_STRIDE;
                 const float w = expf(pq[0] - M);
                 L += pq[1] * w;
                 o += pq[2 + d] * w;
             }
             a.att[(size_t)row * a.heads * HD + (kh * grp + i) * HD + d] = f2bf(rb(o * (1.0f / L)));
         }
-        cl.sync();  // peers may still be reading this CTA's partials
     }
     if (tr) tr[7] = gtimer();
 }
