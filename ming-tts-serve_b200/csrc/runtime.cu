@@ -903,28 +903,43 @@ int cfm_token_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift,
 
 int cfm_ada_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift, int step0, int nsteps) {
     const ming_cfg& f = c->cfg;
-    const int H = f.dit_hidden, LAT = f.dit_latent, F = f.dit_frames, NC = 2 * B, R = NC * F;
+    const int H = f.dit_hidden, LAT = f.dit_latent, F = f.dit_frames, NC = 2 * B, R = NC * F, MS = 6 * H;
     cudaStream_t s = c->stream;
     run_linear(c, c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, NC, s);
+    // The modulations depend on the condition and the step's time embedding
+    // only: SiLU(c + temb[st]) for every step of this call, then each block's
+    // modulation linear (and the final layer's) over all of them at once — one
+    // pass over each modulation weight per call instead of one per step.
+    // Layout: block b's [nsteps][NC][6H] at f_mod + b * NR * 6H, the final
+    // layer's [nsteps][NC][2H] after the blocks.
+    const int NR = nsteps * NC;
+    for (int k = 0; k < nsteps; k++)
+        launch_ada_cond(c->temb + (size_t)(step0 + k) * H, c->f_ce, c->f_sc + (size_t)k * NC * H, NC, H, s);
+    for (size_t bi = 0; bi < c->dit.size(); bi++) {
+        auto& b = c->dit[bi];
+        run_linear(c, b.ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{c->f_mod + bi * NR * MS, nullptr, b.ada.w.bias, MS, 0, MS}, NR,
+                   s);
+    }
+    uint16_t* fmod = c->f_mod + c->dit.size() * NR * MS;
+    run_linear(c, c->final_ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{fmod, nullptr, c->final_ada.w.bias, 2 * H, 0, 2 * H}, NR, s);
     for (int st = step0; st < step0 + nsteps; st++) {
-        launch_ada_cond(c->temb + (size_t)st * H, c->f_ce, c->f_sc, NC, H, s);
+        const size_t k = (size_t)(st - step0);
         run_linear(c, c->x_emb.w, ProLatent{c->f_y, B, F, LAT, 0}, EpiAct{c->f_rows, nullptr, c->x_emb.w.bias, H, 0, H}, R, s);
-        for (auto& b : c->dit) {
-            const int MS = 6 * H;
-            run_linear(c, b.ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{c->f_mod, nullptr, b.ada.w.bias, MS, 0, MS}, NC, s);
-            run_linear(c, b.qkv.w, ProLnMod{c->f_rows, c->f_mod, c->f_mod + H, H, MS, H, F, 0, nullptr},
+        for (size_t bi = 0; bi < c->dit.size(); bi++) {
+            auto& b = c->dit[bi];
+            const uint16_t* mod = c->f_mod + bi * NR * MS + k * NC * MS;
+            run_linear(c, b.qkv.w, ProLnMod{c->f_rows, mod, mod + H, H, MS, H, F, 0, nullptr},
                        EpiDitQKV{b.qkv.w.bias, c->f_qkv, c->inv_freq, H, F, R}, R, s);
             launch_dit_attention(c->f_qkv, c->f_att, R, F, H, f.dit_heads, s);
-            run_linear(c, b.o.w, ProPlain{c->f_att, H, 0}, EpiGatedRes{c->f_rows, c->f_rows, b.o.w.bias, c->f_mod + 2 * H, H, MS, F},
+            run_linear(c, b.o.w, ProPlain{c->f_att, H, 0}, EpiGatedRes{c->f_rows, c->f_rows, b.o.w.bias, mod + 2 * H, H, MS, F},
                        R, s);
-            run_linear(c, b.ff1.w, ProLnMod{c->f_rows, c->f_mod + 3 * H, c->f_mod + 4 * H, H, MS, H, F, 0, nullptr},
+            run_linear(c, b.ff1.w, ProLnMod{c->f_rows, mod + 3 * H, mod + 4 * H, H, MS, H, F, 0, nullptr},
                        EpiAct{c->f_hh, nullptr, b.ff1.w.bias, f.dit_ff, 1, f.dit_ff}, R, s);
             run_linear(c, b.ff2.w, ProPlain{c->f_hh, f.dit_ff, 0},
-                       EpiGatedRes{c->f_rows, c->f_rows, b.ff2.w.bias, c->f_mod + 5 * H, H, MS, F}, R, s);
+                       EpiGatedRes{c->f_rows, c->f_rows, b.ff2.w.bias, mod + 5 * H, H, MS, F}, R, s);
         }
-        run_linear(c, c->final_ada.w, ProPlain{c->f_sc, H, 0}, EpiAct{c->f_mod, nullptr, c->final_ada.w.bias, 2 * H, 0, 2 * H},
-                   NC, s);
-        run_linear(c, c->final_lin.w, ProLnMod{c->f_rows, c->f_mod, c->f_mod + H, H, 2 * H, H, F, 0, nullptr},
+        const uint16_t* fm = fmod + k * NC * 2 * H;
+        run_linear(c, c->final_lin.w, ProLnMod{c->f_rows, fm, fm + H, H, 2 * H, H, F, 0, nullptr},
                    EpiAct{nullptr, c->f_vel, c->final_lin.w.bias, LAT, 3, LAT}, R, s);
         launch_ada_euler(c->f_vel, c->f_y, with_sde ? c->f_sde : nullptr, st, c->flow_dt[st], c->flow_sq[st], cfg, shift, B,
                          F, LAT, s);
@@ -1149,8 +1164,10 @@ int ming_cuda_finalize(ming_ctx* c) {
         c->f_qkv = c->mem.alloc<uint16_t>((size_t)3 * rows * DH, &rc);
         c->f_att = c->mem.alloc<uint16_t>((size_t)rows * DH, &rc);
         c->f_hh = c->mem.alloc<uint16_t>((size_t)rows * f.dit_ff, &rc);
-        c->f_sc = c->mem.alloc<uint16_t>((size_t)2 * MB * DH, &rc);
-        c->f_mod = c->mem.alloc<uint16_t>((size_t)2 * MB * 6 * DH, &rc);
+        // adaLN: every step's SiLU(c + temb) and modulations of one call (up to 10 steps)
+        const size_t nsc = f.dit_mode == MING_DIT_ADALN ? 10 : 1;
+        c->f_sc = c->mem.alloc<uint16_t>(nsc * 2 * MB * DH, &rc);
+        c->f_mod = c->mem.alloc<uint16_t>(nsc * 2 * MB * ((size_t)f.dit_blocks * 6 * DH + 2 * DH), &rc);
         c->f_vel = c->mem.alloc<float>((size_t)rows * LAT, &rc);
         if (rc) return rc;
         if ((rc = build_temb(c, f.dit_freq_dim, DH))) return rc;
@@ -1182,7 +1199,7 @@ int ming_cuda_finalize(ming_ctx* c) {
         int rows_cap = c->maxr, k_cap = std::max(std::max(f.hidden, f.ff), f.heads * HD);
         if (f.dit_mode != MING_DIT_NONE) {
             const int MB = f.dit_max_batch;
-            rows_cap = std::max(rows_cap, std::max(2 * MB * f.dit_frames, 6 * MB));
+            rows_cap = std::max(rows_cap, std::max(2 * MB * f.dit_frames, 20 * MB));  // 20 MB: 10 steps' modulation rows
             k_cap = std::max(k_cap, std::max(std::max(f.dit_hidden, f.dit_ff), std::max(f.dit_cond_dim, f.dit_freq_dim)));
         }
         rows_cap = (rows_cap + 255) / 256 * 256;  // the tcgen05 linear reads whole 256-row blocks
