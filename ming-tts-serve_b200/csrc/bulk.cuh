@@ -19,6 +19,10 @@
 //    bf16 integers in registers, the per-group scale and bias are applied in
 //    f32 (s * sum(q y) + b * sum(y)), sum(y) of each 64-group and row
 //    computed once per CTA.
+//  * Input prologues (PRO): BK_PLAIN rows as they are; BK_LNMOD LayerNorm
+//    (no affine, eps 1e-6) + adaLN modulation, rb(LN(x) (1 + scale) + shift)
+//    with ProLnMod's statistics order, applied to the staged rows in place
+//    (K unsplit); BK_RMS as follows.
 //  * RMSNorm inputs: each rank sums x^2 over its K range; the epilogue adds
 //    the ranks' sums (rank order) and applies rsqrt(mean + eps) to the f32
 //    dot products, as the reference's fused kernels fold the norm
@@ -43,6 +47,8 @@ constexpr int BK_SMEM_MAX = 200 * 1024;
 constexpr long long BK_TIMEOUT = 2000000000LL;  // cycles (~1 s) before a copy wait gives up
 constexpr int BK_ERR_WEIGHTS = 7;               // device error code: a bulk copy never completed
 
+constexpr int BK_PLAIN = 0, BK_RMS = 1, BK_LNMOD = 2;
+
 struct BulkIn {
     const uint16_t* x;   // [rows][ld] bf16 activations
     const uint16_t* nw;  // RMSNorm gains [K] when not all 1, else null
@@ -51,6 +57,10 @@ struct BulkIn {
     int* err;            // device error word
     long long* trace = nullptr;  // launch trace: [CTA][8] globaltimer stamps (entry, wait done, rows in, sums done,
                                  // weights in, mma done, cluster met, exit) or null
+    // BK_LNMOD: modulation rows [cond][mod_ld]; condition of row r = r / rpc
+    const uint16_t* shift = nullptr;
+    const uint16_t* scale = nullptr;
+    int mod_ld = 0, rpc = 1;
 };
 
 // Shared-memory layout of one CTA (bytes): barriers and per-row x^2 sums,
@@ -130,7 +140,7 @@ MING_DEV void dq8_bf16(uint32_t w0, uint32_t w1, uint32_t (&a)[4]) {
 // group's first column; xw: words per staged row; ys: the group's operand
 // sums per row.
 template <int FMT>
-MING_DEV void bk_group(const uint8_t* chunk, const uint32_t* xs, int xw, bool lo, const float* ys, float (&acc)[4][4],
+MING_DEV void bk_group(const uint8_t* chunk, const uint32_t* xs, int xw, bool lo, int ntl, const float* ys, float (&acc)[4][4],
                        int lane) {
     const int g = lane >> 2, t = lane & 3;
     if constexpr (FMT == 16) {
@@ -140,6 +150,7 @@ MING_DEV void bk_group(const uint8_t* chunk, const uint32_t* xs, int xw, bool lo
             const uint32_t a[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
             for (int j = 0; j < 4; j++) {
+                if (j >= ntl) break;
                 const uint32_t* b = xs + (j * 8 + g) * xw + ks * 8 + t;
                 mma_bf16(acc[j], a, b[0], b[4]);
                 if (lo) mma_bf16(acc[j], a, b[BK_ROWS * xw], b[BK_ROWS * xw + 4]);
@@ -171,6 +182,7 @@ MING_DEV void bk_group(const uint8_t* chunk, const uint32_t* xs, int xw, bool lo
             else dq8_bf16(words[(ks >> 1) * 4 + (ks & 1) * 2], words[(ks >> 1) * 4 + (ks & 1) * 2 + 1], a);
 #pragma unroll
             for (int j = 0; j < 4; j++) {
+                if (j >= ntl) break;
                 const uint32_t* b = xs + (j * 8 + g) * xw + ks * 8 + t;
                 mma_bf16(tq[j], a, b[0], b[4]);
                 if (lo) mma_bf16(tq[j], a, b[BK_ROWS * xw], b[BK_ROWS * xw + 4]);
@@ -188,12 +200,13 @@ MING_DEV void bk_group(const uint8_t* chunk, const uint32_t* xs, int xw, bool lo
 }
 
 // Grid: x = tile range * ks + rank (cluster (ks, 1, 1)), y = 32-row block.
-template <int FMT, bool RMS, class Epi>
+template <int FMT, int PRO, class Epi>
 __global__ void __launch_bounds__(BK_THREADS, 1)
     linear_bulk_kernel(PackedW W, BulkIn in, Epi epi, int rows, int ks, int nb, int tmax, int gmax) {
     namespace cg = cooperative_groups;
     extern __shared__ __align__(128) uint8_t smem[];
     constexpr int CB = chunk_b(FMT);
+    constexpr bool RMS = PRO == BK_RMS;
     const bool lo = RMS && in.nw;  // non-unit gains: the normed operand is hi + lo (two bf16 parts)
     const BulkSmem L(tmax, gmax, CB, lo);
     uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [0] weights, [1] rows
@@ -240,8 +253,9 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
             bk_bulk(reinterpret_cast<uint8_t*>(sX) + (size_t)lane * xs_b, in.x + (size_t)(r0 + lane) * in.ld + g0 * 64,
                     (uint32_t)(gc * 128), &bar[1]);
     }
-    // rows past the batch (and their low parts) are zero
-    for (int e = nrows * gc * 8 + tid; e < BK_ROWS * gc * 8; e += BK_THREADS) {
+    // rows past the batch in the n-tiles used (and their low parts) are zero
+    const int ntl = (nrows + 7) / 8;
+    for (int e = nrows * gc * 8 + tid; e < ntl * 8 * gc * 8; e += BK_THREADS) {
         const int r = e / (gc * 8), c = e - r * gc * 8;
         *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sX) + (size_t)r * xs_b + c * 16) = make_uint4(0u, 0u, 0u, 0u);
         if (lo)
@@ -250,6 +264,47 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
     }
     bool ok = bk_wait(&bar[1], 0);
     if (tr) tr[2] = gtimer();
+    if constexpr (PRO == BK_LNMOD) {
+        // LayerNorm statistics of each row (ProLnMod::init's order: lanes
+        // stride the row, then the warp sum), then the modulated operand in place
+        float* sMu = sSS;                                     // [32]
+        float* sInv = reinterpret_cast<float*>(smem + L.xx);  // [32]
+        for (int r = warp; r < nrows; r += BK_WARPS) {
+            const uint16_t* xr = reinterpret_cast<const uint16_t*>(reinterpret_cast<const uint8_t*>(sX) + (size_t)r * xs_b);
+            float sm = 0.f;
+            for (int k = lane; k < W.K; k += 32) sm += bf2f(xr[k]);
+            const float mu = warp_sum(sm) / (float)W.K;
+            float v = 0.f;
+            for (int k = lane; k < W.K; k += 32) {
+                const float d = bf2f(xr[k]) - mu;
+                v += d * d;
+            }
+            v = warp_sum(v) / (float)W.K;
+            if (lane == 0) {
+                sMu[r] = mu;
+                sInv[r] = rsqrtf(v + 1e-6f);
+            }
+        }
+        __syncthreads();
+        for (int e = tid; e < nrows * gc * 8; e += BK_THREADS) {
+            const int r = e / (gc * 8), c = e - r * gc * 8, k = c * 8;
+            uint4* xp = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sX) + (size_t)r * xs_b) + c;
+            const uint4 v = *xp;
+            const size_t mo = (size_t)((r0 + r) / in.rpc) * in.mod_ld + k;
+            const uint4 sc4 = *reinterpret_cast<const uint4*>(in.scale + mo), sh4 = *reinterpret_cast<const uint4*>(in.shift + mo);
+            const uint32_t vv[4] = {v.x, v.y, v.z, v.w}, cc[4] = {sc4.x, sc4.y, sc4.z, sc4.w}, hh[4] = {sh4.x, sh4.y, sh4.z, sh4.w};
+            const float mu = sMu[r], iv = sInv[r];
+            uint32_t out[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const float2 f = unpack_bf16x2(vv[i]), sc2 = unpack_bf16x2(cc[i]), sh2 = unpack_bf16x2(hh[i]);
+                const float n0 = (f.x - mu) * iv, n1 = (f.y - mu) * iv;
+                out[i] = pack_bf16x2(rb(n0 * (1.0f + sc2.x) + sh2.x), rb(n1 * (1.0f + sc2.y) + sh2.y));
+            }
+            *xp = make_uint4(out[0], out[1], out[2], out[3]);
+        }
+        __syncthreads();
+    }
     // 3. one pass over the staged rows, a thread per (64-group, row): the
     //    operand sum of the group (the bias term of the quantized formats)
     //    and, for RMSNorm inputs, the group's x^2 sum; with non-unit gains
@@ -321,7 +376,7 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
         const uint32_t* xs = reinterpret_cast<const uint32_t*>(sX);
 #pragma unroll 1
         for (int gi = warp - t * wpt; gi < gc; gi += wpt)
-            bk_group<FMT>(wbuf + ((size_t)t * gmax + gi) * CB, xs + gi * 32, xs_b / 4, lo, sYs + gi * BK_ROWS, acc, lane);
+            bk_group<FMT>(wbuf + ((size_t)t * gmax + gi) * CB, xs + gi * 32, xs_b / 4, lo, ntl, sYs + gi * BK_ROWS, acc, lane);
     }
     __syncthreads();  // the staged rows are dead: their space takes the partial sums
     if (tr) tr[5] = gtimer();
@@ -379,12 +434,12 @@ struct BulkPlan {
 // memory; the cheapest by a latency model (per-warp mma groups, cluster
 // rounds). (A 512-thread CTA holds most of an SM's registers, so the next
 // kernel's CTAs start on an SM only as this kernel's leave it.)
-inline BulkPlan bulk_plan_cap(int ntiles, int K, int rows, int fmt, int sms, bool lo, int cap) {
+inline BulkPlan bulk_plan_cap(int ntiles, int K, int rows, int fmt, int sms, bool lo, int cap, int ksmax) {
     const int ng = K / 64, cb = fmt == 4 ? 576 : (fmt == 8 ? 1088 : 2048);
     const int rb = (rows + BK_ROWS - 1) / BK_ROWS;
     BulkPlan best;
     long best_cost = -1;
-    for (int ks = 1; ks <= 8 && ks <= ng; ks++) {
+    for (int ks = 1; ks <= ksmax && ks <= ng; ks++) {
         const int nb = std::min(ntiles, sms / (ks * rb));
         if (nb < 1) break;
         BulkPlan p;
@@ -406,22 +461,22 @@ inline BulkPlan bulk_plan_cap(int ntiles, int K, int rows, int fmt, int sms, boo
     return best;
 }
 
-inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, bool lo) {
-    return bulk_plan_cap(ntiles, K, rows, fmt, sms, lo, BK_SMEM_MAX);
+inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, bool lo, int ksmax) {
+    return bulk_plan_cap(ntiles, K, rows, fmt, sms, lo, BK_SMEM_MAX, ksmax);
 }
 
 // Launches the kernel; false when no plan fits (the caller takes another path).
-template <int FMT, bool RMS, class Epi>
+template <int FMT, int PRO, class Epi>
 bool launch_bulk(const PackedW& W, const BulkIn& in, const Epi& e, int rows, int sms, cudaStream_t s) {
     static unsigned attr_devices = 0;  // bit d: attribute set on device d
-    auto kern = linear_bulk_kernel<FMT, RMS, Epi>;
+    auto kern = linear_bulk_kernel<FMT, PRO, Epi>;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_devices & (1u << (dev & 31)))) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BK_SMEM_MAX);
         attr_devices |= 1u << (dev & 31);
     }
-    const BulkPlan p = bulk_plan(W.ntiles, W.K, rows, FMT, sms, RMS && in.nw);
+    const BulkPlan p = bulk_plan(W.ntiles, W.K, rows, FMT, sms, PRO == BK_RMS && in.nw, PRO == BK_LNMOD ? 1 : 8);
     if (p.smem == 0) return false;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(p.nb * p.ks), (unsigned)((rows + BK_ROWS - 1) / BK_ROWS));

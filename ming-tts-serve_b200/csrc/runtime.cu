@@ -285,15 +285,25 @@ void launch_lin_f(const LinScratch& sc, const PackedW& W, const Pro& p, const Ep
             return;
         }
     }
-    // decode batches (9..64 rows) of plain or RMS-normed inputs: bulk.cuh
-    if constexpr (std::is_same_v<Pro, ProRms> || std::is_same_v<Pro, ProPlain>) {
-        if (rows > 8 && rows <= 64 && sc.err && bulk_enabled()) {
+    // up to 64 rows of plain, RMS-normed or LayerNorm-modulated inputs: bulk.cuh
+    if constexpr (std::is_same_v<Pro, ProRms> || std::is_same_v<Pro, ProPlain> || std::is_same_v<Pro, ProLnMod>) {
+        if (rows <= 64 && sc.err && bulk_enabled()) {
             if constexpr (std::is_same_v<Pro, ProRms>) {
                 if (p.K == W.K && p.ld % 8 == 0 &&
-                    launch_bulk<FMT, true>(W, BulkIn{p.x, p.unit ? nullptr : p.nw, p.ld, p.eps, sc.err, sc.trace}, e, rows, sc.sms, s))
+                    launch_bulk<FMT, BK_RMS>(W, BulkIn{p.x, p.unit ? nullptr : p.nw, p.ld, p.eps, sc.err, sc.trace}, e, rows,
+                                             sc.sms, s))
+                    return;
+            } else if constexpr (std::is_same_v<Pro, ProLnMod>) {
+                const bool al = ((uintptr_t)p.shift % 16 == 0) && ((uintptr_t)p.scale % 16 == 0);
+                if (p.K == W.K && p.ld % 8 == 0 && p.mod_ld % 8 == 0 && al &&
+                    launch_bulk<FMT, BK_LNMOD>(W,
+                                               BulkIn{p.x, nullptr, p.ld, 0.f, sc.err, sc.trace, p.shift, p.scale, p.mod_ld,
+                                                      p.rows_per_cond},
+                                               e, rows, sc.sms, s))
                     return;
             } else {
-                if (p.ld % 8 == 0 && launch_bulk<FMT, false>(W, BulkIn{p.x, nullptr, p.ld, 0.f, sc.err, sc.trace}, e, rows, sc.sms, s))
+                if (p.ld % 8 == 0 &&
+                    launch_bulk<FMT, BK_PLAIN>(W, BulkIn{p.x, nullptr, p.ld, 0.f, sc.err, sc.trace}, e, rows, sc.sms, s))
                     return;
             }
         }
