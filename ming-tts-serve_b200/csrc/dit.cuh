@@ -52,9 +52,13 @@ struct EpiGatedRes {
         const int c = row / rows_per_cond;
         const int f0 = tile * 16 + r8, f1 = f0 + 8;
         const size_t i0 = (size_t)row * ld + f0, i1 = (size_t)row * ld + f1;
+        // every load before the first store: out may alias res, so a load after
+        // a store would wait for it
         const float g0 = bf2f(gate[(size_t)c * mod_ld + f0]), g1 = bf2f(gate[(size_t)c * mod_ld + f1]);
-        out[i0] = f2bf(bf2f(res[i0]) + rb(g0 * rb(lo + (bias ? bias[f0] : 0.f))));
-        out[i1] = f2bf(bf2f(res[i1]) + rb(g1 * rb(hi + (bias ? bias[f1] : 0.f))));
+        const float x0 = bf2f(res[i0]), x1 = bf2f(res[i1]);
+        const float b0 = bias ? bias[f0] : 0.f, b1 = bias ? bias[f1] : 0.f;
+        out[i0] = f2bf(x0 + rb(g0 * rb(lo + b0)));
+        out[i1] = f2bf(x1 + rb(g1 * rb(hi + b1)));
     }
 };
 

@@ -522,8 +522,10 @@ struct EpiResidual {
         const int f0 = tile * 16 + r8, f1 = f0 + 8;
         const float b0 = bias ? bias[f0] : 0.f, b1 = bias ? bias[f1] : 0.f;
         const size_t i0 = (size_t)row * ld + f0, i1 = (size_t)row * ld + f1;
-        out[i0] = f2bf(bf2f(res[i0]) + rb(lo + b0));
-        out[i1] = f2bf(bf2f(res[i1]) + rb(hi + b1));
+        // every load before the first store (out may alias res)
+        const float x0 = bf2f(res[i0]), x1 = bf2f(res[i1]);
+        out[i0] = f2bf(x0 + rb(lo + b0));
+        out[i1] = f2bf(x1 + rb(hi + b1));
     }
 };
 
@@ -551,13 +553,16 @@ struct EpiAct {
     }
     MING_DEV void operator()(int tile, int r8, int row, float lo, float hi) const {
         const int f0 = tile * 16 + r8, f1 = f0 + 8;
+        // both results before the first store (a load after a store would wait for it)
         if (act == 3) {
-            if (f0 < nvalid) out_f32[(size_t)row * ld + f0] = lo + (bias ? bias[f0] : 0.f);
-            if (f1 < nvalid) out_f32[(size_t)row * ld + f1] = hi + (bias ? bias[f1] : 0.f);
+            const float v0 = lo + (bias && f0 < nvalid ? bias[f0] : 0.f), v1 = hi + (bias && f1 < nvalid ? bias[f1] : 0.f);
+            if (f0 < nvalid) out_f32[(size_t)row * ld + f0] = v0;
+            if (f1 < nvalid) out_f32[(size_t)row * ld + f1] = v1;
             return;
         }
-        if (f0 < nvalid) out[(size_t)row * ld + f0] = f2bf(f(lo, f0));
-        if (f1 < nvalid) out[(size_t)row * ld + f1] = f2bf(f(hi, f1));
+        const float v0 = f0 < nvalid ? f(lo, f0) : 0.f, v1 = f1 < nvalid ? f(hi, f1) : 0.f;
+        if (f0 < nvalid) out[(size_t)row * ld + f0] = f2bf(v0);
+        if (f1 < nvalid) out[(size_t)row * ld + f1] = f2bf(v1);
     }
 };
 

@@ -56,7 +56,7 @@ struct EpiQKV {
         const int h = lt >> 2, d = (lt & 3) * 8 + r8;
         float x1 = rb(lo + bias[tile * 16 + r8]);
         float x2 = rb(hi + bias[tile * 16 + r8 + 8]);
-        const int pos = rows.pos[row];
+        const int pos = rows.pos[row], seq = which ? rows.seq[row] : 0;
         if (which < 2) {
             // MLX fast_rope (non-traditional): angle = pos * 2^(-(d/32) log2 theta), f32
             const float th = (float)pos * exp2f(-((float)d / 32.0f) * log2_theta);
@@ -71,7 +71,6 @@ struct EpiQKV {
             qr[d] = f2bf(x1);
             qr[d + 32] = f2bf(x2);
         } else {
-            const int seq = rows.seq[row];
             const int page = kv.bt[(size_t)seq * kv.bt_ld + pos / PAGE];
             uint16_t* dst = kv.pool + kv_index(kv, page, layer, which - 1, h, pos % PAGE);
             dst[d] = f2bf(x1);

@@ -913,6 +913,7 @@ int cfm_token_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift,
 
 int cfm_ada_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift, int step0, int nsteps) {
     const ming_cfg& f = c->cfg;
+    c->ktrace_used = 0;
     const int H = f.dit_hidden, LAT = f.dit_latent, F = f.dit_frames, NC = 2 * B, R = NC * F, MS = 6 * H;
     cudaStream_t s = c->stream;
     run_linear(c, c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, NC, s);
