@@ -147,6 +147,16 @@ def aggregate_throughput(local_ms, rows_per_rank, steps, ws):
     return ws * rows_per_rank * steps / (ms / 1e3), ms
 
 
+def profile_range(start):
+    """BENCH_PROFILE_RANGE=1: bracket the timed region with cudaProfilerStart/Stop
+    (for `ncu --profile-from-start off`, which then captures exactly its launches)."""
+    if os.environ.get("BENCH_PROFILE_RANGE") != "1":
+        return
+    import torch
+    torch.cuda.synchronize()
+    (torch.cuda.profiler.start if start else torch.cuda.profiler.stop)()
+
+
 def dist_barrier(ws):
     if ws > 1:
         import torch.distributed as dist
@@ -217,10 +227,12 @@ def run_ours(args, ws, rank, local):
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
+    profile_range(True)
     ev0.record(stream)
     ctx.generate(seqs, xdev, args.steps, kind=M.PTR_DEVICE, out=outdev, stop=stopdev)
     ev1.record(stream)
     ev1.synchronize()
+    profile_range(False)
     torch.cuda.synchronize()
     dist_barrier(ws)
     ck = clocks.stop()
@@ -346,11 +358,13 @@ def run_dit(args, ws, rank, local):
     torch.cuda.synchronize()
     clocks.start()
     time.sleep(0.3)
+    profile_range(True)
     ev0.record(stream)
     for _ in range(args.steps):
         step()
     ev1.record(stream)
     ev1.synchronize()
+    profile_range(False)
     dist_barrier(ws)
     ck = clocks.stop()
     ms_local = ev0.elapsed_time(ev1)
@@ -358,6 +372,12 @@ def run_dit(args, ws, rank, local):
     wbytes = synth.nbytes(W)
     hbm, tf, peak_kind = load_peaks()
     per_sample_bytes = 10 * wbytes  # weights once per Euler step
+    # launches per cfm_sample call, mirroring the library's dispatch: a linear
+    # of <= 64 rows is one kernel (the latent embedding's <= 8), larger ones two
+    R, NC = 8 * B, 2 * B
+    lin = lambda rows, small=64: 1 if rows <= small else 2
+    launches = (lin(NC) + 10 + 7 * lin(10 * NC)
+                + 10 * (lin(R, 8) + 6 * (4 * lin(R) + 1) + lin(R) + 1))
     achieved = per_sample_bytes / (ms_local / args.steps / 1e3) / 1e9
     hz = np.empty_like(noise)
     t0 = time.perf_counter()
@@ -373,7 +393,7 @@ def run_dit(args, ws, rank, local):
                          "frac": achieved / hbm, "peak_kind": peak_kind, "traffic": None},
             "e2e": {"value": ws * B * args.steps / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": z.nbytes + noise.nbytes,
                     "d2h_bytes_per_step": noise.nbytes},
-            "gpu_launches": None, "clocks": ck, "cpu_baseline": None}
+            "gpu_launches": launches * args.steps, "clocks": ck, "cpu_baseline": None}
 
 
 def run_reference(args, ws, rank, local):

@@ -36,6 +36,7 @@
 #include <cooperative_groups.h>
 
 #include "linear.cuh"
+#include "tcgen05.cuh"
 
 namespace ming {
 
@@ -44,6 +45,7 @@ constexpr int BK_THREADS = BK_WARPS * 32;
 constexpr int BK_ROWS = 32;                     // activation rows per CTA (4 mma n-tiles)
 constexpr int BK_TMAX = 8;                      // tiles per CTA at most
 constexpr int BK_SMEM_MAX = 200 * 1024;
+constexpr int BK_SMEM_TC_MAX = 226 * 1024;
 constexpr long long BK_TIMEOUT = 2000000000LL;  // cycles (~1 s) before a copy wait gives up
 constexpr int BK_ERR_WEIGHTS = 7;               // device error code: a bulk copy never completed
 
@@ -63,22 +65,32 @@ struct BulkIn {
     int mod_ld = 0, rpc = 1;
 };
 
-// Shared-memory layout of one CTA (bytes): barriers and per-row x^2 sums,
-// per-(group, row) operand sums and x^2 sums [gmax][32] each, weights
-// [tmax][gmax][chunk], staged rows [32][gmax * 64 + 8] bf16 (reused
-// for the warps' partial sums after the mma loop), per-tile sums.
+// Shared-memory layout of one CTA (bytes): barriers, tensor-memory slot and
+// per-row x^2 sums; per-(group, row) operand sums and x^2 sums [gmax][32]
+// each; with TC the two 1024-aligned stages of the tcgen05 operands (weight
+// block 128 x 64 bf16, row block 32 x 64 bf16 (+ low parts)); packed weights
+// [tmax][gmax][chunk]; staged rows [32 (+ 32 low parts)][gmax * 64 + 8] bf16
+// (reused for the warps' partial sums after the mma.sync loop); per-tile
+// sums [tmax * 16][32]. With TC the kernel aligns its base up to 1024 bytes
+// (the slack is in `total`).
 struct BulkSmem {
-    int ss, ys, xx, w, x, xstride, part, total;
-    __host__ __device__ BulkSmem(int tmax, int gmax, int cb, bool lo) {
-        ss = 16;
+    int ss, ys, xx, a, b, w, x, xstride, part, total;
+    __host__ __device__ BulkSmem(int tmax, int gmax, int cb, bool lo, bool tc = false) {
+        ss = 128;
         ys = 256;
         xx = ys + gmax * BK_ROWS * 4;
+        a = b = 0;
         w = xx + gmax * BK_ROWS * 4;
+        if (tc) {
+            a = (w + 1023) / 1024 * 1024;
+            b = a + 2 * TC_A_BLOCK;
+            w = b + 2 * (lo ? 2 : 1) * BK_ROWS * 128;
+        }
         x = w + tmax * gmax * cb;
         xstride = gmax * 128 + 16;
-        const int xb = (lo ? 2 : 1) * BK_ROWS * xstride, red = BK_WARPS * 16 * BK_ROWS * 4;
+        const int xb = (lo ? 2 : 1) * BK_ROWS * xstride, red = tc ? 0 : BK_WARPS * 16 * BK_ROWS * 4;
         part = x + (xb > red ? xb : red);
-        total = part + tmax * 16 * BK_ROWS * 4;
+        total = part + tmax * 16 * BK_ROWS * 4 + (tc ? 1024 : 0);
     }
 };
 
@@ -200,16 +212,21 @@ MING_DEV void bk_group(const uint8_t* chunk, const uint32_t* xs, int xw, bool lo
 }
 
 // Grid: x = tile range * ks + rank (cluster (ks, 1, 1)), y = 32-row block.
-template <int FMT, int PRO, class Epi>
+// TC: the tile range is one block of 8 tiles (128 features) and the products
+// run on tcgen05 (see the TC section below); otherwise on mma.sync.
+template <int FMT, int PRO, bool TC, class Epi>
 __global__ void __launch_bounds__(BK_THREADS, 1)
     linear_bulk_kernel(PackedW W, BulkIn in, Epi epi, int rows, int ks, int nb, int tmax, int gmax) {
     namespace cg = cooperative_groups;
-    extern __shared__ __align__(128) uint8_t smem[];
+    extern __shared__ __align__(128) uint8_t smem_raw[];
+    // TC: 1024-byte aligned base (the swizzle atoms of the tcgen05 operands)
+    uint8_t* smem = TC ? smem_raw + ((1024u - (bk_saddr(smem_raw) & 1023u)) & 1023u) : smem_raw;
     constexpr int CB = chunk_b(FMT);
     constexpr bool RMS = PRO == BK_RMS;
     const bool lo = RMS && in.nw;  // non-unit gains: the normed operand is hi + lo (two bf16 parts)
-    const BulkSmem L(tmax, gmax, CB, lo);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [0] weights, [1] rows
+    const BulkSmem L(tmax, gmax, CB, lo, TC);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [0] weights, [1] rows; TC: [2], [3] stages read, [4] mma done
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 48);  // TC: tensor-memory base
     float* sSS = reinterpret_cast<float*>(smem + L.ss);  // [32] this rank's x^2 sums (RMS)
     float* sYs = reinterpret_cast<float*>(smem + L.ys);  // [gmax][32] operand sums (quantized formats)
     uint8_t* wbuf = smem + L.w;
@@ -228,9 +245,18 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
     long long* tr = in.trace && tid == 0 ? in.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 : nullptr;
     if (tr) tr[0] = gtimer();
     // 1. this CTA's weights, before the wait on the previous kernel
+    // TC: tensor memory for one 32-column accumulator per K group (gc <= 16)
+    const uint32_t tcols = gc <= 1 ? 32u : (gc <= 2 ? 64u : (gc <= 4 ? 128u : (gc <= 8 ? 256u : 512u)));
+    if (TC && warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(bk_saddr(tslot)), "r"(tcols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+    }
     if (tid == 0) {
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(&bar[0])) : "memory");
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(&bar[1])) : "memory");
+        if (TC)
+            for (int i = 2; i < 5; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(&bar[i])) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bk_saddr(&bar[0])),
                      "r"((uint32_t)(nt * gc * CB))
@@ -239,7 +265,9 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
             bk_bulk(wbuf + (size_t)t * gmax * CB, W.tiles + ((size_t)(tile0 + t) * ng + g0) * CB, (uint32_t)(gc * CB),
                     &bar[0]);
     }
+    if (TC) asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
     __syncthreads();  // the barriers are initialised before anyone waits on them
+    if (TC) asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     // 2. the activation rows are the previous kernel's output
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     if (tr) tr[1] = gtimer();
@@ -254,7 +282,7 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
                     (uint32_t)(gc * 128), &bar[1]);
     }
     // rows past the batch in the n-tiles used (and their low parts) are zero
-    const int ntl = (nrows + 7) / 8;
+    const int ntl = TC ? 4 : (nrows + 7) / 8;  // TC: the mma reads all 32 rows
     for (int e = nrows * gc * 8 + tid; e < ntl * 8 * gc * 8; e += BK_THREADS) {
         const int r = e / (gc * 8), c = e - r * gc * 8;
         *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(sX) + (size_t)r * xs_b + c * 16) = make_uint4(0u, 0u, 0u, 0u);
@@ -367,37 +395,144 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
     ok = bk_wait(&bar[0], 0) && ok;
     if (tr) tr[4] = gtimer();
     if (!ok && tid == 0) atomicCAS(in.err, 0, BK_ERR_WEIGHTS);
-    // 4. warp w: tile w / wpt, groups w % wpt, + wpt, ...
-    float acc[4][4];
+    if constexpr (TC) {
+        // 4. tcgen05: per K group, every thread writes its share of the 128 x 64
+        //    weight block (codes -> exact bf16, 128-byte-swizzled K-major, the
+        //    layout tc_swizzle_kernel gives bf16 weights) and of the 32 x 64 row
+        //    block into one of two stages; after a proxy fence and a barrier
+        //    one thread issues 4 tcgen05.mma (M 128, N 32, K 16) into the
+        //    group's own 32 tensor-memory columns and commits to the stage's
+        //    barrier, so the group scale and bias stay in f32 (below).
+        uint64_t* mbar = bar + 2;
+        uint64_t* dbar = bar + 4;
+        const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot);
+        const int bstage = (lo ? 2 : 1) * BK_ROWS * 128;
+        bool tok = ok;
+        for (int gi = 0; gi < gc; gi++) {
+            const int s = gi & 1;
+            if (gi >= 2 && !bk_wait(&mbar[s], ((gi >> 1) - 1) & 1)) tok = false;
+            uint8_t* A = smem + L.a + s * TC_A_BLOCK;
+            uint8_t* Bs = smem + L.b + s * bstage;
+            for (int e = tid; e < 8 * 32 * 4; e += BK_THREADS) {
+                const int tt = e >> 7, ln = (e >> 2) & 31, kq = e & 3;
+                const uint8_t* ch = wbuf + ((size_t)tt * gmax + gi) * CB;
+                uint32_t av[4];
+                if constexpr (FMT == 4) {
+                    dq4_bf16(reinterpret_cast<const uint32_t*>(ch + ln * 16)[kq], av);
+                } else if constexpr (FMT == 8) {
+                    const uint32_t* wp = reinterpret_cast<const uint32_t*>(ch + ((kq >> 1) * 32 + ln) * 16) + (kq & 1) * 2;
+                    dq8_bf16(wp[0], wp[1], av);
+                } else {
+                    const uint4 w = reinterpret_cast<const uint4*>(ch)[kq * 32 + ln];
+                    av[0] = w.x; av[1] = w.y; av[2] = w.z; av[3] = w.w;
+                }
+                // lane (g, t): (row g, k 16 kq + 2t..+1), (row g + 8, same), (row g, +8), (row g + 8, +8)
+                const int m0 = tt * 16 + (ln >> 2), t4 = (ln & 3) * 4;
+                *reinterpret_cast<uint32_t*>(A + tc_sw128(m0, 2 * kq) + t4) = av[0];
+                *reinterpret_cast<uint32_t*>(A + tc_sw128(m0 + 8, 2 * kq) + t4) = av[1];
+                *reinterpret_cast<uint32_t*>(A + tc_sw128(m0, 2 * kq + 1) + t4) = av[2];
+                *reinterpret_cast<uint32_t*>(A + tc_sw128(m0 + 8, 2 * kq + 1) + t4) = av[3];
+            }
+            for (int e = tid; e < (lo ? 2 : 1) * BK_ROWS * 8; e += BK_THREADS) {
+                const int part = e >> 8, n = (e >> 3) & 31, c = e & 7;
+                const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(sX) +
+                                                                (size_t)(part * BK_ROWS + n) * xs_b + gi * 128 + c * 16);
+                *reinterpret_cast<uint4*>(Bs + part * BK_ROWS * 128 + tc_sw128(n, c)) = v;
+            }
+            asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // thread writes -> tensor-core reads
+            __syncthreads();
+            if (tid == 0) {
+                asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+                const uint32_t a0 = bk_saddr(A), b0 = bk_saddr(Bs);
 #pragma unroll
-    for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
-    const int wpt = BK_WARPS / nt, t = warp / wpt;
-    if (t < nt) {
-        const uint32_t* xs = reinterpret_cast<const uint32_t*>(sX);
-#pragma unroll 1
-        for (int gi = warp - t * wpt; gi < gc; gi += wpt)
-            bk_group<FMT>(wbuf + ((size_t)t * gmax + gi) * CB, xs + gi * 32, xs_b / 4, lo, ntl, sYs + gi * BK_ROWS, acc, lane);
-    }
-    __syncthreads();  // the staged rows are dead: their space takes the partial sums
-    if (tr) tr[5] = gtimer();
-    {
-        const int g = lane >> 2, c = 2 * (lane & 3);
-        float* r = sRed + warp * 16 * BK_ROWS;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            r[g * BK_ROWS + j * 8 + c] = acc[j][0];
-            r[g * BK_ROWS + j * 8 + c + 1] = acc[j][1];
-            r[(g + 8) * BK_ROWS + j * 8 + c] = acc[j][2];
-            r[(g + 8) * BK_ROWS + j * 8 + c + 1] = acc[j][3];
+                for (int kq = 0; kq < 4 * 2; kq++) {
+                    if (kq >= 4 && !lo) break;
+                    const uint64_t da = tc_desc(a0 + 32 * (kq & 3)), db = tc_desc(b0 + (kq >> 2) * BK_ROWS * 128 + 32 * (kq & 3));
+                    const uint32_t accf = kq > 0 ? 1u : 0u;
+                    asm volatile(
+                        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem + (uint32_t)(gi * 32)),
+                        "l"(da), "l"(db), "r"(tc_idesc<BK_ROWS>()), "r"(accf)
+                        : "memory");
+                }
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(
+                                 bk_saddr(&mbar[s]))
+                             : "memory");
+            }
         }
-    }
-    __syncthreads();
-    // per tile: the sum of its warps, in warp order
-    for (int e = tid; e < nt * 16 * BK_ROWS; e += BK_THREADS) {
-        const int tt = e / (16 * BK_ROWS), rc = e - tt * 16 * BK_ROWS;
-        float s = 0.f;
-        for (int w = tt * wpt; w < (tt + 1) * wpt; w++) s += sRed[w * 16 * BK_ROWS + rc];
-        sPart[e] = s;
+        if (tid == 0)
+            asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bk_saddr(dbar))
+                         : "memory");
+        tok = bk_wait(dbar, 0) && tok;
+        asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
+        if (!tok && tid == 0) atomicCAS(in.err, 0, BK_ERR_WEIGHTS);
+        if (tr) tr[5] = gtimer();
+        // the groups' accumulators, scaled in f32: warp w reads tensor-memory
+        // lanes 32 (w % 4) .. (feature m = its lane) and rows 8 (w / 4) .. + 8
+        {
+            const int q = warp & 3, cb = warp >> 2, m = q * 32 + lane, tt = m >> 4, rr = m & 15;
+            float av[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) av[j] = 0.f;
+            for (int gi = 0; gi < gc; gi++) {
+                uint32_t v[8];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                             : "r"(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(gi * 32 + cb * 8)));
+                asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+                if constexpr (FMT == 16) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) av[j] += __uint_as_float(v[j]);
+                } else {
+                    const uint2 sc =
+                        *reinterpret_cast<const uint2*>(wbuf + ((size_t)tt * gmax + gi) * CB + (FMT == 4 ? 512 : 1024) + (rr & 7) * 8);
+                    const uint32_t sw = rr < 8 ? sc.x : sc.y;
+                    const float sf = __uint_as_float(sw << 16), bf = __uint_as_float(sw & 0xffff0000u);
+                    const float* ys = sYs + gi * BK_ROWS + cb * 8;
+#pragma unroll
+                    for (int j = 0; j < 8; j++) av[j] += sf * __uint_as_float(v[j]) + bf * ys[j];
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) sPart[m * BK_ROWS + cb * 8 + j] = av[j];
+        }
+        // the tensor memory goes back once every load above has completed
+        asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+        __syncthreads();
+        if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(tcols) : "memory");
+    } else {
+        // 4. warp w: tile w / wpt, groups w % wpt, + wpt, ...
+        float acc[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+        const int wpt = BK_WARPS / nt, t = warp / wpt;
+        if (t < nt) {
+            const uint32_t* xs = reinterpret_cast<const uint32_t*>(sX);
+#pragma unroll 1
+            for (int gi = warp - t * wpt; gi < gc; gi += wpt)
+                bk_group<FMT>(wbuf + ((size_t)t * gmax + gi) * CB, xs + gi * 32, xs_b / 4, lo, ntl, sYs + gi * BK_ROWS, acc, lane);
+        }
+        __syncthreads();  // the staged rows are dead: their space takes the partial sums
+        if (tr) tr[5] = gtimer();
+        {
+            const int g = lane >> 2, c = 2 * (lane & 3);
+            float* r = sRed + warp * 16 * BK_ROWS;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                r[g * BK_ROWS + j * 8 + c] = acc[j][0];
+                r[g * BK_ROWS + j * 8 + c + 1] = acc[j][1];
+                r[(g + 8) * BK_ROWS + j * 8 + c] = acc[j][2];
+                r[(g + 8) * BK_ROWS + j * 8 + c + 1] = acc[j][3];
+            }
+        }
+        __syncthreads();
+        // per tile: the sum of its warps, in warp order
+        for (int e = tid; e < nt * 16 * BK_ROWS; e += BK_THREADS) {
+            const int tt = e / (16 * BK_ROWS), rc = e - tt * 16 * BK_ROWS;
+            float s = 0.f;
+            for (int w = tt * wpt; w < (tt + 1) * wpt; w++) s += sRed[w * 16 * BK_ROWS + rc];
+            sPart[e] = s;
+        }
     }
     // 5. the ks ranks' partials (and x^2 sums), summed in rank order; rank r
     //    takes every ks-th (tile, row pair, activation row)
@@ -465,19 +600,55 @@ inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, bool lo
     return bulk_plan_cap(ntiles, K, rows, fmt, sms, lo, BK_SMEM_MAX, ksmax);
 }
 
-// Launches the kernel; false when no plan fits (the caller takes another path).
-template <int FMT, int PRO, class Epi>
-bool launch_bulk(const PackedW& W, const BulkIn& in, const Epi& e, int rows, int sms, cudaStream_t s) {
+// tcgen05 plan: blocks of 8 tiles (128 features), K split so that a rank holds
+// at most 16 groups (one 32-column accumulator each in 512 tensor-memory
+// columns), one wave of CTAs; the cheapest by the same kind of latency model
+// (a pipelined step per group, cluster rounds). smem 0 when none fits.
+inline BulkPlan bulk_plan_tc(int ntiles, int K, int rows, int fmt, int sms, bool lo) {
+    BulkPlan best;
+    if (ntiles % 8) return best;
+    const int ng = K / 64, cb = fmt == 4 ? 576 : (fmt == 8 ? 1088 : 2048), mb = ntiles / 8;
+    const int rb = (rows + BK_ROWS - 1) / BK_ROWS;
+    long best_cost = -1;
+    for (int ks = std::max(1, (ng + 15) / 16); ks <= 8 && ks <= ng; ks++) {
+        if ((long)mb * ks * rb > sms) break;
+        BulkPlan p;
+        p.ks = ks;
+        p.nb = mb;
+        p.tmax = 8;
+        p.gmax = (ng + ks - 1) / ks;
+        if (p.gmax > 16) continue;
+        p.smem = BulkSmem(8, p.gmax, cb, lo, true).total;
+        if (p.smem > BK_SMEM_TC_MAX) continue;
+        const long cost = 250L * p.gmax + (ks > 1 ? 800L + 100L * ks : 0L);
+        if (best_cost < 0 || cost < best_cost) {
+            best = p;
+            best_cost = cost;
+        }
+    }
+    return best;
+}
+
+// MING_BULK_TC=1 (read at each launch, so at graph capture) puts 4/8-bit
+// weights in blocks of 128 features on tcgen05. Off by default: at the
+// decode shapes of this model the mma.sync variant is faster (the 128-feature
+// blocks leave 49-76 CTAs, and each K group costs a staging round and a
+// barrier before its MMA; 1.71 vs 1.11 ms per batch-32 step).
+inline bool bulk_tc_enabled() {
+    const char* v = getenv("MING_BULK_TC");
+    return v && v[0] == '1' && v[1] == 0;
+}
+
+template <int FMT, int PRO, bool TC, class Epi>
+void launch_bulk_plan(const PackedW& W, const BulkIn& in, const Epi& e, int rows, const BulkPlan& p, cudaStream_t s) {
     static unsigned attr_devices = 0;  // bit d: attribute set on device d
-    auto kern = linear_bulk_kernel<FMT, PRO, Epi>;
+    auto kern = linear_bulk_kernel<FMT, PRO, TC, Epi>;
     int dev = 0;
     cudaGetDevice(&dev);
     if (!(attr_devices & (1u << (dev & 31)))) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, BK_SMEM_MAX);
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TC ? BK_SMEM_TC_MAX : BK_SMEM_MAX);
         attr_devices |= 1u << (dev & 31);
     }
-    const BulkPlan p = bulk_plan(W.ntiles, W.K, rows, FMT, sms, PRO == BK_RMS && in.nw, PRO == BK_LNMOD ? 1 : 8);
-    if (p.smem == 0) return false;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(p.nb * p.ks), (unsigned)((rows + BK_ROWS - 1) / BK_ROWS));
     cfg.blockDim = dim3(BK_THREADS);
@@ -493,6 +664,26 @@ bool launch_bulk(const PackedW& W, const BulkIn& in, const Epi& e, int rows, int
     cfg.attrs = at;
     cfg.numAttrs = p.ks > 1 ? 2 : 1;
     cudaLaunchKernelEx(&cfg, kern, W, in, e, rows, p.ks, p.nb, p.tmax, p.gmax);  // errors surface at the caller's check
+}
+
+// Launches the kernel; false when no plan fits (the caller takes another
+// path). With MING_BULK_TC=1, 4- and 8-bit weights in blocks of 128 features
+// run on tcgen05.
+template <int FMT, int PRO, class Epi>
+bool launch_bulk(const PackedW& W, const BulkIn& in, const Epi& e, int rows, int sms, cudaStream_t s) {
+    const bool lo = PRO == BK_RMS && in.nw;
+    if constexpr (FMT != 16) {
+        if (PRO != BK_LNMOD && bulk_tc_enabled()) {
+            const BulkPlan p = bulk_plan_tc(W.ntiles, W.K, rows, FMT, sms, lo);
+            if (p.smem) {
+                launch_bulk_plan<FMT, PRO, true>(W, in, e, rows, p, s);
+                return true;
+            }
+        }
+    }
+    const BulkPlan p = bulk_plan(W.ntiles, W.K, rows, FMT, sms, lo, PRO == BK_LNMOD ? 1 : 8);
+    if (p.smem == 0) return false;
+    launch_bulk_plan<FMT, PRO, false>(W, in, e, rows, p, s);
     return true;
 }
 

@@ -914,6 +914,7 @@ int cfm_token_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift,
 int cfm_ada_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift, int step0, int nsteps) {
     const ming_cfg& f = c->cfg;
     c->ktrace_used = 0;
+    c->ktrace_used = 0;
     const int H = f.dit_hidden, LAT = f.dit_latent, F = f.dit_frames, NC = 2 * B, R = NC * F, MS = 6 * H;
     cudaStream_t s = c->stream;
     run_linear(c, c->c_emb.w, ProPlain{c->f_zc, f.dit_cond_dim, 0}, EpiAct{c->f_ce, nullptr, c->c_emb.w.bias, H, 0, H}, NC, s);
@@ -1499,8 +1500,17 @@ int ming_cuda_step_kernels(ming_ctx* c, int B, int* n) {
     if (!c || !n) return fail(MING_ERR_INVALID, "null argument");
     if (!c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
     if (B < 1 || B > c->cfg.max_batch) return fail(MING_ERR_INVALID, "batch size out of range");
-    // persistent: one launch; per-kernel: step_begin + 5 per layer + final
-    *n = (c->mega_on && B <= MG_MAXB) ? 1 : 1 + 5 * c->cfg.layers + 1;
+    // persistent: one launch; per-kernel: step_begin + per layer (4 linears +
+    // attention [+ split combine]) + final, mirroring run_linear's dispatch
+    if (c->mega_on && B <= MG_MAXB) {
+        *n = 1;
+        return MING_OK;
+    }
+    int lin = 2;  // staged: prologue kernel + linear
+    if (B <= 64 && c->lin.err && bulk_enabled()) lin = 1;
+    else if (B <= 8) lin = 1;
+    const int attn = c->nsplit <= 8 ? 1 : 2;
+    *n = 1 + (4 * lin + attn) * c->cfg.layers + 1;
     return MING_OK;
 }
 

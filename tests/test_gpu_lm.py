@@ -205,6 +205,46 @@ def test_batched_decode_many_rows(cuda_ok, bits, B, gains):
     ctx.close()
 
 
+@pytest.mark.parametrize("bits,B", [(4, 20), (8, 12), (4, 40)])
+def test_batched_decode_tcgen05(cuda_ok, monkeypatch, bits, B):
+    """The decode-batch linear's tcgen05 variant (MING_BULK_TC=1: codes
+    dequantized into 128-byte-swizzled weight blocks, one tensor-memory
+    accumulator per K group, the group scale and bias in f32), gated like the
+    mma.sync variant against the oracle."""
+    monkeypatch.setenv("MING_BULK_TC", "1")
+    layers = 2
+    W = synth.lm_weights(seed=12, bits=bits, layers=layers, qscale=QS)
+    ctx = make_ctx(W, bits, layers, max_ctx=256, max_pages=1024, max_batch=64, max_seqs=64)
+    lm = O.Lm(W)
+    lens = np.random.default_rng(B + 1).integers(1, 24, size=B).tolist()
+    seqs, caches, gcaches, fcaches, xs = [], [], [], [], []
+    for i, L in enumerate(lens):
+        s = ctx.seq_alloc()
+        x = synth.normal_bf16(8, f"test.tc.{bits}.{B}.{i}", (L, 896))
+        c, cg, cf = lm.new_cache(L + 2), lm.new_cache(L + 2), lm.new_cache(L + 2)
+        got, _ = ctx.prefill(s, x)
+        ro, _ = lm.forward(c, x)
+        rg, _ = lm.forward(cg, x, O.MODE_GRAPH)
+        rf = lm.forward_f32(cf, x)
+        d, cs, ok = within_reference(got, ro, rg, exact=rf)
+        assert ok, f"prefill row {i} (L={L}): maxabs {d:.4g} cos {cs:.6f}"
+        seqs.append(s)
+        caches.append(c)
+        gcaches.append(cg)
+        fcaches.append(cf)
+        xs.append(ro[-1])
+    x = np.stack(xs)
+    go, gs = ctx.decode(seqs, x)
+    ref, refg, reff = [], [], []
+    for b in range(B):
+        ref.append(lm.forward(caches[b], x[b:b + 1])[0][0])
+        refg.append(lm.forward(gcaches[b], x[b:b + 1], O.MODE_GRAPH)[0][0])
+        reff.append(lm.forward_f32(fcaches[b], x[b:b + 1])[0])
+    d, cs, ok = within_reference(go, np.stack(ref), np.stack(refg), exact=np.stack(reff))
+    assert ok, f"decode: maxabs {d:.4g} cos {cs:.6f}"
+    ctx.close()
+
+
 def test_generate_matches_decode_loop_bitwise(q4_24):
     W, ctx, lm = q4_24
     x = synth.normal_bf16(4, "test.gen", (20, 896))
