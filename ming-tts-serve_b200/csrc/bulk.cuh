@@ -83,8 +83,9 @@ struct BulkSmem {
         w = xx + gmax * BK_ROWS * 4;
         if (tc) {
             a = (w + 1023) / 1024 * 1024;
-            b = a + 2 * TC_A_BLOCK;
-            w = b + 2 * (lo ? 2 : 1) * BK_ROWS * 128;
+            const int nst = lo ? 2 : 4;  // operand stages (4 hide the MMA round trip; 2 leave room for low parts)
+            b = a + nst * TC_A_BLOCK;
+            w = b + nst * (lo ? 2 : 1) * BK_ROWS * 128;
         }
         x = w + tmax * gmax * cb;
         xstride = gmax * 128 + 16;
@@ -225,8 +226,8 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
     constexpr bool RMS = PRO == BK_RMS;
     const bool lo = RMS && in.nw;  // non-unit gains: the normed operand is hi + lo (two bf16 parts)
     const BulkSmem L(tmax, gmax, CB, lo, TC);
-    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [0] weights, [1] rows; TC: [2], [3] stages read, [4] mma done
-    uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 48);  // TC: tensor-memory base
+    uint64_t* bar = reinterpret_cast<uint64_t*>(smem);  // [0] weights, [1] rows; TC: [2..5] stages read, [6] mma done
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + 64);  // TC: tensor-memory base
     float* sSS = reinterpret_cast<float*>(smem + L.ss);  // [32] this rank's x^2 sums (RMS)
     float* sYs = reinterpret_cast<float*>(smem + L.ys);  // [gmax][32] operand sums (quantized formats)
     uint8_t* wbuf = smem + L.w;
@@ -256,7 +257,7 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(&bar[0])) : "memory");
         asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(&bar[1])) : "memory");
         if (TC)
-            for (int i = 2; i < 5; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(&bar[i])) : "memory");
+            for (int i = 2; i < 7; i++) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bk_saddr(&bar[i])) : "memory");
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
         asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bk_saddr(&bar[0])),
                      "r"((uint32_t)(nt * gc * CB))
@@ -404,13 +405,13 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
         //    group's own 32 tensor-memory columns and commits to the stage's
         //    barrier, so the group scale and bias stay in f32 (below).
         uint64_t* mbar = bar + 2;
-        uint64_t* dbar = bar + 4;
+        uint64_t* dbar = bar + 6;
         const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tslot);
-        const int bstage = (lo ? 2 : 1) * BK_ROWS * 128;
+        const int bstage = (lo ? 2 : 1) * BK_ROWS * 128, nst = lo ? 2 : 4, lst = lo ? 1 : 2;
         bool tok = ok;
         for (int gi = 0; gi < gc; gi++) {
-            const int s = gi & 1;
-            if (gi >= 2 && !bk_wait(&mbar[s], ((gi >> 1) - 1) & 1)) tok = false;
+            const int s = gi & (nst - 1);  // the stage of group gi - nst must have been read
+            if (gi >= nst && !bk_wait(&mbar[s], ((gi >> lst) - 1) & 1)) tok = false;
             uint8_t* A = smem + L.a + s * TC_A_BLOCK;
             uint8_t* Bs = smem + L.b + s * bstage;
             for (int e = tid; e < 8 * 32 * 4; e += BK_THREADS) {
@@ -474,23 +475,34 @@ __global__ void __launch_bounds__(BK_THREADS, 1)
             float av[8];
 #pragma unroll
             for (int j = 0; j < 8; j++) av[j] = 0.f;
-            for (int gi = 0; gi < gc; gi++) {
-                uint32_t v[8];
-                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
-                             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-                             : "r"(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(gi * 32 + cb * 8)));
+            // four groups' loads in flight per wait
+            for (int g4 = 0; g4 < gc; g4 += 4) {
+                uint32_t v[4][8];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    if (g4 + u >= gc) break;  // uniform over the warp
+                    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+                                 : "=r"(v[u][0]), "=r"(v[u][1]), "=r"(v[u][2]), "=r"(v[u][3]), "=r"(v[u][4]), "=r"(v[u][5]),
+                                   "=r"(v[u][6]), "=r"(v[u][7])
+                                 : "r"(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((g4 + u) * 32 + cb * 8)));
+                }
                 asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-                if constexpr (FMT == 16) {
 #pragma unroll
-                    for (int j = 0; j < 8; j++) av[j] += __uint_as_float(v[j]);
-                } else {
-                    const uint2 sc =
-                        *reinterpret_cast<const uint2*>(wbuf + ((size_t)tt * gmax + gi) * CB + (FMT == 4 ? 512 : 1024) + (rr & 7) * 8);
-                    const uint32_t sw = rr < 8 ? sc.x : sc.y;
-                    const float sf = __uint_as_float(sw << 16), bf = __uint_as_float(sw & 0xffff0000u);
-                    const float* ys = sYs + gi * BK_ROWS + cb * 8;
+                for (int u = 0; u < 4; u++) {
+                    const int gi = g4 + u;
+                    if (gi >= gc) break;
+                    if constexpr (FMT == 16) {
 #pragma unroll
-                    for (int j = 0; j < 8; j++) av[j] += sf * __uint_as_float(v[j]) + bf * ys[j];
+                        for (int j = 0; j < 8; j++) av[j] += __uint_as_float(v[u][j]);
+                    } else {
+                        const uint2 sc = *reinterpret_cast<const uint2*>(wbuf + ((size_t)tt * gmax + gi) * CB +
+                                                                         (FMT == 4 ? 512 : 1024) + (rr & 7) * 8);
+                        const uint32_t sw = rr < 8 ? sc.x : sc.y;
+                        const float sf = __uint_as_float(sw << 16), bf = __uint_as_float(sw & 0xffff0000u);
+                        const float* ys = sYs + gi * BK_ROWS + cb * 8;
+#pragma unroll
+                        for (int j = 0; j < 8; j++) av[j] += sf * __uint_as_float(v[u][j]) + bf * ys[j];
+                    }
                 }
             }
 #pragma unroll
@@ -604,7 +616,7 @@ inline BulkPlan bulk_plan(int ntiles, int K, int rows, int fmt, int sms, bool lo
 // at most 16 groups (one 32-column accumulator each in 512 tensor-memory
 // columns), one wave of CTAs; the cheapest by the same kind of latency model
 // (a pipelined step per group, cluster rounds). smem 0 when none fits.
-inline BulkPlan bulk_plan_tc(int ntiles, int K, int rows, int fmt, int sms, bool lo) {
+inline BulkPlan bulk_plan_tc(int ntiles, int K, int rows, int fmt, int sms, bool lo, bool force) {
     BulkPlan best;
     if (ntiles % 8) return best;
     const int ng = K / 64, cb = fmt == 4 ? 576 : (fmt == 8 ? 1088 : 2048), mb = ntiles / 8;
@@ -612,6 +624,7 @@ inline BulkPlan bulk_plan_tc(int ntiles, int K, int rows, int fmt, int sms, bool
     long best_cost = -1;
     for (int ks = std::max(1, (ng + 15) / 16); ks <= 8 && ks <= ng; ks++) {
         if ((long)mb * ks * rb > sms) break;
+        if (!force && (long)mb * ks * rb * 2 < sms) continue;  // fewer than half the SMs: the mma.sync variant wins
         BulkPlan p;
         p.ks = ks;
         p.nb = mb;
@@ -629,14 +642,17 @@ inline BulkPlan bulk_plan_tc(int ntiles, int K, int rows, int fmt, int sms, bool
     return best;
 }
 
-// MING_BULK_TC=1 (read at each launch, so at graph capture) puts 4/8-bit
-// weights in blocks of 128 features on tcgen05. Off by default: at the
-// decode shapes of this model the mma.sync variant is faster (the 128-feature
-// blocks leave 49-76 CTAs, and each K group costs a staging round and a
-// barrier before its MMA; 1.71 vs 1.11 ms per batch-32 step).
-inline bool bulk_tc_enabled() {
+// MING_BULK_TC=1 (read at each launch, so at graph capture) runs 4/8-bit
+// weights in blocks of 128 features on the tcgen05 variant wherever a plan
+// fits. Off by default: at this model's decode shapes the mma.sync variant is
+// faster — the 128-feature blocks leave too few CTAs (gate/up: 76 for 148
+// SMs) and each K group costs a staging round and a barrier. Measured per
+// batch-32 step: 1.11 ms mma.sync; 1.25 ms with gate/up alone on tcgen05
+// (4 stages, batched tensor-memory loads); 1.71 ms with every projection on
+// it (2 stages, one load per group).
+inline int bulk_tc_mode() {
     const char* v = getenv("MING_BULK_TC");
-    return v && v[0] == '1' && v[1] == 0;
+    return v && v[0] == '1' && v[1] == 0 ? 2 : 0;
 }
 
 template <int FMT, int PRO, bool TC, class Epi>
@@ -667,14 +683,14 @@ void launch_bulk_plan(const PackedW& W, const BulkIn& in, const Epi& e, int rows
 }
 
 // Launches the kernel; false when no plan fits (the caller takes another
-// path). With MING_BULK_TC=1, 4- and 8-bit weights in blocks of 128 features
-// run on tcgen05.
+// path).
 template <int FMT, int PRO, class Epi>
 bool launch_bulk(const PackedW& W, const BulkIn& in, const Epi& e, int rows, int sms, cudaStream_t s) {
     const bool lo = PRO == BK_RMS && in.nw;
     if constexpr (FMT != 16) {
-        if (PRO != BK_LNMOD && bulk_tc_enabled()) {
-            const BulkPlan p = bulk_plan_tc(W.ntiles, W.K, rows, FMT, sms, lo);
+        const int mode = bulk_tc_mode();
+        if (PRO != BK_LNMOD && mode) {
+            const BulkPlan p = bulk_plan_tc(W.ntiles, W.K, rows, FMT, sms, lo, mode == 2);
             if (p.smem) {
                 launch_bulk_plan<FMT, PRO, true>(W, in, e, rows, p, s);
                 return true;

@@ -205,22 +205,29 @@ def test_batched_decode_many_rows(cuda_ok, bits, B, gains):
     ctx.close()
 
 
-@pytest.mark.parametrize("bits,B", [(4, 20), (8, 12), (4, 40)])
-def test_batched_decode_tcgen05(cuda_ok, monkeypatch, bits, B):
-    """The decode-batch linear's tcgen05 variant (MING_BULK_TC=1: codes
-    dequantized into 128-byte-swizzled weight blocks, one tensor-memory
-    accumulator per K group, the group scale and bias in f32), gated like the
+@pytest.mark.parametrize("bits,B,gains", [(4, 20, False), (8, 12, False), (4, 40, False), (4, 12, True)])
+def test_batched_decode_tcgen05(cuda_ok, monkeypatch, bits, B, gains):
+    """The decode-batch linear's tcgen05 variant forced on every projection
+    (MING_BULK_TC=1: codes dequantized into 128-byte-swizzled weight blocks,
+    one tensor-memory accumulator per K group, the group scale and bias in
+    f32; `gains`: non-unit RMSNorm gains, two operand parts), gated like the
     mma.sync variant against the oracle."""
     monkeypatch.setenv("MING_BULK_TC", "1")
     layers = 2
     W = synth.lm_weights(seed=12, bits=bits, layers=layers, qscale=QS)
+    if gains:
+        g = np.random.default_rng(6)
+        for l in range(layers):
+            for n in ("input_layernorm", "post_attention_layernorm"):
+                v = g.uniform(0.5, 1.5, 896).astype(np.float32)
+                W[f"model.model.layers.{l}.{n}.weight"] = (v.view(np.uint32) >> 16).astype(np.uint16)
     ctx = make_ctx(W, bits, layers, max_ctx=256, max_pages=1024, max_batch=64, max_seqs=64)
     lm = O.Lm(W)
     lens = np.random.default_rng(B + 1).integers(1, 24, size=B).tolist()
     seqs, caches, gcaches, fcaches, xs = [], [], [], [], []
     for i, L in enumerate(lens):
         s = ctx.seq_alloc()
-        x = synth.normal_bf16(8, f"test.tc.{bits}.{B}.{i}", (L, 896))
+        x = synth.normal_bf16(8, f"test.tc.{bits}.{B}.{gains}.{i}", (L, 896))
         c, cg, cf = lm.new_cache(L + 2), lm.new_cache(L + 2), lm.new_cache(L + 2)
         got, _ = ctx.prefill(s, x)
         ro, _ = lm.forward(c, x)
