@@ -46,6 +46,9 @@ CONFIGS = {
             dit=True, batch=1, seed=1),
     41: dict(name="DiT adaLN flow head, 6x768, 4x64 latent patch, 10 Euler steps, CFG, batch 32 (BASELINE configs[3])",
              dit=True, batch=32, seed=1),
+    5: dict(name="LM+DiT loop: 4-bit LM batch 64, 2048-token prefill, then per step an LM decode step, the adaLN head "
+                 "(10 Euler steps, CFG) and the latent's 64->896 projection into the next LM input (BASELINE configs[4])",
+            bits=4, batch=64, prefill=2048, seed=0, loop=True),
 }
 
 
@@ -210,6 +213,8 @@ def run_ours(args, ws, rank, local):
     torch.cuda.set_device(local)
     if c.get("dit"):
         return run_dit(args, ws, rank, local)
+    if c.get("loop"):
+        return run_loop(args, ws, rank, local)
     ctx, seqs, lens, x_last, W = lm_workload(cfgid, local, args.steps, args.warmup)
     B = len(seqs)
     stream = torch.cuda.ExternalStream(ctx.stream, device=local)
@@ -396,6 +401,120 @@ def run_dit(args, ws, rank, local):
             "gpu_launches": launches * args.steps, "clocks": ck, "cpu_baseline": None}
 
 
+def run_loop(args, ws, rank, local):
+    """per step, one LM decode step of all B sequences,
+    the adaLN flow head on the step's hidden states (10 Euler steps, CFG) and
+    the latent's projection into the next LM input; every call on device
+    buffers in the timed region, one replica per GPU."""
+    import torch
+
+    import ming_b200 as M
+    from ming_b200 import synth
+    c = CONFIGS[args.config]
+    B, P = c["batch"], c["prefill"]
+    n_total = args.warmup + args.steps
+    max_ctx = ((P + n_total + 2 + 255) // 256) * 256
+    pages = B * ((P + n_total + 2 + 15) // 16) + 16
+    t0 = time.time()
+    Wl = synth.lm_weights(seed=c["seed"], bits=c["bits"], layers=24)
+    Wd = {**synth.ada_weights(seed=1), **synth.latent_proj_weights(seed=1)}
+    log(f"[bench] weights generated in {time.time() - t0:.1f}s")
+    cfg = M.default_cfg(weight_bits=c["bits"], dit_mode=M.DIT_ADALN, dit_hidden=768, dit_blocks=6, dit_heads=12,
+                        dit_ff=3072, dit_frames=4, dit_max_batch=B, agg_blocks=0, max_ctx=max_ctx, max_pages=pages,
+                        max_batch=B, max_seqs=B, max_prefill=512)
+    ctx = M.Context(cfg, device=local, weights={**Wl, **Wd})
+    t0 = time.time()
+    seqs, last = [], []
+    for b in range(B):
+        s_ = ctx.seq_alloc()
+        out, _ = ctx.prefill(s_, synth.normal_bf16(c["seed"], f"bench.loop.prompt.{b}", (P, 896)))
+        seqs.append(s_)
+        last.append(out[-1])
+    log(f"[bench] prefill of {B} x {P} tokens in {time.time() - t0:.1f}s")
+    dev = f"cuda:{local}"
+    xdev = torch.from_numpy(np.stack(last).view(np.int16).copy()).to(dev)
+    zdev = torch.empty((B, 896), dtype=torch.int16, device=dev)
+    stopdev = torch.empty((B,), dtype=torch.float32, device=dev)
+    ndev = torch.from_numpy(synth.normal_bf16(c["seed"], "bench.loop.noise", (B, 4, 64)).view(np.int16).copy()).to(dev)
+    ydev = torch.empty_like(ndev)
+    L_ = M.lib()
+    ids = (M.ctypes.c_int * B)(*seqs)
+    P_ = lambda t: M.ctypes.c_void_p(t.data_ptr())
+
+    def step():
+        M._check(L_.ming_cuda_lm_decode(ctx._h, B, ids, P_(xdev), P_(zdev), P_(stopdev), M.PTR_DEVICE))
+        M._check(L_.ming_cuda_cfm_sample(ctx._h, B, P_(zdev), None, P_(ndev), None, M.ctypes.c_float(2.0),
+                                         M.ctypes.c_float(0.0), P_(ydev), M.PTR_DEVICE))
+        M._check(L_.ming_cuda_aggregate(ctx._h, B, P_(ydev), P_(xdev), M.PTR_DEVICE))
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    lens_start = [ctx.seq_len(s_) for s_ in seqs]
+    stream = torch.cuda.ExternalStream(ctx.stream, device=local)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local)
+    dist_barrier(ws)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    profile_range(True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    ev1.synchronize()
+    profile_range(False)
+    dist_barrier(ws)
+    ck = clocks.stop()
+    ms_local = ev0.elapsed_time(ev1)
+    value, ms = aggregate_throughput(ms_local, B, args.steps, ws)
+    # algorithmic bytes per step: LM weights + every sequence's KV once, the
+    # head's weights once per Euler step, the projection
+    wl, _ = algorithmic_bytes_lm(Wl, lens_start, B)
+    kv = sum(12288 * (L + args.steps / 2.0 + 1) for L in lens_start)
+    step_bytes = wl + kv + 10 * synth.nbytes(synth.ada_weights(seed=1)) + synth.nbytes(synth.latent_proj_weights(seed=1))
+    hbm, tf, peak_kind = load_peaks()
+    achieved = step_bytes / (ms_local / args.steps / 1e3) / 1e9
+    # e2e: the same loop through the C ABI with pinned host buffers
+    hx = torch.from_numpy(np.stack(last).view(np.int16).copy()).pin_memory()
+    hz = torch.empty((B, 896), dtype=torch.int16).pin_memory()
+    hs = torch.empty((B,), dtype=torch.float32).pin_memory()
+    hn = torch.from_numpy(synth.normal_bf16(c["seed"], "bench.loop.noise", (B, 4, 64)).view(np.int16).copy()).pin_memory()
+    hy = torch.empty_like(hn).pin_memory()
+    for s_, L in zip(seqs, lens_start):
+        ctx.seq_truncate(s_, L)
+    dist_barrier(ws)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        M._check(L_.ming_cuda_lm_decode(ctx._h, B, ids, P_(hx), P_(hz), P_(hs), M.PTR_HOST))
+        M._check(L_.ming_cuda_cfm_sample(ctx._h, B, P_(hz), None, P_(hn), None, M.ctypes.c_float(2.0),
+                                         M.ctypes.c_float(0.0), P_(hy), M.PTR_HOST))
+        M._check(L_.ming_cuda_aggregate(ctx._h, B, P_(hy), P_(hx), M.PTR_HOST))
+    e2e_s = dist_max(time.perf_counter() - t0, ws)
+    # launches per step: the decode graph, the head (bench formula of run_dit), the projection (mean + linear)
+    R, NC = 8 * B, 2 * B
+    lin = lambda rows, small=64: 1 if rows <= small else 2
+    dit_launches = (lin(NC) + 10 + 7 * lin(10 * NC) + 10 * (lin(R, 8) + 6 * (4 * lin(R) + 1) + lin(R) + 1))
+    launches = ctx.step_kernels(B) + dit_launches + 2
+    ctx.close()
+    return {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 act / u4-g64 LM weights, bf16 head, f32 acc",
+            "data": "synthetic (seeded random-init weights and N(0,1) embeddings, SplitMix64/Box-Muller)",
+            "config": {"workload": c["name"], "batch_per_gpu": B, "prompt_len": P, "kv_positions_at_start": lens_start[0],
+                       "token": "one LM decode step of one sequence plus its 10-step flow-head sample and projection",
+                       "parallelism": f"replicas x{ws} (no collective)",
+                       "l2": "inputs larger than L2: every step streams all weights and the KV cache from HBM"},
+            "roofline": {"bound": "hbm", "kernel": "LM decode graph + flow head + projection per step",
+                         "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_step": step_bytes, "traffic": None},
+            "e2e": {"value": ws * B * args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * 896 * 2 + B * 4 * 64 * 2 * 2,
+                    "d2h_bytes_per_step": B * 896 * 2 * 2 + B * 4 + B * 4 * 64 * 2,
+                    "api": "ming_cuda_lm_decode + ming_cuda_cfm_sample + ming_cuda_aggregate (pinned host buffers)"},
+            "gpu_launches": launches * args.steps, "clocks": ck, "cpu_baseline": None}
+
+
 def run_reference(args, ws, rank, local):
     """The reference's CPU path restated (oracle port, all host threads)."""
     if rank != 0:
@@ -407,8 +526,8 @@ def run_reference(args, ws, rank, local):
     O.set_threads(len(os.sched_getaffinity(0)))
     cfgid = args.config
     c = CONFIGS[cfgid]
-    if c.get("dit"):
-        return {"impl": "reference", "unavailable": "reference arm implemented for the LM configs only"}
+    if c.get("dit") or c.get("loop"):
+        return {"impl": "reference", "unavailable": "reference arm implemented for the LM-only configs"}
     B = c["batch"]
     lens = [c["prefill"]] * B if c["prefill"] else np.random.default_rng(c["seed"]).integers(32, 513, size=B).tolist()
     W = synth.lm_weights(seed=c["seed"], bits=c["bits"], layers=24)

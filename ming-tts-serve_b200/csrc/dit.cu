@@ -133,4 +133,19 @@ void launch_ada_euler(const float* vel, uint16_t* y, const uint16_t* sde, int st
     ada_euler_kernel<<<(B * F * latent + 255) / 256, 256, 0, s>>>(vel, y, sde, step, dtv, sqv, cfg, shift, B, F, latent);
 }
 
+// adaLN head's latent path: out[b] = rb(mean over f of lat[b][f]) in f32,
+// frames summed in order.
+__global__ void latent_mean_kernel(const uint16_t* lat, uint16_t* out, int B, int F, int LAT) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * LAT) return;
+    const int b = i / LAT, k = i - b * LAT;
+    float s = 0.f;
+    for (int f = 0; f < F; f++) s += bf2f(lat[((size_t)b * F + f) * LAT + k]);
+    out[i] = f2bf(s / (float)F);
+}
+
+void launch_latent_mean(const uint16_t* lat, uint16_t* out, int B, int F, int LAT, cudaStream_t s) {
+    latent_mean_kernel<<<(B * LAT + 255) / 256, 256, 0, s>>>(lat, out, B, F, LAT);
+}
+
 }  // namespace ming

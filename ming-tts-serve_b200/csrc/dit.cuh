@@ -88,6 +88,8 @@ void launch_tok_final(const uint16_t* x, const uint16_t* nw, const uint16_t* wf,
                       cudaStream_t s);
 // adaLN: c = rb(te + ce); sc = silu chain. [2B][H]
 void launch_ada_cond(const uint16_t* te_step, const uint16_t* ce, uint16_t* sc, int NC, int H, cudaStream_t s);
+// adaLN latent path: out [B][latent] = rb(mean over the F frames of lat [B][F][latent]).
+void launch_latent_mean(const uint16_t* lat, uint16_t* out, int B, int F, int LAT, cudaStream_t s);
 // CFG + Euler on velocities vel [2B*F][latent] (f32 unrounded linear outputs).
 void launch_ada_euler(const float* vel, uint16_t* y, const uint16_t* sde, int step, float dtv, float sqv, float cfg,
                       float shift, int B, int F, int latent, cudaStream_t s);

@@ -174,6 +174,10 @@ struct ming_ctx {
     // aggregator
     std::vector<DitBlockW> agg;
     PackedLin agg_x_emb, agg_final;
+    // adaLN head: latent -> next LM input (mean over frames, then aggregator.proj)
+    PackedLin agg_proj;
+    bool agg_proj_on = false;
+    uint16_t* a_mean = nullptr;
     uint16_t* agg_cls = nullptr;
     uint16_t* agg_norm = nullptr;
     float* agg_inv_freq = nullptr;
@@ -1205,6 +1209,22 @@ int ming_cuda_finalize(ming_ctx* c) {
         c->a_out = c->mem.alloc<uint16_t>((size_t)MB * f.hidden, &rc);
         if (rc) return rc;
     }
+    // ---- adaLN head: the latent's path into the next LM input, when the
+    //      checkpoint has it (mean of the patch's frames, then a linear
+    //      latent -> hidden; no reference code, the choice is pinned here) ----
+    if (f.dit_mode == MING_DIT_ADALN && c->staged.count("aggregator.proj.weight")) {
+        const int MB = f.dit_max_batch;
+        int od = 0;
+        if ((rc = pack_plain(c, "aggregator.proj", true, c->agg_proj, &od))) return rc;
+        if (c->agg_proj.w.K != f.dit_latent || od != f.hidden)
+            return fail(MING_ERR_INVALID, "aggregator.proj must be [hidden, dit_latent]");
+        rc = MING_OK;
+        c->a_lat = c->mem.alloc<uint16_t>((size_t)MB * f.dit_frames * f.dit_latent, &rc);
+        c->a_mean = c->mem.alloc<uint16_t>((size_t)MB * f.dit_latent, &rc);
+        c->a_out = c->mem.alloc<uint16_t>((size_t)MB * f.hidden, &rc);
+        if (rc) return rc;
+        c->agg_proj_on = true;
+    }
     {
         // staging scratch of the many-row linears: every (rows, K) a linear of
         // this context can see; larger calls fall back to in-kernel staging
@@ -1457,6 +1477,22 @@ int ming_cuda_cfm_sample(ming_ctx* c, int B, const uint16_t* z, const uint16_t* 
 int ming_cuda_aggregate(ming_ctx* c, int B, const uint16_t* latent, uint16_t* out, int kind) {
     if (!c || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
     const ming_cfg& f = c->cfg;
+    if (c->agg_proj_on) {
+        // adaLN head: latent [B][dit_frames][dit_latent] -> [B][hidden]
+        if (B < 1 || B > f.dit_max_batch || !latent || !out) return fail(MING_ERR_INVALID, "bad argument");
+        CK(cudaSetDevice(c->device));
+        const int F = f.dit_frames, LAT = f.dit_latent;
+        cudaStream_t s = c->stream;
+        int rc;
+        if ((rc = copy_in(c, c->a_lat, latent, (size_t)B * F * LAT * 2, kind))) return rc;
+        launch_latent_mean(c->a_lat, c->a_mean, B, F, LAT, s);
+        run_linear(c, c->agg_proj.w, ProPlain{c->a_mean, LAT, 0},
+                   EpiAct{c->a_out, nullptr, c->agg_proj.w.bias, f.hidden, 0, f.hidden}, B, s);
+        CK(cudaGetLastError());
+        if ((rc = copy_out(c, out, c->a_out, (size_t)B * f.hidden * 2, kind))) return rc;
+        if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(s));
+        return MING_OK;
+    }
     if (c->agg.empty()) return fail(MING_ERR_INVALID, "no aggregator configured");
     if (B < 1 || B > f.dit_max_batch || !latent || !out) return fail(MING_ERR_INVALID, "bad argument");
     CK(cudaSetDevice(c->device));

@@ -252,5 +252,13 @@ def ada_weights(seed=1, blocks=6, hidden=768, ff=3072, latent=64, cond=896, freq
     return W
 
 
+def latent_proj_weights(seed=1, latent=64, hidden=896, std=0.02):
+    """The adaLN head's latent -> next LM input linear (BASELINE config 5's
+    64 -> 896 projection) under aggregator.proj."""
+    W = {}
+    _lin(W, seed, "aggregator.proj", hidden, latent, std)
+    return W
+
+
 def nbytes(weights):
     return sum(v.nbytes for v in weights.values())

@@ -356,3 +356,26 @@ def pack(codes, bits):
     words = np.empty((rows, cols * bits // 32), dtype=np.uint32)
     lib().mo_pack(codes.ctypes.data_as(ctypes.POINTER(ctypes.c_uint8)), rows, cols, bits, _p(words, U32P))
     return words
+
+
+def ada_latent_proj(W, latent):
+    """The adaLN head's latent path into the next LM input (
+    a 64 -> 896 linear; no reference code, choice pinned with the product):
+    the mean of the patch's frames in f32, frames in order, rounded to bf16;
+    then aggregator.proj as an f32 dot plus bias, rounded to bf16.
+    latent: uint16 bf16 [B][F][64] -> uint16 [B][896]."""
+    def f32(h):
+        return (np.asarray(h, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+    def bf(x):
+        u = np.asarray(x, np.float32).view(np.uint32).astype(np.uint64)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+    lat = f32(latent)
+    s = np.zeros(lat.shape[::2], np.float32)
+    for f in range(lat.shape[1]):
+        s = s + lat[:, f, :]
+    m = f32(bf(s / np.float32(lat.shape[1])))
+    w = f32(W["aggregator.proj.weight"]).astype(np.float64)
+    b = f32(W["aggregator.proj.bias"]).astype(np.float64)
+    return bf((m.astype(np.float64) @ w.T + b).astype(np.float32))

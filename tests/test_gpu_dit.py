@@ -33,7 +33,7 @@ def token_head(cuda_ok):
 
 @pytest.fixture(scope="module")
 def ada_head(cuda_ok):
-    W = synth.ada_weights(seed=1)
+    W = {**synth.ada_weights(seed=1), **synth.latent_proj_weights(seed=1)}
     cfg = M.default_cfg(layers=0, dit_mode=M.DIT_ADALN, dit_hidden=768, dit_blocks=6, dit_heads=12, dit_ff=3072,
                         dit_frames=4, dit_max_batch=32, agg_blocks=0)
     ctx = M.Context(cfg, weights=W)
@@ -115,3 +115,17 @@ def test_cfm_adaln_parity(ada_head, B):
     ref = a.sample(z, noise)
     d, c, ok = close(got.reshape(B * 4, 64), ref.reshape(B * 4, 64), tol=0.2)
     assert ok, ("sample", d, c)
+
+
+@pytest.mark.parametrize("B", [1, 5, 32])
+def test_ada_latent_proj_parity(ada_head, B):
+    """adaLN mode's aggregate: the latent patch [B][4][64] -> the next LM input
+    [B][896] (mean over the frames, then aggregator.proj; BASELINE config 5's
+    64 -> 896 linear), against the oracle's restatement, twice in a row."""
+    W, ctx = ada_head
+    lat = synth.normal_bf16(14, f"ada.lat.{B}", (B, 4, 64))
+    ref = O.ada_latent_proj(W, lat)
+    for _ in range(2):
+        got = ctx.aggregate(lat)
+        d, c, ok = close(got, ref)
+        assert ok, (d, c)
