@@ -401,6 +401,17 @@ struct ProPlain {
     int r0;
     MING_DEV void init(int r0_, int, float*) { r0 = r0_; }
     MING_DEV float y(int row, int k) const { return bf2f(x[(size_t)(r0 + row) * ld + k]); }
+    // y(row, k..k+7) with one 16-byte load (k % 8 == 0, ld % 8 == 0)
+    MING_DEV void y8(int row, int k, float (&y)[8]) const {
+        const uint4 v = *reinterpret_cast<const uint4*>(x + (size_t)(r0 + row) * ld + k);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 f = unpack_bf16x2(w[i]);
+            y[2 * i] = f.x;
+            y[2 * i + 1] = f.y;
+        }
+    }
     MING_DEV float post(int) const { return 1.f; }
 };
 
@@ -490,11 +501,28 @@ struct ProLnMod {
         const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
         for (int r = warp; r < nrows; r += LIN_WARPS) {
             const uint16_t* xr = x + (size_t)(r0 + r) * ld;
-            float s = 0.f;
-            for (int k = lane; k < K; k += 32) s += bf2f(xr[k]);
-            const float mu = warp_sum(s) / (float)K;
-            float v = 0.f;
-            for (int k = lane; k < K; k += 32) { const float d = bf2f(xr[k]) - mu; v += d * d; }
+            float s = 0.f, v = 0.f, mu;
+            if (K <= 1024) {
+                // the lane's values held in registers, all loads in flight at
+                // once; same summation order as the loops below
+                float xv[32];
+#pragma unroll
+                for (int i = 0; i < 32; i++) xv[i] = lane + 32 * i < K ? bf2f(xr[lane + 32 * i]) : 0.f;
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    if (lane + 32 * i < K) s += xv[i];
+                mu = warp_sum(s) / (float)K;
+#pragma unroll
+                for (int i = 0; i < 32; i++)
+                    if (lane + 32 * i < K) {
+                        const float d = xv[i] - mu;
+                        v += d * d;
+                    }
+            } else {
+                for (int k = lane; k < K; k += 32) s += bf2f(xr[k]);
+                mu = warp_sum(s) / (float)K;
+                for (int k = lane; k < K; k += 32) { const float d = bf2f(xr[k]) - mu; v += d * d; }
+            }
             v = warp_sum(v) / (float)K;
             if (lane == 0) { aux[2 * r] = mu; aux[2 * r + 1] = rsqrtf(v + 1e-6f); }
         }
@@ -503,6 +531,28 @@ struct ProLnMod {
         const int ar = r0 + row, c = ar / rows_per_cond;
         const float n = (bf2f(x[(size_t)ar * ld + k]) - st[2 * row]) * st[2 * row + 1];
         return rb(n * (1.0f + bf2f(scale[(size_t)c * mod_ld + k])) + bf2f(shift[(size_t)c * mod_ld + k]));
+    }
+    // y(row, k..k+7) from three 16-byte loads (k % 8 == 0; ld, mod_ld % 8 == 0
+    // and 16-byte aligned modulation rows), each value as y() computes it
+    MING_DEV void y8(int row, int k, float (&y)[8]) const {
+        const int ar = r0 + row, c = ar / rows_per_cond;
+        const uint4 xv = *reinterpret_cast<const uint4*>(x + (size_t)ar * ld + k);
+        const uint4 sc = *reinterpret_cast<const uint4*>(scale + (size_t)c * mod_ld + k);
+        const uint4 sh = *reinterpret_cast<const uint4*>(shift + (size_t)c * mod_ld + k);
+        const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w}, cw[4] = {sc.x, sc.y, sc.z, sc.w}, hw[4] = {sh.x, sh.y, sh.z, sh.w};
+        const float mu = st[2 * row], inv = st[2 * row + 1];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float2 f = unpack_bf16x2(xw[i]), s2 = unpack_bf16x2(cw[i]), h2 = unpack_bf16x2(hw[i]);
+            const float n0 = (f.x - mu) * inv, n1 = (f.y - mu) * inv;
+            y[2 * i] = rb(n0 * (1.0f + s2.x) + h2.x);
+            y[2 * i + 1] = rb(n1 * (1.0f + s2.y) + h2.y);
+        }
+    }
+    // the vector path needs these alignments
+    MING_DEV bool y8_ok() const {
+        return ld % 8 == 0 && mod_ld % 8 == 0 && ((uintptr_t)scale & 15) == 0 && ((uintptr_t)shift & 15) == 0 &&
+               ((uintptr_t)x & 15) == 0;
     }
     MING_DEV float post(int) const { return 1.f; }
 };

@@ -22,6 +22,8 @@
 // descriptor layouts (CUTLASS 4, cute/arch/mma_sm100_desc.hpp).
 #pragma once
 
+#include <type_traits>
+
 #include "linear.cuh"
 
 namespace ming {
@@ -108,11 +110,22 @@ __global__ void __launch_bounds__(LIN_THREADS) stage_rows_kernel(Pro pro, int ro
     __syncthreads();
     // one 16-byte swizzled chunk (8 consecutive k of a row) per item: the 8
     // prologue values are independent, then one store
+    bool vec = false;  // the prologue's 16-byte path (ProPlain, ProLnMod) when the layout allows it
+    if constexpr (std::is_same_v<Pro, ProPlain>) vec = p.ld % 8 == 0 && ((uintptr_t)p.x & 15) == 0;
+    else if constexpr (std::is_same_v<Pro, ProLnMod>) vec = p.y8_ok();
     for (int e = threadIdx.x; e < nrows * (kcl / 8); e += LIN_THREADS) {
         const int row = e / (kcl / 8), k = kc + 8 * (e % (kcl / 8)), n = r0 + row;
         float y[8];
+        if constexpr (std::is_same_v<Pro, ProPlain> || std::is_same_v<Pro, ProLnMod>) {
+            if (vec) p.y8(row, k, y);
+            else {
 #pragma unroll
-        for (int u = 0; u < 8; u++) y[u] = p.y(row, k + u);
+                for (int u = 0; u < 8; u++) y[u] = p.y(row, k + u);
+            }
+        } else {
+#pragma unroll
+            for (int u = 0; u < 8; u++) y[u] = p.y(row, k + u);
+        }
         uint8_t* blk = xs + ((size_t)(n / N) * ng + k / 64) * (N * 128);
         *reinterpret_cast<uint4*>(blk + tc_sw128(n % N, (k & 63) >> 3)) =
             make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
