@@ -239,29 +239,49 @@ void launch_lin_staged(const PackedW& W, const LinScratch& sc, const Pro& p, con
 }
 
 template <int N, class Pro, class Epi>
-void launch_tc_n(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
+void launch_tc_n(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& e, int rows, int ks, cudaStream_t s) {
     static unsigned attr_devices = 0;  // bit d: attribute set on device d
     int dev = 0;
     cudaGetDevice(&dev);
+    constexpr int smax = N <= 128 ? TcSmem<N>::TOTAL_KS : TcSmem<N>::TOTAL;
     if (!(attr_devices & (1u << (dev & 31)))) {
-        cudaFuncSetAttribute(tc_linear_kernel<N, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, TcSmem<N>::TOTAL);
+        cudaFuncSetAttribute(tc_linear_kernel<N, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax);
         attr_devices |= 1u << (dev & 31);
     }
+    if (N > 128) ks = 1;  // no room for the partial sums beside the 256-row stages
     uint8_t* xs = reinterpret_cast<uint8_t*>(sc.frag);
     stage_rows_kernel<N, Pro><<<dim3((rows + 7) / 8, (W.K + STAGE_KC - 1) / STAGE_KC), LIN_THREADS, 0, s>>>(p, rows, W.K, xs,
                                                                                                          sc.post);
-    tc_linear_kernel<N, Epi><<<dim3(W.ntiles / 8, (rows + N - 1) / N), TC_THREADS, TcSmem<N>::TOTAL, s>>>(W.tc, W.K, xs,
-                                                                                                        sc.post, e, rows);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(W.ntiles / 8 * ks), (unsigned)((rows + N - 1) / N));
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = ks > 1 ? (size_t)TcSmem<N>::TOTAL_KS : (size_t)TcSmem<N>::TOTAL;
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = (unsigned)ks;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = ks > 1 ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, tc_linear_kernel<N, Epi>, W.tc, W.K, (const uint8_t*)xs, (const float*)sc.post, e, rows, ks);
 }
 
 // bf16 weights, 64+ rows: the tcgen05 linear with the widest row block that
-// still gives ~96 CTAs.
+// still gives ~96 CTAs; when even 64-row blocks leave fewer than half the SMs
+// a CTA, the K groups are split over a cluster of up to 8 CTAs (at least 12
+// groups each).
 template <class Pro, class Epi>
 void launch_tc(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
     const int mt = W.ntiles / 8;
-    if (mt * ((rows + 255) / 256) >= 96) launch_tc_n<256>(W, sc, p, e, rows, s);
-    else if (mt * ((rows + 127) / 128) >= 96) launch_tc_n<128>(W, sc, p, e, rows, s);
-    else launch_tc_n<64>(W, sc, p, e, rows, s);
+    if (mt * ((rows + 255) / 256) >= 96) launch_tc_n<256>(W, sc, p, e, rows, 1, s);
+    else if (mt * ((rows + 127) / 128) >= 96) launch_tc_n<128>(W, sc, p, e, rows, 1, s);
+    else {
+        const int ctas = mt * ((rows + 63) / 64);
+        int ks = 1;
+        if (2 * ctas <= sc.sms) ks = std::max(1, std::min({8, sc.sms / ctas, W.K / 64 / 12}));
+        launch_tc_n<64>(W, sc, p, e, rows, ks, s);
+    }
 }
 
 bool bulk_enabled() {

@@ -22,6 +22,7 @@
 // descriptor layouts (CUTLASS 4, cute/arch/mma_sm100_desc.hpp).
 #pragma once
 
+#include <cooperative_groups.h>
 #include <type_traits>
 
 #include "linear.cuh"
@@ -39,6 +40,8 @@ struct TcSmem {
     static constexpr int B_BYTES = N * 128;  // N rows x 64 bf16
     static constexpr int STAGE = A_BYTES + B_BYTES;
     static constexpr int TOTAL = 1024 + TC_STAGES * STAGE + 128;  // alignment slack, stages, barriers + tmem slot
+    static constexpr int PART = TC_M * N * 4;                    // K split: this rank's f32 partial sums
+    static constexpr int TOTAL_KS = TOTAL + PART;
 };
 
 // Byte offset of 16-byte chunk c (0..7) of row r in a 128-byte-swizzled
@@ -133,11 +136,15 @@ __global__ void __launch_bounds__(LIN_THREADS) stage_rows_kernel(Pro pro, int ro
     if (blockIdx.y == 0 && threadIdx.x < nrows) post[r0 + threadIdx.x] = p.post(threadIdx.x);
 }
 
-// Grid: x = block of 8 packed tiles (128 features), y = block of N rows.
+// Grid: x = block of 8 packed tiles (128 features) * nks + K rank, y = block
+// of N rows. nks > 1: the K groups are split over a thread-block cluster of
+// nks CTAs; each rank's accumulator goes to shared memory and the ranks' sums
+// meet over distributed shared memory in rank order (deterministic), the
+// ranks splitting the epilogue.
 // Thread 0 produces, thread 32 issues the MMAs, all 16 warps run the epilogue.
 template <int N, class Epi>
 __global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(const uint8_t* wtc, int K, const uint8_t* xs, const float* post,
-                                                               Epi epi, int rows) {
+                                                               Epi epi, int rows, int nks) {
     using S = TcSmem<N>;
     extern __shared__ __align__(16) uint8_t tc_smem_raw[];
     // 1024-byte aligned base: the swizzle atoms are anchored at 1024 bytes
@@ -147,8 +154,11 @@ __global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(const uint8_t* wt
     uint64_t* empty = full + TC_STAGES;                                          // [TC_STAGES]
     uint64_t* done = empty + TC_STAGES;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+    float* part = reinterpret_cast<float*>(smem + S::TOTAL - 1024);  // nks > 1: [128 features][N rows]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int mt = blockIdx.x, nt = blockIdx.y, n0 = nt * N, ng = K / 64;
+    const int mt = blockIdx.x / nks, rank = blockIdx.x % nks, nt = blockIdx.y, n0 = nt * N, ngt = K / 64;
+    // this rank's K groups [gb, gb + ng)
+    const int gb = rank * ngt / nks, ng = (rank + 1) * ngt / nks - gb;
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(tc_saddr(tmem_slot)), "r"(N)
                      : "memory");
@@ -170,8 +180,8 @@ __global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(const uint8_t* wt
     // those warps park at __syncwarp instead of spinning beside them
     if (tid == 0) {
         // producer: the weight block and the activation block of each K group
-        const uint8_t* wa = wtc + (size_t)mt * ng * S::A_BYTES;
-        const uint8_t* xb = xs + (size_t)nt * ng * S::B_BYTES;
+        const uint8_t* wa = wtc + ((size_t)mt * ngt + gb) * S::A_BYTES;
+        const uint8_t* xb = xs + ((size_t)nt * ngt + gb) * S::B_BYTES;
         for (int g = 0; g < ng; g++) {
             const int s = g % TC_STAGES;
             if (g >= TC_STAGES && !tc_mbar_wait(&empty[s], ((g / TC_STAGES) - 1) & 1)) break;
@@ -224,6 +234,44 @@ __global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(const uint8_t* wt
     // one shuffle.
     const int quarter = warp & 3, m = quarter * 32 + lane, hi_lane = lane & 8;
     const int cbeg = (warp >> 2) * (N / 4), cend = cbeg + N / 4;
+    if (nks > 1) {
+        // this rank's partial sums -> shared memory [m][n]
+        for (int c0 = cbeg; c0 < cend; c0 += 16) {
+            uint32_t v[16];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+                  "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+                : "r"(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0));
+            asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+#pragma unroll
+            for (int j = 0; j < 16; j++) part[m * N + c0 + j] = __uint_as_float(v[j]);
+        }
+        // tensor memory back before the cluster barrier (ranks on one SM never wait on each other's columns)
+        asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
+        __syncthreads();
+        if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(N) : "memory");
+        namespace cg = cooperative_groups;
+        cg::cluster_group cl = cg::this_cluster();
+        cl.sync();
+        // rank r: every ks-th (tile, tile row r8, row n); the ranks' sums in rank order
+        for (int e = rank * TC_THREADS + tid; e < 8 * 8 * N; e += nks * TC_THREADS) {
+            const int t = e / (8 * N), rem = e - t * 8 * N, r8 = rem / N, n = rem - r8 * N;
+            if (n0 + n >= rows) continue;
+            float lo = 0.f, hi = 0.f;
+            for (int q = 0; q < nks; q++) {
+                const float* pq = cl.map_shared_rank(part, q);
+                lo += pq[(t * 16 + r8) * N + n];
+                hi += pq[(t * 16 + r8 + 8) * N + n];
+            }
+            if (ok) {
+                const float ps = post[n0 + n];
+                epi(mt * 8 + t, r8, n0 + n, lo * ps, hi * ps);
+            }
+        }
+        cl.sync();  // peers may still be reading this CTA's partials
+        return;
+    }
     for (int c0 = cbeg; c0 < cend; c0 += 16) {
         uint32_t v[16];
         asm volatile(
