@@ -250,20 +250,31 @@ void launch_tc_n(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi
     }
     if (N > 128) ks = 1;  // no room for the partial sums beside the 256-row stages
     uint8_t* xs = reinterpret_cast<uint8_t*>(sc.frag);
-    stage_rows_kernel<N, Pro><<<dim3((rows + 7) / 8, (W.K + STAGE_KC - 1) / STAGE_KC), LIN_THREADS, 0, s>>>(p, rows, W.K, xs,
-                                                                                                         sc.post);
+    cudaLaunchAttribute pdl[1];
+    pdl[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pdl[0].val.programmaticStreamSerializationAllowed = 1;
+    {
+        cudaLaunchConfig_t sg = {};
+        sg.gridDim = dim3((rows + 7) / 8, (W.K + STAGE_KC - 1) / STAGE_KC);
+        sg.blockDim = dim3(LIN_THREADS);
+        sg.stream = s;
+        sg.attrs = pdl;
+        sg.numAttrs = 1;
+        cudaLaunchKernelEx(&sg, stage_rows_kernel<N, Pro>, p, rows, (int)W.K, xs, (float*)sc.post);
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(W.ntiles / 8 * ks), (unsigned)((rows + N - 1) / N));
     cfg.blockDim = dim3(TC_THREADS);
     cfg.dynamicSmemBytes = ks > 1 ? (size_t)TcSmem<N>::TOTAL_KS : (size_t)TcSmem<N>::TOTAL;
     cfg.stream = s;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = (unsigned)ks;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute at[2];
+    at[0] = pdl[0];
+    at[1].id = cudaLaunchAttributeClusterDimension;
+    at[1].val.clusterDim.x = (unsigned)ks;
+    at[1].val.clusterDim.y = 1;
+    at[1].val.clusterDim.z = 1;
     cfg.attrs = at;
-    cfg.numAttrs = ks > 1 ? 1 : 0;
+    cfg.numAttrs = ks > 1 ? 2 : 1;
     cudaLaunchKernelEx(&cfg, tc_linear_kernel<N, Epi>, W.tc, W.K, (const uint8_t*)xs, (const float*)sc.post, e, rows, ks);
 }
 

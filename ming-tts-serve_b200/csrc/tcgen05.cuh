@@ -108,6 +108,10 @@ __global__ void __launch_bounds__(LIN_THREADS) stage_rows_kernel(Pro pro, int ro
     __shared__ float aux[8 * 32];
     const int r0 = blockIdx.x * 8, nrows = min(8, rows - r0);
     const int kc = blockIdx.y * STAGE_KC, kcl = min(STAGE_KC, K - kc), ng = K / 64;
+    // the rows are the previous kernel's output; the linear that reads this
+    // kernel's blocks may launch and fetch its weights meanwhile
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     Pro p = pro;
     p.init(r0, nrows, aux);
     __syncthreads();
@@ -179,20 +183,37 @@ __global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(const uint8_t* wt
     // warp 0 lane 0 produces, warp 1 lane 0 issues the MMAs; the other lanes of
     // those warps park at __syncwarp instead of spinning beside them
     if (tid == 0) {
-        // producer: the weight block and the activation block of each K group
+        // producer: the weight block and the activation block of each K group.
+        // The first stages' weight blocks go out before the wait on the
+        // previous kernel (the launch is its programmatic dependent; weights
+        // do not depend on it), their activation blocks after it.
         const uint8_t* wa = wtc + ((size_t)mt * ngt + gb) * S::A_BYTES;
         const uint8_t* xb = xs + ((size_t)nt * ngt + gb) * S::B_BYTES;
-        for (int g = 0; g < ng; g++) {
-            const int s = g % TC_STAGES;
-            if (g >= TC_STAGES && !tc_mbar_wait(&empty[s], ((g / TC_STAGES) - 1) & 1)) break;
-            uint8_t* sA = smem + s * S::STAGE;
-            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(tc_saddr(&full[s])),
+        const int pre = ng < TC_STAGES ? ng : TC_STAGES;
+        for (int g = 0; g < pre; g++) {
+            uint8_t* sA = smem + g * S::STAGE;
+            asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(tc_saddr(&full[g])),
                          "r"((uint32_t)S::STAGE)
                          : "memory");
             asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
                              tc_saddr(sA)),
-                         "l"(wa + (size_t)g * S::A_BYTES), "r"((uint32_t)S::A_BYTES), "r"(tc_saddr(&full[s]))
+                         "l"(wa + (size_t)g * S::A_BYTES), "r"((uint32_t)S::A_BYTES), "r"(tc_saddr(&full[g]))
                          : "memory");
+        }
+        asm volatile("griddepcontrol.wait;\n" ::: "memory");
+        for (int g = 0; g < ng; g++) {
+            const int s = g % TC_STAGES;
+            uint8_t* sA = smem + s * S::STAGE;
+            if (g >= pre) {
+                if (!tc_mbar_wait(&empty[s], ((g / TC_STAGES) - 1) & 1)) break;
+                asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(tc_saddr(&full[s])),
+                             "r"((uint32_t)S::STAGE)
+                             : "memory");
+                asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                                 tc_saddr(sA)),
+                             "l"(wa + (size_t)g * S::A_BYTES), "r"((uint32_t)S::A_BYTES), "r"(tc_saddr(&full[s]))
+                             : "memory");
+            }
             asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
                              tc_saddr(sA + S::A_BYTES)),
                          "l"(xb + (size_t)g * S::B_BYTES), "r"((uint32_t)S::B_BYTES), "r"(tc_saddr(&full[s]))
@@ -225,7 +246,10 @@ __global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(const uint8_t* wt
                      : "memory");
     }
     if (warp < 2) __syncwarp();
+    // the epilogue reads the row scales and residuals the previous kernels wrote
+    if (tid != 0) asm volatile("griddepcontrol.wait;\n" ::: "memory");
     const bool ok = tc_mbar_wait(done, 0);
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
     // epilogue: warp w reads features m = 32 (w % 4) + lane (its tensor-memory
     // lane quarter) for rows [q N / 4, (q + 1) N / 4), q = w / 4. Feature pairs
