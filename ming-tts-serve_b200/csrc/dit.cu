@@ -9,6 +9,10 @@ namespace ming {
 // One warp per (row, head): scores against the L rows of the row's sequence,
 // two-pass softmax, P.V, rounded (kernel A's attention tail, scale 1/8).
 __global__ void dit_attention_kernel(const uint16_t* qkv, uint16_t* out, int rows, int L, int H, int heads) {
+    // a programmatic dependent: q|k|v come from the previous kernel; the
+    // next linear may launch and fetch its weights while this one runs
+    asm volatile("griddepcontrol.wait;\n" ::: "memory");
+    asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (w >= rows * heads) return;
     const int row = w / heads, h = w % heads, base = (row / L) * L;
@@ -38,7 +42,16 @@ __global__ void dit_attention_kernel(const uint16_t* qkv, uint16_t* out, int row
 
 void launch_dit_attention(const uint16_t* qkv, uint16_t* out, int rows, int L, int H, int heads, cudaStream_t s) {
     const int warps = rows * heads;
-    dit_attention_kernel<<<(warps + 3) / 4, 128, 0, s>>>(qkv, out, rows, L, H, heads);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((warps + 3) / 4);
+    cfg.blockDim = dim3(128);
+    cfg.stream = s;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, dit_attention_kernel, qkv, out, rows, L, H, heads);
 }
 
 // Rows per sequence b: [cond: t+c, hist, y | uncond: t+c0, hist, y], the
