@@ -253,6 +253,7 @@ struct Misc {              // small per-CTA state in shared memory
     float rc[MG_MAXB][HD / 2];           // RoPE cos/sin of each row's position, per frequency
     float rs[MG_MAXB][HD / 2];
     int fail;
+    int last;  // this CTA's attention chunk was the last of its (row, head)
     int prod_done;
     int issued;
     uint32_t epoch;
@@ -693,72 +694,71 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         uint64_t* o = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
         str64(o + 2 + 2 * lane, tagged(tag, ox));
         str64(o + 3 + 2 * lane, tagged(tag, oy));
+        __threadfence();
     }
     cbar();
+    // 7. arrival count of the (row, head): the last of its chunks to finish
+    //    combines them all, o = sum_s acc_s e^(m_s - M) / L (the partials are
+    //    tagged, so one not yet visible is polled), and publishes the 64
+    //    values for every o_proj CTA that reads this head
+    const int ns = (pos + MG_ATT_CH) / MG_ATT_CH;
+    if (tid == 0) {
+        unsigned long long* cnt = acc_ptr(a, ms->epoch, l, MG_ACC_CNT) + (size_t)b * a.acc_w + h;
+        ms->last = atomicAdd(cnt, 1ull) == (unsigned long long)(ns - 1) ? 1 : 0;
+        __threadfence();
+    }
+    cbar();
+    if (ms->last) {
+        const uint64_t* ob = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART;
+        float* cm = sS;       // [ns] chunk maxima
+        float* cl = sS + 64;  // [ns] chunk sums
+        for (int q = tid; q < 2 * ns; q += 256) {
+            const uint64_t* w = ob + (size_t)(q >> 1) * MG_PART + (q & 1);
+            const uint64_t v = ldr64(w);
+            (q & 1 ? cl : cm)[q >> 1] = (uint32_t)(v >> 32) == tag ? __uint_as_float((uint32_t)v) : poll(cx, w, tag);
+        }
+        cbar();
+        if (tid < HD) {
+            float M = -INFINITY, L = 0.f;
+            for (int q = 0; q < ns; q++) {
+                const float nm = fmaxf(M, cm[q]);
+                L = L * expf(M - nm) + cl[q] * expf(cm[q] - nm);
+                M = nm;
+            }
+            const float il = 1.0f / L;
+            float v = 0.f;
+#pragma unroll 1
+            for (int s0 = 0; s0 < ns; s0 += 4) {
+                uint64_t va[4];
+#pragma unroll
+                for (int k = 0; k < 4; k++) va[k] = s0 + k < ns ? ldr64(ob + (size_t)(s0 + k) * MG_PART + 2 + tid) : 0ull;
+#pragma unroll
+                for (int k = 0; k < 4; k++) {
+                    if (s0 + k >= ns) continue;
+                    const uint64_t* w = ob + (size_t)(s0 + k) * MG_PART + 2 + tid;
+                    const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k]) : poll(cx, w, tag);
+                    v += x * (expf(cm[s0 + k] - M) * il);
+                }
+            }
+            str64(a.comb + ((size_t)b * a.heads + h) * HD + tid, tagged(tag, rb(v)));
+        }
+        cbar();
+    }
 }
 
-// o_proj input: the attention output of the heads this CTA's o_proj range
-// reads, combined over the chunks: o = sum_s acc_s e^(m_s - M) / L, rounded,
-// into sT [si][d][b]. The split weights e^(m_s - M) / L live in the B-fragment
-// area (free until the staging that follows).
+// o_proj input: the combined attention output of the heads this CTA's
+// o_proj range reads (published by each head's last chunk), into sT
+// [si][d][b].
 MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int gpt, uint32_t tag) {
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
-    float* wt = reinterpret_cast<float*>(sm.sB);  // [(si * B + b) * max_splits + s]
-    const int B = a.B, tid = threadIdx.x;
-    for (int e = tid; e < nst * B; e += 256) {
-        const int si = divB(e, ms->bm), b = e - si * B, h = si + base < gpt ? si + base : si + base - gpt;
-        const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
-        const uint64_t* o = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART;
-        float M = -INFINITY, L = 0.f;
-#pragma unroll 1
-        for (int s0 = 0; s0 < ns; s0 += 4) {  // 4 chunks' loads in flight; kept rolled (code size)
-            uint64_t vm[4], vl[4];
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                vm[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART) : 0ull;
-                vl[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART + 1) : 0ull;
-            }
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                if (s0 + k >= ns) continue;
-                const float m = (uint32_t)(vm[k] >> 32) == tag ? __uint_as_float((uint32_t)vm[k])
-                                                                : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
-                const float l = (uint32_t)(vl[k] >> 32) == tag ? __uint_as_float((uint32_t)vl[k])
-                                                                : poll(cx, o + (size_t)(s0 + k) * MG_PART + 1, tag);
-                wt[(size_t)e * a.max_splits + s0 + k] = m;
-                const float nm = fmaxf(M, m);
-                L = L * expf(M - nm) + l * expf(m - nm);
-                M = nm;
-            }
-        }
-        const float il = 1.0f / L;
-#pragma unroll 1
-        for (int s2 = 0; s2 < ns; s2++) wt[(size_t)e * a.max_splits + s2] = expf(wt[(size_t)e * a.max_splits + s2] - M) * il;
-    }
-    cbar();
-    const int tot = nst * 64 * B;
-    for (int e = tid; e < tot; e += 256) {
+    const int B = a.B, tot = nst * 64 * B;
+    for (int e = threadIdx.x; e < tot; e += 256) {
         const int qd = divB(e, ms->bm), b = e - qd * B, si = qd >> 6, d = qd & 63;
         const int h = si + base < gpt ? si + base : si + base - gpt;
-        const int ns = (ms->pos[b] + MG_ATT_CH) / MG_ATT_CH;
-        const uint64_t* o = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART + 2 + d;
-        const float* w = wt + (size_t)(si * B + b) * a.max_splits;
-        float v = 0.f;
-#pragma unroll 1
-        for (int s0 = 0; s0 < ns; s0 += 4) {
-            uint64_t va[4];
-#pragma unroll
-            for (int k = 0; k < 4; k++) va[k] = s0 + k < ns ? ldr64(o + (size_t)(s0 + k) * MG_PART) : 0ull;
-#pragma unroll
-            for (int k = 0; k < 4; k++) {
-                if (s0 + k >= ns) continue;
-                const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k])
-                                                                : poll(cx, o + (size_t)(s0 + k) * MG_PART, tag);
-                v += x * w[s0 + k];
-            }
-        }
-        sm.sT[e] = f2bf(v);  // [si][d][b]
+        const uint64_t* p = a.comb + ((size_t)b * a.heads + h) * HD + d;
+        const uint64_t v = ldr64(p);
+        sm.sT[e] = f2bf((uint32_t)(v >> 32) == tag ? __uint_as_float((uint32_t)v) : poll(cx, p, tag));
     }
     cbar();
 }

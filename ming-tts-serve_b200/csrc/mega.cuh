@@ -48,7 +48,7 @@ constexpr int MG_NPH = 4;                         // GEMV phases: P0 qkv, P2 o, 
 constexpr int MG_FIX = 32;                        // fraction bits of the fixed-point accumulators
 constexpr int MG_MAX_STAGE = 32;                  // most 64-groups of activations one CTA stages per phase
 constexpr int MG_TRACE = 64;                      // clock64 stamp slots per (CTA, layer) when tracing
-enum { MG_ACC_QKV = 0, MG_ACC_X1 = 1, MG_ACC_X2 = 2, MG_NACC = 3 };
+enum { MG_ACC_QKV = 0, MG_ACC_X1 = 1, MG_ACC_X2 = 2, MG_ACC_CNT = 3, MG_NACC = 4 };  // CNT: attention chunk arrivals per (row, head)
 constexpr int MG_MAX_TILES = 128;                 // most tiles of a split-K phase (q|k|v, o_proj, down)
 
 struct MegaPhase {
@@ -75,6 +75,7 @@ struct MegaDev {
     int acc_w;
     uint64_t* hbuf;            // [layers][MG_MAXB][FF] SwiGLU outputs: step tag << 32 | bf16
     uint64_t* attn;            // [B][heads][max_splits][MG_PART] tagged attention partials
+    uint64_t* comb;            // [MG_MAXB][heads][64] tagged combined attention outputs (the o_proj input)
     const uint16_t* x_in;      // [B][H] step input
     uint16_t* z;               // [B][H] post-norm hidden
     uint16_t* feed;            // [B][H] copy of z (next step's input)

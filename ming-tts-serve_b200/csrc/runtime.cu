@@ -813,9 +813,12 @@ int setup_mega(ming_ctx* c) {
     const uint8_t** dwb = c->mem.alloc<const uint8_t*>(wb.size(), &rc);
     uint8_t* lpar = c->mem.alloc<uint8_t>((size_t)f.layers * lp_bytes, &rc);
     const int max_splits = (f.max_ctx + MG_ATT_CH - 1) / MG_ATT_CH;
+    if (max_splits > 64) return MING_OK;  // a head's combine keeps up to 64 chunk maxima and sums in shared memory
     if ((H / 64) * MG_MAXB * max_splits > 8192) return MING_OK;  // split weights live in the 32 KB fragment area
     const size_t attn_n = (size_t)MG_MAXB * f.heads * max_splits * MG_PART;
     uint64_t* attn = c->mem.alloc<uint64_t>(attn_n, &rc);
+    const size_t comb_n = (size_t)MG_MAXB * f.heads * HD;
+    uint64_t* comb = c->mem.alloc<uint64_t>(comb_n, &rc);
     const int acc_w = (std::max(qkv_rows, H) + 1) / 2 * 2;
     const size_t acc_n = (size_t)2 * f.layers * MG_NACC * MG_MAXB * acc_w;
     unsigned long long* acc = c->mem.alloc<unsigned long long>(acc_n, &rc);
@@ -831,6 +834,7 @@ int setup_mega(ming_ctx* c) {
         cudaError_t e = cudaMemset(acc, 0, acc_n * 8);
         if (e == cudaSuccess) e = cudaMemset(hbuf, 0, hbuf_n * 8);
         if (e == cudaSuccess) e = cudaMemset(attn, 0, attn_n * 8);
+        if (e == cudaSuccess) e = cudaMemset(comb, 0, comb_n * 8);
         if (e == cudaSuccess) e = cudaMemset(counter, 0, 8);
         return e;
     };
@@ -851,6 +855,7 @@ int setup_mega(ming_ctx* c) {
     a.kv = KvDev{c->pool, c->bt, c->bt_ld, f.layers, f.kv_heads};
     a.seq_len = c->seq_len;
     a.attn = attn;
+    a.comb = comb;
     a.acc = acc;
     a.acc_w = acc_w;
     a.hbuf = hbuf;
