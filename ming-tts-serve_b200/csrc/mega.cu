@@ -718,29 +718,38 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
             (q & 1 ? cl : cm)[q >> 1] = (uint32_t)(v >> 32) == tag ? __uint_as_float((uint32_t)v) : poll(cx, w, tag);
         }
         cbar();
-        if (tid < HD) {
-            float M = -INFINITY, L = 0.f;
-            for (int q = 0; q < ns; q++) {
-                const float nm = fmaxf(M, cm[q]);
-                L = L * expf(M - nm) + cl[q] * expf(cm[q] - nm);
-                M = nm;
-            }
-            const float il = 1.0f / L;
-            float v = 0.f;
+        // every thread: the combined max and sum; thread (d, quarter) sums
+        // the chunks s = quarter, quarter + 4, ... of dim d (all loads at once
+        // for up to 16 chunks), the quarters meet in shared memory
+        float M = -INFINITY, L = 0.f;
+        for (int q = 0; q < ns; q++) {
+            const float nm = fmaxf(M, cm[q]);
+            L = L * expf(M - nm) + cl[q] * expf(cm[q] - nm);
+            M = nm;
+        }
+        const float il = 1.0f / L;
+        const int d = tid & 63, qt = tid >> 6;
+        float v = 0.f;
 #pragma unroll 1
-            for (int s0 = 0; s0 < ns; s0 += 4) {
-                uint64_t va[4];
+        for (int s0 = qt; s0 < ns; s0 += 16) {
+            uint64_t va[4];
 #pragma unroll
-                for (int k = 0; k < 4; k++) va[k] = s0 + k < ns ? ldr64(ob + (size_t)(s0 + k) * MG_PART + 2 + tid) : 0ull;
+            for (int k = 0; k < 4; k++) va[k] = s0 + 4 * k < ns ? ldr64(ob + (size_t)(s0 + 4 * k) * MG_PART + 2 + d) : 0ull;
 #pragma unroll
-                for (int k = 0; k < 4; k++) {
-                    if (s0 + k >= ns) continue;
-                    const uint64_t* w = ob + (size_t)(s0 + k) * MG_PART + 2 + tid;
-                    const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k]) : poll(cx, w, tag);
-                    v += x * (expf(cm[s0 + k] - M) * il);
-                }
+            for (int k = 0; k < 4; k++) {
+                const int sk = s0 + 4 * k;
+                if (sk >= ns) continue;
+                const uint64_t* w = ob + (size_t)sk * MG_PART + 2 + d;
+                const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k]) : poll(cx, w, tag);
+                v += x * (expf(cm[sk] - M) * il);
             }
-            str64(a.comb + ((size_t)b * a.heads + h) * HD + tid, tagged(tag, rb(v)));
+        }
+        float* red = cl + 64;  // [4][64]: the P.V partial area sP, read before the arrival count
+        red[qt * 64 + d] = v;
+        cbar();
+        if (tid < HD) {
+            const float o = (red[tid] + red[64 + tid]) + (red[128 + tid] + red[192 + tid]);
+            str64(a.comb + ((size_t)b * a.heads + h) * HD + tid, tagged(tag, rb(o)));
         }
         cbar();
     }
