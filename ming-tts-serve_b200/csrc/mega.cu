@@ -253,7 +253,7 @@ struct Misc {              // small per-CTA state in shared memory
     float rc[MG_MAXB][HD / 2];           // RoPE cos/sin of each row's position, per frequency
     float rs[MG_MAXB][HD / 2];
     int fail;
-    int last;  // this CTA's attention chunk was the last of its (row, head)
+    float om, ol;  // max and sum of this CTA's attention chunk (the combining chunk keeps its own)
     int prod_done;
     int issued;
     uint32_t epoch;
@@ -559,6 +559,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int grp = a.heads / a.kvh, g = h / grp, pos = ms->pos[b];
     const int p0 = s * MG_ATT_CH, p1 = min(pos + 1, p0 + MG_ATT_CH), pc = min(p1, pos), len = p1 - p0;
+    const int ns = (pos + MG_ATT_CH) / MG_ATT_CH;  // chunks of the (row, head); chunk ns - 1 combines them
     // K/V rows padded to 72 elements (144 B): 16-byte loads of 8 consecutive
     // rows fall on distinct bank groups
     constexpr int KS = HD + 8;
@@ -647,9 +648,14 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         }
         sum = warp_sum(sum);
         if (lane == 0) {
-            uint64_t* o = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
-            str64(o, tagged(tag, m));
-            str64(o + 1, tagged(tag, sum));
+            if (s == ns - 1) {
+                ms->om = m;
+                ms->ol = sum;
+            } else {
+                uint64_t* o = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
+                str64(o, tagged(tag, m));
+                str64(o + 1, tagged(tag, sum));
+            }
         }
     }
     cbar();
@@ -683,6 +689,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         sP[warp * 32 + lane] = make_float2(ac0.x + ac1.x, ac0.y + ac1.y);
     }
     cbar();
+    float* own = sq;  // [64] this chunk's P.V sums when it combines (q is no longer read)
     if (warp == 0) {
         float ox = 0.f, oy = 0.f;
 #pragma unroll
@@ -691,67 +698,68 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
             ox += v.x;
             oy += v.y;
         }
-        uint64_t* o = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
-        str64(o + 2 + 2 * lane, tagged(tag, ox));
-        str64(o + 3 + 2 * lane, tagged(tag, oy));
-        __threadfence();
+        if (s == ns - 1) {
+            own[2 * lane] = ox;
+            own[2 * lane + 1] = oy;
+        } else {
+            uint64_t* o = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
+            str64(o + 2 + 2 * lane, tagged(tag, ox));
+            str64(o + 3 + 2 * lane, tagged(tag, oy));
+        }
+    }
+    if (s != ns - 1) return;  // CTA-uniform; the caller meets at a barrier next
+    // 7. the chunk holding the new position combines the (row, head):
+    //    o = sum_s acc_s e^(m_s - M) / L over the other chunks' tagged partials
+    //    (each word polled until this step's tag shows; every chunk with a
+    //    smaller item index runs on some CTA, so the wait ends) and its own
+    //    sums, then publishes the 64 values for every o_proj CTA that reads
+    //    this head. Thread (d, quarter) sums the chunks s = quarter, quarter +
+    //    4, ... of dim d; the first 4 value loads of each thread and the
+    //    chunk maxima and sums are in flight together.
+    const int no = ns - 1;
+    const uint64_t* ob = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART;
+    float* cm = sS;       // [no] chunk maxima (scores are no longer read)
+    float* cl = sS + 64;  // [no] chunk sums
+    const int d = tid & 63, qt = tid >> 6;
+    uint64_t va[4];
+#pragma unroll
+    for (int k = 0; k < 4; k++) va[k] = qt + 4 * k < no ? ldr64(ob + (size_t)(qt + 4 * k) * MG_PART + 2 + d) : 0ull;
+    if (tid < 2 * no) {
+        const uint64_t* w = ob + (size_t)(tid >> 1) * MG_PART + (tid & 1);
+        const uint64_t v = ldr64(w);
+        (tid & 1 ? cl : cm)[tid >> 1] = (uint32_t)(v >> 32) == tag ? __uint_as_float((uint32_t)v) : poll(cx, w, tag);
     }
     cbar();
-    // 7. arrival count of the (row, head): the last of its chunks to finish
-    //    combines them all, o = sum_s acc_s e^(m_s - M) / L (the partials are
-    //    tagged, so one not yet visible is polled), and publishes the 64
-    //    values for every o_proj CTA that reads this head
-    const int ns = (pos + MG_ATT_CH) / MG_ATT_CH;
-    if (tid == 0) {
-        unsigned long long* cnt = acc_ptr(a, ms->epoch, l, MG_ACC_CNT) + (size_t)b * a.acc_w + h;
-        ms->last = atomicAdd(cnt, 1ull) == (unsigned long long)(ns - 1) ? 1 : 0;
-        __threadfence();
+    float M = -INFINITY, L = 0.f;
+    for (int q = 0; q <= no; q++) {
+        const float mq = q < no ? cm[q] : ms->om, lq = q < no ? cl[q] : ms->ol;
+        const float nm = fmaxf(M, mq);
+        L = L * expf(M - nm) + lq * expf(mq - nm);
+        M = nm;
     }
-    cbar();
-    if (ms->last) {
-        const uint64_t* ob = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART;
-        float* cm = sS;       // [ns] chunk maxima
-        float* cl = sS + 64;  // [ns] chunk sums
-        for (int q = tid; q < 2 * ns; q += 256) {
-            const uint64_t* w = ob + (size_t)(q >> 1) * MG_PART + (q & 1);
-            const uint64_t v = ldr64(w);
-            (q & 1 ? cl : cm)[q >> 1] = (uint32_t)(v >> 32) == tag ? __uint_as_float((uint32_t)v) : poll(cx, w, tag);
-        }
-        cbar();
-        // every thread: the combined max and sum; thread (d, quarter) sums
-        // the chunks s = quarter, quarter + 4, ... of dim d (all loads at once
-        // for up to 16 chunks), the quarters meet in shared memory
-        float M = -INFINITY, L = 0.f;
-        for (int q = 0; q < ns; q++) {
-            const float nm = fmaxf(M, cm[q]);
-            L = L * expf(M - nm) + cl[q] * expf(cm[q] - nm);
-            M = nm;
-        }
-        const float il = 1.0f / L;
-        const int d = tid & 63, qt = tid >> 6;
-        float v = 0.f;
+    const float il = 1.0f / L;
+    float v = 0.f;
 #pragma unroll 1
-        for (int s0 = qt; s0 < ns; s0 += 16) {
-            uint64_t va[4];
+    for (int s0 = qt; s0 < no; s0 += 16) {
+        if (s0 != qt) {
 #pragma unroll
-            for (int k = 0; k < 4; k++) va[k] = s0 + 4 * k < ns ? ldr64(ob + (size_t)(s0 + 4 * k) * MG_PART + 2 + d) : 0ull;
+            for (int k = 0; k < 4; k++) va[k] = s0 + 4 * k < no ? ldr64(ob + (size_t)(s0 + 4 * k) * MG_PART + 2 + d) : 0ull;
+        }
 #pragma unroll
-            for (int k = 0; k < 4; k++) {
-                const int sk = s0 + 4 * k;
-                if (sk >= ns) continue;
-                const uint64_t* w = ob + (size_t)sk * MG_PART + 2 + d;
-                const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k]) : poll(cx, w, tag);
-                v += x * (expf(cm[sk] - M) * il);
-            }
+        for (int k = 0; k < 4; k++) {
+            const int sk = s0 + 4 * k;
+            if (sk >= no) continue;
+            const uint64_t* w = ob + (size_t)sk * MG_PART + 2 + d;
+            const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k]) : poll(cx, w, tag);
+            v += x * (expf(cm[sk] - M) * il);
         }
-        float* red = cl + 64;  // [4][64]: the P.V partial area sP, read before the arrival count
-        red[qt * 64 + d] = v;
-        cbar();
-        if (tid < HD) {
-            const float o = (red[tid] + red[64 + tid]) + (red[128 + tid] + red[192 + tid]);
-            str64(a.comb + ((size_t)b * a.heads + h) * HD + tid, tagged(tag, rb(o)));
-        }
-        cbar();
+    }
+    float* red = cl + 64;  // [4][64]: the P.V partial area sP, read by warp 0 before the barrier above
+    red[qt * 64 + d] = v;
+    cbar();
+    if (tid < HD) {
+        const float o = (red[tid] + red[64 + tid]) + (red[128 + tid] + red[192 + tid]) + own[tid] * (expf(ms->om - M) * il);
+        str64(a.comb + ((size_t)b * a.heads + h) * HD + tid, tagged(tag, rb(o)));
     }
 }
 

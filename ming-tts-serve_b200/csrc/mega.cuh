@@ -28,9 +28,11 @@
 //   * every CTA keeps the residual stream of its rows in shared memory and
 //     applies the reference's epilogue math (bias, bf16 rounding, RoPE,
 //     residual, SwiGLU) where the values are consumed;
-//   * attention is split by (row, kv head, 128-position chunk); a chunk's
+//   * attention is split by (row, query head, 128-position chunk); a chunk's
 //     K/V rows are prefetched with cp.async before the CTA waits for q; its
-//     (max, sum, P.V) partials carry the step's epoch in each 64-bit word.
+//     (max, sum, P.V) partials carry the step's epoch in each 64-bit word,
+//     and the chunk holding the new position combines them with its own and
+//     publishes the head's 64 outputs (tagged words) for o_proj.
 // Every wait is bounded: on timeout the kernel records an error code, waits
 // (bounded) for its own copies in flight and returns.
 #pragma once
@@ -48,7 +50,7 @@ constexpr int MG_NPH = 4;                         // GEMV phases: P0 qkv, P2 o, 
 constexpr int MG_FIX = 32;                        // fraction bits of the fixed-point accumulators
 constexpr int MG_MAX_STAGE = 32;                  // most 64-groups of activations one CTA stages per phase
 constexpr int MG_TRACE = 64;                      // clock64 stamp slots per (CTA, layer) when tracing
-enum { MG_ACC_QKV = 0, MG_ACC_X1 = 1, MG_ACC_X2 = 2, MG_ACC_CNT = 3, MG_NACC = 4 };  // CNT: attention chunk arrivals per (row, head)
+enum { MG_ACC_QKV = 0, MG_ACC_X1 = 1, MG_ACC_X2 = 2, MG_NACC = 3 };
 constexpr int MG_MAX_TILES = 128;                 // most tiles of a split-K phase (q|k|v, o_proj, down)
 
 struct MegaPhase {
