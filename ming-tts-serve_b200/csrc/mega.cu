@@ -30,12 +30,34 @@ MING_DEV bool mbar_try(uint64_t* b, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait on an mbarrier phase; false on timeout.
+MING_DEV bool mbar_test(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait on an mbarrier phase; false on timeout. A completed phase is
+// seen by the non-blocking test first.
 MING_DEV bool mbar_wait(uint64_t* b, uint32_t parity) {
-    if (mbar_try(b, parity)) return true;
+    if (mbar_test(b, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try(b, parity))
         if (clock64() - t0 > MG_TIMEOUT) return false;
+    return true;
+}
+// The producer's wait for a released slot: it runs a layer or more ahead, so
+// it backs off between tests instead of competing with the consumer warps
+// for issue slots and the shared-memory pipe.
+MING_DEV bool mbar_wait_idle(uint64_t* b, uint32_t parity) {
+    if (mbar_test(b, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_test(b, parity)) {
+        __nanosleep(128);
+        if (clock64() - t0 > MG_TIMEOUT) return false;
+    }
     return true;
 }
 MING_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
@@ -441,10 +463,18 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
     // longer than the ring (the producer refills released slots meanwhile).
     // A warp releases use u+1 of a slot only after waiting for its fill, which
     // needs every warp's release of use u: arrivals of two uses never mix.
+    // With the phase inside the ring (every use a distinct slot; the barrier
+    // ending the previous phase orders its releases first), a warp releases
+    // the slots before and after its run without waiting for their fill: some
+    // warp uses every slot and releases it only after its wait and use, so
+    // the producer never refills a slot still being filled or read.
+    const bool skip = nsc <= a.nslots;
+    int sl = cons_base % a.nslots;
+    uint32_t par = (uint32_t)(cons_base / a.nslots) & 1u;
     for (int jj = 0; jj < nsc; jj++) {
-        const int use = cons_base + jj, sl = use % a.nslots;
-        if (!mbar_wait(&full[sl], (use / a.nslots) & 1)) atomicCAS(cx.fail, 0, 2);
         const int w0 = max(i0, jj * a.gps), w1 = min(i1, (jj + 1) * a.gps);
+        if ((!skip || w0 < w1) && !mbar_wait(&full[sl], par)) atomicCAS(cx.fail, 0, 2);
+        if (sm.st && lane == 0 && p == 2 && w0 == i0 && w0 < w1) sm.st[56 + warp] = clock64();
         if (w0 < w1 && !*(volatile int*)cx.fail) {
             const uint8_t* sbase = ring + (size_t)sl * a.slot_bytes;
 #pragma unroll 1
@@ -494,6 +524,11 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[sl]);  // before any global write of this phase
+        if (sm.st && lane == 0 && p >= 2 && w1 == i1 && w0 < w1) sm.st[40 + (p - 2) * 8 + warp] = clock64();
+        if (++sl == a.nslots) {
+            sl = 0;
+            par ^= 1u;
+        }
     }
     MG_SUB(2)
     {
@@ -858,7 +893,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             bool ok = true;
             for (int l = 0; l < a.layers && ok; l++) {
                 const int lb = l & 1;  // the layer's parameter block, double-buffered
-                if (l >= 2 && !mbar_wait(&lp_empty[lb], ((l >> 1) - 1) & 1)) {
+                if (l >= 2 && !mbar_wait_idle(&lp_empty[lb], ((l >> 1) - 1) & 1)) {
                     atomicCAS(&ms->fail, 0, 3);
                     break;
                 }
@@ -869,7 +904,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
                     const uint8_t* src = a.wbase[l * MG_NPH + p] + (size_t)g0 * a.cb;
                     for (int j = 0; j * a.gps < n; j++, sc++) {
                         const int slot = sc % a.nslots;
-                        if (sc >= a.nslots && !mbar_wait(&empty[slot], ((sc / a.nslots) - 1) & 1)) {
+                        if (sc >= a.nslots && !mbar_wait_idle(&empty[slot], ((sc / a.nslots) - 1) & 1)) {
                             atomicCAS(&ms->fail, 0, 3);
                             ok = false;
                             break;
