@@ -29,10 +29,10 @@ MING_DEV void att_cp16(void* dst, const void* src) {
 
 // One (split, kv head, row): the row's causal positions [p0, p1) of one
 // 256-position split, every query head of the kv group. All K/V rows of the
-// split are prefetched with cp.async (one round trip), then scores (a thread
-// per position keeps its key row in registers), a per-head softmax inside
-// the split, and P.V (a warp per 32 positions, a lane per dim pair, all the
-// group's heads per V load).
+// split are prefetched with cp.async (one round trip), then scores on the
+// tensor cores (mma.sync, the group's heads as the 16-row A operand), a
+// per-head softmax inside the split in f32, and P.V on the tensor cores (a
+// warp per 8 dims, P as bf16 hi + lo parts).
 // CL = false: (max, sum, unnormalised P.V) per head go to `part`, combined by
 // attn_combine_kernel. CL = true: the splits of one (kv head, row) are one
 // thread-block cluster; each keeps its partials in shared memory, copies
@@ -78,37 +78,49 @@ __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
     if (live) {
         fetch(pre, p1);
         asm volatile("cp.async.commit_group;\n" ::: "memory");
-        for (int e = tid; e < grp * HD; e += 256) {
+        // q of the group's heads as bf16 (the mma A operand; heads >= grp are
+        // zero rows); the 1/8 scale is applied to the f32 sums
+        uint16_t* sQ = reinterpret_cast<uint16_t*>(sq);  // [ATT_MAXG][ATT_KS]
+        for (int e = tid; e < ATT_MAXG * HD; e += 256) {
             const int i = e / HD, d = e % HD;
-            sq[i * HD + d] = 0.125f * bf2f(a.q[(size_t)row * a.heads * HD + (kh * grp + i) * HD + d]);
+            sQ[i * ATT_KS + d] = i < grp ? a.q[(size_t)row * a.heads * HD + (kh * grp + i) * HD + d] : (uint16_t)0;
         }
         asm volatile("cp.async.wait_all;\n" ::: "memory");
+        // V rows from len up to the next 16-position k-step are read by the
+        // last P.V k-step with P = 0: make them finite
+        for (int e = tid; e < (((len + 15) & ~15) - len) * (HD / 2); e += 256) {
+            const int j = len + e / (HD / 2), d2 = e % (HD / 2);
+            *reinterpret_cast<uint32_t*>(sV + j * ATT_KS + 2 * d2) = 0u;
+        }
         __syncthreads();
         if (tr) tr[2] = gtimer();
-        if (tid < len) {
-            // the key row, unpacked once for every head of the group
-            float kf[HD];
-            const uint4* src = reinterpret_cast<const uint4*>(sK + tid * ATT_KS);
+        const int g = lane >> 2, t4 = lane & 3;
+        {
+            // scores S = Q K^T on the tensor cores: rows = query heads (8 of
+            // the 16 used), 8-position n-tiles strided over the warps, 4
+            // k-steps of 16 dims; key columns past len are computed and
+            // dropped (each output column reads only its own key row)
+            uint32_t qa[4][2];
 #pragma unroll
-            for (int q = 0; q < HD / 8; q++) {
-                const uint4 v = src[q];
-                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const float2 f = unpack_bf16x2(w[u]);
-                    kf[8 * q + 2 * u] = f.x;
-                    kf[8 * q + 2 * u + 1] = f.y;
-                }
+            for (int ks = 0; ks < 4; ks++) {
+                qa[ks][0] = *reinterpret_cast<const uint32_t*>(sQ + g * ATT_KS + ks * 16 + 2 * t4);
+                qa[ks][1] = *reinterpret_cast<const uint32_t*>(sQ + g * ATT_KS + ks * 16 + 8 + 2 * t4);
             }
-            for (int i = 0; i < grp; i++) {
-                float s0 = 0.f, s1 = 0.f;
+            const int nte = (len + 7) >> 3;
+            for (int nt = warp; nt < nte; nt += 8) {
+                float c[4] = {0.f, 0.f, 0.f, 0.f};
+                const uint16_t* kr = sK + (nt * 8 + g) * ATT_KS + 2 * t4;
 #pragma unroll
-                for (int q = 0; q < HD / 2; q += 2) {
-                    const float4 qv = *reinterpret_cast<const float4*>(sq + i * HD + 2 * q);
-                    s0 += qv.x * kf[2 * q] + qv.y * kf[2 * q + 1];
-                    s1 += qv.z * kf[2 * q + 2] + qv.w * kf[2 * q + 3];
+                for (int ks = 0; ks < 4; ks++) {
+                    const uint32_t af[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
+                    mma_bf16(c, af, *reinterpret_cast<const uint32_t*>(kr + ks * 16),
+                             *reinterpret_cast<const uint32_t*>(kr + ks * 16 + 8));
                 }
-                sc[i * ATT_SPLIT + tid] = s0 + s1;
+                const int j = nt * 8 + 2 * t4;
+                if (g < grp) {
+                    if (j < len) sc[g * ATT_SPLIT + j] = 0.125f * c[0];
+                    if (j + 1 < len) sc[g * ATT_SPLIT + j + 1] = 0.125f * c[1];
+                }
             }
         }
         __syncthreads();
@@ -132,42 +144,40 @@ __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
         }
         __syncthreads();
         if (tr) tr[4] = gtimer();
-        // P.V: warp w takes positions [32 w, 32 w + 32), lane = dim pair, every
-        // head of the group at once (one V load feeds 7 heads); the 8 warps'
-        // sums meet in shared memory (the key area, unused since the scores),
-        // in warp order
         {
-            float2 ac[ATT_MAXG];
-#pragma unroll
-            for (int i = 0; i < ATT_MAXG; i++) ac[i] = make_float2(0.f, 0.f);
-            const int j0 = warp * 32, j1 = min(len, j0 + 32);
-            for (int j = j0; j < j1; j++) {
-                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * ATT_KS + 2 * lane));
-#pragma unroll
-                for (int i = 0; i < ATT_MAXG; i++) {
-                    if (i < grp) {
-                        const float pw = sc[i * ATT_SPLIT + j];
-                        ac[i].x += pw * v.x;
-                        ac[i].y += pw * v.y;
-                    }
+            // P.V on the tensor cores: warp w owns dims [8w, 8w + 8) over all
+            // 16-position k-steps. P (f32) enters as bf16 hi + lo parts (two
+            // mma on the same V fragment, ~2^-16 relative), V fragments come
+            // from the row-major rows with ldmatrix.trans; positions past len
+            // have P = 0
+            const int n0 = warp * 8, kte = (len + 15) >> 4;
+            const float* pr = sc + (g < grp ? g : 0) * ATT_SPLIT;
+            float c[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int kt = 0; kt < kte; kt++) {
+                const int j = kt * 16 + 2 * t4;
+                float2 pa, pb;
+                if (j + 9 < len) {
+                    pa = *reinterpret_cast<const float2*>(pr + j);
+                    pb = *reinterpret_cast<const float2*>(pr + j + 8);
+                } else {
+                    pa = make_float2(j < len ? pr[j] : 0.f, j + 1 < len ? pr[j + 1] : 0.f);
+                    pb = make_float2(j + 8 < len ? pr[j + 8] : 0.f, j + 9 < len ? pr[j + 9] : 0.f);
                 }
+                const float ha = rb(pa.x), hb = rb(pa.y), hc = rb(pb.x), hd = rb(pb.y);
+                const uint32_t ah[4] = {pack_bf16x2(ha, hb), 0u, pack_bf16x2(hc, hd), 0u};
+                const uint32_t al[4] = {pack_bf16x2(pa.x - ha, pa.y - hb), 0u, pack_bf16x2(pb.x - hc, pb.y - hd), 0u};
+                uint32_t b0, b1;
+                const uint16_t* vr = sV + (kt * 16 + (lane & 15)) * ATT_KS + n0;
+                asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];\n"
+                             : "=r"(b0), "=r"(b1)
+                             : "r"(att_su32(vr)));
+                mma_bf16(c, ah, b0, b1);
+                mma_bf16(c, al, b0, b1);
             }
-            float2* red = reinterpret_cast<float2*>(sK);  // [8 warps][ATT_MAXG][32 lanes]: 16 KB of the 36 KB
-#pragma unroll
-            for (int i = 0; i < ATT_MAXG; i++)
-                if (i < grp) red[(warp * ATT_MAXG + i) * 32 + lane] = ac[i];
-            __syncthreads();
-            for (int e = tid; e < grp * 32; e += 256) {
-                const int i = e >> 5, dp = e & 31;
-                float2 o = make_float2(0.f, 0.f);
-                for (int w = 0; w < 8; w++) {
-                    const float2 r = red[(w * ATT_MAXG + i) * 32 + dp];
-                    o.x += r.x;
-                    o.y += r.y;
-                }
-                float* ob = out + (size_t)i * PART_STRIDE;
-                ob[2 + 2 * dp] = o.x;
-                ob[3 + 2 * dp] = o.y;
+            if (g < grp) {
+                float* ob = out + (size_t)g * PART_STRIDE;
+                ob[2 + n0 + 2 * t4] = c[0];
+                ob[3 + n0 + 2 * t4] = c[1];
             }
         }
         if (tr) tr[5] = gtimer();
