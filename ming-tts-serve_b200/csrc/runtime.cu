@@ -144,6 +144,8 @@ struct ming_ctx {
     MegaDev mega{};
     int mega_smem = 0;
     int* dev_err = nullptr;
+    int* err_host = nullptr;  // pinned: the device error flag read back with a call's outputs
+    bool cells_null = false;  // out_cell / stop_cell known to hold null (decode); generate sets them
     // launch trace of the per-kernel step (MING_KTRACE=1): KT_SLOTS launches x
     // KT_CTAS CTAs x 8 globaltimer stamps, slot = launch order in the step
     long long* ktrace = nullptr;
@@ -1282,6 +1284,10 @@ int ming_cuda_finalize(ming_ctx* c) {
         CK(cudaDeviceGetAttribute(&c->lin.sms, cudaDevAttrMultiProcessorCount, c->device));
         if (!c->dev_err) c->dev_err = c->mem.alloc<int>(1, &rc);
         if (rc) return rc;
+        if (!c->err_host && cudaHostAlloc(reinterpret_cast<void**>(&c->err_host), 4, cudaHostAllocDefault) != cudaSuccess) {
+            cudaGetLastError();
+            c->err_host = nullptr;  // the error flag is then read with a synchronous copy
+        }
         c->lin.err = c->dev_err;
         const char* kt = getenv("MING_KTRACE");
         if (kt && std::string(kt) == "1") {
@@ -1387,18 +1393,30 @@ int ming_cuda_lm_decode(ming_ctx* c, int B, const int* ids, const uint16_t* x, u
     const int H = c->cfg.hidden;
     cudaGraphExec_t g;
     if ((rc = decode_graph(c, B, &g))) return rc;
-    uint16_t* null_out = nullptr;
-    float* null_stop = nullptr;
-    CK(cudaMemcpyAsync(c->out_cell, &null_out, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
-    CK(cudaMemcpyAsync(c->stop_cell, &null_stop, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
+    if (!c->cells_null) {
+        // the step's kernels write per-step outputs only through non-null
+        // cells (generate); the cells stay null until the next generate
+        static uint16_t* const null_out = nullptr;
+        static float* const null_stop = nullptr;
+        CK(cudaMemcpyAsync(c->out_cell, &null_out, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
+        CK(cudaMemcpyAsync(c->stop_cell, &null_stop, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
+        c->cells_null = true;
+    }
     if ((rc = copy_in(c, c->x, x, (size_t)B * H * 2, kind))) return rc;
     CK(cudaGraphLaunch(g, c->stream));
     for (int i = 0; i < B; i++) c->seqs[ids[i]].len += 1;
     if ((rc = copy_out(c, out, c->z, (size_t)B * H * 2, kind))) return rc;
     if ((rc = copy_out(c, stop, c->stop, (size_t)B * 4, kind))) return rc;
     if (kind == MING_PTR_HOST) {
-        CK(cudaStreamSynchronize(c->stream));
-        if ((rc = check_dev_err(c))) return rc;
+        if (c->err_host && c->dev_err) {
+            // the error flag travels with the outputs: one synchronisation
+            CK(cudaMemcpyAsync(c->err_host, c->dev_err, 4, cudaMemcpyDeviceToHost, c->stream));
+            CK(cudaStreamSynchronize(c->stream));
+            if (*c->err_host) return check_dev_err(c);
+        } else {
+            CK(cudaStreamSynchronize(c->stream));
+            if ((rc = check_dev_err(c))) return rc;
+        }
     }
     return MING_OK;
 }
@@ -1446,6 +1464,7 @@ int ming_cuda_lm_generate(ming_ctx* c, int B, const int* ids, const uint16_t* x0
     }
     CK(cudaMemcpyAsync(c->out_cell, &o, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
     CK(cudaMemcpyAsync(c->stop_cell, &sp, sizeof(void*), cudaMemcpyHostToDevice, c->stream));
+    c->cells_null = !o && !sp;
     CK(cudaMemsetAsync(c->step_counter, 0, 8, c->stream));
     if (c->mega_counter) CK(cudaMemsetAsync(c->mega_counter + 1, 0, 4, c->stream));  // the epoch is never reset
     if ((rc = copy_in(c, c->x, x0, (size_t)B * H * 2, kind))) return rc;
@@ -1599,6 +1618,7 @@ int ming_cuda_destroy(ming_ctx* c) {
     cudaStreamSynchronize(c->stream);
     if (c->gen_out) cudaFree(c->gen_out);
     if (c->gen_stop) cudaFree(c->gen_stop);
+    if (c->err_host) cudaFreeHost(c->err_host);
     delete c;
     return MING_OK;
 }
