@@ -102,7 +102,7 @@ int ming_cuda_lm_decode(ming_ctx* ctx, int B, const int* seq_ids, const uint16_t
                         int ptr_kind);
 
 /* `steps` decode steps feeding each step's output hidden state back as the
- * next input (BASELINE's LM token loop): out [steps][B][hidden],
+ * next input (the benchmark's LM token loop): out [steps][B][hidden],
  * stop [steps][B] (either may be NULL). */
 int ming_cuda_lm_generate(ming_ctx* ctx, int B, const int* seq_ids, const uint16_t* x0, int steps, uint16_t* out,
                           float* stop, int ptr_kind);

@@ -3,7 +3,8 @@
 // Token mode is the reference's head (src/ming_model.zig:770-797,1159-1215;
 // fused kernels A-F, src/ming_fused.zig:144-289): rows [t+c, x_emb(hist),
 // x_emb(y)] per CFG half, RMSNorm blocks, interleaved rotary.
-// adaLN mode is BASELINE config 4: frames of the latent patch as rows,
+// adaLN mode is the benchmark's adaLN-Zero head (6 blocks x 768, a 4 x 64
+// latent patch, no reference code): frames of the latent patch as rows,
 // LayerNorm + (shift, scale, gate) modulation from SiLU(c), same rotary,
 // attention, gelu MLP and Euler/CFG update.
 #pragma once

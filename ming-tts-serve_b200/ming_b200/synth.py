@@ -12,9 +12,9 @@ depend only on (seed, name), not on generation order:
 
 Names follow src/ming_model.zig (LM, flow head, aggregator); quantized linears
 use MLX's QuantizedLinear layout (.weight U32, .scales/.biases BF16).
-BASELINE's choices: LM weights N(0, 0.02), RMSNorm gains 1; 4-bit codes
+The benchmark's stated choices: LM weights N(0, 0.02), RMSNorm gains 1; 4-bit codes
 uniform 0..15 with scales U(0.005, 0.02) and biases -8*scale (zero-centred,
-this build's choice: BASELINE leaves them open). The DiT rotary inv_freq for
+this build's choice: the benchmark leaves them open). The DiT rotary inv_freq for
 random init is 10000^(-2i/64) (the checkpoint buffer is absent here).
 """
 import numpy as np
@@ -157,7 +157,7 @@ LM_SHAPE = dict(hidden=896, layers=24, heads=14, kv_heads=2, head_dim=64, ff=486
 def lm_weights(seed=0, bits=16, layers=24, hidden=896, heads=14, kv_heads=2, ff=4864, std=0.02, group=64,
                qscale=(0.005, 0.02)):
     """Qwen2 LM weights under model.model.* plus the stop head. qscale is the
-    U(lo, hi) range of the 4/8-bit group scales (BASELINE: 0.005..0.02)."""
+    U(lo, hi) range of the 4/8-bit group scales (the benchmark's: 0.005..0.02)."""
     W = {}
     H, QD, KD = hidden, heads * 64, kv_heads * 64
 
@@ -239,7 +239,7 @@ def agg_weights(seed=1, blocks=8, hidden=1024, ff=4096, latent=64, out=896, std=
 
 
 def ada_weights(seed=1, blocks=6, hidden=768, ff=3072, latent=64, cond=896, freq=256, std=0.02):
-    """adaLN-Zero head under adaln_head.*."""
+    """The adaLN-Zero head (6 blocks x 768, latent 4 x 64) under adaln_head.*."""
     W = {}
     D = "adaln_head"
     _dit_blocks(W, seed, D, blocks, hidden, ff, std, True)
@@ -253,8 +253,8 @@ def ada_weights(seed=1, blocks=6, hidden=768, ff=3072, latent=64, cond=896, freq
 
 
 def latent_proj_weights(seed=1, latent=64, hidden=896, std=0.02):
-    """The adaLN head's latent -> next LM input linear (BASELINE config 5's
-    64 -> 896 projection) under aggregator.proj."""
+    """The adaLN head's latent -> next LM input linear (the LM + flow-head
+    loop's 64 -> 896 projection) under aggregator.proj."""
     W = {}
     _lin(W, seed, "aggregator.proj", hidden, latent, std)
     return W

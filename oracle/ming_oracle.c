@@ -618,7 +618,7 @@ void mo_aggregate(const mo_agg* a, const uint16_t* latent, int B, uint16_t* out,
 }
 
 /* ------------------------------------------------------------------ */
-/* adaLN-Zero DiT head (no reference code).           */
+/* adaLN-Zero DiT head (the benchmark's flow head; no reference code). */
 /* Pinned choices: LayerNorm without affine (eps 1e-6); modulation        */
 /* h = LN(x) * (1 + scale) + shift; gated residuals; SiLU(c) feeds every */
 /* modulation linear; interleaved rotary over the frame positions; CFG   */

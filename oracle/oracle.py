@@ -359,8 +359,8 @@ def pack(codes, bits):
 
 
 def ada_latent_proj(W, latent):
-    """The adaLN head's latent path into the next LM input (
-    a 64 -> 896 linear; no reference code, choice pinned with the product):
+    """The adaLN head's latent path into the next LM input (the LM + flow-head
+    loop's 64 -> 896 linear; no reference code, choice pinned with the product):
     the mean of the patch's frames in f32, frames in order, rounded to bf16;
     then aggregator.proj as an f32 dot plus bias, rounded to bf16.
     latent: uint16 bf16 [B][F][64] -> uint16 [B][896]."""

@@ -1,5 +1,5 @@
 """GPU parity of the flow head (token mode = the reference's head; adaLN mode
-= BASELINE config 4) and the aggregator, through the C ABI, against the CPU
+= the benchmark's adaLN-Zero head) and the aggregator, through the C ABI, against the CPU
 oracle.
 
 Gate: each Euler step teacher-forced (both sides start the step from the
@@ -120,8 +120,8 @@ def test_cfm_adaln_parity(ada_head, B):
 @pytest.mark.parametrize("B", [1, 5, 32])
 def test_ada_latent_proj_parity(ada_head, B):
     """adaLN mode's aggregate: the latent patch [B][4][64] -> the next LM input
-    [B][896] (mean over the frames, then aggregator.proj; BASELINE config 5's
-    64 -> 896 linear), against the oracle's restatement, twice in a row."""
+    [B][896] (mean over the frames, then aggregator.proj; the LM + flow-head
+    loop's 64 -> 896 linear), against the oracle's restatement, twice in a row."""
     W, ctx = ada_head
     lat = synth.normal_bf16(14, f"ada.lat.{B}", (B, 4, 64))
     ref = O.ada_latent_proj(W, lat)

@@ -1,17 +1,17 @@
 """GPU parity of the LM decode path through the C ABI against the CPU oracle.
 
-Tolerance: per-step post-norm hidden states within
+Tolerance (the benchmark's stated bf16 tolerance): per-step post-norm hidden states within
 max-abs 2e-2 and cosine > 0.999 (bf16), gated on teacher-forced steps (both
 sides get the oracle's input each step, as the reference's parity tool does,
 src/ming_parity.zig:6-8). Integer work — KV placement through the block table
 and quantized-weight unpacking — is compared bit for bit.
 
-Conditioning: with BASELINE's 4-bit init (uniform codes, scales
+Conditioning: with the benchmark's 4-bit init (uniform codes, scales
 U(0.005, 0.02): weight std ~0.058) attention scores are large and peaky, and a
 bf16 rounding difference can move a row's attention to another position: the
 oracle's own fused and plain-graph rounding modes then disagree on a few rows
 by O(1). The strict gates therefore run 4/8-bit models with scales
-U(0.002, 0.005) (weight std ~0.016, like the bf16 config); the BASELINE
+U(0.002, 0.005) (weight std ~0.016, like the bf16 config); the benchmark's
 distribution is gated against that fused-vs-graph spread instead
 (test_q4_baseline_init_within_reference_spread).
 """
@@ -359,7 +359,7 @@ def test_errors_are_reported(q4_24):
 
 
 def test_q4_baseline_init_within_reference_spread(cuda_ok):
-    """BASELINE's 4-bit distribution: every row of the GPU's output is at least
+    """The benchmark's 4-bit distribution: every row of the GPU's output is at least
     as close to the oracle's fused-rounding result as the oracle's two
     rounding modes (the reference's fused kernels vs its plain MLX graph) are
     to each other, plus the strict tolerance; and most rows meet the strict

@@ -61,7 +61,7 @@ def test_dequant_is_mlx_affine():
         ref = (sf * codes + bfv).astype(np.float32)
         for r in range(5):
             assert (O.lin_row(W, "t", r) == ref[r]).all()
-        # BASELINE's distribution: codes uniform over 0..2^bits-1, scales in [0.005, 0.02]
+        # the benchmark's distribution: codes uniform over 0..2^bits-1, scales in [0.005, 0.02]
         assert codes.max() == (1 << bits) - 1 and codes.min() == 0
         assert 0.0049 <= synth.bf16_to_f32(s).min() and synth.bf16_to_f32(s).max() <= 0.0201
 
