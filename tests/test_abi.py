@@ -67,3 +67,33 @@ def test_null_arguments_are_errors():
     assert L.ming_cuda_finalize(None) == 1
     assert L.ming_cuda_sync(None) == 1
     assert L.ming_cuda_destroy(None) == 0
+
+
+def test_every_call_rejects_a_null_context():
+    """Each entry point checks its context before any CUDA call and returns
+    MING_ERR_INVALID with a message, as the reference's check(rc) expects."""
+    _ensure_built()
+    L = M.lib()
+    i32, u16, f32 = ctypes.c_int(0), (ctypes.c_uint16 * 8)(), (ctypes.c_float * 8)()
+    ids = (ctypes.c_int * 1)(0)
+    calls = {
+        "seq_alloc": lambda: L.ming_cuda_seq_alloc(None, ctypes.byref(i32)),
+        "seq_free": lambda: L.ming_cuda_seq_free(None, 0),
+        "seq_len": lambda: L.ming_cuda_seq_len(None, 0, ctypes.byref(i32)),
+        "seq_truncate": lambda: L.ming_cuda_seq_truncate(None, 0, 0),
+        "lm_prefill": lambda: L.ming_cuda_lm_prefill(None, 0, u16, 1, u16, f32, 0),
+        "lm_decode": lambda: L.ming_cuda_lm_decode(None, 1, ids, u16, u16, f32, 0),
+        "lm_decode_noalloc": lambda: L.ming_cuda_lm_decode_noalloc(None, 1, ids, u16, u16, f32, 0),
+        "lm_generate": lambda: L.ming_cuda_lm_generate(None, 1, ids, u16, 1, u16, f32, 0),
+        "cfm_sample": lambda: L.ming_cuda_cfm_sample(None, 1, u16, u16, u16, None, ctypes.c_float(2.0), ctypes.c_float(0.0),
+                                                     u16, 0),
+        "cfm_steps": lambda: L.ming_cuda_cfm_steps(None, 1, u16, u16, u16, None, ctypes.c_float(2.0), ctypes.c_float(0.0),
+                                                   0, 1, u16, 0),
+        "aggregate": lambda: L.ming_cuda_aggregate(None, 1, u16, u16, 0),
+        "kv_read": lambda: L.ming_cuda_kv_read(None, 0, 0, 0, 1, u16, u16),
+        "step_kernels": lambda: L.ming_cuda_step_kernels(None, 1, ctypes.byref(i32)),
+        "flow_temb": lambda: L.ming_cuda_flow_temb(None, u16),
+    }
+    for name, call in calls.items():
+        assert call() == 1, name
+        assert L.ming_cuda_last_error(), name
