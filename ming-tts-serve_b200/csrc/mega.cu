@@ -70,7 +70,7 @@ MING_DEV void cp16(void* dst, const void* src) {
 }
 MING_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 MING_DEV void cp_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
-MING_DEV void cbar() { asm volatile("bar.sync 1, 256;\n" ::: "memory"); }  // consumer warps only
+MING_DEV void cbar() { asm volatile("bar.sync 1, %0;\n" ::"n"(MG_CT) : "memory"); }  // consumer warps only
 MING_DEV uint64_t ldr64(const void* p) {
     uint64_t v;
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
@@ -316,11 +316,11 @@ template <bool F16>
 MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint16_t* nw) {
     const int tid = threadIdx.x;
     uint4* z = reinterpret_cast<uint4*>(sm.sB);
-    for (int e = tid; e < nstage * 4 * 32 / 2; e += 256) z[e] = make_uint4(0u, 0u, 0u, 0u);
+    for (int e = tid; e < nstage * 4 * 32 / 2; e += MG_CT) z[e] = make_uint4(0u, 0u, 0u, 0u);
     cbar();
     const int tot = nstage * B * 16;
     const int totr = (tot + 31) & ~31;  // warp-uniform trip count: every lane reaches the shuffles
-    for (int e = tid; e < totr; e += 256) {
+    for (int e = tid; e < totr; e += MG_CT) {
         const bool act = e < tot;
         const int q16 = e & 15, sb = e >> 4, si = act ? divB(sb, sm.ms->bm) : 0, b = act ? sb - si * B : 0;
         const int ks = q16 >> 2, tq = q16 & 3, kk = ks * 16 + 2 * tq;
@@ -374,7 +374,7 @@ MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, const MegaDev& a, cons
     int b = 0, f = tid * 2;
     while (f >= H) f -= H, b++;
 #pragma unroll 1
-    for (int idx = tid * 2; idx < B * H; idx += 512) {
+    for (int idx = tid * 2; idx < B * H; idx += 2 * MG_CT) {
         float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sm.sX + idx));
         if (acc) {
             const unsigned long long* pw = acc + (size_t)b * a.acc_w + f;
@@ -394,7 +394,7 @@ MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, const MegaDev& a, cons
                 ss[bb] += dss;
                 am[bb] = fmaxf(am[bb], dam);
             }
-        f += 512;
+        f += 2 * MG_CT;
         while (f >= H) f -= H, b++;
     }
 #pragma unroll 1
@@ -474,7 +474,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
     for (int jj = 0; jj < nsc; jj++) {
         const int w0 = max(i0, jj * a.gps), w1 = min(i1, (jj + 1) * a.gps);
         if ((!skip || w0 < w1) && !mbar_wait(&full[sl], par)) atomicCAS(cx.fail, 0, 2);
-        if (sm.st && lane == 0 && p == 2 && w0 == i0 && w0 < w1) sm.st[56 + warp] = clock64();
+        if (sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p == 2 && w0 == i0 && w0 < w1) sm.st[56 + warp] = clock64();
         if (w0 < w1 && !*(volatile int*)cx.fail) {
             const uint8_t* sbase = ring + (size_t)sl * a.slot_bytes;
 #pragma unroll 1
@@ -524,7 +524,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[sl]);  // before any global write of this phase
-        if (sm.st && lane == 0 && p >= 2 && w1 == i1 && w0 < w1) sm.st[40 + (p - 2) * 8 + warp] = clock64();
+        if (sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p >= 2 && w1 == i1 && w0 < w1) sm.st[40 + (p - 2) * 8 + warp] = clock64();
         if (++sl == a.nslots) {
             sl = 0;
             par ^= 1u;
@@ -547,7 +547,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
     const int t0 = g0 / gpt, nt = (g1 - 1) / gpt - t0 + 1, B = a.B;
     if (out == OUT_ACC) {
         // entries (tile, row r, batch row b) with b padded to 4
-        for (int e = threadIdx.x; e < nt * 64; e += 256) {
+        for (int e = threadIdx.x; e < nt * 64; e += MG_CT) {
             const int b = e & 3, r = (e >> 2) & 15, t = t0 + (e >> 6);
             if (b >= B) continue;
             float s = 0.f;
@@ -562,7 +562,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
         }
     } else {
         // whole gate|up tiles: rows 0..7 gate, 8..15 up of features 8t..8t+7
-        for (int e = threadIdx.x; e < nt * 32; e += 256) {
+        for (int e = threadIdx.x; e < nt * 32; e += MG_CT) {
             const int b = e & 3, r = (e >> 2) & 7, t = t0 + (e >> 5);
             if (b >= B) continue;
             float gs = 0.f, us = 0.f;
@@ -581,6 +581,19 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
         }
     }
     MG_SUB(4)
+}
+
+// The combine's per-dim partial sums of the MG_NQ thread groups, in a fixed
+// order (pairwise for four groups).
+MING_DEV float sum_groups(const float* red, int d) {
+    if constexpr (MG_NQ == 4) {
+        return (red[d] + red[64 + d]) + (red[128 + d] + red[192 + d]);
+    } else {
+        float o = red[d];
+#pragma unroll
+        for (int q = 1; q < MG_NQ; q++) o += red[q * 64 + d];
+        return o;
+    }
 }
 
 // Attention of one (row, query head, 128-position chunk) item. q of the head
@@ -607,7 +620,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     float2* sP = reinterpret_cast<float2*>(sS + MG_ATT_CH);     // [8 warps][32]
     const int* bt = sm.bt + b * MG_BT_INTS;
     // 1. prefetch cached K/V rows [p0, pc)
-    for (int e = tid; e < (pc - p0) * 8; e += 256) {
+    for (int e = tid; e < (pc - p0) * 8; e += MG_CT) {
         const int j = e >> 3, piece = e & 7, p = p0 + j;
         const int page = bt[p / PAGE];
         cp16(sK + j * KS + piece * 8, a.kv.pool + kv_index(a.kv, page, l, 0, g, p % PAGE) + piece * 8);
@@ -755,10 +768,10 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     const uint64_t* ob = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART;
     float* cm = sS;       // [no] chunk maxima (scores are no longer read)
     float* cl = sS + 64;  // [no] chunk sums
-    const int d = tid & 63, qt = tid >> 6;
+    const int d = tid & 63, qt = tid >> 6;  // qt < MG_NQ
     uint64_t va[4];
 #pragma unroll
-    for (int k = 0; k < 4; k++) va[k] = qt + 4 * k < no ? ldr64(ob + (size_t)(qt + 4 * k) * MG_PART + 2 + d) : 0ull;
+    for (int k = 0; k < 4; k++) va[k] = qt + MG_NQ * k < no ? ldr64(ob + (size_t)(qt + MG_NQ * k) * MG_PART + 2 + d) : 0ull;
     if (tid < 2 * no) {
         const uint64_t* w = ob + (size_t)(tid >> 1) * MG_PART + (tid & 1);
         const uint64_t v = ldr64(w);
@@ -775,14 +788,14 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     const float il = 1.0f / L;
     float v = 0.f;
 #pragma unroll 1
-    for (int s0 = qt; s0 < no; s0 += 16) {
+    for (int s0 = qt; s0 < no; s0 += 4 * MG_NQ) {
         if (s0 != qt) {
 #pragma unroll
-            for (int k = 0; k < 4; k++) va[k] = s0 + 4 * k < no ? ldr64(ob + (size_t)(s0 + 4 * k) * MG_PART + 2 + d) : 0ull;
+            for (int k = 0; k < 4; k++) va[k] = s0 + MG_NQ * k < no ? ldr64(ob + (size_t)(s0 + MG_NQ * k) * MG_PART + 2 + d) : 0ull;
         }
 #pragma unroll
         for (int k = 0; k < 4; k++) {
-            const int sk = s0 + 4 * k;
+            const int sk = s0 + MG_NQ * k;
             if (sk >= no) continue;
             const uint64_t* w = ob + (size_t)sk * MG_PART + 2 + d;
             const float x = (uint32_t)(va[k] >> 32) == tag ? __uint_as_float((uint32_t)va[k]) : poll(cx, w, tag);
@@ -793,7 +806,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     red[qt * 64 + d] = v;
     cbar();
     if (tid < HD) {
-        const float o = (red[tid] + red[64 + tid]) + (red[128 + tid] + red[192 + tid]) + own[tid] * (expf(ms->om - M) * il);
+        const float o = sum_groups(red, tid) + own[tid] * (expf(ms->om - M) * il);
         str64(a.comb + ((size_t)b * a.heads + h) * HD + tid, tagged(tag, rb(o)));
     }
 }
@@ -805,7 +818,7 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
     const int B = a.B, tot = nst * 64 * B;
-    for (int e = threadIdx.x; e < tot; e += 256) {
+    for (int e = threadIdx.x; e < tot; e += MG_CT) {
         const int qd = divB(e, ms->bm), b = e - qd * B, si = qd >> 6, d = qd & 63;
         const int h = si + base < gpt ? si + base : si + base - gpt;
         const uint64_t* p = a.comb + ((size_t)b * a.heads + h) * HD + d;
@@ -887,8 +900,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
     const uint32_t epoch = ms->epoch;
 
     // ---------------- producer warp: stream this CTA's weight ranges ----------------
-    if (tid >= 256) {
-        if (tid == 256) {
+    if (tid >= MG_CT) {
+        if (tid == MG_CT) {
             int sc = 0;
             bool ok = true;
             for (int l = 0; l < a.layers && ok; l++) {
@@ -941,9 +954,9 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
         const size_t per = (size_t)a.layers * MG_NACC * MG_MAXB * a.acc_w;  // int64 per parity
         uint4* z = reinterpret_cast<uint4*>(a.acc + (size_t)((epoch + 1) & 1) * per);
         const size_t n2 = per / 2, lo = n2 * c / a.C, hi = n2 * (c + 1) / a.C;
-        for (size_t i = lo + tid; i < hi; i += 256) z[i] = make_uint4(0u, 0u, 0u, 0u);
+        for (size_t i = lo + tid; i < hi; i += MG_CT) z[i] = make_uint4(0u, 0u, 0u, 0u);
     }
-    for (int idx = tid; idx < B * H; idx += 256) sm.sX[idx] = a.x_in[idx];
+    for (int idx = tid; idx < B * H; idx += MG_CT) sm.sX[idx] = a.x_in[idx];
     cbar();
     long long* tr = a.trace ? a.trace + (size_t)c * a.layers * MG_TRACE : nullptr;
 #define MG_STAMP(k) \
@@ -1009,7 +1022,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
                     if ((uint32_t)(ldr64(hp) >> 32) != tag) poll(cx, hp, tag);
                 }
                 if (check()) break;
-                for (int e = tid; e < nst * 16 * B; e += 256) {
+                for (int e = tid; e < nst * 16 * B; e += MG_CT) {
                     const int qq = divB(e, ms->bm), b = e - qq * B, si = qq >> 4, k4 = qq & 15;
                     const int kg = si + base < gpt ? si + base : si + base - gpt;
                     const uint64_t* src = hb + (size_t)b * a.FF + kg * 64 + k4 * 4;
@@ -1051,7 +1064,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             uint16_t* ob = a.out_cell ? *a.out_cell : nullptr;
             uint16_t* oo = ob ? ob + ((size_t)ms->step * B + b) * H : nullptr;
             float l0 = 0.f, l1 = 0.f;
-            for (int f = tid; f < H; f += 256) {
+            for (int f = tid; f < H; f += MG_CT) {
                 const float zf = rb(bf2f(a.norm[f]) * rb(bf2f(sm.sX[b * H + f]) * inv));
                 const uint16_t zb = f2bf(zf);
                 a.z[(size_t)b * H + f] = zb;
@@ -1064,14 +1077,14 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             l1 = warp_sum(l1);
             if (lane == 0) {
                 ms->red[warp] = l0;
-                ms->red[8 + warp] = l1;
+                ms->red[MG_CWARPS + warp] = l1;
             }
             cbar();
             if (tid == 0) {
                 float s0 = 0.f, s1 = 0.f;
                 for (int w = 0; w < MG_CWARPS; w++) {
                     s0 += ms->red[w];
-                    s1 += ms->red[8 + w];
+                    s1 += ms->red[MG_CWARPS + w];
                 }
                 s0 = rb(s0 + bf2f(a.stop_b[0]));
                 s1 = rb(s1 + bf2f(a.stop_b[1]));

@@ -43,13 +43,19 @@ namespace ming {
 
 constexpr int MG_CWARPS = 8;                      // consumer warps
 constexpr int MG_THREADS = (MG_CWARPS + 1) * 32;  // + one producer warp
+constexpr int MG_CT = MG_CWARPS * 32;             // consumer threads
+constexpr int MG_NQ = MG_CT / 64;                 // groups of 64 threads (one per head dim) in the attention combine
+static_assert(MG_CT >= 128 && MG_CT % 64 == 0, "consumer threads: whole 64-thread groups, at least one per chunk position");
 constexpr int MG_MAXB = 4;                        // rows per step (mma n-tile of 8, half used)
 constexpr int MG_ATT_CH = 128;                    // positions per attention item
 constexpr int MG_PART = 2 + HD;                   // m, l, acc[64] per attention partial
 constexpr int MG_NPH = 4;                         // GEMV phases: P0 qkv, P2 o, P3 gate/up, P4 down
 constexpr int MG_FIX = 32;                        // fraction bits of the fixed-point accumulators
 constexpr int MG_MAX_STAGE = 32;                  // most 64-groups of activations one CTA stages per phase
-constexpr int MG_TRACE = 64;                      // clock64 stamp slots per (CTA, layer) when tracing
+// clock64 stamp slots per (CTA, layer) when tracing: 0-9 phase boundaries,
+// 10-35 sub-steps of the four GEMV phases, 40-55 the end of each of the first
+// 8 warps' runs in gate|up and down, 56-63 their first gate|up slot in hand
+constexpr int MG_TRACE = 64;
 enum { MG_ACC_QKV = 0, MG_ACC_X1 = 1, MG_ACC_X2 = 2, MG_NACC = 3 };
 constexpr int MG_MAX_TILES = 128;                 // most tiles of a split-K phase (q|k|v, o_proj, down)
 
