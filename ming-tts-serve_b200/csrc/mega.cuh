@@ -15,7 +15,7 @@
 //     cp.async.bulk into a shared-memory ring guarded by mbarriers, running
 //     ahead by the ring's capacity (several layers at 4 bits), together with
 //     each layer's norm weights and q|k|v bias;
-//   * 8 consumer warps run mma.sync on the ring; split-K partial sums are
+//   * MG_CWARPS (8) consumer warps run mma.sync on the ring; split-K sums are
 //     reduced with red.global.add.u64 on int64 fixed-point accumulators
 //     (integer addition is associative: the result is bit-deterministic);
 //   * every contribution also adds 2^56, so the top byte of an accumulator
