@@ -1667,14 +1667,15 @@ int ming_cuda_unpack_linear(ming_ctx* c, const char* name, float* out) {
 }
 
 // Diagnostics: copies the persistent kernel's phase trace (MING_MEGA_TRACE=1):
-// [C][layers][32] clock64 stamps of the last step. Returns the CTA count in *n.
-// Without it, the per-kernel step's launch trace (MING_KTRACE=1):
+// [C][layers][MG_TRACE = 64] clock64 stamps of the last step (slot meanings
+// beside MG_TRACE; ming_b200/mega_trace.py prints them). Returns the CTA
+// count in *n. Without it, the per-kernel step's launch trace (MING_KTRACE=1):
 // [160 slots][1024 CTAs][8] globaltimer stamps, *n = -(slots used).
 extern "C" int ming_cuda_debug_trace(ming_ctx* c, long long* out, int cap, int* n) {
     if (!c || !n) return fail(MING_ERR_INVALID, "null argument");
     *n = 0;
     if (!c->mega_on || !c->mega.trace) {
-        // the per-kernel step's launch trace (MING_KTRACE=1): [slot][CTA][4] globaltimer stamps
+        // the per-kernel step's launch trace (MING_KTRACE=1): [slot][CTA][8] globaltimer stamps
         if (!c->ktrace) return MING_OK;
         const size_t cnt = (size_t)KT_SLOTS * KT_CTAS * 8;
         if ((size_t)cap < cnt) return fail(MING_ERR_INVALID, "trace buffer too small");
