@@ -120,7 +120,10 @@ int ming_cuda_lm_generate(ming_ctx* ctx, int B, const int* seq_ids, const uint16
  * address; make that first call before any stream capture. All calls on a
  * device share the array and its contents persist between calls; nothing in
  * it needs to start at zero, but calls that overlap on the GPU (other
- * streams, other contexts on the same device) race on it.
+ * streams, other contexts on the same device) race on it. At most 16 query
+ * heads. With host pointers a bounded device wait that gave up is reported
+ * by this call (MING_ERR_CUDA); with device pointers, by the next
+ * ming_cuda_sync.
  * No reference counterpart: the reference's MLX allocator owns all memory. */
 int ming_cuda_lm_decode_noalloc(ming_ctx* ctx, int B, const int* seq_ids, const uint16_t* x, uint16_t* out, float* stop,
                                 int ptr_kind);
@@ -144,6 +147,60 @@ int ming_cuda_cfm_steps(ming_ctx* ctx, int B, const uint16_t* z, const uint16_t*
  * -> next LM input rows [B][hidden]. */
 int ming_cuda_aggregate(ming_ctx* ctx, int B, const uint16_t* latent, uint16_t* out, int ptr_kind);
 
+/* ---- the autoregressive loop: sampleLatents and a request scheduler ---- */
+
+/* SampleParams (src/ming_model.zig:1368-1373) plus the position cap the
+ * reference fixes at MAX_CACHE_LEN (src/ming_model.zig:46-47). */
+typedef struct ming_sample_params {
+    int max_steps;     /* latents per request at most (1000) */
+    int max_len;       /* prompt + generated positions (512) */
+    float cfg;         /* classifier-free guidance scale (2.0) */
+    float sigma;       /* SDE scale (0.25) */
+    float temperature; /* SDE temperature (0.0: shift = sigma * sqrt(temperature) = 0, no SDE term) */
+} ming_sample_params;
+
+void ming_cuda_default_sample_params(ming_sample_params* p);
+
+/* sampleLatents (src/ming_model.zig:1388-1480) for one sequence, on the
+ * device: prefill `embeds` [L][hidden]; then per step the flow head on the
+ * last hidden state z (cfmSample, with the previous latent as history in
+ * token mode; prompt_latent [latent] seeds it, NULL = zeros), the aggregator,
+ * one LM step, and the stop rule on z's stop probability: the step's latent
+ * is emitted, then the loop ends if p > 0.5 and step > 3, or after
+ * min(max_steps, max_len - L) steps. Noise: the reference's replay bank
+ * noise_bank [bank_steps][11][frames * latent] (row 0 the start noise, rows
+ * 1..10 the SDE draws; at most bank_steps steps), or, with noise_bank NULL,
+ * the library's seeded stream (SplitMix64 + Box-Muller over
+ * (seed, "loop.noise.<step>"), 11 rows per step). Host pointers. latents
+ * [cap][frames * latent], *n = latents emitted; z_trace [cap][hidden] and
+ * stop_trace [cap] (either may be NULL) receive each step's z and p(stop),
+ * the reference's Trace (src/ming_model.zig:1376-1385). */
+int ming_cuda_sample_latents(ming_ctx* ctx, const uint16_t* embeds, int L, const uint16_t* prompt_latent,
+                             const ming_sample_params* p, const uint16_t* noise_bank, int bank_steps, uint64_t seed,
+                             uint16_t* latents, int cap, int* n, uint16_t* z_trace, float* stop_trace);
+
+/* The same loop over up to max_rows concurrent requests (continuous
+ * batching in place of the reference's one-at-a-time FIFO,
+ * src/ming_service.zig:175-206,277-287). One CUDA graph per row count runs a
+ * whole step for every active row; stop flags come back one step behind
+ * (the next step is already queued); finished rows retire and queued
+ * requests take their places, their prompts prefilling between two steps.
+ * The context must not run other work while a loop has active rows (the
+ * loop uses its step buffers). */
+typedef struct ming_loop ming_loop;
+int ming_cuda_loop_create(ming_ctx* ctx, int max_rows, const ming_sample_params* p, ming_loop** out);
+/* Queues one request (arguments as in ming_cuda_sample_latents; want_trace
+ * keeps per-step z for loop_result) and admits it at once if a row is free. */
+int ming_cuda_loop_submit(ming_loop* lp, const uint16_t* embeds, int L, const uint16_t* prompt_latent,
+                          const uint16_t* noise_bank, int bank_steps, uint64_t seed, int want_trace, int* req);
+/* Runs one step of every active row; *active and *queued (may be NULL)
+ * report the rows still running and the requests waiting for a row. */
+int ming_cuda_loop_step(ming_loop* lp, int* active, int* queued);
+/* A finished request's latents [cap][frames * latent] and traces; *n = -1
+ * while it is still queued or running. Fetching releases the request. */
+int ming_cuda_loop_result(ming_loop* lp, int req, uint16_t* latents, int cap, int* n, uint16_t* z_trace, float* stop_trace);
+int ming_cuda_loop_destroy(ming_loop* lp);
+
 /* The context's CUDA stream (a cudaStream_t), for event timing by callers. */
 int ming_cuda_get_stream(ming_ctx* ctx, void** stream);
 int ming_cuda_sync(ming_ctx* ctx);
@@ -159,6 +216,15 @@ const char* ming_cuda_last_error(void);
 /* Reads positions [pos0, pos0+n) of one layer's cache through the block
  * table: k, v host [kv_heads][n][head_dim] bf16. */
 int ming_cuda_kv_read(ming_ctx* ctx, int seq_id, int layer, int pos0, int n, uint16_t* k, uint16_t* v);
+/* Writes positions [pos0, pos0+n) of one layer's cache through the block
+ * table (k, v host [kv_heads][n][head_dim] bf16), allocating pages as needed;
+ * pos0 <= the sequence's length, which grows to pos0 + n if shorter. The
+ * device side indexes the pool with the same function the decode kernels
+ * append with, so a write followed by ming_cuda_kv_read round-trips bit for
+ * bit. Restores a saved prompt cache; tests inject known caches with it.
+ * No reference counterpart (the reference's KvCache holds MLX arrays,
+ * src/ming_model.zig:638-662). */
+int ming_cuda_kv_write(ming_ctx* ctx, int seq_id, int layer, int pos0, int n, const uint16_t* k, const uint16_t* v);
 /* Dequantizes a loaded linear back from its device tiles (the kernels' own
  * unpack path): out host [out][in] f32 in the reference's row order. */
 int ming_cuda_unpack_linear(ming_ctx* ctx, const char* weight_name, float* out);

@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
     if (tr) tr[7] = gtimer();
 }
 
-void launch_attn(const AttnArgs& a, int rows, cudaStream_t s) {
+cudaError_t launch_attn(const AttnArgs& a, int rows, cudaStream_t s) {
     static int attr_set[64] = {};  // per device: the dynamic shared memory opt-ins
     int dev = 0;
     cudaGetDevice(&dev);
@@ -242,8 +242,10 @@ void launch_attn(const AttnArgs& a, int rows, cudaStream_t s) {
     at[1].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = cl && a.nsplit_max > 1 ? 2 : 1;
-    if (cl) cudaLaunchKernelEx(&cfg, attn_partial_kernel<true>, a);
-    else cudaLaunchKernelEx(&cfg, attn_partial_kernel<false>, a);
+    // a cluster launch can fail where a plain one would not (e.g. the cluster's
+    // shared memory does not fit); the caller checks the result
+    if (cl) return cudaLaunchKernelEx(&cfg, attn_partial_kernel<true>, a);
+    return cudaLaunchKernelEx(&cfg, attn_partial_kernel<false>, a);
 }
 
 bool attn_fused_combine(const AttnArgs& a) { return a.att && a.nsplit_max <= 8; }
@@ -286,8 +288,8 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* part, Ro
     }
 }
 
-void launch_attn_combine(const float* part, RowsDev rows, int nsplit_max, int heads, uint16_t* att, int nrows,
-                         cudaStream_t s) {
+cudaError_t launch_attn_combine(const float* part, RowsDev rows, int nsplit_max, int heads, uint16_t* att, int nrows,
+                                cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(nrows);
     cfg.blockDim = dim3(256);
@@ -298,7 +300,7 @@ void launch_attn_combine(const float* part, RowsDev rows, int nsplit_max, int he
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    cudaLaunchKernelEx(&cfg, attn_combine_kernel, part, rows, nsplit_max, heads, att);
+    return cudaLaunchKernelEx(&cfg, attn_combine_kernel, part, rows, nsplit_max, heads, att);
 }
 
 // Final RMSNorm (MLX fast_rms_norm: rb(w * rb(x * inv))) and the stop head:

@@ -166,10 +166,10 @@ struct FinalArgs {
 };
 
 // Launchers (lm.cu)
-void launch_attn(const AttnArgs& a, int rows, cudaStream_t s);
+cudaError_t launch_attn(const AttnArgs& a, int rows, cudaStream_t s);
 bool attn_fused_combine(const AttnArgs& a);  // launch_attn wrote att itself (no combine launch needed)
-void launch_attn_combine(const float* part, RowsDev rows, int nsplit_max, int heads, uint16_t* att, int nrows,
-                         cudaStream_t s);
+cudaError_t launch_attn_combine(const float* part, RowsDev rows, int nsplit_max, int heads, uint16_t* att, int nrows,
+                                cudaStream_t s);
 void launch_final(const FinalArgs& a, int rows, cudaStream_t s);
 void launch_step_begin(const StepDev& st, int rows, cudaStream_t s);
 

@@ -14,7 +14,7 @@
 #include <type_traits>
 #include <vector>
 
-#include "../../include/ming_cuda.h"
+#include "runtime.h"
 #include "bulk.cuh"
 #include "dit.cuh"
 #include "lm.cuh"
@@ -23,6 +23,7 @@
 #include "pack.h"
 
 using namespace ming;
+using namespace ming::rt;
 
 // ---------------------------------------------------------------------
 // errors
@@ -30,175 +31,17 @@ using namespace ming;
 
 static thread_local std::string g_err;
 
-namespace {
-
-struct Err {
-    int code;
-    std::string msg;
-};
-
-int fail(int code, const std::string& m) {
+int ming::rt::fail(int code, const std::string& m) {
     g_err = m;
     return code;
 }
-
-#define CK(call)                                                                                      \
-    do {                                                                                              \
-        cudaError_t e_ = (call);                                                                      \
-        if (e_ != cudaSuccess)                                                                        \
-            return fail(MING_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_));           \
-    } while (0)
-
-struct HostTensor {
-    int dtype = 0;
-    std::vector<int64_t> shape;
-    std::vector<uint8_t> data;
-    int64_t dim(int i) const { return i < (int)shape.size() ? shape[i] : 1; }
-};
-
-// A device allocation freed with the context.
-struct DevMem {
-    std::vector<void*> ptrs;
-    ~DevMem() {
-        for (void* p : ptrs) cudaFree(p);
-    }
-    template <class T>
-    T* alloc(size_t count, int* rc) {
-        void* p = nullptr;
-        if (count == 0) count = 1;
-        cudaError_t e = cudaMalloc(&p, count * sizeof(T));
-        if (e != cudaSuccess) {
-            *rc = fail(MING_ERR_NOMEM, std::string("cudaMalloc: ") + cudaGetErrorString(e));
-            return nullptr;
-        }
-        cudaMemset(p, 0, count * sizeof(T));
-        ptrs.push_back(p);
-        return static_cast<T*>(p);
-    }
-};
-
-struct PackedLin {
-    PackedW w;
-    std::vector<std::string> src_names;  // weight names of the sources
-    std::vector<RowRef> rows;
-    std::vector<int> src_out, src_in;
-};
-
-struct DitBlockW {
-    PackedLin ada, qkv, o, ff1, ff2;
-    uint16_t* norm1 = nullptr;
-    uint16_t* norm2 = nullptr;
-};
-
-struct SeqInfo {
-    bool live = false;
-    int len = 0;
-};
-
-}  // namespace
-
-struct ming_ctx {
-    int device = 0;
-    cudaStream_t stream = nullptr;
-    ming_cfg cfg{};
-    bool finalized = false;
-    std::map<std::string, HostTensor> staged;
-    DevMem mem;
-    std::vector<PackedLin*> all_lins;
-
-    // LM
-    struct Layer {
-        PackedLin qkv, o, gu, down;
-        uint16_t* ln1 = nullptr;
-        uint16_t* ln2 = nullptr;
-        bool ln1_unit = false, ln2_unit = false;  // every gain is exactly 1
-    };
-    std::vector<Layer> layers;
-    uint16_t* norm = nullptr;
-    uint16_t* stop_w = nullptr;
-    uint16_t* stop_b = nullptr;
-    float log2_theta = 0;
-
-    // KV
-    uint16_t* pool = nullptr;
-    int* bt = nullptr;
-    int bt_ld = 0;
-    std::vector<int> bt_host;
-    std::vector<int> free_pages;
-    std::vector<SeqInfo> seqs;
-
-    // activations / step state
-    int maxr = 0, nsplit = 0;
-    uint16_t *x = nullptr, *x1 = nullptr, *q = nullptr, *h = nullptr, *z = nullptr;
-    uint16_t* att = nullptr;  // [maxr][heads * 64] combined attention output (o_proj input)
-    LinScratch lin;           // staged activations of linears over more than 8 rows
-    float* stop = nullptr;
-    float* part = nullptr;
-    int *seq_len = nullptr, *row_seq = nullptr, *row_pos = nullptr, *step_counter = nullptr;
-    uint16_t** out_cell = nullptr;
-    float** stop_cell = nullptr;
-    std::vector<int> row_seq_host;
-    std::map<int, cudaGraphExec_t> decode_graphs;
-    // persistent decode kernel (batches of up to MG_MAXB rows)
-    bool mega_on = false;
-    MegaDev mega{};
-    int mega_smem = 0;
-    int* dev_err = nullptr;
-    int* err_host = nullptr;  // pinned: the device error flag read back with a call's outputs
-    bool cells_null = false;  // out_cell / stop_cell known to hold null (decode); generate sets them
-    // launch trace of the per-kernel step (MING_KTRACE=1): KT_SLOTS launches x
-    // KT_CTAS CTAs x 8 globaltimer stamps, slot = launch order in the step
-    long long* ktrace = nullptr;
-    int ktrace_used = 0;
-    int* mega_counter = nullptr;  // [2]: epoch (monotonic), generate step index
-    std::function<cudaError_t()> mega_reset;  // clean persistent-kernel state after a device error
-    uint16_t* gen_out = nullptr;
-    size_t gen_out_elems = 0;
-    float* gen_stop = nullptr;
-    size_t gen_stop_elems = 0;
-
-    // flow head
-    std::vector<DitBlockW> dit;
-    PackedLin t_mlp0, t_mlp2, x_emb, c_emb, final_ada, final_lin;
-    uint16_t* final_norm = nullptr;
-    uint16_t* final_w = nullptr;  // token final linear, raw bf16 [latent][H]
-    uint16_t* final_b = nullptr;
-    float* inv_freq = nullptr;
-    uint16_t* temb = nullptr;  // [10][H]
-    float flow_dt[10] = {0}, flow_sq[10] = {0};
-    uint16_t *f_z = nullptr, *f_zc = nullptr, *f_hist = nullptr, *f_y = nullptr, *f_sde = nullptr;
-    uint16_t *f_ce = nullptr, *f_xh = nullptr, *f_xy = nullptr, *f_rows = nullptr, *f_x1 = nullptr, *f_qkv = nullptr;
-    uint16_t *f_att = nullptr, *f_hh = nullptr, *f_sc = nullptr, *f_mod = nullptr;
-    float* f_vel = nullptr;
-    std::map<int, cudaGraphExec_t> cfm_graphs;  // (B, sde?, step0, nsteps) -> graph
-    float cfm_cfg = NAN, cfm_shift = NAN;
-
-    // aggregator
-    std::vector<DitBlockW> agg;
-    PackedLin agg_x_emb, agg_final;
-    // adaLN head: latent -> next LM input (mean over frames, then aggregator.proj)
-    PackedLin agg_proj;
-    bool agg_proj_on = false;
-    uint16_t* a_mean = nullptr;
-    uint16_t* agg_cls = nullptr;
-    uint16_t* agg_norm = nullptr;
-    float* agg_inv_freq = nullptr;
-    uint16_t *a_lat = nullptr, *a_rows = nullptr, *a_x1 = nullptr, *a_qkv = nullptr, *a_att = nullptr, *a_hh = nullptr,
-             *a_xe = nullptr, *a_out = nullptr;
-
-    ~ming_ctx() {
-        for (auto& kv : decode_graphs) cudaGraphExecDestroy(kv.second);
-        for (auto& kv : cfm_graphs) cudaGraphExecDestroy(kv.second);
-        for (PackedLin* l : all_lins) (void)l;
-        if (stream) cudaStreamDestroy(stream);
-    }
-};
 
 // ---------------------------------------------------------------------
 // linear launch dispatch
 // ---------------------------------------------------------------------
 
-namespace {
+namespace ming {
+namespace rt {
 
 template <int FMT, int NT, class Pro, class Epi>
 void launch_lin_t(const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
@@ -414,6 +257,16 @@ __global__ void unpack_tiles_kernel(PackedW W, float* out) {
             o[1] = hi;
         }
     }
+}
+
+// Writes K/V rows [n][64] of one layer into the paged pool through the block
+// table and kv_index, the same index function the decode kernels append
+// with (ming_cuda_kv_write). Grid (n, kv_heads, K|V), 64 threads: one value each.
+__global__ void kv_write_kernel(KvDev kv, int seq, int layer, int pos0, int n, const uint16_t* k, const uint16_t* v) {
+    const int j = blockIdx.x, h = blockIdx.y, which = blockIdx.z, d = threadIdx.x, pos = pos0 + j;
+    const int page = kv.bt[(size_t)seq * kv.bt_ld + pos / PAGE];
+    const uint16_t* src = which ? v : k;
+    kv.pool[kv_index(kv, page, layer, which, h, pos % PAGE) + d] = src[((size_t)h * n + j) * HD + d];
 }
 
 // ---------------------------------------------------------------------
@@ -675,7 +528,9 @@ long long* ktrace_slot(ming_ctx* c) {
 }
 
 // The 24-layer step over `rows` rows whose row_seq/row_pos are on the device.
-void enqueue_layers(ming_ctx* c, int rows, bool decode) {
+// Returns the first failed attention launch (the linears' launches are
+// checked by the caller's cudaGetLastError).
+cudaError_t enqueue_layers(ming_ctx* c, int rows, bool decode) {
     const ming_cfg& f = c->cfg;
     c->ktrace_used = 0;
     RowsDev rd{c->row_seq, c->row_pos};
@@ -686,18 +541,42 @@ void enqueue_layers(ming_ctx* c, int rows, bool decode) {
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, rows, c->stream);
         AttnArgs aa{c->q, c->part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, decode ? 1 : 0, c->att};
         aa.trace = (long)aa.nsplit_max * aa.kv_heads * rows <= KT_CTAS ? ktrace_slot(c) : nullptr;
-        launch_attn(aa, rows, c->stream);
-        if (!attn_fused_combine(aa)) launch_attn_combine(c->part, rd, c->nsplit, f.heads, c->att, rows, c->stream);
+        cudaError_t e = launch_attn(aa, rows, c->stream);
+        if (e == cudaSuccess && !attn_fused_combine(aa))
+            e = launch_attn_combine(c->part, rd, c->nsplit, f.heads, c->att, rows, c->stream);
+        if (e != cudaSuccess) return e;
         run_linear(c, L.o.w, ProPlain{c->att, f.heads * HD, 0},
                    EpiResidual{c->x, c->x1, nullptr, f.hidden}, rows, c->stream);
         run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln2_unit}, EpiSwiGLU{c->h, f.ff}, rows,
                    c->stream);
         run_linear(c, L.down.w, ProPlain{c->h, f.ff, 0}, EpiResidual{c->x1, c->x, nullptr, f.hidden}, rows, c->stream);
     }
+    return cudaSuccess;
 }
 
 StepDev step_dev(ming_ctx* c) {
     return StepDev{c->seq_len, c->row_seq, c->row_pos, c->step_counter, c->out_cell, c->stop_cell};
+}
+
+cudaError_t decode_enqueue(ming_ctx* c, int B) {
+    if (c->mega_on && B <= MG_MAXB) {
+        // one persistent launch per step: it reads the positions, bumps them,
+        // and writes z, the fed-back input and the stop probabilities
+        MegaDev a = c->mega;
+        a.B = B;
+        a.row_seq = c->row_seq;
+        a.x_in = c->x;
+        a.z = c->z;
+        a.feed = c->x;
+        a.stop = c->stop;
+        return launch_mega(a, c->mega_smem, c->stream);
+    }
+    launch_step_begin(step_dev(c), B, c->stream);
+    const cudaError_t le = enqueue_layers(c, B, true);
+    launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, c->x, step_dev(c), c->cfg.hidden, 0, 1,
+                           c->cfg.rms_eps},
+                 B, c->stream);
+    return le;
 }
 
 // Decode graph for B rows: step_begin, layers, final (+ feedback into x).
@@ -709,29 +588,11 @@ int decode_graph(ming_ctx* c, int B, cudaGraphExec_t* out) {
     }
     cudaGraph_t g;
     CK(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-    cudaError_t le = cudaSuccess;
-    if (c->mega_on && B <= MG_MAXB) {
-        // one persistent launch per step: it reads the positions, bumps them,
-        // and writes z, the fed-back input and the stop probabilities
-        MegaDev a = c->mega;
-        a.B = B;
-        a.row_seq = c->row_seq;
-        a.x_in = c->x;
-        a.z = c->z;
-        a.feed = c->x;
-        a.stop = c->stop;
-        le = launch_mega(a, c->mega_smem, c->stream);
-    } else {
-        launch_step_begin(step_dev(c), B, c->stream);
-        enqueue_layers(c, B, true);
-        launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, c->x, step_dev(c), c->cfg.hidden, 0, 1,
-                               c->cfg.rms_eps},
-                     B, c->stream);
-    }
+    const cudaError_t le = decode_enqueue(c, B);
     cudaError_t ce = cudaStreamEndCapture(c->stream, &g);
     if (le != cudaSuccess) {
         if (ce == cudaSuccess) cudaGraphDestroy(g);
-        return fail(MING_ERR_CUDA, std::string("persistent kernel launch: ") + cudaGetErrorString(le));
+        return fail(MING_ERR_CUDA, std::string("decode step launch: ") + cudaGetErrorString(le));
     }
     if (ce != cudaSuccess) return fail(MING_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
     cudaGraphExec_t ge;
@@ -1001,7 +862,61 @@ int cfm_ada_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift, i
     return MING_OK;
 }
 
-}  // namespace
+int cfm_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift, int step0, int nsteps) {
+    if (c->cfg.dit_mode == MING_DIT_ADALN) return cfm_ada_enqueue(c, B, with_sde, cfg, shift, step0, nsteps);
+    return cfm_token_enqueue(c, B, with_sde, cfg, shift, step0, nsteps);
+}
+
+int agg_enqueue(ming_ctx* c, int B, const uint16_t* latent) {
+    const ming_cfg& f = c->cfg;
+    cudaStream_t s = c->stream;
+    if (c->agg_proj_on) {
+        // adaLN head: latent [B][dit_frames][dit_latent] -> [B][hidden]
+        launch_latent_mean(latent, c->a_mean, B, f.dit_frames, f.dit_latent, s);
+        run_linear(c, c->agg_proj.w, ProPlain{c->a_mean, f.dit_latent, 0},
+                   EpiAct{c->a_out, nullptr, c->agg_proj.w.bias, f.hidden, 0, f.hidden}, B, s);
+        return MING_OK;
+    }
+    if (c->agg.empty()) return fail(MING_ERR_INVALID, "no aggregator configured");
+    const int H = f.dit_hidden, R = 2 * B;
+    run_linear(c, c->agg_x_emb.w, ProPlain{latent, f.dit_latent, 0}, EpiAct{c->a_xe, nullptr, c->agg_x_emb.w.bias, H, 0, H}, B,
+               s);
+    // rows [cls, x_emb(latent)] per sequence
+    for (int b = 0; b < B; b++)
+        CK(cudaMemcpyAsync(c->a_rows + (size_t)(2 * b) * H, c->agg_cls, (size_t)H * 2, cudaMemcpyDeviceToDevice, s));
+    CK(cudaMemcpy2DAsync(c->a_rows + H, (size_t)2 * H * 2, c->a_xe, (size_t)H * 2, (size_t)H * 2, B, cudaMemcpyDeviceToDevice,
+                         s));
+    for (auto& b : c->agg) {
+        run_linear(c, b.qkv.w, ProRms{c->a_rows, b.norm1, H, H, 1e-6f, 0, nullptr},
+                   EpiDitQKV{b.qkv.w.bias, c->a_qkv, c->agg_inv_freq, H, 2, R}, R, s);
+        launch_dit_attention(c->a_qkv, c->a_att, R, 2, H, f.dit_heads, s);
+        run_linear(c, b.o.w, ProPlain{c->a_att, H, 0}, EpiResidual{c->a_rows, c->a_x1, b.o.w.bias, H}, R, s);
+        run_linear(c, b.ff1.w, ProRms{c->a_x1, b.norm2, H, H, 1e-6f, 0, nullptr},
+                   EpiAct{c->a_hh, nullptr, b.ff1.w.bias, f.dit_ff, 1, f.dit_ff}, R, s);
+        run_linear(c, b.ff2.w, ProPlain{c->a_hh, f.dit_ff, 0}, EpiResidual{c->a_x1, c->a_rows, b.ff2.w.bias, H}, R, s);
+    }
+    // final RMSNorm + linear on each CLS row (row stride 2H selects them)
+    run_linear(c, c->agg_final.w, ProRmsGraph{c->a_rows, c->agg_norm, 2 * H, H, 1e-6f, 0, nullptr},
+               EpiAct{c->a_out, nullptr, c->agg_final.w.bias, f.hidden, 0, f.hidden}, B, s);
+    return MING_OK;
+}
+
+int seq_release(ming_ctx* c, int id) {
+    int rc = check_seq(c, id);
+    if (rc) return rc;
+    for (int p = 0; p < c->bt_ld; p++) {
+        int& e = c->bt_host[(size_t)id * c->bt_ld + p];
+        if (e >= 0) c->free_pages.push_back(e);
+        e = -1;
+    }
+    // -1 bytes are 0xff: the whole row reset in one queued fill
+    CK(cudaMemsetAsync(c->bt + (size_t)id * c->bt_ld, 0xff, (size_t)c->bt_ld * 4, c->stream));
+    c->seqs[id] = SeqInfo{};
+    return MING_OK;
+}
+
+}  // namespace rt
+}  // namespace ming
 
 // ---------------------------------------------------------------------
 // C ABI
@@ -1318,15 +1233,8 @@ int ming_cuda_seq_free(ming_ctx* c, int id) {
     if (!c) return fail(MING_ERR_INVALID, "null context");
     int rc = check_seq(c, id);
     if (rc) return rc;
-    CK(cudaStreamSynchronize(c->stream));  // no kernel may still read its pages
-    for (int p = 0; p < c->bt_ld; p++) {
-        int& e = c->bt_host[(size_t)id * c->bt_ld + p];
-        if (e >= 0) c->free_pages.push_back(e);
-        e = -1;
-    }
-    CK(cudaMemcpy(c->bt + (size_t)id * c->bt_ld, c->bt_host.data() + (size_t)id * c->bt_ld, c->bt_ld * 4,
-                  cudaMemcpyHostToDevice));
-    c->seqs[id] = SeqInfo{};
+    if ((rc = seq_release(c, id))) return rc;
+    CK(cudaStreamSynchronize(c->stream));
     return MING_OK;
 }
 
@@ -1366,7 +1274,8 @@ int ming_cuda_lm_prefill(ming_ctx* c, int s, const uint16_t* x, int L, uint16_t*
         CK(cudaMemcpyAsync(c->row_seq, seqv.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
         CK(cudaMemcpyAsync(c->row_pos, posv.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
         if ((rc = copy_in(c, c->x, x + (size_t)c0 * H, (size_t)n * H * 2, kind))) return rc;
-        enqueue_layers(c, n, false);
+        const cudaError_t le = enqueue_layers(c, n, false);
+        if (le != cudaSuccess) return fail(MING_ERR_CUDA, std::string("prefill attention launch: ") + cudaGetErrorString(le));
         if (out || stop) {
             launch_final(FinalArgs{c->x, c->norm, c->stop_w, c->stop_b, c->z, c->stop, nullptr, step_dev(c), H, 0, 0,
                                    c->cfg.rms_eps},
@@ -1532,52 +1441,16 @@ int ming_cuda_cfm_sample(ming_ctx* c, int B, const uint16_t* z, const uint16_t* 
 int ming_cuda_aggregate(ming_ctx* c, int B, const uint16_t* latent, uint16_t* out, int kind) {
     if (!c || !c->finalized) return fail(MING_ERR_INVALID, "context not finalized");
     const ming_cfg& f = c->cfg;
-    if (c->agg_proj_on) {
-        // adaLN head: latent [B][dit_frames][dit_latent] -> [B][hidden]
-        if (B < 1 || B > f.dit_max_batch || !latent || !out) return fail(MING_ERR_INVALID, "bad argument");
-        CK(cudaSetDevice(c->device));
-        const int F = f.dit_frames, LAT = f.dit_latent;
-        cudaStream_t s = c->stream;
-        int rc;
-        if ((rc = copy_in(c, c->a_lat, latent, (size_t)B * F * LAT * 2, kind))) return rc;
-        launch_latent_mean(c->a_lat, c->a_mean, B, F, LAT, s);
-        run_linear(c, c->agg_proj.w, ProPlain{c->a_mean, LAT, 0},
-                   EpiAct{c->a_out, nullptr, c->agg_proj.w.bias, f.hidden, 0, f.hidden}, B, s);
-        CK(cudaGetLastError());
-        if ((rc = copy_out(c, out, c->a_out, (size_t)B * f.hidden * 2, kind))) return rc;
-        if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(s));
-        return MING_OK;
-    }
-    if (c->agg.empty()) return fail(MING_ERR_INVALID, "no aggregator configured");
+    if (!c->agg_proj_on && c->agg.empty()) return fail(MING_ERR_INVALID, "no aggregator configured");
     if (B < 1 || B > f.dit_max_batch || !latent || !out) return fail(MING_ERR_INVALID, "bad argument");
     CK(cudaSetDevice(c->device));
-    const int H = f.dit_hidden, R = 2 * B;
-    cudaStream_t s = c->stream;
+    const int frames = c->agg_proj_on ? f.dit_frames : 1;
     int rc;
-    if ((rc = copy_in(c, c->a_lat, latent, (size_t)B * f.dit_latent * 2, kind))) return rc;
-    run_linear(c, c->agg_x_emb.w, ProPlain{c->a_lat, f.dit_latent, 0}, EpiAct{c->a_xe, nullptr, c->agg_x_emb.w.bias, H, 0, H}, B,
-               s);
-    // rows [cls, x_emb(latent)] per sequence
-    for (int b = 0; b < B; b++) {
-        CK(cudaMemcpyAsync(c->a_rows + (size_t)(2 * b) * H, c->agg_cls, (size_t)H * 2, cudaMemcpyDeviceToDevice, s));
-        CK(cudaMemcpyAsync(c->a_rows + (size_t)(2 * b + 1) * H, c->a_xe + (size_t)b * H, (size_t)H * 2,
-                           cudaMemcpyDeviceToDevice, s));
-    }
-    for (auto& b : c->agg) {
-        run_linear(c, b.qkv.w, ProRms{c->a_rows, b.norm1, H, H, 1e-6f, 0, nullptr},
-                   EpiDitQKV{b.qkv.w.bias, c->a_qkv, c->agg_inv_freq, H, 2, R}, R, s);
-        launch_dit_attention(c->a_qkv, c->a_att, R, 2, H, f.dit_heads, s);
-        run_linear(c, b.o.w, ProPlain{c->a_att, H, 0}, EpiResidual{c->a_rows, c->a_x1, b.o.w.bias, H}, R, s);
-        run_linear(c, b.ff1.w, ProRms{c->a_x1, b.norm2, H, H, 1e-6f, 0, nullptr},
-                   EpiAct{c->a_hh, nullptr, b.ff1.w.bias, f.dit_ff, 1, f.dit_ff}, R, s);
-        run_linear(c, b.ff2.w, ProPlain{c->a_hh, f.dit_ff, 0}, EpiResidual{c->a_x1, c->a_rows, b.ff2.w.bias, H}, R, s);
-    }
-    // final RMSNorm + linear on each CLS row (row stride 2H selects them)
-    run_linear(c, c->agg_final.w, ProRmsGraph{c->a_rows, c->agg_norm, 2 * H, H, 1e-6f, 0, nullptr},
-               EpiAct{c->a_out, nullptr, c->agg_final.w.bias, f.hidden, 0, f.hidden}, B, s);
+    if ((rc = copy_in(c, c->a_lat, latent, (size_t)B * frames * f.dit_latent * 2, kind))) return rc;
+    if ((rc = agg_enqueue(c, B, c->a_lat))) return rc;
     CK(cudaGetLastError());
     if ((rc = copy_out(c, out, c->a_out, (size_t)B * f.hidden * 2, kind))) return rc;
-    if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(s));
+    if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(c->stream));
     return MING_OK;
 }
 
@@ -1643,6 +1516,36 @@ int ming_cuda_kv_read(ming_ctx* c, int s, int layer, int pos0, int n, uint16_t* 
     return MING_OK;
 }
 
+int ming_cuda_kv_write(ming_ctx* c, int s, int layer, int pos0, int n, const uint16_t* k, const uint16_t* v) {
+    if (!c || !c->finalized || !k || !v) return fail(MING_ERR_INVALID, "bad argument");
+    int rc = check_seq(c, s);
+    if (rc) return rc;
+    if (layer < 0 || layer >= c->cfg.layers || pos0 < 0 || n < 1 || pos0 > c->seqs[s].len)
+        return fail(MING_ERR_INVALID, "range out of bounds");
+    CK(cudaSetDevice(c->device));
+    if ((rc = ensure_pages(c, s, pos0, pos0 + n))) return rc;
+    const int KH = c->cfg.kv_heads;
+    const size_t bytes = (size_t)KH * n * HD * 2;
+    uint16_t* d = nullptr;
+    CK(cudaMalloc(&d, 2 * bytes));
+    cudaError_t e = cudaMemcpyAsync(d, k, bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(d + bytes / 2, v, bytes, cudaMemcpyHostToDevice, c->stream);
+    if (e == cudaSuccess) {
+        kv_write_kernel<<<dim3(n, KH, 2), HD, 0, c->stream>>>(KvDev{c->pool, c->bt, c->bt_ld, c->cfg.layers, KH}, s, layer, pos0,
+                                                            n, d, d + bytes / 2);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaStreamSynchronize(c->stream);
+    cudaFree(d);
+    if (e != cudaSuccess) return fail(MING_ERR_CUDA, std::string("kv_write: ") + cudaGetErrorString(e));
+    if (pos0 + n > c->seqs[s].len) {
+        c->seqs[s].len = pos0 + n;
+        CK(cudaMemcpyAsync(c->seq_len + s, &c->seqs[s].len, 4, cudaMemcpyHostToDevice, c->stream));
+        CK(cudaStreamSynchronize(c->stream));
+    }
+    return MING_OK;
+}
+
 int ming_cuda_unpack_linear(ming_ctx* c, const char* name, float* out) {
     if (!c || !c->finalized || !name || !out) return fail(MING_ERR_INVALID, "bad argument");
     for (PackedLin* pl : c->all_lins) {
@@ -1668,7 +1571,7 @@ int ming_cuda_unpack_linear(ming_ctx* c, const char* name, float* out) {
 
 // Diagnostics: copies the persistent kernel's phase trace (MING_MEGA_TRACE=1):
 // [C][layers][MG_TRACE = 64] clock64 stamps of the last step (slot meanings
-// beside MG_TRACE; ming_b200/mega_trace.py prints them). Returns the CTA
+// beside MG_TRACE). Returns the CTA
 // count in *n. Without it, the per-kernel step's launch trace (MING_KTRACE=1):
 // [160 slots][1024 CTAs][8] globaltimer stamps, *n = -(slots used).
 extern "C" int ming_cuda_debug_trace(ming_ctx* c, long long* out, int cap, int* n) {
@@ -1753,6 +1656,10 @@ extern "C" int ming_cuda_lm_decode_noalloc(ming_ctx* c, int B, const int* ids, c
     if (!ids || !x) return fail(MING_ERR_INVALID, "null argument");
     if (B < 1 || B > c->cfg.max_batch) return fail(MING_ERR_INVALID, "batch size out of range");
     const ming_cfg& f = c->cfg;
+    // o_proj combines the attention splits in its prologue, which keeps (max,
+    // 1/sum) of every (row, head) in the linear kernels' 32-float per-row
+    // scratch: 2 x heads must fit in it
+    if (2 * f.heads > 32) return fail(MING_ERR_INVALID, "allocation-free decode supports at most 16 query heads");
     const size_t need = (size_t)B * c->nsplit * f.heads * PART_STRIDE * sizeof(float);
     if (need > NOALLOC_SCRATCH_BYTES)
         return fail(MING_ERR_INVALID, "allocation-free decode: " + std::to_string(B) + " rows at max_ctx " +
@@ -1782,7 +1689,7 @@ extern "C" int ming_cuda_lm_decode_noalloc(ming_ctx* c, int B, const int* ids, c
         auto& L = c->layers[l];
         run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln1_unit},
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, B, s);
-        launch_attn(AttnArgs{c->q, part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, 1}, B, s);
+        CK(launch_attn(AttnArgs{c->q, part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, 1}, B, s));
         run_linear(c, L.o.w, ProAttn{part, rd, c->nsplit, f.heads, 0, nullptr}, EpiResidual{c->x, c->x1, nullptr, f.hidden}, B,
                    s);
         run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln2_unit}, EpiSwiGLU{c->h, f.ff}, B, s);
@@ -1793,6 +1700,20 @@ extern "C" int ming_cuda_lm_decode_noalloc(ming_ctx* c, int B, const int* ids, c
     for (int i = 0; i < B; i++) c->seqs[ids[i]].len += 1;
     if ((rc = copy_out(c, out, c->z, (size_t)B * H * 2, kind))) return rc;
     if ((rc = copy_out(c, stop, c->stop, (size_t)B * 4, kind))) return rc;
-    if (kind == MING_PTR_HOST) CK(cudaStreamSynchronize(s));
+    if (kind == MING_PTR_HOST) {
+        // The decode-batch linears give up on a weight copy that never lands
+        // (a bounded wait) and set the device error flag instead of hanging:
+        // read it back with the outputs, as ming_cuda_lm_decode does, so a
+        // step that gave up is reported here and not blamed on a later call.
+        // With device pointers the flag is read by the next ming_cuda_sync.
+        if (c->err_host && c->dev_err) {
+            CK(cudaMemcpyAsync(c->err_host, c->dev_err, 4, cudaMemcpyDeviceToHost, s));
+            CK(cudaStreamSynchronize(s));
+            if (*c->err_host) return check_dev_err(c);
+        } else {
+            CK(cudaStreamSynchronize(s));
+            if ((rc = check_dev_err(c))) return rc;
+        }
+    }
     return MING_OK;
 }

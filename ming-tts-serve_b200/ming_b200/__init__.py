@@ -29,7 +29,9 @@ SYMBOLS = [
     "ming_cuda_cfm_steps",
     "ming_cuda_aggregate", "ming_cuda_get_stream", "ming_cuda_sync", "ming_cuda_destroy",
     "ming_cuda_last_error", "ming_cuda_kv_read", "ming_cuda_unpack_linear", "ming_cuda_flow_temb",
-    "ming_cuda_step_kernels", "ming_cuda_lm_decode_noalloc",
+    "ming_cuda_step_kernels", "ming_cuda_lm_decode_noalloc", "ming_cuda_kv_write",
+    "ming_cuda_default_sample_params", "ming_cuda_sample_latents", "ming_cuda_loop_create", "ming_cuda_loop_submit",
+    "ming_cuda_loop_step", "ming_cuda_loop_result", "ming_cuda_loop_destroy",
 ]
 
 
@@ -40,6 +42,12 @@ class Cfg(ctypes.Structure):
             "weight_bits", "group_size", "page_size", "max_seqs", "max_pages", "max_ctx", "max_batch", "max_prefill",
             "dit_mode", "dit_hidden", "dit_blocks", "dit_heads", "dit_ff", "dit_latent", "dit_frames",
             "dit_cond_dim", "dit_freq_dim", "dit_max_batch", "agg_blocks")]
+
+
+class SampleParams(ctypes.Structure):
+    """ming_sample_params: SampleParams (src/ming_model.zig:1368-1373) + max_len."""
+    _fields_ = [("max_steps", ctypes.c_int), ("max_len", ctypes.c_int), ("cfg", ctypes.c_float),
+                ("sigma", ctypes.c_float), ("temperature", ctypes.c_float)]
 
 
 class MingError(RuntimeError):
@@ -79,8 +87,17 @@ def lib():
         "ming_cuda_destroy": (I, [P]),
         "ming_cuda_last_error": (ctypes.c_char_p, []),
         "ming_cuda_kv_read": (I, [P, I, I, I, I, P, P]),
+        "ming_cuda_kv_write": (I, [P, I, I, I, I, P, P]),
         "ming_cuda_unpack_linear": (I, [P, ctypes.c_char_p, P]),
         "ming_cuda_flow_temb": (I, [P, P]),
+        "ming_cuda_default_sample_params": (None, [ctypes.POINTER(SampleParams)]),
+        "ming_cuda_sample_latents": (I, [P, P, I, P, ctypes.POINTER(SampleParams), P, I, ctypes.c_uint64, P, I, IP, P,
+                                         P]),
+        "ming_cuda_loop_create": (I, [P, I, ctypes.POINTER(SampleParams), ctypes.POINTER(P)]),
+        "ming_cuda_loop_submit": (I, [P, P, I, P, P, I, ctypes.c_uint64, I, IP]),
+        "ming_cuda_loop_step": (I, [P, IP, IP]),
+        "ming_cuda_loop_result": (I, [P, I, P, I, IP, P, P]),
+        "ming_cuda_loop_destroy": (I, [P]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -104,6 +121,18 @@ def default_cfg(**kw):
             raise KeyError(k)
         setattr(c, k, v)
     return c
+
+
+def sample_params(**kw):
+    """Default sampling parameters (max_steps 1000, max_len 512, cfg 2.0,
+    sigma 0.25, temperature 0.0) with overrides."""
+    p = SampleParams()
+    lib().ming_cuda_default_sample_params(ctypes.byref(p))
+    for k, v in kw.items():
+        if not hasattr(p, k):
+            raise KeyError(k)
+        setattr(p, k, v)
+    return p
 
 
 def _ptr(a):
@@ -241,6 +270,39 @@ class Context:
         _check(lib().ming_cuda_kv_read(self._h, s, layer, pos0, n, _ptr(k), _ptr(v)))
         return k, v
 
+    def _latent_width(self):
+        return self.cfg.dit_frames * self.cfg.dit_latent
+
+    def sample_latents(self, embeds, prompt_latent=None, params=None, bank=None, seed=0, trace=False):
+        """sampleLatents: embeds [L, hidden] -> (latents [n, frames*latent],
+        z trace [n, hidden] or None, stop trace [n]). bank: replay noise
+        [steps, 11, frames*latent] or None (the library's seeded stream)."""
+        embeds = np.ascontiguousarray(embeds, dtype=np.uint16)
+        p = params if params is not None else sample_params()
+        FL = self._latent_width()
+        cap = p.max_steps
+        bank_steps = 0
+        if bank is not None:
+            bank = np.ascontiguousarray(bank, dtype=np.uint16)
+            bank_steps = bank.shape[0]
+            cap = min(cap, bank_steps)
+        lat = np.empty((cap, FL), dtype=np.uint16)
+        zt = np.empty((cap, self.cfg.hidden), dtype=np.uint16) if trace else None
+        st = np.empty(cap, dtype=np.float32)
+        n = ctypes.c_int(0)
+        pl = None if prompt_latent is None else np.ascontiguousarray(prompt_latent, dtype=np.uint16)
+        _check(lib().ming_cuda_sample_latents(self._h, _ptr(embeds), embeds.shape[0], _ptr(pl), ctypes.byref(p), _ptr(bank),
+                                              bank_steps, seed, _ptr(lat), cap, ctypes.byref(n), _ptr(zt), _ptr(st)))
+        k = n.value
+        return lat[:k], (zt[:k] if trace else None), st[:k]
+
+    def kv_write(self, s, layer, pos0, k, v):
+        """k, v: uint16 [kv_heads, n, 64] bf16 written at positions pos0.."""
+        k = np.ascontiguousarray(k, dtype=np.uint16)
+        v = np.ascontiguousarray(v, dtype=np.uint16)
+        assert k.shape == v.shape and k.shape[0] == self.cfg.kv_heads and k.shape[2] == 64
+        _check(lib().ming_cuda_kv_write(self._h, s, layer, pos0, k.shape[1], _ptr(k), _ptr(v)))
+
     def unpack_linear(self, weight_name, out_dim, in_dim):
         out = np.empty((out_dim, in_dim), dtype=np.float32)
         _check(lib().ming_cuda_unpack_linear(self._h, weight_name.encode(), _ptr(out)))
@@ -269,6 +331,60 @@ class Context:
     def close(self):
         if self._h:
             lib().ming_cuda_destroy(self._h)
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Loop:
+    """ming_loop: the sampling loop over up to max_rows concurrent requests
+    (continuous batching). submit() queues a request, step() runs one step
+    of every active row, result() returns a finished request's latents."""
+
+    def __init__(self, ctx, max_rows, params=None):
+        self.ctx = ctx
+        self.params = params if params is not None else sample_params()
+        self._h = ctypes.c_void_p()
+        _check(lib().ming_cuda_loop_create(ctx._h, max_rows, ctypes.byref(self.params), ctypes.byref(self._h)))
+
+    def submit(self, embeds, prompt_latent=None, bank=None, seed=0, trace=False):
+        embeds = np.ascontiguousarray(embeds, dtype=np.uint16)
+        pl = None if prompt_latent is None else np.ascontiguousarray(prompt_latent, dtype=np.uint16)
+        bank_steps = 0
+        if bank is not None:
+            bank = np.ascontiguousarray(bank, dtype=np.uint16)
+            bank_steps = bank.shape[0]
+        rid = ctypes.c_int(-1)
+        _check(lib().ming_cuda_loop_submit(self._h, _ptr(embeds), embeds.shape[0], _ptr(pl), _ptr(bank), bank_steps, seed,
+                                           1 if trace else 0, ctypes.byref(rid)))
+        return rid.value
+
+    def step(self):
+        a, q = ctypes.c_int(0), ctypes.c_int(0)
+        _check(lib().ming_cuda_loop_step(self._h, ctypes.byref(a), ctypes.byref(q)))
+        return a.value, q.value
+
+    def result(self, rid, trace=False):
+        """None while the request runs; else (latents, z trace or None, stop trace)."""
+        cap = self.params.max_steps
+        FL = self.ctx._latent_width()
+        lat = np.empty((cap, FL), dtype=np.uint16)
+        zt = np.empty((cap, self.ctx.cfg.hidden), dtype=np.uint16) if trace else None
+        st = np.empty(cap, dtype=np.float32)
+        n = ctypes.c_int(0)
+        _check(lib().ming_cuda_loop_result(self._h, rid, _ptr(lat), cap, ctypes.byref(n), _ptr(zt), _ptr(st)))
+        if n.value < 0:
+            return None
+        k = n.value
+        return lat[:k], (zt[:k] if trace else None), st[:k]
+
+    def close(self):
+        if self._h:
+            lib().ming_cuda_loop_destroy(self._h)
             self._h = ctypes.c_void_p()
 
     def __del__(self):
