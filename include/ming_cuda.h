@@ -76,6 +76,17 @@ int ming_cuda_create(int device, const ming_cfg* cfg, ming_ctx** out);
  * [out, in/group]), MLX's QuantizedLinear layout. The data is copied. */
 int ming_cuda_load_tensor(ming_ctx* ctx, const char* name, int dtype, const int64_t* shape, int ndim, const void* host);
 
+/* Model.load's file side (src/ming_model.zig:316-350,923-1005): reads a
+ * safetensors checkpoint (`path` a file, or a directory holding
+ * model.safetensors) and loads the hot path's tensors (names under
+ * model.model., stop_head, flowloss., linear_proj_audio, adaln_head,
+ * aggregator.) with ming_cuda_load_tensor: BF16 and U32 as stored, F32 and
+ * F16 rounded to bf16 (the reference casts to its bf16 model dtype) except
+ * rotary inv_freq buffers, which stay F32; other names and dtypes are
+ * skipped. *n_loaded (may be NULL) = tensors loaded. With ctx NULL the file
+ * is only validated (no GPU needed). */
+int ming_cuda_load_safetensors(ming_ctx* ctx, const char* path, int* n_loaded);
+
 /* Checks that every weight is present, repacks them into the kernels' tile
  * layout on the device, precomputes the flow schedule tables, frees the
  * staged copies. Must precede any compute call. */

@@ -31,7 +31,7 @@ SYMBOLS = [
     "ming_cuda_last_error", "ming_cuda_kv_read", "ming_cuda_unpack_linear", "ming_cuda_flow_temb",
     "ming_cuda_step_kernels", "ming_cuda_lm_decode_noalloc", "ming_cuda_kv_write",
     "ming_cuda_default_sample_params", "ming_cuda_sample_latents", "ming_cuda_loop_create", "ming_cuda_loop_submit",
-    "ming_cuda_loop_step", "ming_cuda_loop_result", "ming_cuda_loop_destroy",
+    "ming_cuda_loop_step", "ming_cuda_loop_result", "ming_cuda_loop_destroy", "ming_cuda_load_safetensors",
 ]
 
 
@@ -98,6 +98,7 @@ def lib():
         "ming_cuda_loop_step": (I, [P, IP, IP]),
         "ming_cuda_loop_result": (I, [P, I, P, I, IP, P, P]),
         "ming_cuda_loop_destroy": (I, [P]),
+        "ming_cuda_load_safetensors": (I, [P, ctypes.c_char_p, IP]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -135,6 +136,14 @@ def sample_params(**kw):
     return p
 
 
+def check_safetensors(path):
+    """Validates a safetensors checkpoint without a context (no GPU needed);
+    returns how many hot-path tensors it would load."""
+    n = ctypes.c_int(0)
+    _check(lib().ming_cuda_load_safetensors(None, os.fsencode(path), ctypes.byref(n)))
+    return n.value
+
+
 def _ptr(a):
     """Host numpy array -> void*; device tensor (has data_ptr) -> its address."""
     if a is None:
@@ -160,13 +169,23 @@ class Context:
     surface: load, lm_prefill/lm_decode (lmForward), generate (the token loop),
     cfm_sample (cfmSample), aggregate."""
 
-    def __init__(self, cfg=None, device=0, weights=None):
+    def __init__(self, cfg=None, device=0, weights=None, checkpoint=None):
+        """weights: {name: array} loaded tensor by tensor; checkpoint: a
+        safetensors file (or a directory holding model.safetensors)."""
         self.cfg = cfg if cfg is not None else default_cfg()
         self._h = ctypes.c_void_p()
         _check(lib().ming_cuda_create(device, ctypes.byref(self.cfg), ctypes.byref(self._h)))
+        if checkpoint is not None:
+            self.load_safetensors(checkpoint)
         if weights is not None:
             self.load(weights)
+        if weights is not None or checkpoint is not None:
             self.finalize()
+
+    def load_safetensors(self, path):
+        n = ctypes.c_int(0)
+        _check(lib().ming_cuda_load_safetensors(self._h, os.fsencode(path), ctypes.byref(n)))
+        return n.value
 
     def load(self, weights):
         for name, arr in weights.items():

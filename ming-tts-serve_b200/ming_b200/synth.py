@@ -262,3 +262,30 @@ def latent_proj_weights(seed=1, latent=64, hidden=896, std=0.02):
 
 def nbytes(weights):
     return sum(v.nbytes for v in weights.values())
+
+
+_ST_DTYPES = {np.dtype(np.uint16): "BF16", np.dtype(np.uint32): "U32", np.dtype(np.float32): "F32",
+              np.dtype(np.float16): "F16", np.dtype(np.int32): "I32", np.dtype(np.int64): "I64"}
+
+
+def save_safetensors(path, tensors, metadata=None):
+    """Writes {name: array} as a safetensors file (uint16 arrays are bf16 bit
+    patterns): an 8-byte little-endian header length, the JSON header of
+    dtypes, shapes and data offsets, then the tensors' bytes in order."""
+    import json
+    header, off, blobs = {}, 0, []
+    if metadata:
+        header["__metadata__"] = {str(k): str(v) for k, v in metadata.items()}
+    for name, a in tensors.items():
+        a = np.ascontiguousarray(a)
+        b = a.tobytes()
+        header[name] = {"dtype": _ST_DTYPES[a.dtype], "shape": list(a.shape), "data_offsets": [off, off + len(b)]}
+        blobs.append(b)
+        off += len(b)
+    h = json.dumps(header, separators=(",", ":")).encode()
+    h += b" " * (-len(h) % 8)  # the format pads the header to 8 bytes with spaces
+    with open(path, "wb") as f:
+        f.write(len(h).to_bytes(8, "little"))
+        f.write(h)
+        for b in blobs:
+            f.write(b)

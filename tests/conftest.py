@@ -14,6 +14,18 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA GPU (B200); runs the CUDA path through the C ABI")
 
 
+# Gate calls that passed only through within_reference's widening (the strict
+# 2e-2 / 0.999 bound failed): listed at the end of the run.
+WIDENED = []
+
+
+def pytest_terminal_summary(terminalreporter):
+    if WIDENED:
+        terminalreporter.write_line(f"within_reference widened {len(WIDENED)} gate(s) past the strict bound:")
+        for w in WIDENED[:40]:
+            terminalreporter.write_line("  " + w)
+
+
 @pytest.fixture(scope="session")
 def cuda_ok():
     import torch
@@ -74,4 +86,7 @@ def within_reference(got, fused, graph, tol=2e-2, min_cos=0.999, ulps=2, exact=N
 
     cg, cr = cos(g, f), cos(r, f)
     ok = bool((diff <= bound).all() and (cg > np.minimum(min_cos, cr - 1e-6)).all())
+    strict = bool((diff <= np.maximum(tol, ulps * bf16_ulp(f))).all() and (cg > min_cos).all())
+    if ok and not strict:
+        WIDENED.append(f"{os.environ.get('PYTEST_CURRENT_TEST', '?').split(' ')[0]}: maxabs {diff.max():.4g} cos {cg.min():.6f}")
     return diff.max(), cg.min(), ok

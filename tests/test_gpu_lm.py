@@ -310,22 +310,21 @@ def test_errors_are_reported(q4_24):
     ctx.seq_free(s)
 
 
-def test_q4_baseline_init_within_reference_spread(cuda_ok):
-    """The benchmark's 4-bit distribution: every row of the GPU's output is at least
-    as close to the oracle's fused-rounding result as the oracle's two
-    rounding modes (the reference's fused kernels vs its plain MLX graph) are
-    to each other, plus the strict tolerance; and most rows meet the strict
-    tolerance outright."""
+def test_q4_baseline_init_prefill_strict(cuda_ok):
+    """The benchmark's 4-bit distribution (scales U(0.005, 0.02)) on a 100-row
+    prefill of 2 layers: every row within the strict tolerance of the
+    oracle's FUSED result."""
     W = synth.lm_weights(seed=7, bits=4, layers=2)
     ctx = make_ctx(W, 4, 2)
     lm = O.Lm(W)
     x = synth.normal_bf16(8, "dbg.100", (100, 896))
     s = ctx.seq_alloc()
     go, _ = ctx.prefill(s, x)
-    fused = bf(lm.forward(lm.new_cache(104), x, O.MODE_FUSED)[0])
+    fused = lm.forward(lm.new_cache(104), x, O.MODE_FUSED)[0]
     graph = bf(lm.forward(lm.new_cache(104), x, O.MODE_GRAPH)[0])
-    err = np.abs(bf(go) - fused).max(1)
-    spread = np.abs(graph - fused).max(1)
-    assert (err <= 2e-2 + 2 * spread).all(), (err.max(), spread[err.argmax()])
-    assert (err <= 3.2e-2).mean() >= 0.9
+    d, c, ok = close(go, fused)
+    err = np.abs(bf(go) - bf(fused)).max(1)
+    spread = np.abs(graph - bf(fused)).max(1)
+    assert ok, f"maxabs {d:.4g} cos {c:.6f}; rows over 2e-2: {np.nonzero(err > 2e-2)[0].tolist()[:10]}, " \
+               f"their fused-vs-graph spread {spread[err > 2e-2][:10].round(4).tolist()}"
     ctx.close()
