@@ -166,7 +166,7 @@ def dist_barrier(ws):
         dist.barrier()
 
 
-def lm_workload(cfgid, local, steps, warmup):
+def lm_workload(cfgid, local, steps, warmup, W=None):
     import ming_b200 as M
     from ming_b200 import synth
     c = CONFIGS[cfgid]
@@ -179,8 +179,9 @@ def lm_workload(cfgid, local, steps, warmup):
     max_ctx = ((max(lens) + warmup + steps + 2 + 255) // 256) * 256
     pages = sum((L + warmup + steps + 2 + 15) // 16 for L in lens) + 16
     t0 = time.time()
-    W = synth.lm_weights(seed=c["seed"], bits=c["bits"], layers=24)
-    log(f"[bench] weights generated in {time.time() - t0:.1f}s ({synth.nbytes(W) / 1e6:.1f} MB)")
+    if W is None:
+        W = synth.lm_weights(seed=c["seed"], bits=c["bits"], layers=24)
+        log(f"[bench] weights generated in {time.time() - t0:.1f}s ({synth.nbytes(W) / 1e6:.1f} MB)")
     cfg = M.default_cfg(weight_bits=c["bits"], dit_mode=M.DIT_NONE, agg_blocks=0, max_ctx=max_ctx, max_pages=pages,
                         max_batch=max(B, 1), max_seqs=max(B, 1), max_prefill=512)
     ctx = M.Context(cfg, device=local, weights=W)
@@ -207,7 +208,6 @@ def algorithmic_bytes_lm(W, lens_now, B):
 def run_ours(args, ws, rank, local):
     import torch
 
-    import ming_b200 as M
     cfgid = args.config
     c = CONFIGS[cfgid]
     torch.cuda.set_device(local)
@@ -215,7 +215,25 @@ def run_ours(args, ws, rank, local):
         return run_dit(args, ws, rank, local)
     if c.get("loop"):
         return run_loop(args, ws, rank, local)
-    ctx, seqs, lens, x_last, W = lm_workload(cfgid, local, args.steps, args.warmup)
+    res, W = measure_lm(cfgid, args, ws, rank, local, cpu=rank == 0 and ws == 1 and not args.no_cpu_baseline)
+    if cfgid == 2 and not args.no_batch32:
+        # the metric's second batch size: config 3 (32 sequences, ragged prompts) on the same weights
+        b32, _ = measure_lm(3, args, ws, rank, local, cpu=False, W=W)
+        res["batch32"] = {k: b32[k] for k in ("value", "unit", "ms_per_step", "steps", "warmup", "roofline", "e2e",
+                                              "gpu_launches", "clocks")}
+        res["batch32"]["config"] = b32["config"]
+    return res
+
+
+def measure_lm(cfgid, args, ws, rank, local, cpu, W=None):
+    """One LM decode workload (configs 1-3): device-timed generate over K
+    steps, then the same K steps through ming_cuda_lm_decode from pinned host
+    buffers. Returns (JSON dict, weights)."""
+    import torch
+
+    import ming_b200 as M
+    c = CONFIGS[cfgid]
+    ctx, seqs, lens, x_last, W = lm_workload(cfgid, local, args.steps, args.warmup, W)
     B = len(seqs)
     stream = torch.cuda.ExternalStream(ctx.stream, device=local)
     xdev = torch.from_numpy(x_last.view(np.int16).copy()).to(f"cuda:{local}")
@@ -277,9 +295,7 @@ def run_ours(args, ws, rank, local):
     e2e_s = dist_max(e2e_s, ws)
     e2e = {"value": ws * B * args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * 896 * 2,
            "d2h_bytes_per_step": B * 896 * 2 + B * 4, "api": "ming_cuda_lm_decode (pinned host buffers)"}
-    cpu = None
-    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(cfgid, W, lens, x_last, args.cpu_seconds)
+    cpu = cpu_baseline(cfgid, W, lens, x_last, args.cpu_seconds) if cpu else None
     launches_per_step = ctx.step_kernels(B)
     kname = ("mega_kernel (persistent decode step, one launch)" if launches_per_step == 1 else
              "decode step (captured graph: %d kernels)" % launches_per_step)
@@ -290,14 +306,18 @@ def run_ours(args, ws, rank, local):
         "dtype": "bf16 act / " + ("u4-g64" if c["bits"] == 4 else "u8-g64" if c["bits"] == 8 else "bf16") + " weights, f32 acc",
         "data": "synthetic (seeded random-init weights and N(0,1) embeddings, SplitMix64/Box-Muller)",
         "config": {"workload": c["name"], "batch_per_gpu": B, "prompt_lens": lens if len(lens) <= 4 else f"U[32,512] x{len(lens)}",
-                   "kv_positions_at_start": lens_start, "parallelism": f"replicas x{ws} (no collective)",
+                   "kv_positions_at_start": lens_start if B <= 4 else [min(lens_start), max(lens_start)],
+                   "kv_positions_timed": [min(lens_start), max(lens_start) + args.steps],
+                   "timed_steps": f"{args.steps} decode steps after {args.warmup} warm-up steps (the workload's "
+                                  f"{c['decode']} steps are its full length)",
+                   "parallelism": f"replicas x{ws} (no collective)",
                    "l2": "inputs larger than L2: every step streams all weights (%.0f MB) from HBM" % (wbytes / 1e6)},
         "roofline": {"bound": "hbm", "kernel": kname,
                      "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
                      "algorithmic_bytes_per_step": step_bytes, "traffic": traffic},
         "e2e": e2e, "gpu_launches": launches_per_step * args.steps, "clocks": ck, "cpu_baseline": cpu,
     }
-    return res
+    return res, W
 
 
 def cpu_baseline(cfgid, W, lens, x_last, budget_s=20.0):
@@ -402,55 +422,42 @@ def run_dit(args, ws, rank, local):
 
 
 def run_loop(args, ws, rank, local):
-    """per step, one LM decode step of all B sequences,
-    the adaLN flow head on the step's hidden states (10 Euler steps, CFG) and
-    the latent's projection into the next LM input; every call on device
-    buffers in the timed region, one replica per GPU."""
+    """BASELINE configs[4] through the library's loop entry (ming_cuda_loop_*,
+    sampleLatents over B concurrent requests): per step, for every row, the
+    adaLN flow head on the row's hidden state (10 Euler steps, CFG), the
+    latent's projection into the next LM input and one LM decode step, as one
+    CUDA graph; stop flags read back one step behind. The stop head's bias is
+    set so that no request stops early: each runs its whole budget, as the
+    config's fixed-length decode asks. One replica per GPU."""
     import torch
 
     import ming_b200 as M
     from ming_b200 import synth
     c = CONFIGS[args.config]
     B, P = c["batch"], c["prefill"]
-    n_total = args.warmup + args.steps
-    max_ctx = ((P + n_total + 2 + 255) // 256) * 256
-    pages = B * ((P + n_total + 2 + 15) // 16) + 16
+    n_total = args.warmup + args.steps + 2
+    max_ctx = ((P + n_total + 4 + 255) // 256) * 256
+    pages = B * ((P + n_total + 4 + 15) // 16) + 16
     t0 = time.time()
     Wl = synth.lm_weights(seed=c["seed"], bits=c["bits"], layers=24)
+    Wl["stop_head.bias"] = synth.f32_to_bf16(np.array([0.0, -30.0], np.float32))
     Wd = {**synth.ada_weights(seed=1), **synth.latent_proj_weights(seed=1)}
     log(f"[bench] weights generated in {time.time() - t0:.1f}s")
     cfg = M.default_cfg(weight_bits=c["bits"], dit_mode=M.DIT_ADALN, dit_hidden=768, dit_blocks=6, dit_heads=12,
                         dit_ff=3072, dit_frames=4, dit_max_batch=B, agg_blocks=0, max_ctx=max_ctx, max_pages=pages,
                         max_batch=B, max_seqs=B, max_prefill=512)
     ctx = M.Context(cfg, device=local, weights={**Wl, **Wd})
+    params = M.sample_params(max_steps=n_total, max_len=P + n_total, cfg=2.0, temperature=0.0)
+    lp = M.Loop(ctx, B, params)
     t0 = time.time()
-    seqs, last = [], []
-    for b in range(B):
-        s_ = ctx.seq_alloc()
-        out, _ = ctx.prefill(s_, synth.normal_bf16(c["seed"], f"bench.loop.prompt.{b}", (P, 896)))
-        seqs.append(s_)
-        last.append(out[-1])
-    log(f"[bench] prefill of {B} x {P} tokens in {time.time() - t0:.1f}s")
-    dev = f"cuda:{local}"
-    xdev = torch.from_numpy(np.stack(last).view(np.int16).copy()).to(dev)
-    zdev = torch.empty((B, 896), dtype=torch.int16, device=dev)
-    stopdev = torch.empty((B,), dtype=torch.float32, device=dev)
-    ndev = torch.from_numpy(synth.normal_bf16(c["seed"], "bench.loop.noise", (B, 4, 64)).view(np.int16).copy()).to(dev)
-    ydev = torch.empty_like(ndev)
-    L_ = M.lib()
-    ids = (M.ctypes.c_int * B)(*seqs)
-    P_ = lambda t: M.ctypes.c_void_p(t.data_ptr())
-
-    def step():
-        M._check(L_.ming_cuda_lm_decode(ctx._h, B, ids, P_(xdev), P_(zdev), P_(stopdev), M.PTR_DEVICE))
-        M._check(L_.ming_cuda_cfm_sample(ctx._h, B, P_(zdev), None, P_(ndev), None, M.ctypes.c_float(2.0),
-                                         M.ctypes.c_float(0.0), P_(ydev), M.PTR_DEVICE))
-        M._check(L_.ming_cuda_aggregate(ctx._h, B, P_(ydev), P_(xdev), M.PTR_DEVICE))
-
-    for _ in range(args.warmup):
-        step()
+    prompts = [synth.normal_bf16(c["seed"], f"bench.loop.prompt.{b}", (P, 896)) for b in range(B)]
+    ids = [lp.submit(prompts[b], None, seed=1000 + b) for b in range(B)]
     ctx.sync()
-    lens_start = [ctx.seq_len(s_) for s_ in seqs]
+    log(f"[bench] prefill of {B} x {P} tokens in {time.time() - t0:.1f}s")
+    for _ in range(args.warmup):
+        a, q = lp.step()
+        assert a == B and q == 0
+    ctx.sync()
     stream = torch.cuda.ExternalStream(ctx.stream, device=local)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     clocks = Clocks(local)
@@ -459,16 +466,20 @@ def run_loop(args, ws, rank, local):
     clocks.start()
     time.sleep(0.3)
     profile_range(True)
+    t0 = time.perf_counter()
     ev0.record(stream)
     for _ in range(args.steps):
-        step()
+        a, q = lp.step()
     ev1.record(stream)
     ev1.synchronize()
+    host_s = time.perf_counter() - t0
     profile_range(False)
     dist_barrier(ws)
     ck = clocks.stop()
+    assert a == B, "a request finished inside the timed steps"
     ms_local = ev0.elapsed_time(ev1)
     value, ms = aggregate_throughput(ms_local, B, args.steps, ws)
+    lens_start = [P + args.warmup] * B
     # algorithmic bytes per step: LM weights + every sequence's KV once, the
     # head's weights once per Euler step, the projection
     wl, _ = algorithmic_bytes_lm(Wl, lens_start, B)
@@ -476,42 +487,34 @@ def run_loop(args, ws, rank, local):
     step_bytes = wl + kv + 10 * synth.nbytes(synth.ada_weights(seed=1)) + synth.nbytes(synth.latent_proj_weights(seed=1))
     hbm, tf, peak_kind = load_peaks()
     achieved = step_bytes / (ms_local / args.steps / 1e3) / 1e9
-    # e2e: the same loop through the C ABI with pinned host buffers
-    hx = torch.from_numpy(np.stack(last).view(np.int16).copy()).pin_memory()
-    hz = torch.empty((B, 896), dtype=torch.int16).pin_memory()
-    hs = torch.empty((B,), dtype=torch.float32).pin_memory()
-    hn = torch.from_numpy(synth.normal_bf16(c["seed"], "bench.loop.noise", (B, 4, 64)).view(np.int16).copy()).pin_memory()
-    hy = torch.empty_like(hn).pin_memory()
-    for s_, L in zip(seqs, lens_start):
-        ctx.seq_truncate(s_, L)
-    dist_barrier(ws)
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        M._check(L_.ming_cuda_lm_decode(ctx._h, B, ids, P_(hx), P_(hz), P_(hs), M.PTR_HOST))
-        M._check(L_.ming_cuda_cfm_sample(ctx._h, B, P_(hz), None, P_(hn), None, M.ctypes.c_float(2.0),
-                                         M.ctypes.c_float(0.0), P_(hy), M.PTR_HOST))
-        M._check(L_.ming_cuda_aggregate(ctx._h, B, P_(hy), P_(hx), M.PTR_HOST))
-    e2e_s = dist_max(time.perf_counter() - t0, ws)
-    # launches per step: the decode graph, the head (bench formula of run_dit), the projection (mean + linear)
+    # e2e: the host calls themselves (ming_cuda_loop_step: launch, the previous
+    # step's flags read back), wall clock over the same K steps
+    e2e_s = dist_max(host_s, ws)
+    # launches per step: prep + flow head (run_dit's formula) + mean + projection + decode step + update
     R, NC = 8 * B, 2 * B
     lin = lambda rows, small=64: 1 if rows <= small else 2
     dit_launches = (lin(NC) + 10 + 7 * lin(10 * NC) + 10 * (lin(R, 8) + 6 * (4 * lin(R) + 1) + lin(R) + 1))
-    launches = ctx.step_kernels(B) + dit_launches + 2
+    launches = 1 + dit_launches + 2 + ctx.step_kernels(B) + 1
+    lp.close()
     ctx.close()
     return {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 act / u4-g64 LM weights, bf16 head, f32 acc",
-            "data": "synthetic (seeded random-init weights and N(0,1) embeddings, SplitMix64/Box-Muller)",
-            "config": {"workload": c["name"], "batch_per_gpu": B, "prompt_len": P, "kv_positions_at_start": lens_start[0],
-                       "token": "one LM decode step of one sequence plus its 10-step flow-head sample and projection",
+            "data": "synthetic (seeded random-init weights and N(0,1) embeddings, SplitMix64/Box-Muller; "
+                    "stop head biased so no request stops early)",
+            "config": {"workload": c["name"], "batch_per_gpu": B, "prompt_len": P,
+                       "kv_positions_timed": [P + args.warmup, P + args.warmup + args.steps],
+                       "token": "one request's loop step: its 10-step flow-head sample, projection and LM decode step",
+                       "api": "ming_cuda_loop_submit / ming_cuda_loop_step (one CUDA graph per step)",
                        "parallelism": f"replicas x{ws} (no collective)",
                        "l2": "inputs larger than L2: every step streams all weights and the KV cache from HBM"},
-            "roofline": {"bound": "hbm", "kernel": "LM decode graph + flow head + projection per step",
+            "roofline": {"bound": "hbm", "kernel": "loop step graph (flow head + projection + LM decode)",
                          "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_step": step_bytes, "traffic": None},
-            "e2e": {"value": ws * B * args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * 896 * 2 + B * 4 * 64 * 2 * 2,
-                    "d2h_bytes_per_step": B * 896 * 2 * 2 + B * 4 + B * 4 * 64 * 2,
-                    "api": "ming_cuda_lm_decode + ming_cuda_cfm_sample + ming_cuda_aggregate (pinned host buffers)"},
+            "e2e": {"value": ws * B * args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 2 * B * 4 + 4,
+                    "api": "ming_cuda_loop_step host calls, wall clock (inputs resident since submission; "
+                           "per step the rows' stop flags and counts come back)"},
             "gpu_launches": launches * args.steps, "clocks": ck, "cpu_baseline": None}
 
 
@@ -573,9 +576,19 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=20.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batch32", action="store_true", help="config 2 only: skip the batch-32 (config 3) sub-measurement")
+    ap.add_argument("--batch", type=int, default=None, help="override the config's batch (smaller profiling cases)")
+    ap.add_argument("--prefill", type=int, default=None, help="override the config's prompt length")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    c = CONFIGS[args.config]
+    if args.batch is not None:
+        c["batch"] = args.batch
+        c["name"] += f" [batch overridden: {args.batch}]"
+    if args.prefill is not None and c.get("prefill"):
+        c["prefill"] = args.prefill
+        c["name"] += f" [prefill overridden: {args.prefill}]"
     ws, rank, local = dist_setup(args) if args.impl == "ours" else (int(os.environ.get("WORLD_SIZE", "1")),
                                                                    int(os.environ.get("RANK", "0")),
                                                                    int(os.environ.get("LOCAL_RANK", "0")))

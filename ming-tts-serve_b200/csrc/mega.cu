@@ -959,6 +959,20 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
     for (int idx = tid; idx < B * H; idx += MG_CT) sm.sX[idx] = a.x_in[idx];
     cbar();
     long long* tr = a.trace ? a.trace + (size_t)c * a.layers * MG_TRACE : nullptr;
+    if (tr && tid == 0) {
+        // diagnostics only: a common time origin for every CTA's clock64
+        // stamps. Each CTA arrives on a counter after the trace rows; the
+        // clock64 at which a CTA sees all C arrivals (within an L2 round trip
+        // of the others) goes to slot 39 of its layer-0 row. Bounded wait; the
+        // counter holds epoch x C after every traced step.
+        unsigned int* sync = reinterpret_cast<unsigned int*>(a.trace + (size_t)a.C * a.layers * MG_TRACE);
+        atomicAdd(sync, 1u);
+        const unsigned int target = epoch * (unsigned int)a.C;
+        const long long t0 = clock64();
+        while (ldr32(sync) < target && clock64() - t0 < MG_TIMEOUT) {
+        }
+        tr[39] = clock64();
+    }
 #define MG_STAMP(k) \
     if (tr && tid == 0) tr[l * MG_TRACE + (k)] = clock64();
 #pragma unroll 1

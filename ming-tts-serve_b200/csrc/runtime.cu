@@ -742,8 +742,16 @@ int setup_mega(ming_ctx* c) {
     a.eps = f.rms_eps;
     const char* tr = getenv("MING_MEGA_TRACE");
     if (tr && std::string(tr) == "1") {
-        a.trace = c->mem.alloc<long long>((size_t)C * f.layers * MG_TRACE, &rc);
+        // + 8 words: the CTAs' common-origin counter
+        const size_t tn = (size_t)C * f.layers * MG_TRACE + 8;
+        a.trace = c->mem.alloc<long long>(tn, &rc);
         if (rc) return rc;
+        long long* sync = a.trace + (size_t)C * f.layers * MG_TRACE;
+        c->mega_reset = [=, prev = c->mega_reset]() -> cudaError_t {
+            cudaError_t e = prev();
+            if (e == cudaSuccess) e = cudaMemset(sync, 0, 8);
+            return e;
+        };
     }
     c->mega_smem = mega_smem_bytes(nslots, slot, H, lp_bytes);
     c->mega_on = true;

@@ -3,9 +3,14 @@ through the C ABI against the oracle (the reference's parity method: both
 sides take the oracle's previous output each step, src/ming_parity.zig:6-8).
 
 Config 2 (the headline: 4-bit g64, scales U(0.005, 0.02), 128-token prompt,
-1,024 decode steps to position 1,152) is gated at the north star's bf16
-tolerance on every step: max-abs 2e-2 (two bf16 steps where |v| >= 2) and
-cosine > 0.999 against the oracle's FUSED mode, p(stop) within 1e-2.
+1,024 decode steps to position 1,152): every decode step is gated at the
+north star's bf16 tolerance: max-abs 2e-2 (two bf16 steps where |v| >= 2)
+and cosine > 0.999 against the oracle's FUSED mode, p(stop) within 1e-2.
+The 128 prompt rows (the prefill, on the tiled many-row linear) meet cosine
+> 0.999 but reach 0.031 max-abs on some rows, where the reference's own
+FUSED and GRAPH paths differ by as much: they are gated like the other
+many-row outputs (within_reference), and as accurate as the reference
+against exact arithmetic.
 
 Config 1 (bf16, N(0, 0.02) weights, 64-token prompt, 256 steps): the
 reference's own fused kernels are 0.094 max-abs away from exact f32
@@ -24,7 +29,7 @@ import ming_b200 as M
 import oracle as O
 from ming_b200 import synth
 
-from conftest import bf, close
+from conftest import as_accurate_as_reference, bf, close, within_reference
 
 pytestmark = pytest.mark.gpu
 
@@ -45,8 +50,12 @@ def test_config2_q4_baseline_init_1024_steps(cuda_ok):
     cache = lm.new_cache(n)
     go, gs = ctx.prefill(s, x)
     ro, rs = lm.forward(cache, x)
-    d, c, ok = close(go, ro)
+    rg, _ = lm.forward(lm.new_cache(n), x, O.MODE_GRAPH)
+    re_ = lm.forward_f32(lm.new_cache(n), x)
+    d, c, ok = within_reference(go, ro, rg, exact=re_)
     assert ok, ("prefill", d, c)
+    rr, mr, cd, ok = as_accurate_as_reference(go, ro, rg, re_)
+    assert ok, ("prefill accuracy", rr, mr, cd)
     assert np.abs(gs - rs).max() < 1e-2
     xin = ro[-1:]
     worst = (0.0, 1.0)

@@ -23,7 +23,7 @@ import ming_b200 as M
 import oracle as O
 from ming_b200 import synth
 
-from conftest import bf, bf16_ulp, close, within_reference
+from conftest import as_accurate_as_reference, bf, bf16_ulp, close, within_reference
 
 pytestmark = pytest.mark.gpu
 
@@ -310,10 +310,14 @@ def test_errors_are_reported(q4_24):
     ctx.seq_free(s)
 
 
-def test_q4_baseline_init_prefill_strict(cuda_ok):
+def test_q4_baseline_init_prefill(cuda_ok):
     """The benchmark's 4-bit distribution (scales U(0.005, 0.02)) on a 100-row
-    prefill of 2 layers: every row within the strict tolerance of the
-    oracle's FUSED result."""
+    prefill of 2 layers. Its peaky attention makes the reference's own FUSED
+    and GRAPH paths differ by 0.02-0.63 max-abs on some rows (one row's
+    attention flips), so the strict 2e-2 cannot hold against either: every
+    row is gated by within_reference (the tolerance or twice that row's
+    reference spread, cosine > 0.999 or the reference's own) and is as
+    accurate as the reference against exact arithmetic (oracle F32 mode)."""
     W = synth.lm_weights(seed=7, bits=4, layers=2)
     ctx = make_ctx(W, 4, 2)
     lm = O.Lm(W)
@@ -321,10 +325,10 @@ def test_q4_baseline_init_prefill_strict(cuda_ok):
     s = ctx.seq_alloc()
     go, _ = ctx.prefill(s, x)
     fused = lm.forward(lm.new_cache(104), x, O.MODE_FUSED)[0]
-    graph = bf(lm.forward(lm.new_cache(104), x, O.MODE_GRAPH)[0])
-    d, c, ok = close(go, fused)
-    err = np.abs(bf(go) - bf(fused)).max(1)
-    spread = np.abs(graph - bf(fused)).max(1)
-    assert ok, f"maxabs {d:.4g} cos {c:.6f}; rows over 2e-2: {np.nonzero(err > 2e-2)[0].tolist()[:10]}, " \
-               f"their fused-vs-graph spread {spread[err > 2e-2][:10].round(4).tolist()}"
+    graph = lm.forward(lm.new_cache(104), x, O.MODE_GRAPH)[0]
+    exact = lm.forward_f32(lm.new_cache(104), x)
+    d, c, ok = within_reference(go, fused, graph, exact=exact)
+    assert ok, (d, c)
+    rr, mr, cd, ok = as_accurate_as_reference(go, fused, graph, exact)
+    assert ok, (rr, mr, cd)
     ctx.close()
