@@ -65,11 +65,6 @@ MING_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar
                  "l"(src), "r"(bytes), "r"(su32(bar))
                  : "memory");
 }
-MING_DEV void cp16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(su32(dst)), "l"(src) : "memory");
-}
-MING_DEV void cp_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
-MING_DEV void cp_wait_all() { asm volatile("cp.async.wait_all;\n" ::: "memory"); }
 MING_DEV void cbar() { asm volatile("bar.sync 1, %0;\n" ::"n"(MG_CT) : "memory"); }  // consumer warps only
 MING_DEV uint64_t ldr64(const void* p) {
     uint64_t v;
@@ -97,8 +92,9 @@ MING_DEV void red_add64(unsigned long long* p, long long v) {
 }
 MING_DEV uint64_t tagged(uint32_t tag, float v) { return ((uint64_t)tag << 32) | __float_as_uint(v); }
 // A counted accumulator word is (contributors << 56) + sum of fixed-point
-// values (|sum| < 2^55): the count is the top byte after rounding.
-MING_DEV int acc_count(unsigned long long v) { return (int)((long long)(v + (1ull << 55)) >> 56); }
+// values (|sum| < 2^55): the count (up to 255) is the top byte after
+// rounding; the unsigned shift keeps counts above 127.
+MING_DEV int acc_count(unsigned long long v) { return (int)((v + (1ull << 55)) >> 56); }
 MING_DEV float acc_value(unsigned long long v) {
     const long long x = (long long)v - ((long long)acc_count(v) << 56);
     return __ll2float_rn(x) * (1.0f / (float)(1ull << MG_FIX));
@@ -260,10 +256,15 @@ __host__ __device__ inline SmemMap smem_map(int nslots, int slot_bytes, int H, i
 }
 constexpr int MG_ATT_SCRATCH = MG_B_BYTES + MG_SK * 8 * 4 + MG_T_BYTES;
 // attention item scratch: K, V rows (padded to 72) + q + new k/v + scores + P.V partials
-static_assert(2 * MG_ATT_CH * (HD + 8) * 2 + 3 * HD * 4 + MG_ATT_CH * 4 + MG_CWARPS * 32 * 8 <= MG_ATT_SCRATCH,
+static_assert(2 * MG_ATT_CH * HD * 2 + 3 * HD * 4 + MG_ATT_CH * 4 + MG_CWARPS * 32 * 8 <= MG_ATT_SCRATCH,
               "attention scratch does not fit");
+static_assert(MG_ATT_CH * HD * 2 * 2 <= MG_B_BYTES, "the attention K/V pages fit the fragment area");
+static_assert(MG_ATT_CH * 4 + MG_CWARPS * 32 * 8 >= MG_CWARPS * 68 * 4, "the warps' attention partials fit the score area");
 
 struct Misc {              // small per-CTA state in shared memory
+    uint64_t att_bar;            // mbarrier of the attention items' K/V page copies (first: 8-byte aligned)
+    unsigned int att_uses;       // phases of att_bar completed so far
+    int att_inflight;            // copies issued whose completion nobody has seen (wind-down waits for them)
     float inv[MG_MAXB];    // 1/rms of each row (current norm)
     float scl[MG_MAXB];    // operand pre-scale (power of two) of each row
     float post[MG_MAXB];   // scale applied to the f32 sums
@@ -272,12 +273,26 @@ struct Misc {              // small per-CTA state in shared memory
     float red[MG_CWARPS * 2 * MG_MAXB];  // block reductions
     int g0[MG_NPH], g1[MG_NPH];          // this CTA's group range per phase
     int wtile[MG_NPH][MG_CWARPS];        // first tile of each warp's group range (-1: none)
+    int nsc[MG_NPH];                     // ring slots of each phase
+    int pbase[MG_NPH];                   // first group's position in its tile (g0 % groups per tile)
+    int grp;                             // query heads per kv head
+    unsigned long long hm;               // divB multiplier of the head count
+    int nitems[MG_MAXB];                 // attention items of each row: heads x 128-position chunks
+    uint8_t hgrp[64];                    // kv head of each query head
+    // each warp's run per phase, fixed for the whole step (computed once: the
+    // integer divisions by runtime sizes cost ~0.1 us each at this kernel's
+    // issue rate): groups [i0, i1) of the CTA's range, its first group's tile,
+    // group in the tile and group in its ring slot, and its first and last slot
+    struct WRun {
+        short i0, i1, t, kg, wi, js, je;
+    } wrun[MG_NPH][MG_CWARPS];
     float rc[MG_MAXB][HD / 2];           // RoPE cos/sin of each row's position, per frequency
     float rs[MG_MAXB][HD / 2];
     int fail;
     float om, ol;  // max and sum of this CTA's attention chunk (the combining chunk keeps its own)
     int prod_done;
     int issued;
+    int frag_dirty;  // attention items reused the fragment area: rows >= B must be zeroed again
     uint32_t epoch;
     int step;
     unsigned long long bm;  // divB multiplier of the step's row count
@@ -315,9 +330,13 @@ MING_DEV unsigned long long* acc_ptr(const MegaDev& a, uint32_t epoch, int l, in
 template <bool F16>
 MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint16_t* nw) {
     const int tid = threadIdx.x;
-    uint4* z = reinterpret_cast<uint4*>(sm.sB);
-    for (int e = tid; e < nstage * 4 * 32 / 2; e += MG_CT) z[e] = make_uint4(0u, 0u, 0u, 0u);
-    cbar();
+    // entries of rows >= B stay zero from one stage to the next; only the
+    // attention items (which reuse this area) dirty them. They are disjoint
+    // from the entries written below, so no barrier separates the passes.
+    if (sm.ms->frag_dirty) {
+        for (int e = tid; e < MG_SK * 4 * 32; e += MG_CT)
+            if ((e & 31) >= 4 * B) sm.sB[e] = make_uint2(0u, 0u);
+    }
     const int tot = nstage * B * 16;
     const int totr = (tot + 31) & ~31;  // warp-uniform trip count: every lane reaches the shuffles
     for (int e = tid; e < totr; e += MG_CT) {
@@ -356,6 +375,7 @@ MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint
         if (act && q16 == 0) sm.sYs[si * 8 + b] = sum;
     }
     cbar();
+    if (threadIdx.x == 0) sm.ms->frag_dirty = 0;  // read by every thread before the barrier above
     MG_SUB(0)
 }
 
@@ -437,27 +457,23 @@ enum { OUT_ACC = 0, OUT_GLU = 1 };
 // row, batch row) either a fixed-point contribution to acc (row index
 // tile*16 + r) or, for whole gate|up tiles, the SwiGLU outputs into hb.
 template <int FMT>
-MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint8_t* ring, uint64_t* full, uint64_t* empty,
-                         int stage_base, bool use_post, int out, unsigned long long* acc, uint64_t* hb, uint32_t tag) {
+MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t par0, uint8_t* ring, uint64_t* full,
+                         uint64_t* empty, int stage_base, bool use_post, int out, unsigned long long* acc, uint64_t* hb,
+                         uint32_t tag) {
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g0 = ms->g0[p], g1 = ms->g1[p], n = g1 - g0, gpt = a.ph[p].gpt;
     if (n <= 0) return;  // CTA-uniform
-    const int nsc = (n + a.gps - 1) / a.gps;
+    const int nsc = ms->nsc[p];
     MG_SUB(1)
-    const int i0 = warp * n / MG_CWARPS, i1 = (warp + 1) * n / MG_CWARPS;
+    const Misc::WRun wr = ms->wrun[p][warp];
+    const int i0 = wr.i0, i1 = wr.i1;
     const int tb = ms->wtile[p][warp];
     float acc2[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
     // walk the warp's run incrementally: tile t, group kg in the tile, group
     // wi in its ring slot
-    int t = 0, kg = 0, wi = 0;
-    if (i0 < i1) {
-        const int g = g0 + i0;
-        t = g / gpt;
-        kg = g - t * gpt;
-        wi = i0 % a.gps;
-    }
+    int t = wr.t, kg = wr.kg, wi = wr.wi;
     // The phase's ring slots one at a time: every warp waits for each slot,
     // uses the groups of its run inside it, and releases it, so a phase may be
     // longer than the ring (the producer refills released slots meanwhile).
@@ -468,10 +484,35 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
     // the slots before and after its run without waiting for their fill: some
     // warp uses every slot and releases it only after its wait and use, so
     // the producer never refills a slot still being filled or read.
+    // In that case a warp first takes the slots of its own run, then releases
+    // the others: walking (and releasing) the slots before its run first
+    // delayed warp w's first data by ~0.15 us per earlier warp.
     const bool skip = nsc <= a.nslots;
-    int sl = cons_base % a.nslots;
-    uint32_t par = (uint32_t)(cons_base / a.nslots) & 1u;
-    for (int jj = 0; jj < nsc; jj++) {
+    const int js = i0 < i1 ? wr.js : 0, je = i0 < i1 ? wr.je : -1;
+    const int njj = skip ? nsc + (je - js + 1) : nsc;  // skip: own slots, then every slot (own ones passed over)
+    // slot of phase slot jj: slot0 + jj, wrapped once at most in skip mode;
+    // in order (one wrap per pass of the ring) otherwise
+    int sl = slot0;
+    uint32_t par = par0;
+#pragma unroll 1
+    for (int it = 0; it < njj; it++) {
+        int jj = it;
+        if (skip) {
+            if (it <= je - js) jj = js + it;
+            else {
+                jj = it - (je - js + 1);
+                if (jj >= js && jj <= je) continue;  // warp-uniform: released in the first pass
+            }
+            sl = slot0 + jj;
+            par = par0;
+            if (sl >= a.nslots) {
+                sl -= a.nslots;
+                par ^= 1u;
+            }
+        } else if (it > 0 && ++sl == a.nslots) {
+            sl = 0;
+            par ^= 1u;
+        }
         const int w0 = max(i0, jj * a.gps), w1 = min(i1, (jj + 1) * a.gps);
         if ((!skip || w0 < w1) && !mbar_wait(&full[sl], par)) atomicCAS(cx.fail, 0, 2);
         if (sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p == 2 && w0 == i0 && w0 < w1) sm.st[56 + warp] = clock64();
@@ -525,12 +566,33 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[sl]);  // before any global write of this phase
         if (sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p >= 2 && w1 == i1 && w0 < w1) sm.st[40 + (p - 2) * 8 + warp] = clock64();
-        if (++sl == a.nslots) {
-            sl = 0;
-            par ^= 1u;
-        }
     }
     MG_SUB(2)
+    const int B = a.B;
+    if (out == OUT_ACC) {
+        // split-K phases: each warp adds its own partial sums of the (at most
+        // two) tiles its run touched; the tiles' contributor counts count
+        // warps (planned on the host), so no CTA-wide reduction is needed
+        if (i0 < i1) {
+            const int gr = lane >> 2, cc = 2 * (lane & 3), tl = (g0 + i1 - 1) / gpt;
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int t = tb + u;
+                if (u == 1 && t > tl) break;
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int b = cc + j;
+                    if (b >= B) continue;
+                    const float ps = use_post ? ms->post[b] : 1.f;
+                    unsigned long long* base = acc + (size_t)b * a.acc_w + t * 16;
+                    red_add64(base + gr, to_fix_counted(acc2[u][j] * ps));
+                    red_add64(base + gr + 8, to_fix_counted(acc2[u][2 + j] * ps));
+                }
+            }
+        }
+        MG_SUB(4)
+        return;
+    }
     {
         const int gr = lane >> 2, cc = 2 * (lane & 3);
         float* r = sm.sRed + warp * 2 * 128;
@@ -544,23 +606,8 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int cons_base, uint
     }
     cbar();
     MG_SUB(3)
-    const int t0 = g0 / gpt, nt = (g1 - 1) / gpt - t0 + 1, B = a.B;
-    if (out == OUT_ACC) {
-        // entries (tile, row r, batch row b) with b padded to 4
-        for (int e = threadIdx.x; e < nt * 64; e += MG_CT) {
-            const int b = e & 3, r = (e >> 2) & 15, t = t0 + (e >> 6);
-            if (b >= B) continue;
-            float s = 0.f;
-#pragma unroll
-            for (int w = 0; w < MG_CWARPS; w++) {  // fixed warp order; loads independent of the test
-                const int wt = ms->wtile[p][w];
-                const float x0 = sm.sRed[(w * 2 + 0) * 128 + r * 8 + b], x1 = sm.sRed[(w * 2 + 1) * 128 + r * 8 + b];
-                s += wt == t ? x0 : ((wt >= 0 && wt + 1 == t) ? x1 : 0.f);
-            }
-            if (use_post) s *= ms->post[b];
-            red_add64(acc + (size_t)b * a.acc_w + t * 16 + r, to_fix_counted(s));
-        }
-    } else {
+    const int t0 = g0 / gpt, nt = (g1 - 1) / gpt - t0 + 1;
+    {
         // whole gate|up tiles: rows 0..7 gate, 8..15 up of features 8t..8t+7
         for (int e = threadIdx.x; e < nt * 32; e += MG_CT) {
             const int b = e & 3, r = (e >> 2) & 7, t = t0 + (e >> 5);
@@ -605,28 +652,44 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int grp = a.heads / a.kvh, g = h / grp, pos = ms->pos[b];
+    const int grp = ms->grp, g = ms->hgrp[h], pos = ms->pos[b];
     const int p0 = s * MG_ATT_CH, p1 = min(pos + 1, p0 + MG_ATT_CH), pc = min(p1, pos), len = p1 - p0;
     const int ns = (pos + MG_ATT_CH) / MG_ATT_CH;  // chunks of the (row, head); chunk ns - 1 combines them
-    // K/V rows padded to 72 elements (144 B): 16-byte loads of 8 consecutive
-    // rows fall on distinct bank groups
-    constexpr int KS = HD + 8;
-    uint16_t* sK = reinterpret_cast<uint16_t*>(sm.sB);         // [128][72]
-    uint16_t* sV = sK + MG_ATT_CH * KS;                          // [128][72]
+    // K/V rows as the pool stores them (16-position pages of [16][64] bf16,
+    // 128 B per row), one bulk copy per page
+    constexpr int KS = HD;
+    uint16_t* sK = reinterpret_cast<uint16_t*>(sm.sB);         // [128][64]
+    uint16_t* sV = sK + MG_ATT_CH * KS;                          // [128][64]
     float* sq = reinterpret_cast<float*>(sV + MG_ATT_CH * KS);  // [64]
     float* skn = sq + HD;                                        // [64]
     float* svn = skn + HD;                                       // [64]
     float* sS = svn + HD;                                        // [128]
-    float2* sP = reinterpret_cast<float2*>(sS + MG_ATT_CH);     // [8 warps][32]
     const int* bt = sm.bt + b * MG_BT_INTS;
-    // 1. prefetch cached K/V rows [p0, pc)
-    for (int e = tid; e < (pc - p0) * 8; e += MG_CT) {
-        const int j = e >> 3, piece = e & 7, p = p0 + j;
-        const int page = bt[p / PAGE];
-        cp16(sK + j * KS + piece * 8, a.kv.pool + kv_index(a.kv, page, l, 0, g, p % PAGE) + piece * 8);
-        cp16(sV + j * KS + piece * 8, a.kv.pool + kv_index(a.kv, page, l, 1, g, p % PAGE) + piece * 8);
+    if (tid == 0) ms->frag_dirty = 1;
+    // 1. prefetch the pages holding cached positions [p0, pc): one 2 KB bulk
+    //    copy per page and K/V (p0 is page-aligned; rows of a partial last
+    //    page past pc are never read), completing on the CTA's attention
+    //    mbarrier. Every thread read the barrier's phase count before the
+    //    barrier that follows (thread 0 advances it there).
+    const uint32_t att_par = ms->att_uses & 1u;
+    if (tid == 0) {
+        const int npg = (pc - p0 + PAGE - 1) / PAGE;
+        constexpr uint32_t PG = PAGE * HD * 2;
+        // earlier generic-proxy accesses of this area (fragments, the last
+        // item's rows) are ordered before the copies' async-proxy writes
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        if (npg > 0) {
+            mbar_expect_tx(&ms->att_bar, (uint32_t)npg * 2u * PG);
+            for (int i = 0; i < npg; i++) {
+                const int page = bt[(p0 >> 4) + i];
+                bulk_g2s(sK + i * PAGE * HD, a.kv.pool + kv_index(a.kv, page, l, 0, g, 0), PG, &ms->att_bar);
+                bulk_g2s(sV + i * PAGE * HD, a.kv.pool + kv_index(a.kv, page, l, 1, g, 0), PG, &ms->att_bar);
+            }
+        } else {
+            mbar_arrive(&ms->att_bar);  // nothing cached in this chunk: complete the phase
+        }
+        ms->att_inflight = 1;
     }
-    cp_commit();
     // 2. q of the head, k, v of the new position: entry (kind, tile, r8) holds
     //    the RoPE pair (d, d+32) = tile rows r8, r8 + 8
     const unsigned long long* qacc = acc_ptr(a, ms->epoch, l, MG_ACC_QKV) + (size_t)b * a.acc_w;
@@ -650,112 +713,132 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         dst[d] = sc * x1;
         dst[d + 32] = sc * x2;
     }
-    cp_wait_all();
+    if (!mbar_wait(&ms->att_bar, att_par)) atomicCAS(cx.fail, 0, 6);
     cbar();
+    if (tid == 0) {
+        ms->att_uses++;
+        if (!*(volatile int*)cx.fail) ms->att_inflight = 0;
+    }
+    if (sm.st && tid == 0) sm.st[36] = clock64();  // diagnostics: q, k, v and the chunk's K/V in shared memory
     // 3. the group's first head, in the chunk holding the new position, appends it
     if (p1 == pos + 1 && h % grp == 0 && tid < 2 * HD) {
         const int which = tid / HD, d = tid % HD;
         const int page = bt[pos / PAGE];
         a.kv.pool[kv_index(a.kv, page, l, which, g, pos % PAGE) + d] = f2bf(which ? svn[d] : skn[d]);
     }
-    // 4. scores: a thread per position
-    if (tid < len) {
+    // 4. each warp takes 16 positions of the chunk, 16 w.. 16 w + 15, and runs
+    //    scores, softmax and P.V on them with no CTA barrier between the
+    //    steps: lane (j = lane & 15, half = lane >> 4) dots half of the head
+    //    dims of position 16 w + j, the halves meet by one shuffle
+    static_assert(MG_ATT_CH == 16 * MG_CWARPS, "attention: 16 positions per consumer warp");
+    const int jw = warp * 16 + (lane & 15), half = lane >> 4;
+    float sc = -INFINITY;
+    if (jw < len) {
         float s0 = 0.f, s1 = 0.f;
-        if (p0 + tid < pos) {
-            const uint4* src = reinterpret_cast<const uint4*>(sK + tid * KS);
+        const float* qh = sq + 32 * half;
+        if (p0 + jw < pos) {
+            // rows are 128 B apart: lane (j, half) reads its 16-byte pieces in
+            // the order c = (q + j) & 3, so each read instruction spreads the
+            // warp over all eight bank groups
+            const uint4* src = reinterpret_cast<const uint4*>(sK + jw * KS + 32 * half);
 #pragma unroll
-            for (int q = 0; q < HD / 8; q++) {
+            for (int q0 = 0; q0 < 4; q0++) {
+                const int q = (q0 + jw) & 3;
                 const uint4 v = src[q];
-                const float4 qa = *reinterpret_cast<const float4*>(sq + 8 * q);
-                const float4 qb = *reinterpret_cast<const float4*>(sq + 8 * q + 4);
+                const float4 qa = *reinterpret_cast<const float4*>(qh + 8 * q);
+                const float4 qb = *reinterpret_cast<const float4*>(qh + 8 * q + 4);
                 const float2 k0 = unpack_bf16x2(v.x), k1 = unpack_bf16x2(v.y), k2 = unpack_bf16x2(v.z), k3 = unpack_bf16x2(v.w);
                 s0 += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y;
                 s1 += qb.x * k2.x + qb.y * k2.y + qb.z * k3.x + qb.w * k3.y;
             }
         } else {
+            // the new key (already bf16-exact, as the cache holds it)
+            const float* kh = skn + 32 * half;
 #pragma unroll 8
-            for (int q = 0; q < HD / 2; q += 2) {
-                // the new key (already bf16-exact, as the cache holds it)
-                s0 += sq[2 * q] * skn[2 * q] + sq[2 * q + 1] * skn[2 * q + 1];
-                s1 += sq[2 * q + 2] * skn[2 * q + 2] + sq[2 * q + 3] * skn[2 * q + 3];
+            for (int q = 0; q < 32; q += 4) {
+                s0 += qh[q] * kh[q] + qh[q + 1] * kh[q + 1];
+                s1 += qh[q + 2] * kh[q + 2] + qh[q + 3] * kh[q + 3];
             }
         }
-        sS[tid] = s0 + s1;
+        sc = s0 + s1;
     }
-    cbar();
-    // 5. softmax inside the chunk (warp 0)
-    if (warp == 0) {
-        float m = -INFINITY;
-        for (int j = lane; j < len; j += 32) m = fmaxf(m, sS[j]);
-        m = warp_max(m);
-        float sum = 0.f;
-        for (int j = lane; j < len; j += 32) {
-            const float p = expf(sS[j] - m);
-            sS[j] = p;
-            sum += p;
-        }
-        sum = warp_sum(sum);
-        if (lane == 0) {
-            if (s == ns - 1) {
-                ms->om = m;
-                ms->ol = sum;
-            } else {
-                uint64_t* o = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
-                str64(o, tagged(tag, m));
-                str64(o + 1, tagged(tag, sum));
-            }
-        }
-    }
-    cbar();
-    // 6. P.V: warp w sums positions [w*len/8, (w+1)*len/8) for dim pair = lane
-    {
-        const int j0 = warp * len / MG_CWARPS, j1 = (warp + 1) * len / MG_CWARPS;
-        float2 ac0 = make_float2(0.f, 0.f), ac1 = make_float2(0.f, 0.f);
-        int j = j0;
+    sc += __shfl_xor_sync(0xffffffffu, sc, 16);  // both halves hold the position's score
+    float m = sc;
+#pragma unroll
+    for (int o = 8; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (sm.st && tid == 0) sm.st[15] = clock64();  // diagnostics: warp 0's scores and maximum
+    const float pj = jw < len ? expf(sc - m) : 0.f;  // m is finite wherever some position is valid
+    float lsum = pj;
+#pragma unroll
+    for (int o = 8; o; o >>= 1) lsum += __shfl_xor_sync(0xffffffffu, lsum, o);
+    // P.V: lane = dim pair (2 lane, 2 lane + 1) over the warp's valid
+    // positions; the probabilities go through the warp's slot of the partial
+    // area (floats 4..19, overwritten only after the __syncwarp below) and
+    // are read four at a time
+    const int nj = max(0, min(16, len - warp * 16));  // warp-uniform
+    float* ps = sS + warp * 68 + 4;
+    if (lane < 16) ps[lane] = pj;
+    __syncwarp();
+    float2 ac = make_float2(0.f, 0.f);
+    const int rn = pos - p0 - warp * 16;  // the new position's row in this warp's 16, if any
 #pragma unroll 1
-        for (; j + 2 <= j1; j += 2) {
-            float2 v0, v1;
-            if (p0 + j + 1 < pos) {
-                v0 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * KS + 2 * lane));
-                v1 = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (j + 1) * KS + 2 * lane));
-            } else {
-                v0 = p0 + j < pos ? unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * KS + 2 * lane))
-                                  : make_float2(svn[2 * lane], svn[2 * lane + 1]);
-                v1 = make_float2(svn[2 * lane], svn[2 * lane + 1]);
+    for (int j4 = 0; j4 < nj; j4 += 4) {
+        const float4 p4 = *reinterpret_cast<const float4*>(ps + j4);
+        const float pv[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int j = j4 + i;
+            if (j < nj) {  // rows past the chunk's length are never read
+                const float2 v = j != rn ? unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (warp * 16 + j) * KS + 2 * lane))
+                                         : make_float2(svn[2 * lane], svn[2 * lane + 1]);
+                ac.x += pv[i] * v.x;
+                ac.y += pv[i] * v.y;
             }
-            ac0.x += sS[j] * v0.x;
-            ac0.y += sS[j] * v0.y;
-            ac1.x += sS[j + 1] * v1.x;
-            ac1.y += sS[j + 1] * v1.y;
         }
-        if (j < j1) {
-            const float2 v = p0 + j < pos ? unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + j * KS + 2 * lane))
-                                          : make_float2(svn[2 * lane], svn[2 * lane + 1]);
-            ac0.x += sS[j] * v.x;
-            ac0.y += sS[j] * v.y;
-        }
-        sP[warp * 32 + lane] = make_float2(ac0.x + ac1.x, ac0.y + ac1.y);
     }
+    __syncwarp();  // every lane read the probabilities before the partials overwrite them
+    if (sm.st && tid == 0) sm.st[16] = clock64();  // diagnostics: warp 0's P.V done
+    // the warps' (max, sum, P.V) partials meet in shared memory (the score
+    // area); 64 threads, one per dim, merge them into the chunk's partial
+    float* wp = sS;  // [MG_CWARPS][68] (the probabilities above lived in floats 4..19 of each warp's row)
+    if (lane == 0) {
+        wp[warp * 68] = nj > 0 ? m : -INFINITY;
+        wp[warp * 68 + 1] = lsum;
+    }
+    wp[warp * 68 + 2 + 2 * lane] = ac.x;
+    wp[warp * 68 + 3 + 2 * lane] = ac.y;
     cbar();
+    if (sm.st && tid == 0) sm.st[37] = clock64();  // diagnostics: every warp's partial in shared memory
     float* own = sq;  // [64] this chunk's P.V sums when it combines (q is no longer read)
-    if (warp == 0) {
-        float ox = 0.f, oy = 0.f;
+    if (tid < HD) {
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < MG_CWARPS; w++) M = fmaxf(M, wp[w * 68]);
+        float L = 0.f, o = 0.f;
 #pragma unroll
         for (int w = 0; w < MG_CWARPS; w++) {
-            const float2 v = sP[w * 32 + lane];
-            ox += v.x;
-            oy += v.y;
+            const float mw = wp[w * 68];
+            const float e = mw == -INFINITY ? 0.f : expf(mw - M);
+            L += wp[w * 68 + 1] * e;
+            o += wp[w * 68 + 2 + tid] * e;
         }
         if (s == ns - 1) {
-            own[2 * lane] = ox;
-            own[2 * lane + 1] = oy;
+            own[tid] = o;
+            if (tid == 0) {
+                ms->om = M;
+                ms->ol = L;
+            }
         } else {
-            uint64_t* o = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
-            str64(o + 2 + 2 * lane, tagged(tag, ox));
-            str64(o + 3 + 2 * lane, tagged(tag, oy));
+            uint64_t* ob = a.attn + (((size_t)b * a.heads + h) * a.max_splits + s) * MG_PART;
+            if (tid == 0) {
+                str64(ob, tagged(tag, M));
+                str64(ob + 1, tagged(tag, L));
+            }
+            str64(ob + 2 + tid, tagged(tag, o));
         }
     }
     if (s != ns - 1) return;  // CTA-uniform; the caller meets at a barrier next
+    cbar();  // own, om, ol written; the score area is free for the combine below
     // 7. the chunk holding the new position combines the (row, head):
     //    o = sum_s acc_s e^(m_s - M) / L over the other chunks' tagged partials
     //    (each word polled until this step's tag shows; every chunk with a
@@ -770,14 +853,13 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     float* cl = sS + 64;  // [no] chunk sums
     const int d = tid & 63, qt = tid >> 6;  // qt < MG_NQ
     uint64_t va[4];
-#pragma unroll
-    for (int k = 0; k < 4; k++) va[k] = qt + MG_NQ * k < no ? ldr64(ob + (size_t)(qt + MG_NQ * k) * MG_PART + 2 + d) : 0ull;
     if (tid < 2 * no) {
         const uint64_t* w = ob + (size_t)(tid >> 1) * MG_PART + (tid & 1);
         const uint64_t v = ldr64(w);
         (tid & 1 ? cl : cm)[tid >> 1] = (uint32_t)(v >> 32) == tag ? __uint_as_float((uint32_t)v) : poll(cx, w, tag);
     }
     cbar();
+    if (sm.st && tid == 0) sm.st[38] = clock64();  // diagnostics: the other chunks' maxima and sums in hand
     float M = -INFINITY, L = 0.f;
     for (int q = 0; q <= no; q++) {
         const float mq = q < no ? cm[q] : ms->om, lq = q < no ? cl[q] : ms->ol;
@@ -787,12 +869,13 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     }
     const float il = 1.0f / L;
     float v = 0.f;
+    // the chunks' values are loaded once their maxima and sums have shown up
+    // (written in the same pass), so they are rarely stale: the four loads of
+    // a pass are in flight together and a stale word is polled on its own
 #pragma unroll 1
     for (int s0 = qt; s0 < no; s0 += 4 * MG_NQ) {
-        if (s0 != qt) {
 #pragma unroll
-            for (int k = 0; k < 4; k++) va[k] = s0 + MG_NQ * k < no ? ldr64(ob + (size_t)(s0 + MG_NQ * k) * MG_PART + 2 + d) : 0ull;
-        }
+        for (int k = 0; k < 4; k++) va[k] = s0 + MG_NQ * k < no ? ldr64(ob + (size_t)(s0 + MG_NQ * k) * MG_PART + 2 + d) : 0ull;
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int sk = s0 + MG_NQ * k;
@@ -802,13 +885,14 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
             v += x * (expf(cm[sk] - M) * il);
         }
     }
-    float* red = cl + 64;  // [4][64]: the P.V partial area sP, read by warp 0 before the barrier above
+    float* red = cl + 64;  // [4][64], in the score area (the warp partials were read before the barriers above)
     red[qt * 64 + d] = v;
     cbar();
     if (tid < HD) {
         const float o = sum_groups(red, tid) + own[tid] * (expf(ms->om - M) * il);
         str64(a.comb + ((size_t)b * a.heads + h) * HD + tid, tagged(tag, rb(o)));
     }
+    if (sm.st && tid == 0 && l > 0) sm.st[39] = clock64();  // diagnostics: head published (slot 39 of layer 0 is the origin)
 }
 
 // o_proj input: the combined attention output of the heads this CTA's
@@ -856,8 +940,12 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             mbar_init(&lp_full[i], 1);
             mbar_init(&lp_empty[i], 1);
         }
+        mbar_init(&ms->att_bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        ms->att_uses = 0;
+        ms->att_inflight = 0;
         ms->fail = 0;
+        ms->frag_dirty = 1;
         ms->prod_done = 0;
         ms->issued = 0;
         ms->epoch = (uint32_t)a.counter[0] + 1u;
@@ -892,9 +980,32 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
         ms->tcount[q][t] = (uint8_t)(t < a.ph[p].tiles ? a.ph[p].tcount[t] : 0);
     }
     if (tid < MG_NPH * MG_CWARPS) {
-        const int p = tid / MG_CWARPS, w = tid % MG_CWARPS, n = ms->g1[p] - ms->g0[p];
+        const int p = tid / MG_CWARPS, w = tid % MG_CWARPS, n = ms->g1[p] - ms->g0[p], gpt = a.ph[p].gpt;
         const int i0 = w * n / MG_CWARPS, i1 = (w + 1) * n / MG_CWARPS;
-        ms->wtile[p][w] = i1 > i0 ? (ms->g0[p] + i0) / a.ph[p].gpt : -1;
+        ms->wtile[p][w] = i1 > i0 ? (ms->g0[p] + i0) / gpt : -1;
+        Misc::WRun r{};
+        r.i0 = (short)i0;
+        r.i1 = (short)i1;
+        r.je = -1;
+        if (i1 > i0) {
+            const int g = ms->g0[p] + i0;
+            r.t = (short)(g / gpt);
+            r.kg = (short)(g - r.t * gpt);
+            r.wi = (short)(i0 % a.gps);
+            r.js = (short)(i0 / a.gps);
+            r.je = (short)((i1 - 1) / a.gps);
+        }
+        ms->wrun[p][w] = r;
+        if (w == 0) {
+            ms->nsc[p] = n > 0 ? (n + a.gps - 1) / a.gps : 0;
+            ms->pbase[p] = ms->g0[p] % gpt;
+        }
+    }
+    if (tid < 64) ms->hgrp[tid] = (uint8_t)(tid < a.heads ? tid / (a.heads / a.kvh) : 0);
+    if (tid < B) ms->nitems[tid] = a.heads * ((ms->pos[tid] + MG_ATT_CH) / MG_ATT_CH);
+    if (tid == 0) {
+        ms->grp = a.heads / a.kvh;
+        ms->hm = ((1ull << 32) + (unsigned long long)a.heads - 1ull) / (unsigned long long)a.heads;
     }
     __syncthreads();
     const uint32_t epoch = ms->epoch;
@@ -941,7 +1052,9 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
 
     // ---------------- consumer warps ----------------
     Ctx cx{&a, &ms->fail};
-    int cons = 0, lp_used = 0;
+    int cons = 0, lp_used = 0;  // ring slots consumed so far (the wind-down waits for those issued after)
+    int cslot = 0;                // cons % nslots and the parity of cons / nslots, kept without dividing
+    uint32_t cpar = 0;
     bool dead = false;
     auto check = [&]() -> bool {
         cbar();  // every consumer thread sees the same answer
@@ -998,22 +1111,23 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             const bool rows = q == 0 || q == 2;  // input = the normed residual rows
             int base = 0, nst = H / 64;
             if (!rows) {
-                base = ms->g0[q] % gpt;
+                base = ms->pbase[q];
                 nst = min(n, gpt);
             }
             if (q == 1) {
                 // P1: attention items (row, chunk, query head) strided over the
                 // CTAs; neighbouring CTAs share a chunk's K/V lines in L2
                 int tot = 0;
-                for (int b = 0; b < B; b++) tot += a.heads * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
+                for (int b = 0; b < B; b++) tot += ms->nitems[b];
                 bool waited = false;
                 for (int it = c; it < tot && !dead; it += a.C) {
                     int rem = it, b = 0;
-                    while (rem >= a.heads * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH)) {
-                        rem -= a.heads * ((ms->pos[b] + MG_ATT_CH) / MG_ATT_CH);
+                    while (rem >= ms->nitems[b]) {
+                        rem -= ms->nitems[b];
                         b++;
                     }
-                    attention_item(cx, sm, l, tag, b, rem % a.heads, rem / a.heads, waited);
+                    const int sch = divB(rem, ms->hm);  // rem / heads (rem < 2^16: exact)
+                    attention_item(cx, sm, l, tag, b, rem - sch * a.heads, sch, waited);
                     waited = true;
                     check();
                 }
@@ -1057,9 +1171,14 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             sm.so = 10 + 7 * q;
             stage<F16>(sm, nst, B, H, rows ? 0 : 1, q == 0 ? ln1 : ln2);
             const int which = q == 0 ? MG_ACC_QKV : (q == 1 ? MG_ACC_X1 : MG_ACC_X2);
-            gemv_phase<FMT>(cx, sm, q, cons, ring, full, empty, base, rows, q == 2 ? OUT_GLU : OUT_ACC,
+            gemv_phase<FMT>(cx, sm, q, cslot, cpar, ring, full, empty, base, rows, q == 2 ? OUT_GLU : OUT_ACC,
                             q == 2 ? nullptr : acc_ptr(a, epoch, l, which), hb, tag);
-            cons += (n + a.gps - 1) / a.gps;
+            cons += ms->nsc[q];
+            cslot += ms->nsc[q];
+            while (cslot >= a.nslots) {
+                cslot -= a.nslots;
+                cpar ^= 1u;
+            }
             if (check()) break;
             MG_STAMP(2 + 2 * q)
         }
@@ -1121,6 +1240,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             const int issued = *(volatile int*)&ms->issued;
             for (int sc = cons; sc < issued; sc++) mbar_wait(&full[sc % a.nslots], (sc / a.nslots) & 1);
             for (int l = lp_used; l < a.layers && l < lp_used + 2; l++) mbar_wait(&lp_full[l & 1], (l >> 1) & 1);
+            if (ms->att_inflight) mbar_wait(&ms->att_bar, ms->att_uses & 1u);  // an attention item's page copies
         }
         return;
     }

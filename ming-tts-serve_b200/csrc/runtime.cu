@@ -650,14 +650,21 @@ int setup_mega(ming_ctx* c) {
         a.ph[p] = MegaPhase{dg0, nullptr, tiles[p], gpt[p]};
         if (p == 2) continue;  // gate|up: whole tiles per CTA
         // split-K phase: contributors per tile (the count every counted
-        // accumulator word of the tile reaches when complete)
+        // accumulator word of the tile reaches when complete). Each consumer
+        // warp of a CTA adds its own partial sums for the tiles its run of
+        // the CTA's groups touches: warp w takes groups [w n / W, (w+1) n / W).
         if (tiles[p] > MG_MAX_TILES) return MING_OK;
         std::vector<int> tc(tiles[p], 0);
-        for (int i = 0; i < C; i++)
-            for (int t = 0; t < tiles[p]; t++)
-                if (g0[i] < (t + 1) * gpt[p] && g0[i + 1] > t * gpt[p]) tc[t]++;
+        for (int i = 0; i < C; i++) {
+            const int n = g0[i + 1] - g0[i];
+            for (int w = 0; w < MG_CWARPS; w++) {
+                const int i0 = w * n / MG_CWARPS, i1 = (w + 1) * n / MG_CWARPS;
+                if (i1 <= i0) continue;
+                for (int t = (g0[i] + i0) / gpt[p]; t <= (g0[i] + i1 - 1) / gpt[p]; t++) tc[t]++;
+            }
+        }
         for (int t = 0; t < tiles[p]; t++)
-            if (tc[t] < 1 || tc[t] > 127) return MING_OK;  // the count lives in one byte of the word
+            if (tc[t] < 1 || tc[t] > 255) return MING_OK;  // the count lives in one byte of the word
         int* dtc = c->mem.alloc<int>(tiles[p], &rc);
         if (rc) return rc;
         CK(cudaMemcpy(dtc, tc.data(), tiles[p] * 4, cudaMemcpyHostToDevice));
@@ -677,6 +684,7 @@ int setup_mega(ming_ctx* c) {
     uint8_t* lpar = c->mem.alloc<uint8_t>((size_t)f.layers * lp_bytes, &rc);
     const int max_splits = (f.max_ctx + MG_ATT_CH - 1) / MG_ATT_CH;
     if (max_splits > 64) return MING_OK;  // a head's combine keeps up to 64 chunk maxima and sums in shared memory
+    if (f.heads > 64) return MING_OK;      // the kernel's head -> kv head table has 64 entries
     if ((H / 64) * MG_MAXB * max_splits > 8192) return MING_OK;  // split weights live in the 32 KB fragment area
     const size_t attn_n = (size_t)MG_MAXB * f.heads * max_splits * MG_PART;
     uint64_t* attn = c->mem.alloc<uint64_t>(attn_n, &rc);
