@@ -61,6 +61,11 @@ typedef struct ming_cfg {
     int dit_max_batch;
     /* aggregator (token mode only; 0 blocks = none) */
     int agg_blocks;
+    /* VAE decoder (audio.decoder.*; 0 layers = none, the reference's is 24):
+     * Qwen2 layers of the LM's width with a causal sliding window, latents
+     * upsampled x4, an ISTFT head (n_fft 3528, hop 882) */
+    int vae_layers, vae_ff, vae_window;
+    int vae_max_latents; /* latents per ming_cuda_vae_decode call */
 } ming_cfg;
 
 void ming_cuda_default_cfg(ming_cfg* cfg);
@@ -211,6 +216,17 @@ int ming_cuda_loop_step(ming_loop* lp, int* active, int* queued);
  * while it is still queued or running. Fetching releases the request. */
 int ming_cuda_loop_result(ming_loop* lp, int req, uint16_t* latents, int cap, int* n, uint16_t* z_trace, float* stop_trace);
 int ming_cuda_loop_destroy(ming_loop* lp);
+
+/* Model.vaeDecode (src/ming_model.zig:1257-1300): latents [T][64] (bf16) ->
+ * waveform [T * 4 * 882] f32 at 44.1 kHz. fc1 (64 -> hidden), linear upsample
+ * x4 in f32 (linearUpsample, :1303-1342), the decoder's Qwen2 layers in f32
+ * activations with a causal sliding window of vae_window positions
+ * (QStack.forward with a window, :566-614, slidingMask :617-635), final norm,
+ * the head linear (hidden -> 3530), then the ISTFT: magnitude
+ * min(exp(m), 100) and phase of 1765 bins, irfft of 3528 points, the
+ * checkpoint's window, overlap-add at hop 882, division by the window
+ * envelope and the "same" trim of 1323 samples per side. */
+int ming_cuda_vae_decode(ming_ctx* ctx, const uint16_t* latents, int T, float* wave, int ptr_kind);
 
 /* The context's CUDA stream (a cudaStream_t), for event timing by callers. */
 int ming_cuda_get_stream(ming_ctx* ctx, void** stream);

@@ -169,6 +169,22 @@ struct ming_ctx {
     uint16_t *a_lat = nullptr, *a_rows = nullptr, *a_x1 = nullptr, *a_qkv = nullptr, *a_att = nullptr, *a_hh = nullptr,
              *a_xe = nullptr, *a_out = nullptr;
 
+    // VAE decoder (vae.cu): linears packed with their K doubled ([W | W]) so
+    // f32 activations enter as bf16 hi / lo halves; the ISTFT's irfft as a
+    // linear with the DFT basis (K tripled: hi, lo and hi parts)
+    struct VaeLayer {
+        ming::rt::PackedLin qkv, o, gu, down;
+        uint16_t* ln1 = nullptr;
+        uint16_t* ln2 = nullptr;
+    };
+    std::vector<VaeLayer> vae;
+    ming::rt::PackedLin vae_fc1, vae_head, vae_dft;
+    uint16_t* vae_norm = nullptr;
+    float* vae_win = nullptr;
+    uint16_t *v_lat = nullptr, *v_fc1 = nullptr;
+    float *v_x = nullptr, *v_q = nullptr, *v_k = nullptr, *v_v = nullptr, *v_att = nullptr, *v_h = nullptr;
+    float *v_head = nullptr, *v_spec = nullptr, *v_frames = nullptr, *v_wave = nullptr;
+
     ~ming_ctx() {
         for (auto& kv : decode_graphs) cudaGraphExecDestroy(kv.second);
         for (auto& kv : cfm_graphs) cudaGraphExecDestroy(kv.second);
@@ -181,6 +197,19 @@ namespace ming {
 namespace rt {
 
 // Shared host helpers (runtime.cu). All work goes on the context's stream.
+// The next launch-trace slot of a step (MING_KTRACE=1) or null.
+long long* ktrace_slot(ming_ctx* c);
+// A weight from the staged tensors: "<prefix>.weight" bf16, or U32 + .scales
+// + .biases; its bias when want_bias.
+int lin_src(ming_ctx* c, const std::string& prefix, LinearSrc& s, bool want_bias);
+// Packs sources into the kernels' tiles (rows in the given order) on the device.
+int upload_packed(ming_ctx* c, const std::vector<LinearSrc>& srcs, const std::vector<std::string>& names,
+                  const std::vector<RowRef>& rows, PackedLin& pl);
+// A staged tensor copied to the device as is (checked dtype and element count).
+int upload_raw(ming_ctx* c, const std::string& name, int dtype, int64_t count, void** out);
+const HostTensor* find_staged(ming_ctx* c, const std::string& name);
+// A linear in plain row order (tile row r = output 16 t + r), its out dim in *out_dim.
+int pack_plain(ming_ctx* c, const std::string& prefix, bool bias, PackedLin& pl, int* out_dim = nullptr);
 int check_seq(ming_ctx* c, int s);
 // Gives positions [from, to) of sequence s pages; uploads new block-table entries.
 int ensure_pages(ming_ctx* c, int s, int from, int to);
@@ -197,6 +226,8 @@ int cfm_enqueue(ming_ctx* c, int B, bool with_sde, float cfg, float shift, int s
 // Model.aggregate of B latents on the device (token mode: the aggregator's
 // blocks; adaLN mode: frame mean + aggregator.proj) into c->a_out.
 int agg_enqueue(ming_ctx* c, int B, const uint16_t* latent);
+// The VAE decoder's weights and buffers (vae.cu), when cfg.vae_layers > 0.
+int vae_finalize(ming_ctx* c);
 // Returns a sequence's pages to the pool without synchronising: the block
 // table reset is queued on the stream, behind every kernel that reads it.
 int seq_release(ming_ctx* c, int s);

@@ -83,7 +83,7 @@ MING_DEV bool tc_mbar_wait(uint64_t* bar, uint32_t parity) {
 
 // Packed bf16 tiles -> swizzled weight blocks [ntiles / 8][K / 64][16 KB]:
 // block (mt, g) is the shared-memory image of features 128 mt.. and K group g.
-__global__ void __launch_bounds__(TC_THREADS) tc_swizzle_kernel(const uint8_t* tiles, int ng, uint8_t* out) {
+static __global__ void __launch_bounds__(TC_THREADS) tc_swizzle_kernel(const uint8_t* tiles, int ng, uint8_t* out) {
     const int mt = blockIdx.x, g = blockIdx.y;
     uint8_t* dst = out + ((size_t)mt * ng + g) * TC_A_BLOCK;
     for (int e = threadIdx.x; e < 8 * 4 * 32; e += TC_THREADS) {

@@ -32,6 +32,7 @@ SYMBOLS = [
     "ming_cuda_step_kernels", "ming_cuda_lm_decode_noalloc", "ming_cuda_kv_write",
     "ming_cuda_default_sample_params", "ming_cuda_sample_latents", "ming_cuda_loop_create", "ming_cuda_loop_submit",
     "ming_cuda_loop_step", "ming_cuda_loop_result", "ming_cuda_loop_destroy", "ming_cuda_load_safetensors",
+    "ming_cuda_vae_decode",
 ]
 
 
@@ -41,7 +42,8 @@ class Cfg(ctypes.Structure):
         (n, ctypes.c_int) for n in (
             "weight_bits", "group_size", "page_size", "max_seqs", "max_pages", "max_ctx", "max_batch", "max_prefill",
             "dit_mode", "dit_hidden", "dit_blocks", "dit_heads", "dit_ff", "dit_latent", "dit_frames",
-            "dit_cond_dim", "dit_freq_dim", "dit_max_batch", "agg_blocks")]
+            "dit_cond_dim", "dit_freq_dim", "dit_max_batch", "agg_blocks", "vae_layers", "vae_ff", "vae_window",
+            "vae_max_latents")]
 
 
 class SampleParams(ctypes.Structure):
@@ -99,6 +101,7 @@ def lib():
         "ming_cuda_loop_result": (I, [P, I, P, I, IP, P, P]),
         "ming_cuda_loop_destroy": (I, [P]),
         "ming_cuda_load_safetensors": (I, [P, ctypes.c_char_p, IP]),
+        "ming_cuda_vae_decode": (I, [P, P, I, P, I]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -314,6 +317,14 @@ class Context:
                                               bank_steps, seed, _ptr(lat), cap, ctypes.byref(n), _ptr(zt), _ptr(st)))
         k = n.value
         return lat[:k], (zt[:k] if trace else None), st[:k]
+
+    def vae_decode(self, latents):
+        """Model.vaeDecode: latents uint16 bf16 [T, 64] -> waveform f32 [T * 4 * 882]."""
+        latents = np.ascontiguousarray(latents, dtype=np.uint16)
+        T = latents.shape[0]
+        wave = np.empty(T * 4 * 882, dtype=np.float32)
+        _check(lib().ming_cuda_vae_decode(self._h, _ptr(latents), T, _ptr(wave), PTR_HOST))
+        return wave
 
     def kv_write(self, s, layer, pos0, k, v):
         """k, v: uint16 [kv_heads, n, 64] bf16 written at positions pos0.."""

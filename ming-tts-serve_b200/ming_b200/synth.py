@@ -289,3 +289,39 @@ def save_safetensors(path, tensors, metadata=None):
         f.write(h)
         for b in blobs:
             f.write(b)
+
+
+def hann_periodic(n):
+    """A periodic Hann window, 0.5 - 0.5 cos(2 pi k / n), f32: the stand-in for
+    the checkpoint's audio.decoder.head.istft.window buffer (this build's
+    choice for random init)."""
+    k = np.arange(n, dtype=np.float64)
+    return (0.5 - 0.5 * np.cos(2.0 * np.pi * k / n)).astype(np.float32)
+
+
+def vae_weights(seed=2, layers=24, hidden=896, heads=14, kv_heads=2, ff=4864, latent=64, std=0.02, head_std=0.04,
+                gains=False):
+    """The VAE decoder under audio.decoder.*: fc1 (latent -> hidden), Qwen2
+    layers (decoder.layers.i, decoder.norm), the ISTFT head (head.out, hidden ->
+    3530 = log-magnitudes and phases of 1765 bins; head.istft.window). bf16
+    weights N(0, std) (head.out N(0, head_std), large enough that the spectra
+    vary); RMSNorm gains 1, or U(0.5, 1.5) with gains=True."""
+    W = {}
+    D = "audio.decoder"
+    H, QD, KD = hidden, heads * 64, kv_heads * 64
+    _lin(W, seed, D + ".fc1", H, latent, std)
+    g = np.random.default_rng(seed)
+    for i in range(layers):
+        p = f"{D}.decoder.layers.{i}"
+        for n in ("input_layernorm", "post_attention_layernorm"):
+            W[f"{p}.{n}.weight"] = (f32_to_bf16(g.uniform(0.5, 1.5, H).astype(np.float32)) if gains else ones_bf16((H,)))
+        for n, o, k, b in (("self_attn.q_proj", QD, H, True), ("self_attn.k_proj", KD, H, True),
+                           ("self_attn.v_proj", KD, H, True), ("self_attn.o_proj", H, QD, False),
+                           ("mlp.gate_proj", ff, H, False), ("mlp.up_proj", ff, H, False), ("mlp.down_proj", H, ff, False)):
+            W[f"{p}.{n}.weight"] = normal_bf16(seed, f"{p}.{n}.weight", (o, k), std)
+            if b:
+                W[f"{p}.{n}.bias"] = normal_bf16(seed, f"{p}.{n}.bias", (o,), std)
+    W[D + ".decoder.norm.weight"] = ones_bf16((H,))
+    _lin(W, seed, D + ".head.out", 3530, H, head_std)
+    W[D + ".head.istft.window"] = hann_periodic(3528)
+    return W

@@ -379,3 +379,126 @@ def ada_latent_proj(W, latent):
     w = f32(W["aggregator.proj.weight"]).astype(np.float64)
     b = f32(W["aggregator.proj.bias"]).astype(np.float64)
     return bf((m.astype(np.float64) @ w.T + b).astype(np.float32))
+
+
+# ---------------------------------------------------------------------------
+# VAE decoder (numpy restatement; test infrastructure like the rest of this
+# module). Follows Model.vaeDecode (src/ming_model.zig:1257-1300),
+# linearUpsample (:1303-1342) and QStack.forward with a sliding window
+# (:566-614, slidingMask :617-635): the backbone in f32 (MLX promotes the bf16
+# weights), fc1 in bf16 (the latents' dtype).
+# ---------------------------------------------------------------------------
+
+VAE_HOP, VAE_NFFT, VAE_PATCH = 882, 3528, 4
+
+
+def _f32(h):
+    return (np.asarray(h, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def _bf16_round(x):
+    u = np.ascontiguousarray(x, np.float32).view(np.uint32).astype(np.uint64)
+    return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16).astype(np.uint32).view(np.float32)
+
+
+def vae_upsample(x, scale=VAE_PATCH):
+    """Decoder._linear_upsample_1d (align_corners=False) in f32 over rows of x [T][C]:
+    row i reads source position p = (i + 0.5) / scale - 0.5 (src/ming_model.zig:1303-1342)."""
+    x = np.asarray(x, np.float32)
+    T = x.shape[0]
+    i = np.arange(T * scale, dtype=np.float32)
+    p = (i + np.float32(0.5)) / np.float32(scale) - np.float32(0.5)
+    lf = np.floor(p)
+    w = (p - lf).astype(np.float32)
+    l = lf.astype(np.int64)
+    a, b = np.clip(l, 0, T - 1), np.clip(l + 1, 0, T - 1)
+    return (x[a] * (np.float32(1) - w)[:, None] + x[b] * w[:, None]).astype(np.float32)
+
+
+def vae_istft_w(p, win):
+    """The ISTFT head on the head's output p [F][3530] with the window win [3528]
+    (src/ming_model.zig:1262-1299): magnitude min(exp(m), 100), phase, irfft of
+    3528 points ("backward" norm), the window, overlap-add at hop 882 (frame
+    parts in the reference's order), the window envelope and the "same" trim
+    of (3528 - 882) / 2 samples per side."""
+    p = np.asarray(p, np.float32)
+    nb = VAE_NFFT // 2 + 1
+    mag = np.minimum(np.exp(p[:, :nb]), np.float32(100.0))
+    ph = p[:, nb:]
+    spec = mag.astype(np.complex64) * (np.cos(ph) + 1j * np.sin(ph)).astype(np.complex64)
+    frames = np.fft.irfft(spec, n=VAE_NFFT, axis=-1).astype(np.float32) * np.asarray(win, np.float32)[None, :]
+    F = frames.shape[0]
+    total = (F + 3) * VAE_HOP
+    out = np.zeros(total, np.float32)
+    parts = frames.reshape(F, 4, VAE_HOP)
+    for j in (3, 2, 1, 0):  # part j of frame t lands in hop block t + j; added j = 3 first
+        out[j * VAE_HOP:(j + F) * VAE_HOP] += parts[:, j, :].reshape(-1)
+    env = np.zeros(total, np.float32)
+    w2 = (np.asarray(win, np.float32) * np.asarray(win, np.float32))
+    for t in range(F):
+        env[t * VAE_HOP:t * VAE_HOP + VAE_NFFT] += w2
+    pad = (VAE_NFFT - VAE_HOP) // 2
+    n_out = total - 2 * pad
+    return (out[pad:pad + n_out] / np.maximum(env[pad:pad + n_out], np.float32(1e-11))).astype(np.float32)
+
+
+def vae_decode(W, latents, layers, window=64, heads=14, kv_heads=2, eps=1e-6, theta=1e6):
+    """latents uint16 bf16 [T][64] -> waveform f32 [T * 4 * 882]."""
+    D = "audio.decoder"
+    lat = _f32(latents)
+    x = _bf16_round(lat @ _f32(W[D + ".fc1.weight"]).T + _f32(W[D + ".fc1.bias"]))
+    xn = vae_backbone(W, vae_upsample(x), layers, window, heads, kv_heads, eps, theta)
+    pr = xn @ _f32(W[D + ".head.out.weight"]).T + _f32(W[D + ".head.out.bias"])
+    return vae_istft_w(pr, W[D + ".head.istft.window"])
+
+
+def vae_backbone(W, x, layers, window=64, heads=14, kv_heads=2, eps=1e-6, theta=1e6):
+    """The decoder's Qwen2 layers in f32 over upsampled rows x [F][H] with the
+    causal sliding window, then the final norm (QStack.forward,
+    src/ming_model.zig:566-614)."""
+    D = "audio.decoder"
+    x = np.asarray(x, np.float32)
+    F, H = x.shape
+    hd = 64
+    half = hd // 2
+    l2t = np.float32(np.log2(np.float32(theta)))
+    inv_freq = np.exp2(-(np.arange(half, dtype=np.float32) / np.float32(half)) * l2t).astype(np.float32)
+    ang = np.arange(F, dtype=np.float32)[:, None] * inv_freq[None, :]
+    cs, sn = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+    def rms(v, g):
+        inv = (np.float32(1) / np.sqrt((v * v).mean(-1, keepdims=True, dtype=np.float32) + np.float32(eps))).astype(np.float32)
+        return (v * inv) * _f32(g)[None, :]
+
+    def lin(v, name, bias=False):
+        y = v @ _f32(W[name + ".weight"]).T
+        return (y + _f32(W[name + ".bias"])) if bias else y
+
+    def rope(t):
+        t = t.reshape(F, -1, hd)
+        a, b = t[..., :half], t[..., half:]
+        c, s = cs[:, None, :], sn[:, None, :]
+        return np.concatenate([a * c - b * s, a * s + b * c], -1)
+
+    idx = np.arange(F)
+    mask = np.where((idx[None, :] > idx[:, None] - window) & (idx[:, None] >= idx[None, :]), np.float32(0),
+                    np.float32(-3.4028235e38)).astype(np.float32)
+    grp = heads // kv_heads
+    for l in range(layers):
+        p = f"{D}.decoder.layers.{l}"
+        h = rms(x, W[p + ".input_layernorm.weight"])
+        q = rope(lin(h, p + ".self_attn.q_proj", True))
+        k = rope(lin(h, p + ".self_attn.k_proj", True))
+        v = lin(h, p + ".self_attn.v_proj", True).reshape(F, kv_heads, hd)
+        o = np.empty((F, heads, hd), np.float32)
+        for hh in range(heads):
+            g = hh // grp
+            sc = (q[:, hh, :] @ k[:, g, :].T) * np.float32(1.0 / 8.0) + mask
+            sc = sc - sc.max(-1, keepdims=True)
+            e = np.exp(sc)
+            o[:, hh, :] = (e / e.sum(-1, keepdims=True)) @ v[:, g, :]
+        x = x + lin(o.reshape(F, heads * hd), p + ".self_attn.o_proj")
+        h2 = rms(x, W[p + ".post_attention_layernorm.weight"])
+        gt, up = lin(h2, p + ".mlp.gate_proj"), lin(h2, p + ".mlp.up_proj")
+        x = x + lin((gt * (np.float32(1) / (np.float32(1) + np.exp(-gt)))) * up, p + ".mlp.down_proj")
+    return rms(x, W[D + ".decoder.norm.weight"]).astype(np.float32)
