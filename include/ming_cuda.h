@@ -83,9 +83,9 @@ int ming_cuda_load_tensor(ming_ctx* ctx, const char* name, int dtype, const int6
 
 /* Model.load's file side (src/ming_model.zig:316-350,923-1005): reads a
  * safetensors checkpoint (`path` a file, or a directory holding
- * model.safetensors) and loads the hot path's tensors (names under
+ * model.safetensors) and loads the tensors this library runs (names under
  * model.model., stop_head, flowloss., linear_proj_audio, adaln_head,
- * aggregator.) with ming_cuda_load_tensor: BF16 and U32 as stored, F32 and
+ * aggregator., audio.decoder.) with ming_cuda_load_tensor: BF16 and U32 as stored, F32 and
  * F16 rounded to bf16 (the reference casts to its bf16 model dtype) except
  * rotary inv_freq buffers, which stay F32; other names and dtypes are
  * skipped. *n_loaded (may be NULL) = tensors loaded. With ctx NULL the file

@@ -14,39 +14,93 @@ namespace ming {
 // Partial (m, l, acc) go to `part` for the O prologue to combine.
 namespace {
 constexpr int ATT_MAXG = 8;     // query heads per kv head (<= 8)
-constexpr int ATT_KS = HD + 8;  // padded K/V row in shared memory (elements): 8 rows hit distinct bank groups
-constexpr int ATT_SMEM = 2 * ATT_SPLIT * ATT_KS * 2 + ATT_MAXG * HD * 4 + ATT_MAXG * ATT_SPLIT * 4;
+constexpr int ATT_KS = HD + 8;  // padded q row (elements) of the mma A operand
+constexpr int ATT_ROWB = HD * 2;                       // K/V row in shared memory: 128 B, as a page stores it
+constexpr int ATT_KV = ATT_SPLIT * ATT_ROWB;           // one split's K (or V) rows
+constexpr int ATT_BODY = 2 * ATT_KV + ATT_MAXG * HD * 4 + ATT_MAXG * ATT_SPLIT * 4;
+constexpr int ATT_SMEM = 1024 + ATT_BODY + 16;         // 1024-byte alignment slack (128-byte swizzle) + mbarrier
 constexpr int ATT_SMEM_CL = ATT_SMEM + ATT_MAXG * PART_STRIDE * 4;
-static_assert(8 * ATT_MAXG * 32 * 8 <= ATT_SPLIT * ATT_KS * 2, "P.V partial sums fit in the key area");
-static_assert(8 * ATT_MAXG * PART_STRIDE * 4 <= ATT_SPLIT * ATT_KS * 2 && (ATT_MAXG * PART_STRIDE) % 4 == 0,
+constexpr long long ATT_TIMEOUT = 4000000000LL;        // cycles (~2 s) before a page-copy wait gives up
+static_assert(8 * ATT_MAXG * 32 * 8 <= ATT_KV, "P.V partial sums fit in the key area");
+static_assert(8 * ATT_MAXG * PART_STRIDE * 4 <= ATT_KV && (ATT_MAXG * PART_STRIDE) % 4 == 0,
               "eight ranks' partials fit in the key area as float4");
 
 MING_DEV uint32_t att_su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-MING_DEV void att_cp16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(att_su32(dst)), "l"(src) : "memory");
+// Element offset of (row, dim) in a 128-byte-swizzled K/V block: 16-byte
+// chunk c of row r sits at chunk c ^ (r % 8) (the TMA's SWIZZLE_128B on a
+// 1024-byte-aligned block).
+MING_DEV int att_sw(int r, int d) { return r * HD + ((((d >> 3) ^ (r & 7))) << 3) + (d & 7); }
+MING_DEV bool att_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(att_su32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+MING_DEV bool att_wait(uint64_t* bar, uint32_t parity) {
+    const long long t0 = clock64();
+    while (!att_try(bar, parity))
+        if (clock64() - t0 > ATT_TIMEOUT) return false;
+    return true;
+}
+// One 16-row page of K or V (2 KB) by TMA into a 1024-byte-aligned slot
+MING_DEV void att_page(void* dst, const CUtensorMap* m, int row0, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+            att_su32(dst)),
+        "l"(reinterpret_cast<uint64_t>(m)), "r"(0), "r"(row0), "r"(att_su32(bar))
+        : "memory");
 }
 }  // namespace
 
+bool make_kv_tensor_map(CUtensorMap* m, uint16_t* pool, long long rows) {
+    using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*, const cuuint64_t*,
+                                const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess || !fn ||
+        q != cudaDriverEntryPointSuccess)
+        return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)HD, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)HD * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)HD, (cuuint32_t)PAGE};
+    const cuuint32_t estr[2] = {1, 1};
+    return reinterpret_cast<Encode>(fn)(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, pool, dims, strides, box, estr,
+                                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // One (split, kv head, row): the row's causal positions [p0, p1) of one
-// 256-position split, every query head of the kv group. All K/V rows of the
-// split are prefetched with cp.async (one round trip), then scores on the
-// tensor cores (mma.sync, the group's heads as the 16-row A operand), a
-// per-head softmax inside the split in f32, and P.V on the tensor cores (a
-// warp per 8 dims, P as bf16 hi + lo parts).
+// 256-position split, every query head of the kv group. The split's K and V
+// pages (16 positions x 128 B each) come in by TMA, one tiled copy per page on
+// one mbarrier, landing 128-byte-swizzled so that the mma fragment reads and
+// the ldmatrix rows hit 32 distinct banks. Then scores on the tensor cores
+// (mma.sync, the group's heads as the 16-row A operand), a per-head softmax
+// inside the split in f32, and P.V on the tensor cores (a warp per 8 dims, P
+// as bf16 hi + lo parts).
 // CL = false: (max, sum, unnormalised P.V) per head go to `part`, combined by
 // attn_combine_kernel. CL = true: the splits of one (kv head, row) are one
 // thread-block cluster; each keeps its partials in shared memory, copies
 // every rank's partials over distributed shared memory after a cluster
 // barrier, and rank r combines heads r, r + ns, ... (the combine kernel's
 // formula and split order) into `att`.
+// A page copy that never lands (bounded wait) sets ATT_ERR_PAGES in a.err; the
+// CTA then skips its compute, still takes the cluster barriers, and waits
+// (bounded again) for its copies before it exits.
 template <bool CL>
-__global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    uint16_t* sK = reinterpret_cast<uint16_t*>(smem);              // [ATT_SPLIT][ATT_KS]
-    uint16_t* sV = sK + ATT_SPLIT * ATT_KS;                         // [ATT_SPLIT][ATT_KS]
-    float* sq = reinterpret_cast<float*>(sV + ATT_SPLIT * ATT_KS);  // [ATT_MAXG][HD]
-    float* sc = sq + ATT_MAXG * HD;                                 // [ATT_MAXG][ATT_SPLIT]
-    float* sO = sc + ATT_MAXG * ATT_SPLIT;                          // CL: [ATT_MAXG][PART_STRIDE]
+__global__ void __launch_bounds__(256, 2) attn_partial_kernel(const AttnArgs a, const __grid_constant__ CUtensorMap tmap) {
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    uint8_t* smem = smem_raw + ((1024u - (att_su32(smem_raw) & 1023u)) & 1023u);
+    uint16_t* sK = reinterpret_cast<uint16_t*>(smem);                          // [ATT_SPLIT][HD], swizzled
+    uint16_t* sV = reinterpret_cast<uint16_t*>(smem + ATT_KV);                 // [ATT_SPLIT][HD], swizzled
+    float* sq = reinterpret_cast<float*>(smem + 2 * ATT_KV);                   // [ATT_MAXG][HD]
+    float* sc = sq + ATT_MAXG * HD;                                            // [ATT_MAXG][ATT_SPLIT]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sc + ATT_MAXG * ATT_SPLIT);   // the pages' mbarrier
+    float* sO = reinterpret_cast<float*>(bar + 2);                             // CL: [ATT_MAXG][PART_STRIDE]
+    uint16_t* sQ = reinterpret_cast<uint16_t*>(sq);                            // q as bf16: [ATT_MAXG][ATT_KS]
     const int split = blockIdx.x, kh = blockIdx.y, row = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int grp = a.heads / a.kv_heads;
@@ -59,38 +113,58 @@ __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
     float* out = CL ? sO : a.part + ((size_t)row * a.nsplit_max + split) * a.heads * PART_STRIDE + (size_t)kh * grp * PART_STRIDE;
     if (!CL && !live) return;  // split unused for this row (never read by the combine)
     const int* bt = a.kv.bt + (size_t)seq * a.kv.bt_ld;
-    auto fetch = [&](int pa, int pb) {
-        for (int e = tid; e < (pb - pa) * 8; e += 256) {
-            const int p = pa + (e >> 3), j = p - p0, piece = e & 7;
-            const int page = bt[p / PAGE];
-            att_cp16(sK + j * ATT_KS + piece * 8, a.kv.pool + kv_index(a.kv, page, a.layer, 0, kh, p % PAGE) + piece * 8);
-            att_cp16(sV + j * ATT_KS + piece * 8, a.kv.pool + kv_index(a.kv, page, a.layer, 1, kh, p % PAGE) + piece * 8);
+    const int np = (len + PAGE - 1) / PAGE;  // pages of the split (p0 is page-aligned)
+    // page i of the split: its K (which = 0) or V (1) rows in the pool as rows of the tensor map
+    auto page_row = [&](int i, int which) {
+        return (((bt[p0 / PAGE + i] * a.kv.layers + a.layer) * 2 + which) * a.kv.kv_heads + kh) * PAGE;
+    };
+    auto fetch = [&](int ia, int ib) {
+        for (int i = ia; i < ib; i++) {
+            att_page(sK + i * PAGE * HD, &tmap, page_row(i, 0), bar);
+            att_page(sV + i * PAGE * HD, &tmap, page_row(i, 1), bar);
         }
     };
-    // Decode: positions before the row's own were cached by earlier steps and
-    // are fetched before the wait on the q|k|v kernel (launched with
-    // programmatic stream serialization); the rest after it.
-    const int pre = live ? (a.decode ? min(p1, pos) : p0) : p0;
-    if (live) fetch(p0, pre);
+    // Decode: pages wholly before the row's own position were cached by
+    // earlier steps and are fetched before the wait on the q|k|v kernel
+    // (launched with programmatic stream serialization); the rest after it.
+    const int pre = live && a.decode ? max(0, min(np, pos / PAGE - p0 / PAGE)) : 0;
+    if (live && tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(att_su32(bar)) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(att_su32(bar)),
+                     "r"(np * 2 * PAGE * HD * 2)
+                     : "memory");
+        fetch(0, pre);
+    }
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     if (tr) tr[1] = gtimer();
+    bool failed = false;
     if (live) {
-        fetch(pre, p1);
-        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        if (tid == 0) fetch(pre, np);
         // q of the group's heads as bf16 (the mma A operand; heads >= grp are
         // zero rows); the 1/8 scale is applied to the f32 sums
-        uint16_t* sQ = reinterpret_cast<uint16_t*>(sq);  // [ATT_MAXG][ATT_KS]
         for (int e = tid; e < ATT_MAXG * HD; e += 256) {
             const int i = e / HD, d = e % HD;
             sQ[i * ATT_KS + d] = i < grp ? a.q[(size_t)row * a.heads * HD + (kh * grp + i) * HD + d] : (uint16_t)0;
         }
-        asm volatile("cp.async.wait_all;\n" ::: "memory");
+        __syncthreads();  // the barrier's initialisation is visible to every thread
+        failed = __syncthreads_or(!att_wait(bar, 0));
+    }
+    if (failed) {
+        if (tid == 0) {
+            if (a.err) atomicCAS(a.err, 0, ATT_ERR_PAGES);
+            att_wait(bar, 0);  // the copies in flight land before the CTA's shared memory is released
+        }
+        // an empty partial (weight 0) in place of this split's
+        for (int e = tid; e < grp * PART_STRIDE; e += 256) out[e] = e % PART_STRIDE == 0 ? -INFINITY : 0.f;
+    } else if (live) {
         // V rows from len up to the next 16-position k-step are read by the
-        // last P.V k-step with P = 0: make them finite
+        // last P.V k-step with P = 0: make them finite (whole rows, so the
+        // swizzle does not matter)
         for (int e = tid; e < (((len + 15) & ~15) - len) * (HD / 2); e += 256) {
             const int j = len + e / (HD / 2), d2 = e % (HD / 2);
-            *reinterpret_cast<uint32_t*>(sV + j * ATT_KS + 2 * d2) = 0u;
+            *reinterpret_cast<uint32_t*>(sV + j * HD + 2 * d2) = 0u;
         }
         __syncthreads();
         if (tr) tr[2] = gtimer();
@@ -109,12 +183,12 @@ __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
             const int nte = (len + 7) >> 3;
             for (int nt = warp; nt < nte; nt += 8) {
                 float c[4] = {0.f, 0.f, 0.f, 0.f};
-                const uint16_t* kr = sK + (nt * 8 + g) * ATT_KS + 2 * t4;
+                const int R = nt * 8 + g;
 #pragma unroll
                 for (int ks = 0; ks < 4; ks++) {
                     const uint32_t af[4] = {qa[ks][0], 0u, qa[ks][1], 0u};
-                    mma_bf16(c, af, *reinterpret_cast<const uint32_t*>(kr + ks * 16),
-                             *reinterpret_cast<const uint32_t*>(kr + ks * 16 + 8));
+                    mma_bf16(c, af, *reinterpret_cast<const uint32_t*>(sK + att_sw(R, ks * 16 + 2 * t4)),
+                             *reinterpret_cast<const uint32_t*>(sK + att_sw(R, ks * 16 + 8 + 2 * t4)));
                 }
                 const int j = nt * 8 + 2 * t4;
                 if (g < grp) {
@@ -167,7 +241,7 @@ __global__ void __launch_bounds__(256, 2) attn_partial_kernel(AttnArgs a) {
                 const uint32_t ah[4] = {pack_bf16x2(ha, hb), 0u, pack_bf16x2(hc, hd), 0u};
                 const uint32_t al[4] = {pack_bf16x2(pa.x - ha, pa.y - hb), 0u, pack_bf16x2(pb.x - hc, pb.y - hd), 0u};
                 uint32_t b0, b1;
-                const uint16_t* vr = sV + (kt * 16 + (lane & 15)) * ATT_KS + n0;
+                const uint16_t* vr = sV + att_sw(kt * 16 + (lane & 15), n0);
                 asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0, %1}, [%2];\n"
                              : "=r"(b0), "=r"(b1)
                              : "r"(att_su32(vr)));
@@ -227,6 +301,7 @@ cudaError_t launch_attn(const AttnArgs& a, int rows, cudaStream_t s) {
         cudaFuncSetAttribute(attn_partial_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, ATT_SMEM_CL);
         attr_set[dev] = 1;
     }
+    if (!a.tmap) return cudaErrorInvalidValue;
     const bool cl = a.att && a.nsplit_max <= 8;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.nsplit_max, a.kv_heads, rows);
@@ -244,56 +319,43 @@ cudaError_t launch_attn(const AttnArgs& a, int rows, cudaStream_t s) {
     cfg.numAttrs = cl && a.nsplit_max > 1 ? 2 : 1;
     // a cluster launch can fail where a plain one would not (e.g. the cluster's
     // shared memory does not fit); the caller checks the result
-    if (cl) return cudaLaunchKernelEx(&cfg, attn_partial_kernel<true>, a);
-    return cudaLaunchKernelEx(&cfg, attn_partial_kernel<false>, a);
+    if (cl) return cudaLaunchKernelEx(&cfg, attn_partial_kernel<true>, a, *a.tmap);
+    return cudaLaunchKernelEx(&cfg, attn_partial_kernel<false>, a, *a.tmap);
 }
 
 bool attn_fused_combine(const AttnArgs& a) { return a.att && a.nsplit_max <= 8; }
 
 // Combines the splits of each (row, head) once into att [rows][heads * 64]
 // bf16, the o_proj input: o = rb(sum_s acc_s e^(m_s - M) * (1 / L)) with
-// L = sum_s l_s e^(m_s - M).
-__global__ void __launch_bounds__(256) attn_combine_kernel(const float* part, RowsDev rows, int nsplit_max, int heads,
-                                                           uint16_t* att) {
-    extern __shared__ float sw[];  // [heads][nsplit_max] e^(m_s - M), then [heads] 1/L
-    const int row = blockIdx.x, tid = threadIdx.x;
+// L = sum_s l_s e^(m_s - M). One CTA per (head, row), a thread per dim (each
+// computes M and L itself: the split loads are the same addresses for all).
+__global__ void __launch_bounds__(64) attn_combine_kernel(const float* part, RowsDev rows, int nsplit_max, int heads,
+                                                          uint16_t* att) {
+    const int h = blockIdx.x, row = blockIdx.y, d = threadIdx.x;
     asm volatile("griddepcontrol.wait;\n" ::: "memory");
     asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
     const int ns = (rows.pos[row] + 1 + ATT_SPLIT - 1) / ATT_SPLIT;
-    const float* pr = part + (size_t)row * nsplit_max * heads * PART_STRIDE;
-    float* il = sw + heads * nsplit_max;
-    // a warp per head, lanes over the splits (all (m, l) loads of a head at once)
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int h = warp; h < heads; h += 8) {
-        float M = -INFINITY;
-        for (int s = lane; s < ns; s += 32) M = fmaxf(M, pr[((size_t)s * heads + h) * PART_STRIDE]);
-        M = warp_max(M);
-        float L = 0.f;
-        for (int s = lane; s < ns; s += 32) {
-            const float* p = pr + ((size_t)s * heads + h) * PART_STRIDE;
-            const float w = expf(p[0] - M);
-            sw[h * nsplit_max + s] = w;
-            L += p[1] * w;
-        }
-        L = warp_sum(L);
-        if (lane == 0) il[h] = 1.0f / L;
-    }
-    __syncthreads();
-    for (int e = tid; e < heads * HD; e += 256) {
-        const int h = e / HD, d = e % HD;
-        float o = 0.f;
+    const float* pr = part + ((size_t)row * nsplit_max * heads + h) * PART_STRIDE;
+    const size_t ss = (size_t)heads * PART_STRIDE;  // split stride
+    float M = -INFINITY;
+    for (int s = 0; s < ns; s++) M = fmaxf(M, pr[s * ss]);
+    float L = 0.f, o = 0.f;
 #pragma unroll 4
-        for (int s = 0; s < ns; s++) o += pr[((size_t)s * heads + h) * PART_STRIDE + 2 + d] * sw[h * nsplit_max + s];
-        att[(size_t)row * heads * HD + e] = f2bf(rb(o * il[h]));
+    for (int s = 0; s < ns; s++) {
+        const float* p = pr + s * ss;
+        const float w = expf(p[0] - M);
+        L += p[1] * w;
+        o += p[2 + d] * w;
     }
+    att[(size_t)row * heads * HD + h * HD + d] = f2bf(rb(o * (1.0f / L)));
 }
 
 cudaError_t launch_attn_combine(const float* part, RowsDev rows, int nsplit_max, int heads, uint16_t* att, int nrows,
                                 cudaStream_t s) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(nrows);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = (size_t)(heads * nsplit_max + heads) * 4;
+    cfg.gridDim = dim3(heads, nrows);
+    cfg.blockDim = dim3(HD);
+    cfg.dynamicSmemBytes = 0;
     cfg.stream = s;
     cudaLaunchAttribute at[1];
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

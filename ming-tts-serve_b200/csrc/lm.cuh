@@ -14,6 +14,8 @@
 // then the final RMSNorm + stop head.
 #pragma once
 
+#include <cuda.h>
+
 #include "linear.cuh"
 
 namespace ming {
@@ -131,6 +133,8 @@ struct EpiSwiGLU {
     }
 };
 
+constexpr int ATT_ERR_PAGES = 8;  // device error code: a K/V page copy of attn_partial_kernel never landed
+
 struct AttnArgs {
     const uint16_t* q;  // [rows][heads*64]
     float* part;        // [rows][nsplit_max][heads][PART_STRIDE]
@@ -140,7 +144,16 @@ struct AttnArgs {
     int decode = 0;  // 1: every row appends only its own position (positions before it are already cached)
     uint16_t* att = nullptr;  // when set (and at most 8 splits): the splits combine in-kernel into att [rows][heads*64]
     long long* trace = nullptr;  // launch trace: [CTA][8] globaltimer stamps (entry, wait done, keys in, .., exit at 7) or null
+    // Tensor map over the page pool viewed as [pages x layers x 2 x kv_heads x
+    // 16 rows][64] bf16, 16-row boxes with 128-byte swizzle (host memory; the
+    // launcher passes a copy as a kernel parameter). Required.
+    const CUtensorMap* tmap = nullptr;
+    int* err = nullptr;  // device error word: set when a page copy never lands (bounded wait)
 };
+
+// The page pool's tensor map for attn_partial_kernel (lm.cu): false if the
+// driver entry point is unavailable or rejects the shape.
+bool make_kv_tensor_map(CUtensorMap* m, uint16_t* pool, long long rows);
 
 // Step state kept on the device so one captured graph replays every decode step.
 struct StepDev {

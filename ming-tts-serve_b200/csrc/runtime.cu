@@ -375,6 +375,8 @@ cudaError_t enqueue_layers(ming_ctx* c, int rows, bool decode) {
         run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln1_unit},
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, rows, c->stream);
         AttnArgs aa{c->q, c->part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, decode ? 1 : 0, c->att};
+        aa.tmap = &c->kv_tmap;
+        aa.err = c->dev_err;
         aa.trace = (long)aa.nsplit_max * aa.kv_heads * rows <= KT_CTAS ? ktrace_slot(c) : nullptr;
         cudaError_t e = launch_attn(aa, rows, c->stream);
         if (e == cudaSuccess && !attn_fused_combine(aa))
@@ -610,7 +612,9 @@ int check_dev_err(ming_ctx* c) {
         const int zero = 0;
         cudaMemcpy(c->dev_err, &zero, 4, cudaMemcpyHostToDevice);
         if (c->mega_reset) c->mega_reset();
-        return fail(MING_ERR_CUDA, std::string(e == BK_ERR_WEIGHTS ? "decode-batch linear: weight copy" : "persistent decode kernel") +
+        return fail(MING_ERR_CUDA, std::string(e == BK_ERR_WEIGHTS   ? "decode-batch linear: weight copy"
+                                               : e == ATT_ERR_PAGES ? "attention: K/V page copy"
+                                                                    : "persistent decode kernel") +
                                        ": a bounded device wait expired (code " + std::to_string(e) + ")");
     }
     return MING_OK;
@@ -946,6 +950,10 @@ int ming_cuda_finalize(ming_ctx* c) {
     c->out_cell = c->mem.alloc<uint16_t*>(1, &rc);
     c->stop_cell = c->mem.alloc<float*>(1, &rc);
     if (rc) return rc;
+    if ((long long)f.max_pages * f.layers * 2 * f.kv_heads * PAGE >= (1LL << 31))
+        return fail(MING_ERR_INVALID, "max_pages x layers x 2 x kv_heads x 16 must stay below 2^31 (the page copies' row coordinate)");
+    if (f.layers > 0 && !make_kv_tensor_map(&c->kv_tmap, c->pool, (long long)f.max_pages * f.layers * 2 * f.kv_heads * PAGE))
+        return fail(MING_ERR_CUDA, "the KV page pool's tensor map could not be encoded (cuTensorMapEncodeTiled)");
     c->bt_host.assign((size_t)f.max_seqs * c->bt_ld, -1);
     CK(cudaMemcpy(c->bt, c->bt_host.data(), c->bt_host.size() * 4, cudaMemcpyHostToDevice));
     for (int p = f.max_pages - 1; p >= 0; p--) c->free_pages.push_back(p);
@@ -1550,7 +1558,10 @@ extern "C" int ming_cuda_lm_decode_noalloc(ming_ctx* c, int B, const int* ids, c
         auto& L = c->layers[l];
         run_linear(c, L.qkv.w, ProRms{c->x, L.ln1, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln1_unit},
                    EpiQKV{L.qkv.w.bias, c->q, kv, rd, l, f.heads, f.kv_heads, c->log2_theta}, B, s);
-        CK(launch_attn(AttnArgs{c->q, part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, 1}, B, s));
+        AttnArgs aa{c->q, part, kv, rd, l, f.heads, f.kv_heads, c->nsplit, 1};
+        aa.tmap = &c->kv_tmap;
+        aa.err = c->dev_err;
+        CK(launch_attn(aa, B, s));
         run_linear(c, L.o.w, ProAttn{part, rd, c->nsplit, f.heads, 0, nullptr}, EpiResidual{c->x, c->x1, nullptr, f.hidden}, B,
                    s);
         run_linear(c, L.gu.w, ProRms{c->x1, L.ln2, f.hidden, f.hidden, f.rms_eps, 0, nullptr, L.ln2_unit}, EpiSwiGLU{c->h, f.ff}, B, s);

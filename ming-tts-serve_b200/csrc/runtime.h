@@ -126,6 +126,7 @@ struct ming_ctx {
     bool mega_on = false;
     ming::MegaDev mega{};
     int mega_smem = 0;
+    CUtensorMap kv_tmap;  // the page pool as attn_partial_kernel's TMA source (lm.cuh)
     int* dev_err = nullptr;
     int* err_host = nullptr;  // pinned: the device error flag read back with a call's outputs
     bool cells_null = false;  // out_cell / stop_cell known to hold null (decode); generate sets them

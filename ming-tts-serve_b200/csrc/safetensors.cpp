@@ -7,9 +7,9 @@
 // "__metadata__" entry maps strings to strings), then the tensor bytes.
 //
 // The reference loads every tensor and casts all but int32 ones to the model
-// dtype (bf16). Here only the tensors of the hot path are read — names under
-// model.model., stop_head, flowloss., linear_proj_audio, adaln_head and
-// aggregator. — and handed to ming_cuda_load_tensor: BF16 and U32 (MLX
+// dtype (bf16). Here only the tensors this library runs are read — names
+// under model.model., stop_head, flowloss., linear_proj_audio, adaln_head,
+// aggregator. and audio.decoder. — and handed to ming_cuda_load_tensor: BF16 and U32 (MLX
 // packed quantized weights) as stored, F32 and F16 rounded to bf16 (nearest
 // even), except rotary inv_freq buffers, which stay F32. Other dtypes and
 // names are skipped.
@@ -260,7 +260,8 @@ float f16_to_f32(uint16_t h) {
 }
 
 bool hot_path_name(const std::string& n) {
-    static const char* pre[] = {"model.model.", "stop_head.", "flowloss.", "linear_proj_audio.", "adaln_head.", "aggregator."};
+    static const char* pre[] = {"model.model.", "stop_head.", "flowloss.", "linear_proj_audio.", "adaln_head.", "aggregator.",
+                                "audio.decoder."};
     for (const char* p : pre)
         if (n.compare(0, std::strlen(p), p) == 0) return true;
     return false;

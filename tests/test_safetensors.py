@@ -31,12 +31,13 @@ def test_validate_counts_hot_path_tensors(tmp_path):
         "stop_head.weight": synth.normal_bf16(1, "sw", (2, 896)),
         "flowloss.cfm.model.rotary_embed.inv_freq": synth.inv_freq(),
         "model.model.embed_tokens.index": np.arange(4, dtype=np.int32),  # integer table: skipped
-        "audio.decoder.fc1.weight": synth.normal_bf16(1, "dec", (4, 4)),  # off the hot path: skipped
+        "audio.decoder.fc1.weight": synth.normal_bf16(1, "dec", (4, 4)),  # the VAE decoder: read
+        "model.lm_head.weight": synth.normal_bf16(1, "lm_head", (4, 4)),  # not used by this library: skipped
     }
     p = tmp_path / "model.safetensors"
     synth.save_safetensors(p, W, metadata={"format": "mlx"})
-    assert M.check_safetensors(str(p)) == 3
-    assert M.check_safetensors(str(tmp_path)) == 3  # a model directory, as Model.load takes
+    assert M.check_safetensors(str(p)) == 4
+    assert M.check_safetensors(str(tmp_path)) == 4  # a model directory, as Model.load takes
 
 
 @pytest.mark.parametrize("case", ["short", "hdr_len", "json", "offsets", "dtype", "shape", "trailing"])
