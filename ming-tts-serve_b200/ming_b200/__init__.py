@@ -14,7 +14,9 @@ import numpy as np
 from . import synth  # noqa: F401
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(os.path.dirname(HERE), "libming_cuda.so")
+# MING_CUDA_LIB selects another build of the library (e.g. one compiled with
+# different tuning constants) for side-by-side timing; default: the in-tree build
+LIB_PATH = os.environ.get("MING_CUDA_LIB") or os.path.join(os.path.dirname(HERE), "libming_cuda.so")
 
 MING_OK = 0
 DTYPE_BF16, DTYPE_F32, DTYPE_U32 = 0, 1, 2
