@@ -660,10 +660,8 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     constexpr int KS = HD;
     uint16_t* sK = reinterpret_cast<uint16_t*>(sm.sB);         // [128][64]
     uint16_t* sV = sK + MG_ATT_CH * KS;                          // [128][64]
-    float* sq = reinterpret_cast<float*>(sV + MG_ATT_CH * KS);  // [64]
-    float* skn = sq + HD;                                        // [64]
-    float* svn = skn + HD;                                       // [64]
-    float* sS = svn + HD;                                        // [128]
+    float* sq = reinterpret_cast<float*>(sV + MG_ATT_CH * KS);  // [64] q, pre-scaled by 1/8
+    float* sS = sq + HD;                                         // scores, warp partials, the combine
     const int* bt = sm.bt + b * MG_BT_INTS;
     if (tid == 0) ms->frag_dirty = 1;
     // 1. prefetch the pages holding cached positions [p0, pc): one 2 KB bulk
@@ -695,37 +693,50 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     const unsigned long long* qacc = acc_ptr(a, ms->epoch, l, MG_ACC_QKV) + (size_t)b * a.acc_w;
     if (!waited) hint_acc(cx, qacc + (size_t)(a.ph[0].tiles - 1) * 16 + 15, ms->tcount[0][a.ph[0].tiles - 1]);
     const float* bias = reinterpret_cast<const float*>(sm.lp + 4 * a.H);
+    const int kind = tid >> 5, dq = ((tid >> 3) & 3) * 8 + (tid & 7);  // this thread's q|k|v dims dq, dq + 32
+    uint16_t kv1 = 0, kv2 = 0;  // kind 1 / 2: the new key / value pair (dims d, d + 32) in bf16
     if (tid < 96) {
-        const int kind = tid >> 5, tl = (tid >> 3) & 3, r8 = tid & 7;
+        const int tl = (tid >> 3) & 3, r8 = tid & 7;
         const int t = kind == 0 ? h * 4 + tl : (kind == 1 ? a.heads * 4 + g * 4 + tl : a.heads * 4 + a.kvh * 4 + g * 4 + tl);
         const uint64_t vlo = ldr64(qacc + t * 16 + r8), vhi = ldr64(qacc + t * 16 + r8 + 8);
-        const int d = tl * 8 + r8, expect = ms->tcount[0][t];
+        const int expect = ms->tcount[0][t];
         float x1 = rb(acc_get(cx, qacc + t * 16 + r8, vlo, expect) + bias[t * 16 + r8]);
         float x2 = rb(acc_get(cx, qacc + t * 16 + r8 + 8, vhi, expect) + bias[t * 16 + r8 + 8]);
         if (kind < 2) {
-            const float cs = ms->rc[b][d], sn = ms->rs[b][d];
+            const float cs = ms->rc[b][dq], sn = ms->rs[b][dq];
             const float p_ = x1 * cs - x2 * sn, q_ = x1 * sn + x2 * cs;
             x1 = rb(p_);
             x2 = rb(q_);
         }
-        float* dst = kind == 0 ? sq : (kind == 1 ? skn : svn);
-        const float sc = kind == 0 ? 0.125f : 1.f;
-        dst[d] = sc * x1;
-        dst[d + 32] = sc * x2;
+        if (kind == 0) {
+            sq[dq] = 0.125f * x1;
+            sq[dq + 32] = 0.125f * x2;
+        } else {
+            kv1 = f2bf(x1);
+            kv2 = f2bf(x2);
+        }
     }
     if (!mbar_wait(&ms->att_bar, att_par)) atomicCAS(cx.fail, 0, 6);
+    // 3. in the chunk holding the new position, its key and value go into
+    //    their rows of sK / sV (after this thread saw the page copies land:
+    //    the rows are then read like every cached one), and the group's first
+    //    head appends them to the cache
+    if (kind >= 1 && kind <= 2 && p1 == pos + 1) {
+        uint16_t* row = (kind == 1 ? sK : sV) + (pos - p0) * KS;
+        row[dq] = kv1;
+        row[dq + 32] = kv2;
+        if (h % grp == 0) {
+            uint16_t* dst = a.kv.pool + kv_index(a.kv, bt[pos / PAGE], l, kind - 1, g, pos % PAGE);
+            dst[dq] = kv1;
+            dst[dq + 32] = kv2;
+        }
+    }
     cbar();
     if (tid == 0) {
         ms->att_uses++;
         if (!*(volatile int*)cx.fail) ms->att_inflight = 0;
     }
     if (sm.st && tid == 0) sm.st[36] = clock64();  // diagnostics: q, k, v and the chunk's K/V in shared memory
-    // 3. the group's first head, in the chunk holding the new position, appends it
-    if (p1 == pos + 1 && h % grp == 0 && tid < 2 * HD) {
-        const int which = tid / HD, d = tid % HD;
-        const int page = bt[pos / PAGE];
-        a.kv.pool[kv_index(a.kv, page, l, which, g, pos % PAGE) + d] = f2bf(which ? svn[d] : skn[d]);
-    }
     // 4. each warp takes 16 positions of the chunk, 16 w.. 16 w + 15, and runs
     //    scores, softmax and P.V on them with no CTA barrier between the
     //    steps: lane (j = lane & 15, half = lane >> 4) dots half of the head
@@ -734,31 +745,21 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     const int jw = warp * 16 + (lane & 15), half = lane >> 4;
     float sc = -INFINITY;
     if (jw < len) {
+        // rows are 128 B apart: lane (j, half) reads its 16-byte pieces in
+        // the order c = (q + j) & 3, so each read instruction spreads the
+        // warp over all eight bank groups
         float s0 = 0.f, s1 = 0.f;
         const float* qh = sq + 32 * half;
-        if (p0 + jw < pos) {
-            // rows are 128 B apart: lane (j, half) reads its 16-byte pieces in
-            // the order c = (q + j) & 3, so each read instruction spreads the
-            // warp over all eight bank groups
-            const uint4* src = reinterpret_cast<const uint4*>(sK + jw * KS + 32 * half);
+        const uint4* src = reinterpret_cast<const uint4*>(sK + jw * KS + 32 * half);
 #pragma unroll
-            for (int q0 = 0; q0 < 4; q0++) {
-                const int q = (q0 + jw) & 3;
-                const uint4 v = src[q];
-                const float4 qa = *reinterpret_cast<const float4*>(qh + 8 * q);
-                const float4 qb = *reinterpret_cast<const float4*>(qh + 8 * q + 4);
-                const float2 k0 = unpack_bf16x2(v.x), k1 = unpack_bf16x2(v.y), k2 = unpack_bf16x2(v.z), k3 = unpack_bf16x2(v.w);
-                s0 += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y;
-                s1 += qb.x * k2.x + qb.y * k2.y + qb.z * k3.x + qb.w * k3.y;
-            }
-        } else {
-            // the new key (already bf16-exact, as the cache holds it)
-            const float* kh = skn + 32 * half;
-#pragma unroll 8
-            for (int q = 0; q < 32; q += 4) {
-                s0 += qh[q] * kh[q] + qh[q + 1] * kh[q + 1];
-                s1 += qh[q + 2] * kh[q + 2] + qh[q + 3] * kh[q + 3];
-            }
+        for (int q0 = 0; q0 < 4; q0++) {
+            const int q = (q0 + jw) & 3;
+            const uint4 v = src[q];
+            const float4 qa = *reinterpret_cast<const float4*>(qh + 8 * q);
+            const float4 qb = *reinterpret_cast<const float4*>(qh + 8 * q + 4);
+            const float2 k0 = unpack_bf16x2(v.x), k1 = unpack_bf16x2(v.y), k2 = unpack_bf16x2(v.z), k3 = unpack_bf16x2(v.w);
+            s0 += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y;
+            s1 += qb.x * k2.x + qb.y * k2.y + qb.z * k3.x + qb.w * k3.y;
         }
         sc = s0 + s1;
     }
@@ -780,7 +781,6 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     if (lane < 16) ps[lane] = pj;
     __syncwarp();
     float2 ac = make_float2(0.f, 0.f);
-    const int rn = pos - p0 - warp * 16;  // the new position's row in this warp's 16, if any
 #pragma unroll 1
     for (int j4 = 0; j4 < nj; j4 += 4) {
         const float4 p4 = *reinterpret_cast<const float4*>(ps + j4);
@@ -789,8 +789,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         for (int i = 0; i < 4; i++) {
             const int j = j4 + i;
             if (j < nj) {  // rows past the chunk's length are never read
-                const float2 v = j != rn ? unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (warp * 16 + j) * KS + 2 * lane))
-                                         : make_float2(svn[2 * lane], svn[2 * lane + 1]);
+                const float2 v = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sV + (warp * 16 + j) * KS + 2 * lane));
                 ac.x += pv[i] * v.x;
                 ac.y += pv[i] * v.y;
             }
@@ -815,7 +814,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
 #pragma unroll
         for (int w = 0; w < MG_CWARPS; w++) M = fmaxf(M, wp[w * 68]);
         float L = 0.f, o = 0.f;
-#pragma unroll
+#pragma unroll 1
         for (int w = 0; w < MG_CWARPS; w++) {
             const float mw = wp[w * 68];
             const float e = mw == -INFINITY ? 0.f : expf(mw - M);
@@ -845,8 +844,9 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     //    smaller item index runs on some CTA, so the wait ends) and its own
     //    sums, then publishes the 64 values for every o_proj CTA that reads
     //    this head. Thread (d, quarter) sums the chunks s = quarter, quarter +
-    //    4, ... of dim d; the first 4 value loads of each thread and the
-    //    chunk maxima and sums are in flight together.
+    //    4, ... of dim d; the values are loaded once the chunk maxima and
+    //    sums have shown up (written in the same pass, so they are rarely
+    //    stale; loading them earlier found them stale and polled each one)
     const int no = ns - 1;
     const uint64_t* ob = a.attn + ((size_t)b * a.heads + h) * a.max_splits * MG_PART;
     float* cm = sS;       // [no] chunk maxima (scores are no longer read)
@@ -860,22 +860,25 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     }
     cbar();
     if (sm.st && tid == 0) sm.st[38] = clock64();  // diagnostics: the other chunks' maxima and sums in hand
-    float M = -INFINITY, L = 0.f;
-    for (int q = 0; q <= no; q++) {
-        const float mq = q < no ? cm[q] : ms->om, lq = q < no ? cl[q] : ms->ol;
-        const float nm = fmaxf(M, mq);
-        L = L * expf(M - nm) + lq * expf(mq - nm);
-        M = nm;
-    }
+    // the first pass's values are requested before the maxima and sums are
+    // combined (M first, then L = sum_s l_s e^(m_s - M) in chunk order)
+#pragma unroll
+    for (int k = 0; k < 4; k++) va[k] = qt + MG_NQ * k < no ? ldr64(ob + (size_t)(qt + MG_NQ * k) * MG_PART + 2 + d) : 0ull;
+    float M = ms->om;
+    for (int q = 0; q < no; q++) M = fmaxf(M, cm[q]);
+    float L = 0.f;
+    for (int q = 0; q < no; q++) L += cl[q] * expf(cm[q] - M);
+    L += ms->ol * expf(ms->om - M);
     const float il = 1.0f / L;
     float v = 0.f;
-    // the chunks' values are loaded once their maxima and sums have shown up
-    // (written in the same pass), so they are rarely stale: the four loads of
-    // a pass are in flight together and a stale word is polled on its own
+    // the four loads of a pass are in flight together; a stale word is
+    // polled on its own
 #pragma unroll 1
     for (int s0 = qt; s0 < no; s0 += 4 * MG_NQ) {
+        if (s0 != qt) {
 #pragma unroll
-        for (int k = 0; k < 4; k++) va[k] = s0 + MG_NQ * k < no ? ldr64(ob + (size_t)(s0 + MG_NQ * k) * MG_PART + 2 + d) : 0ull;
+            for (int k = 0; k < 4; k++) va[k] = s0 + MG_NQ * k < no ? ldr64(ob + (size_t)(s0 + MG_NQ * k) * MG_PART + 2 + d) : 0ull;
+        }
 #pragma unroll
         for (int k = 0; k < 4; k++) {
             const int sk = s0 + MG_NQ * k;
