@@ -312,8 +312,10 @@ struct Sm {  // shared-memory views used by the phases
     long long* st;      // optional stamp row of the current layer (diagnostics)
     int so;             // stamp slot of the current phase's sub-steps
 };
+// Trace stamps compile only into the tracing instantiation (TR): the kernel's
+// speed depends on its instruction footprint, so production code carries none.
 #define MG_SUB(k) \
-    if (sm.st && threadIdx.x == 0) sm.st[sm.so + (k)] = clock64();
+    if (TR && sm.st && threadIdx.x == 0) sm.st[sm.so + (k)] = clock64();
 
 // accumulator rows of (step parity, layer, kind); row b at + b * acc_w
 MING_DEV unsigned long long* acc_ptr(const MegaDev& a, uint32_t epoch, int l, int which) {
@@ -327,7 +329,7 @@ MING_DEV unsigned long long* acc_ptr(const MegaDev& a, uint32_t epoch, int l, in
 // threads, which also reduce the row's group sum (the quantized formats'
 // bias term) with shuffles. Sources: mode 0, sX times the norm weight nw and
 // the row pre-scale; mode 1, the bf16 values sT [stage][64][row].
-template <bool F16>
+template <bool F16, bool TR>
 MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint16_t* nw) {
     const int tid = threadIdx.x;
     // entries of rows >= B stay zero from one stage to the next; only the
@@ -386,56 +388,44 @@ MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint
 MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, const MegaDev& a, const unsigned long long* acc, const uint8_t* tcount,
                                const uint16_t* nw, bool f16) {
     const int H = a.H, B = a.B, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    float ss[MG_MAXB], am[MG_MAXB];
-#pragma unroll
-    for (int b = 0; b < MG_MAXB; b++) ss[b] = am[b] = 0.f;
-    // two features per thread per pass, in increasing (row, feature) order;
-    // kept rolled (this code runs once per layer: its size is its cost)
-    int b = 0, f = tid * 2;
-    while (f >= H) f -= H, b++;
+    // row by row, two features per thread per pass (f = 2 tid, + 2 x 256, ...);
+    // each pass's accumulator pair is requested one pass ahead, so the passes'
+    // L2 round trips overlap. Kept rolled: this code runs once per layer and
+    // the kernel's speed follows its instruction footprint.
 #pragma unroll 1
-    for (int idx = tid * 2; idx < B * H; idx += 2 * MG_CT) {
-        float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(sm.sX + idx));
-        if (acc) {
-            const unsigned long long* pw = acc + (size_t)b * a.acc_w + f;
-            const uint4 v = ldcg16(pw);
-            const int expect = tcount[f >> 4];  // f, f + 1: same tile
-            const float d0 = acc_get(cx, pw, ((unsigned long long)v.y << 32) | v.x, expect);
-            const float d1 = acc_get(cx, pw + 1, ((unsigned long long)v.w << 32) | v.z, expect);
-            x.x = rb(x.x + rb(d0));
-            x.y = rb(x.y + rb(d1));
-            *reinterpret_cast<uint32_t*>(sm.sX + idx) = pack_bf16x2(x.x, x.y);
+    for (int b = 0; b < B; b++) {
+        const unsigned long long* ar = acc ? acc + (size_t)b * a.acc_w : nullptr;
+        uint16_t* xr = sm.sX + b * H;
+        float ss = 0.f, am = 0.f;
+        uint4 v = ar && tid * 2 < H ? ldcg16(ar + tid * 2) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll 1
+        for (int f = tid * 2; f < H; f += 2 * MG_CT) {
+            const uint4 cur = v;
+            if (ar && f + 2 * MG_CT < H) v = ldcg16(ar + f + 2 * MG_CT);
+            float2 x = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(xr + f));
+            if (ar) {
+                const int expect = tcount[f >> 4];  // f, f + 1: same tile
+                const float d0 = acc_get(cx, ar + f, ((unsigned long long)cur.y << 32) | cur.x, expect);
+                const float d1 = acc_get(cx, ar + f + 1, ((unsigned long long)cur.w << 32) | cur.z, expect);
+                x.x = rb(x.x + rb(d0));
+                x.y = rb(x.y + rb(d1));
+                *reinterpret_cast<uint32_t*>(xr + f) = pack_bf16x2(x.x, x.y);
+            }
+            const float2 w = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(nw + f));
+            ss += x.x * x.x + x.y * x.y;
+            am = fmaxf(am, fmaxf(fabsf(x.x * w.x), fabsf(x.y * w.y)));
         }
-        const float2 w = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(nw + f));
-        const float dss = x.x * x.x + x.y * x.y, dam = fmaxf(fabsf(x.x * w.x), fabsf(x.y * w.y));
-#pragma unroll
-        for (int bb = 0; bb < MG_MAXB; bb++)
-            if (bb == b) {
-                ss[bb] += dss;
-                am[bb] = fmaxf(am[bb], dam);
-            }
-        f += 2 * MG_CT;
-        while (f >= H) f -= H, b++;
-    }
-#pragma unroll 1
-    for (int bb = 0; bb < B; bb++) {
-        // the row's values out of the register arrays without dynamic indexing
-        float s0 = 0.f, a0 = 0.f;
-#pragma unroll
-        for (int k = 0; k < MG_MAXB; k++)
-            if (k == bb) {
-                s0 = ss[k];
-                a0 = am[k];
-            }
-        const float s1 = warp_sum(s0), a1 = warp_max(a0);
+        ss = warp_sum(ss);
+        am = warp_max(am);
         if (lane == 0) {
-            sm.ms->red[(warp * MG_MAXB + bb) * 2] = s1;
-            sm.ms->red[(warp * MG_MAXB + bb) * 2 + 1] = a1;
+            sm.ms->red[(warp * MG_MAXB + b) * 2] = ss;
+            sm.ms->red[(warp * MG_MAXB + b) * 2 + 1] = am;
         }
     }
     cbar();
     if (tid < B) {
         float s1 = 0.f, a1 = 0.f;
+#pragma unroll 1
         for (int w = 0; w < MG_CWARPS; w++) {
             s1 += sm.ms->red[(w * MG_MAXB + tid) * 2];
             a1 = fmaxf(a1, sm.ms->red[(w * MG_MAXB + tid) * 2 + 1]);
@@ -456,7 +446,7 @@ enum { OUT_ACC = 0, OUT_GLU = 1 };
 // at most two tiles), meet in shared memory, and the CTA emits per (tile,
 // row, batch row) either a fixed-point contribution to acc (row index
 // tile*16 + r) or, for whole gate|up tiles, the SwiGLU outputs into hb.
-template <int FMT>
+template <int FMT, bool TR>
 MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t par0, uint8_t* ring, uint64_t* full,
                          uint64_t* empty, int stage_base, bool use_post, int out, unsigned long long* acc, uint64_t* hb,
                          uint32_t tag) {
@@ -515,7 +505,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
         }
         const int w0 = max(i0, jj * a.gps), w1 = min(i1, (jj + 1) * a.gps);
         if ((!skip || w0 < w1) && !mbar_wait(&full[sl], par)) atomicCAS(cx.fail, 0, 2);
-        if (sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p == 2 && w0 == i0 && w0 < w1) sm.st[56 + warp] = clock64();
+        if (TR && sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p == 2 && w0 == i0 && w0 < w1) sm.st[56 + warp] = clock64();
         if (w0 < w1 && !*(volatile int*)cx.fail) {
             const uint8_t* sbase = ring + (size_t)sl * a.slot_bytes;
 #pragma unroll 1
@@ -565,7 +555,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[sl]);  // before any global write of this phase
-        if (sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p >= 2 && w1 == i1 && w0 < w1) sm.st[40 + (p - 2) * 8 + warp] = clock64();
+        if (TR && sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p >= 2 && w1 == i1 && w0 < w1) sm.st[40 + (p - 2) * 8 + warp] = clock64();
     }
     MG_SUB(2)
     const int B = a.B;
@@ -590,6 +580,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
                 }
             }
         }
+        if (TR && sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0) sm.st[64 + (p < 3 ? p : 2) * 8 + warp] = clock64();
         MG_SUB(4)
         return;
     }
@@ -648,6 +639,7 @@ MING_DEV float sum_groups(const float* red, int d) {
 // RoPE on q and k as MLX fast_rope); the chunk's cached K/V rows are
 // prefetched with cp.async before the wait for q|k|v. The first head of the
 // group appends the new position to the cache (in the chunk holding it).
+template <bool TR>
 MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, int b, int h, int s, bool waited) {
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
@@ -678,10 +670,15 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         if (npg > 0) {
             mbar_expect_tx(&ms->att_bar, (uint32_t)npg * 2u * PG);
+            // the (layer, K, kv head) block of page 0, and the page stride
+            const uint16_t* k0 = a.kv.pool + kv_index(a.kv, 0, l, 0, g, 0);
+            const size_t pstride = (size_t)a.kv.layers * 2 * a.kv.kv_heads * (PAGE * HD);
+            const int vofs = a.kv.kv_heads * (PAGE * HD);
+#pragma unroll 1
             for (int i = 0; i < npg; i++) {
-                const int page = bt[(p0 >> 4) + i];
-                bulk_g2s(sK + i * PAGE * HD, a.kv.pool + kv_index(a.kv, page, l, 0, g, 0), PG, &ms->att_bar);
-                bulk_g2s(sV + i * PAGE * HD, a.kv.pool + kv_index(a.kv, page, l, 1, g, 0), PG, &ms->att_bar);
+                const uint16_t* kp = k0 + (size_t)bt[(p0 >> 4) + i] * pstride;
+                bulk_g2s(sK + i * PAGE * HD, kp, PG, &ms->att_bar);
+                bulk_g2s(sV + i * PAGE * HD, kp + vofs, PG, &ms->att_bar);
             }
         } else {
             mbar_arrive(&ms->att_bar);  // nothing cached in this chunk: complete the phase
@@ -736,7 +733,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         ms->att_uses++;
         if (!*(volatile int*)cx.fail) ms->att_inflight = 0;
     }
-    if (sm.st && tid == 0) sm.st[36] = clock64();  // diagnostics: q, k, v and the chunk's K/V in shared memory
+    if (TR && sm.st && tid == 0) sm.st[36] = clock64();  // diagnostics: q, k, v and the chunk's K/V in shared memory
     // 4. each warp takes 16 positions of the chunk, 16 w.. 16 w + 15, and runs
     //    scores, softmax and P.V on them with no CTA barrier between the
     //    steps: lane (j = lane & 15, half = lane >> 4) dots half of the head
@@ -767,7 +764,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     float m = sc;
 #pragma unroll
     for (int o = 8; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (sm.st && tid == 0) sm.st[15] = clock64();  // diagnostics: warp 0's scores and maximum
+    if (TR && sm.st && tid == 0) sm.st[15] = clock64();  // diagnostics: warp 0's scores and maximum
     const float pj = jw < len ? expf(sc - m) : 0.f;  // m is finite wherever some position is valid
     float lsum = pj;
 #pragma unroll
@@ -796,7 +793,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         }
     }
     __syncwarp();  // every lane read the probabilities before the partials overwrite them
-    if (sm.st && tid == 0) sm.st[16] = clock64();  // diagnostics: warp 0's P.V done
+    if (TR && sm.st && tid == 0) sm.st[16] = clock64();  // diagnostics: warp 0's P.V done
     // the warps' (max, sum, P.V) partials meet in shared memory (the score
     // area); 64 threads, one per dim, merge them into the chunk's partial
     float* wp = sS;  // [MG_CWARPS][68] (the probabilities above lived in floats 4..19 of each warp's row)
@@ -807,7 +804,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     wp[warp * 68 + 2 + 2 * lane] = ac.x;
     wp[warp * 68 + 3 + 2 * lane] = ac.y;
     cbar();
-    if (sm.st && tid == 0) sm.st[37] = clock64();  // diagnostics: every warp's partial in shared memory
+    if (TR && sm.st && tid == 0) sm.st[37] = clock64();  // diagnostics: every warp's partial in shared memory
     float* own = sq;  // [64] this chunk's P.V sums when it combines (q is no longer read)
     if (tid < HD) {
         float M = -INFINITY;
@@ -859,7 +856,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         (tid & 1 ? cl : cm)[tid >> 1] = (uint32_t)(v >> 32) == tag ? __uint_as_float((uint32_t)v) : poll(cx, w, tag);
     }
     cbar();
-    if (sm.st && tid == 0) sm.st[38] = clock64();  // diagnostics: the other chunks' maxima and sums in hand
+    if (TR && sm.st && tid == 0) sm.st[38] = clock64();  // diagnostics: the other chunks' maxima and sums in hand
     // the first pass's values are requested before the maxima and sums are
     // combined (M first, then L = sum_s l_s e^(m_s - M) in chunk order)
 #pragma unroll
@@ -895,7 +892,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         const float o = sum_groups(red, tid) + own[tid] * (expf(ms->om - M) * il);
         str64(a.comb + ((size_t)b * a.heads + h) * HD + tid, tagged(tag, rb(o)));
     }
-    if (sm.st && tid == 0 && l > 0) sm.st[39] = clock64();  // diagnostics: head published (slot 39 of layer 0 is the origin)
+    if (TR && sm.st && tid == 0 && l > 0) sm.st[39] = clock64();  // diagnostics: head published (slot 39 of layer 0 is the origin)
 }
 
 // o_proj input: the combined attention output of the heads this CTA's
@@ -915,7 +912,7 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
     cbar();
 }
 
-template <int FMT>
+template <int FMT, bool TR>
 __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_constant__ MegaDev a) {
     extern __shared__ __align__(128) uint8_t smem[];
     const SmemMap mp = smem_map(a.nslots, a.slot_bytes, a.H, a.lp_bytes);
@@ -1074,8 +1071,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
     }
     for (int idx = tid; idx < B * H; idx += MG_CT) sm.sX[idx] = a.x_in[idx];
     cbar();
-    long long* tr = a.trace ? a.trace + (size_t)c * a.layers * MG_TRACE : nullptr;
-    if (tr && tid == 0) {
+    long long* tr = TR && a.trace ? a.trace + (size_t)c * a.layers * MG_TRACE : nullptr;
+    if (TR && tr && tid == 0) {
         // diagnostics only: a common time origin for every CTA's clock64
         // stamps. Each CTA arrives on a counter after the trace rows; the
         // clock64 at which a CTA sees all C arrivals (within an L2 round trip
@@ -1090,7 +1087,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
         tr[39] = clock64();
     }
 #define MG_STAMP(k) \
-    if (tr && tid == 0) tr[l * MG_TRACE + (k)] = clock64();
+    if (TR && tr && tid == 0) tr[l * MG_TRACE + (k)] = clock64();
 #pragma unroll 1
     for (int l = 0; l < a.layers && !dead; l++) {
         const uint32_t tag = epoch * 32u + (uint32_t)l;
@@ -1130,7 +1127,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
                         b++;
                     }
                     const int sch = divB(rem, ms->hm);  // rem / heads (rem < 2^16: exact)
-                    attention_item(cx, sm, l, tag, b, rem - sch * a.heads, sch, waited);
+                    attention_item<TR>(cx, sm, l, tag, b, rem - sch * a.heads, sch, waited);
                     waited = true;
                     check();
                 }
@@ -1172,9 +1169,9 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             if (check()) break;
             MG_STAMP(1 + 2 * q)
             sm.so = 10 + 7 * q;
-            stage<F16>(sm, nst, B, H, rows ? 0 : 1, q == 0 ? ln1 : ln2);
+            stage<F16, TR>(sm, nst, B, H, rows ? 0 : 1, q == 0 ? ln1 : ln2);
             const int which = q == 0 ? MG_ACC_QKV : (q == 1 ? MG_ACC_X1 : MG_ACC_X2);
-            gemv_phase<FMT>(cx, sm, q, cslot, cpar, ring, full, empty, base, rows, q == 2 ? OUT_GLU : OUT_ACC,
+            gemv_phase<FMT, TR>(cx, sm, q, cslot, cpar, ring, full, empty, base, rows, q == 2 ? OUT_GLU : OUT_ACC,
                             q == 2 ? nullptr : acc_ptr(a, epoch, l, which), hb, tag);
             cons += ms->nsc[q];
             cslot += ms->nsc[q];
@@ -1272,16 +1269,14 @@ cudaError_t launch_mega(const MegaDev& a, int smem, cudaStream_t s) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     cudaError_t e;
-    if (a.fmt == 4) {
-        e = cudaFuncSetAttribute(mega_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, mega_kernel<4>, a);
-    } else if (a.fmt == 8) {
-        e = cudaFuncSetAttribute(mega_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, mega_kernel<8>, a);
-    } else {
-        e = cudaFuncSetAttribute(mega_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e == cudaSuccess) e = cudaLaunchKernelEx(&cfg, mega_kernel<16>, a);
-    }
+    auto go = [&](auto kern) {
+        cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        return r == cudaSuccess ? cudaLaunchKernelEx(&cfg, kern, a) : r;
+    };
+    const bool tr = a.trace != nullptr;
+    if (a.fmt == 4) e = tr ? go(mega_kernel<4, true>) : go(mega_kernel<4, false>);
+    else if (a.fmt == 8) e = tr ? go(mega_kernel<8, true>) : go(mega_kernel<8, false>);
+    else e = tr ? go(mega_kernel<16, true>) : go(mega_kernel<16, false>);
     return e;
 }
 

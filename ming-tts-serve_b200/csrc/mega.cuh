@@ -53,9 +53,11 @@ constexpr int MG_NPH = 4;                         // GEMV phases: P0 qkv, P2 o, 
 constexpr int MG_FIX = 32;                        // fraction bits of the fixed-point accumulators
 constexpr int MG_MAX_STAGE = 32;                  // most 64-groups of activations one CTA stages per phase
 // clock64 stamp slots per (CTA, layer) when tracing: 0-9 phase boundaries,
-// 10-35 sub-steps of the four GEMV phases, 40-55 the end of each of the first
-// 8 warps' runs in gate|up and down, 56-63 their first gate|up slot in hand
-constexpr int MG_TRACE = 64;
+// 10-35 sub-steps of the four GEMV phases, 36-39 attention, 40-55 the end of
+// each of the first 8 warps' runs in gate|up and down, 56-63 their first
+// gate|up slot in hand, 64-87 the end of their split-K reductions in q|k|v,
+// o_proj and down
+constexpr int MG_TRACE = 96;
 enum { MG_ACC_QKV = 0, MG_ACC_X1 = 1, MG_ACC_X2 = 2, MG_NACC = 3 };
 constexpr int MG_MAX_TILES = 128;                 // most tiles of a split-K phase (q|k|v, o_proj, down)
 

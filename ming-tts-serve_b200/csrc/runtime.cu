@@ -1439,7 +1439,7 @@ int ming_cuda_unpack_linear(ming_ctx* c, const char* name, float* out) {
 }
 
 // Diagnostics: copies the persistent kernel's phase trace (MING_MEGA_TRACE=1):
-// [C][layers][MG_TRACE = 64] clock64 stamps of the last step (slot meanings
+// [C][layers][MG_TRACE = 96] clock64 stamps of the last step (slot meanings
 // beside MG_TRACE). Returns the CTA
 // count in *n. Without it, the per-kernel step's launch trace (MING_KTRACE=1):
 // [160 slots][1024 CTAs][8] globaltimer stamps, *n = -(slots used).
