@@ -137,6 +137,12 @@ __device__ __noinline__ float poll_word(const uint64_t* p, uint32_t tag, int* fa
     }
 }
 MING_DEV float poll(const Ctx& x, const uint64_t* p, uint32_t tag) { return poll_word(p, tag, x.fail, x.a->err); }
+// Four consecutive tagged words whose bf16 payloads go to dst[0], dst[B],
+// dst[2B], dst[3B], each polled until it carries `tag` (the rare path of the
+// SwiGLU-output gather, out of line).
+__device__ __noinline__ void poll4_bf16(const uint64_t* src, uint16_t* dst, int B, uint32_t tag, int* fail, const int* err) {
+    for (int u = 0; u < 4; u++) dst[u * B] = (uint16_t)__float_as_uint(poll_word(src + u, tag, fail, err));
+}
 
 // Re-reads a counted accumulator word until `expect` CTAs have contributed
 // (bounded); returns the word (complete, or whatever it holds on failure).
@@ -216,19 +222,28 @@ MING_DEV void mma_k(float (&t)[4], const uint32_t (&a)[4], uint2 b) {
     if constexpr (FMT == 16) mma_bf16(t, a, b.x, b.y);
     else mma_f16(t, a, b.x, b.y);
 }
-// acc += W_group . y_group (t: the group's own sums; the quantized scale and
-// bias apply per group: s * sum(q y) + b * sum(y)).
+// acc[tu] += W_group . y_group (t: the group's own sums; the quantized scale
+// and bias apply per group: s * sum(q y) + b * sum(y)). Branch-free: the
+// contribution is added to both accumulators with weights 1 and 0 (exact),
+// so one copy of the code serves either tile.
 template <int FMT>
-MING_DEV void group_finish(const GroupW& g, const float (&t)[4], const float* ys, int lane, float (&acc)[4]) {
+MING_DEV void group_finish(const GroupW& g, const float (&t)[4], const float* ys, int lane, int tu, float (&acc)[2][4]) {
+    float c[4];
     if constexpr (FMT == 16) {
-        acc[0] += t[0]; acc[1] += t[1]; acc[2] += t[2]; acc[3] += t[3];
+        c[0] = t[0]; c[1] = t[1]; c[2] = t[2]; c[3] = t[3];
     } else {
-        const int c = 2 * (lane & 3);
-        const float y0 = ys[c], y1 = ys[c + 1];
-        acc[0] += g.s_lo * t[0] + g.b_lo * y0;
-        acc[1] += g.s_lo * t[1] + g.b_lo * y1;
-        acc[2] += g.s_hi * t[2] + g.b_hi * y0;
-        acc[3] += g.s_hi * t[3] + g.b_hi * y1;
+        const int cc = 2 * (lane & 3);
+        const float y0 = ys[cc], y1 = ys[cc + 1];
+        c[0] = g.s_lo * t[0] + g.b_lo * y0;
+        c[1] = g.s_lo * t[1] + g.b_lo * y1;
+        c[2] = g.s_hi * t[2] + g.b_hi * y0;
+        c[3] = g.s_hi * t[3] + g.b_hi * y1;
+    }
+    const float m1 = tu ? 1.f : 0.f, m0 = 1.f - m1;
+#pragma unroll
+    for (int k = 0; k < 4; k++) {
+        acc[0][k] = fmaf(c[k], m0, acc[0][k]);
+        acc[1][k] = fmaf(c[k], m1, acc[1][k]);
     }
 }
 
@@ -284,7 +299,7 @@ struct Misc {              // small per-CTA state in shared memory
     // issue rate): groups [i0, i1) of the CTA's range, its first group's tile,
     // group in the tile and group in its ring slot, and its first and last slot
     struct WRun {
-        short i0, i1, t, kg, wi, js, je;
+        short i0, i1, t, kg, wi, js, je, tl;  // tl: the run's last tile
     } wrun[MG_NPH][MG_CWARPS];
     float rc[MG_MAXB][HD / 2];           // RoPE cos/sin of each row's position, per frequency
     float rs[MG_MAXB][HD / 2];
@@ -296,6 +311,7 @@ struct Misc {              // small per-CTA state in shared memory
     uint32_t epoch;
     int step;
     unsigned long long bm;  // divB multiplier of the step's row count
+    long long pg_el;        // elements between consecutive pages of the KV pool
     uint8_t tcount[3][MG_MAX_TILES];  // contributors per tile of the split-K phases q 0, 1, 3
 };
 static_assert(sizeof(Misc) <= 4096, "Misc must fit its shared-memory slot");
@@ -430,11 +446,15 @@ MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, const MegaDev& a, cons
             s1 += sm.ms->red[(w * MG_MAXB + tid) * 2];
             a1 = fmaxf(a1, sm.ms->red[(w * MG_MAXB + tid) * 2 + 1]);
         }
+        // e = the frexp exponent of amax / 4096 when above 1 (a normal float:
+        // its biased exponent - 126), else 0; 2^-e and 2^e built from their
+        // exponent bits (e stays far inside the normal range)
         int e = 0;
-        if (f16 && a1 > 4096.f) frexpf(a1 / 4096.f, &e);
-        sm.ms->inv[tid] = rsqrtf(s1 / (float)H + a.eps);
-        sm.ms->scl[tid] = ldexpf(1.f, -e);
-        sm.ms->post[tid] = sm.ms->inv[tid] * ldexpf(1.f, e);
+        if (f16 && a1 > 4096.f) e = ((__float_as_int(a1 * (1.0f / 4096.f)) >> 23) & 0xff) - 126;
+        const float inv = rsqrtf(s1 / (float)H + a.eps);
+        sm.ms->inv[tid] = inv;
+        sm.ms->scl[tid] = __int_as_float((127 - e) << 23);
+        sm.ms->post[tid] = inv * __int_as_float((127 + e) << 23);
     }
     cbar();
 }
@@ -457,6 +477,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
     if (n <= 0) return;  // CTA-uniform
     const int nsc = ms->nsc[p];
     MG_SUB(1)
+    if (TR && sm.st && p == 0 && (warp == 1 || warp == 3) && lane == 0) sm.st[88 + (warp >> 1) * 4] = clock64();
     const Misc::WRun wr = ms->wrun[p][warp];
     const int i0 = wr.i0, i1 = wr.i1;
     const int tb = ms->wtile[p][warp];
@@ -505,6 +526,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
         }
         const int w0 = max(i0, jj * a.gps), w1 = min(i1, (jj + 1) * a.gps);
         if ((!skip || w0 < w1) && !mbar_wait(&full[sl], par)) atomicCAS(cx.fail, 0, 2);
+        if (TR && sm.st && p == 0 && (warp == 1 || warp == 3) && lane == 0 && w0 == i0 && w0 < w1) sm.st[89 + (warp >> 1) * 4] = clock64();
         if (TR && sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p == 2 && w0 == i0 && w0 < w1) sm.st[56 + warp] = clock64();
         if (w0 < w1 && !*(volatile int*)cx.fail) {
             const uint8_t* sbase = ring + (size_t)sl * a.slot_bytes;
@@ -545,16 +567,14 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
                     mma_k<FMT>(t0, a0, b0);
                     mma_k<FMT>(t1, a1, b1);
                 }
-                if (tu[0] == 0) group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc2[0]);
-                else group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, acc2[1]);
-                if (two) {
-                    if (tu[1] == 0) group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc2[0]);
-                    else group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, acc2[1]);
-                }
+                group_finish<FMT>(gw[0], t0, sm.sYs + si[0] * 8, lane, tu[0], acc2);
+                if (two) group_finish<FMT>(gw[1], t1, sm.sYs + si[1] * 8, lane, tu[1], acc2);
             }
         }
         __syncwarp();
+        if (TR && sm.st && p == 0 && (warp == 1 || warp == 3) && lane == 0 && w1 == i1 && w0 < w1) sm.st[90 + (warp >> 1) * 4] = clock64();
         if (lane == 0) mbar_arrive(&empty[sl]);  // before any global write of this phase
+        if (TR && sm.st && p == 0 && (warp == 1 || warp == 3) && lane == 0 && w1 == i1 && w0 < w1) sm.st[91 + (warp >> 1) * 4] = clock64();
         if (TR && sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p >= 2 && w1 == i1 && w0 < w1) sm.st[40 + (p - 2) * 8 + warp] = clock64();
     }
     MG_SUB(2)
@@ -564,7 +584,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
         // two) tiles its run touched; the tiles' contributor counts count
         // warps (planned on the host), so no CTA-wide reduction is needed
         if (i0 < i1) {
-            const int gr = lane >> 2, cc = 2 * (lane & 3), tl = (g0 + i1 - 1) / gpt;
+            const int gr = lane >> 2, cc = 2 * (lane & 3), tl = wr.tl;
 #pragma unroll
             for (int u = 0; u < 2; u++) {
                 const int t = tb + u;
@@ -670,15 +690,18 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
         if (npg > 0) {
             mbar_expect_tx(&ms->att_bar, (uint32_t)npg * 2u * PG);
-            // the (layer, K, kv head) block of page 0, and the page stride
-            const uint16_t* k0 = a.kv.pool + kv_index(a.kv, 0, l, 0, g, 0);
-            const size_t pstride = (size_t)a.kv.layers * 2 * a.kv.kv_heads * (PAGE * HD);
-            const int vofs = a.kv.kv_heads * (PAGE * HD);
+            // the (layer, K, kv head) block of page 0; pages ms->pg_el
+            // elements apart, V kv_heads x 1024 elements after K
+            const uint16_t* k0 = a.kv.pool + ((l * 2) * a.kvh + g) * (PAGE * HD);
+            const uint32_t bar = su32(&ms->att_bar), d0 = su32(sK);
 #pragma unroll 1
             for (int i = 0; i < npg; i++) {
-                const uint16_t* kp = k0 + (size_t)bt[(p0 >> 4) + i] * pstride;
-                bulk_g2s(sK + i * PAGE * HD, kp, PG, &ms->att_bar);
-                bulk_g2s(sV + i * PAGE * HD, kp + vofs, PG, &ms->att_bar);
+                const uint16_t* kp = k0 + (size_t)bt[(p0 >> 4) + i] * ms->pg_el;
+                asm volatile(
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+                    "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%4], [%5], %2, [%3];\n" ::"r"(d0 + i * PG),
+                    "l"(kp), "r"(PG), "r"(bar), "r"(d0 + MG_ATT_CH * HD * 2 + i * PG), "l"(kp + a.kvh * (PAGE * HD))
+                    : "memory");
             }
         } else {
             mbar_arrive(&ms->att_bar);  // nothing cached in this chunk: complete the phase
@@ -994,6 +1017,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
             r.wi = (short)(i0 % a.gps);
             r.js = (short)(i0 / a.gps);
             r.je = (short)((i1 - 1) / a.gps);
+            r.tl = (short)((ms->g0[p] + i1 - 1) / gpt);
         }
         ms->wrun[p][w] = r;
         if (w == 0) {
@@ -1004,6 +1028,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
     if (tid < 64) ms->hgrp[tid] = (uint8_t)(tid < a.heads ? tid / (a.heads / a.kvh) : 0);
     if (tid < B) ms->nitems[tid] = a.heads * ((ms->pos[tid] + MG_ATT_CH) / MG_ATT_CH);
     if (tid == 0) {
+        ms->pg_el = (long long)a.layers * 2 * a.kvh * (PAGE * HD);
         ms->grp = a.heads / a.kvh;
         ms->hm = ((1ull << 32) + (unsigned long long)a.heads - 1ull) / (unsigned long long)a.heads;
     }
@@ -1154,14 +1179,16 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
                     const int qq = divB(e, ms->bm), b = e - qq * B, si = qq >> 4, k4 = qq & 15;
                     const int kg = si + base < gpt ? si + base : si + base - gpt;
                     const uint64_t* src = hb + (size_t)b * a.FF + kg * 64 + k4 * 4;
+                    uint16_t* dst = sm.sT + (si * 64 + k4 * 4) * B + b;
                     const uint4 v0 = ldcg16(src), v1 = ldcg16(src + 2);
-                    const uint64_t w[4] = {((uint64_t)v0.y << 32) | v0.x, ((uint64_t)v0.w << 32) | v0.z,
-                                           ((uint64_t)v1.y << 32) | v1.x, ((uint64_t)v1.w << 32) | v1.z};
-#pragma unroll
-                    for (int u = 0; u < 4; u++) {
-                        // the low half is a bf16 bit pattern; poll() returns it as the f32 bits
-                        const uint32_t x = (uint32_t)(w[u] >> 32) == tag ? (uint32_t)w[u] : __float_as_uint(poll(cx, src + u, tag));
-                        sm.sT[(si * 64 + k4 * 4 + u) * B + b] = (uint16_t)(x & 0xFFFFu);
+                    // the low half of each word is a bf16 bit pattern
+                    if (v0.y == tag && v0.w == tag && v1.y == tag && v1.w == tag) {
+                        dst[0] = (uint16_t)v0.x;
+                        dst[B] = (uint16_t)v0.z;
+                        dst[2 * B] = (uint16_t)v1.x;
+                        dst[3 * B] = (uint16_t)v1.z;
+                    } else {
+                        poll4_bf16(src, dst, B, tag, cx.fail, a.err);
                     }
                 }
                 cbar();
