@@ -21,6 +21,9 @@ MING_DEV void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
 MING_DEV void mbar_arrive(uint64_t* b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(su32(b)) : "memory");
 }
+MING_DEV void mbar_arrive_n(uint64_t* b, uint32_t n) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;\n" ::"r"(su32(b)), "r"(n) : "memory");
+}
 MING_DEV bool mbar_try(uint64_t* b, uint32_t parity) {
     uint32_t ok;
     asm volatile(
@@ -276,6 +279,7 @@ static_assert(2 * MG_ATT_CH * HD * 2 + 3 * HD * 4 + MG_ATT_CH * 4 + MG_CWARPS * 
 static_assert(MG_ATT_CH * HD * 2 * 2 <= MG_B_BYTES, "the attention K/V pages fit the fragment area");
 static_assert(MG_ATT_CH * 4 + MG_CWARPS * 32 * 8 >= MG_CWARPS * 68 * 4, "the warps' attention partials fit the score area");
 
+constexpr int MG_SLOT_META = 32;  // ring slots of one phase with precomputed users
 struct Misc {              // small per-CTA state in shared memory
     uint64_t att_bar;            // mbarrier of the attention items' K/V page copies (first: 8-byte aligned)
     unsigned int att_uses;       // phases of att_bar completed so far
@@ -313,6 +317,11 @@ struct Misc {              // small per-CTA state in shared memory
     unsigned long long bm;  // divB multiplier of the step's row count
     long long pg_el;        // elements between consecutive pages of the KV pool
     uint8_t tcount[3][MG_MAX_TILES];  // contributors per tile of the split-K phases q 0, 1, 3
+    // per phase and ring slot of the phase (phases of at most MG_SLOT_META
+    // slots): the lowest warp whose run uses the slot, and the arrivals it adds
+    // on the slot's empty barrier for the warps that do not use it
+    uint8_t sl_first[MG_NPH][MG_SLOT_META];
+    uint8_t sl_extra[MG_NPH][MG_SLOT_META];
 };
 static_assert(sizeof(Misc) <= 4096, "Misc must fit its shared-memory slot");
 
@@ -477,7 +486,6 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
     if (n <= 0) return;  // CTA-uniform
     const int nsc = ms->nsc[p];
     MG_SUB(1)
-    if (TR && sm.st && p == 0 && (warp == 1 || warp == 3) && lane == 0) sm.st[88 + (warp >> 1) * 4] = clock64();
     const Misc::WRun wr = ms->wrun[p][warp];
     const int i0 = wr.i0, i1 = wr.i1;
     const int tb = ms->wtile[p][warp];
@@ -485,22 +493,24 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
     // walk the warp's run incrementally: tile t, group kg in the tile, group
     // wi in its ring slot
     int t = wr.t, kg = wr.kg, wi = wr.wi;
-    // The phase's ring slots one at a time: every warp waits for each slot,
-    // uses the groups of its run inside it, and releases it, so a phase may be
-    // longer than the ring (the producer refills released slots meanwhile).
-    // A warp releases use u+1 of a slot only after waiting for its fill, which
-    // needs every warp's release of use u: arrivals of two uses never mix.
-    // With the phase inside the ring (every use a distinct slot; the barrier
-    // ending the previous phase orders its releases first), a warp releases
-    // the slots before and after its run without waiting for their fill: some
-    // warp uses every slot and releases it only after its wait and use, so
-    // the producer never refills a slot still being filled or read.
-    // In that case a warp first takes the slots of its own run, then releases
-    // the others: walking (and releasing) the slots before its run first
-    // delayed warp w's first data by ~0.15 us per earlier warp.
-    const bool skip = nsc <= a.nslots;
+    // The phase's ring slots one at a time: a warp waits for a slot's fill,
+    // uses the groups of its run inside it and releases it (one arrival on the
+    // slot's empty barrier, which expects MG_CWARPS), so a phase may be longer
+    // than the ring (the producer refills released slots meanwhile).
+    // With the phase inside the ring (skip mode: every use a distinct slot)
+    // a warp visits only the slots of its own run. The lowest warp using a
+    // slot also arrives for the warps that do not use it (sl_extra), after it
+    // waited for the fill: the barrier's previous phase has completed by then
+    // (the producer waited for it before refilling), and this phase completes
+    // only once every user has arrived, so the producer never refills a slot
+    // that is still read. Walking the other warps' slots to release them
+    // cost ~0.2 us per slot per warp.
+    // Otherwise every warp walks every slot in order: it releases use u+1 of
+    // a slot only after waiting for its fill, which needs every warp's
+    // release of use u, so arrivals of two uses never mix.
+    const bool skip = nsc <= a.nslots && nsc <= MG_SLOT_META;
     const int js = i0 < i1 ? wr.js : 0, je = i0 < i1 ? wr.je : -1;
-    const int njj = skip ? nsc + (je - js + 1) : nsc;  // skip: own slots, then every slot (own ones passed over)
+    const int njj = skip ? je - js + 1 : nsc;
     // slot of phase slot jj: slot0 + jj, wrapped once at most in skip mode;
     // in order (one wrap per pass of the ring) otherwise
     int sl = slot0;
@@ -509,11 +519,7 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
     for (int it = 0; it < njj; it++) {
         int jj = it;
         if (skip) {
-            if (it <= je - js) jj = js + it;
-            else {
-                jj = it - (je - js + 1);
-                if (jj >= js && jj <= je) continue;  // warp-uniform: released in the first pass
-            }
+            jj = js + it;
             sl = slot0 + jj;
             par = par0;
             if (sl >= a.nslots) {
@@ -526,7 +532,6 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
         }
         const int w0 = max(i0, jj * a.gps), w1 = min(i1, (jj + 1) * a.gps);
         if ((!skip || w0 < w1) && !mbar_wait(&full[sl], par)) atomicCAS(cx.fail, 0, 2);
-        if (TR && sm.st && p == 0 && (warp == 1 || warp == 3) && lane == 0 && w0 == i0 && w0 < w1) sm.st[89 + (warp >> 1) * 4] = clock64();
         if (TR && sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p == 2 && w0 == i0 && w0 < w1) sm.st[56 + warp] = clock64();
         if (w0 < w1 && !*(volatile int*)cx.fail) {
             const uint8_t* sbase = ring + (size_t)sl * a.slot_bytes;
@@ -572,9 +577,10 @@ MING_DEV void gemv_phase(const Ctx& cx, const Sm& sm, int p, int slot0, uint32_t
             }
         }
         __syncwarp();
-        if (TR && sm.st && p == 0 && (warp == 1 || warp == 3) && lane == 0 && w1 == i1 && w0 < w1) sm.st[90 + (warp >> 1) * 4] = clock64();
-        if (lane == 0) mbar_arrive(&empty[sl]);  // before any global write of this phase
-        if (TR && sm.st && p == 0 && (warp == 1 || warp == 3) && lane == 0 && w1 == i1 && w0 < w1) sm.st[91 + (warp >> 1) * 4] = clock64();
+        if (lane == 0) {  // before any global write of this phase
+            if (skip && ms->sl_first[p][jj] == warp) mbar_arrive_n(&empty[sl], 1u + ms->sl_extra[p][jj]);
+            else mbar_arrive(&empty[sl]);
+        }
         if (TR && sm.st && (MG_CWARPS <= 8 || warp < 8) && lane == 0 && p >= 2 && w1 == i1 && w0 < w1) sm.st[40 + (p - 2) * 8 + warp] = clock64();
     }
     MG_SUB(2)
@@ -1031,6 +1037,22 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
         ms->pg_el = (long long)a.layers * 2 * a.kvh * (PAGE * HD);
         ms->grp = a.heads / a.kvh;
         ms->hm = ((1ull << 32) + (unsigned long long)a.heads - 1ull) / (unsigned long long)a.heads;
+    }
+    __syncthreads();
+    if (tid < MG_NPH) {
+        const int p = tid;
+        for (int jj = 0; jj < ms->nsc[p] && jj < MG_SLOT_META; jj++) {
+            int users = 0, first = 0;
+            for (int w = MG_CWARPS - 1; w >= 0; w--) {
+                const Misc::WRun r = ms->wrun[p][w];
+                if (r.i0 < r.i1 && r.js <= jj && jj <= r.je) {
+                    users++;
+                    first = w;
+                }
+            }
+            ms->sl_first[p][jj] = (uint8_t)first;
+            ms->sl_extra[p][jj] = (uint8_t)(MG_CWARPS - users);
+        }
     }
     __syncthreads();
     const uint32_t epoch = ms->epoch;
