@@ -56,14 +56,16 @@ void launch_lin_staged(const PackedW& W, const LinScratch& sc, const Pro& p, con
     else launch_lin_frag<FMT, NT, 1>(W, sc, e, rows, s);
 }
 
-template <int N, class Pro, class Epi>
+// F16: f16 operands (the prefill copies of quantized weights), else bf16
+template <int N, bool F16, class Pro, class Epi>
 void launch_tc_n(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& e, int rows, int ks, cudaStream_t s) {
+    const int KT = W.tck;  // K of the weight blocks (the rows are staged over it)
     static unsigned attr_devices = 0;  // bit d: attribute set on device d
     int dev = 0;
     cudaGetDevice(&dev);
     constexpr int smax = N <= 128 ? TcSmem<N>::TOTAL_KS : TcSmem<N>::TOTAL;
     if (!(attr_devices & (1u << (dev & 31)))) {
-        cudaFuncSetAttribute(tc_linear_kernel<N, Epi>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax);
+        cudaFuncSetAttribute(tc_linear_kernel<N, Epi, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax);
         attr_devices |= 1u << (dev & 31);
     }
     if (N > 128) ks = 1;  // no room for the partial sums beside the 256-row stages
@@ -73,12 +75,12 @@ void launch_tc_n(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi
     pdl[0].val.programmaticStreamSerializationAllowed = 1;
     {
         cudaLaunchConfig_t sg = {};
-        sg.gridDim = dim3((rows + 7) / 8, (W.K + STAGE_KC - 1) / STAGE_KC);
+        sg.gridDim = dim3((rows + 7) / 8, (KT + STAGE_KC - 1) / STAGE_KC);
         sg.blockDim = dim3(LIN_THREADS);
         sg.stream = s;
         sg.attrs = pdl;
         sg.numAttrs = 1;
-        cudaLaunchKernelEx(&sg, stage_rows_kernel<N, Pro>, p, rows, (int)W.K, xs, (float*)sc.post);
+        cudaLaunchKernelEx(&sg, stage_rows_kernel<N, Pro, F16>, p, rows, KT, xs, (float*)sc.post);
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)(W.ntiles / 8 * ks), (unsigned)((rows + N - 1) / N));
@@ -93,29 +95,39 @@ void launch_tc_n(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi
     at[1].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = ks > 1 ? 2 : 1;
-    cudaLaunchKernelEx(&cfg, tc_linear_kernel<N, Epi>, W.tc, W.K, (const uint8_t*)xs, (const float*)sc.post, e, rows, ks);
+    cudaLaunchKernelEx(&cfg, tc_linear_kernel<N, Epi, F16>, W.tc, KT, (const uint8_t*)xs, (const float*)sc.post, e, rows, ks);
 }
 
 // bf16 weights, 64+ rows: the tcgen05 linear with the widest row block that
 // still gives ~96 CTAs; when even 64-row blocks leave fewer than half the SMs
 // a CTA, the K groups are split over a cluster of up to 8 CTAs (at least 12
 // groups each).
-template <class Pro, class Epi>
+template <bool F16, class Pro, class Epi>
 void launch_tc(const PackedW& W, const LinScratch& sc, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
     const int mt = W.ntiles / 8;
-    if (mt * ((rows + 255) / 256) >= 96) launch_tc_n<256>(W, sc, p, e, rows, 1, s);
-    else if (mt * ((rows + 127) / 128) >= 96) launch_tc_n<128>(W, sc, p, e, rows, 1, s);
+    if (mt * ((rows + 255) / 256) >= 96) launch_tc_n<256, F16>(W, sc, p, e, rows, 1, s);
+    else if (mt * ((rows + 127) / 128) >= 96) launch_tc_n<128, F16>(W, sc, p, e, rows, 1, s);
     else {
         const int ctas = mt * ((rows + 63) / 64);
         int ks = 1;
-        if (2 * ctas <= sc.sms) ks = std::max(1, std::min({8, sc.sms / ctas, W.K / 64 / 12}));
-        launch_tc_n<64>(W, sc, p, e, rows, ks, s);
+        if (2 * ctas <= sc.sms) ks = std::max(1, std::min({8, sc.sms / ctas, W.tck / 64 / 12}));
+        launch_tc_n<64, F16>(W, sc, p, e, rows, ks, s);
     }
 }
 
 inline bool bulk_enabled() {
     static const bool on = [] {
         const char* v = getenv("MING_BULK");
+        return !(v && std::string(v) == "0");
+    }();
+    return on;
+}
+
+// MING_TC_COPIES=0: no f16 prefill copies of quantized linears (their
+// prefill then stays on the mma.sync kernels)
+inline bool tc_copies_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("MING_TC_COPIES");
         return !(v && std::string(v) == "0");
     }();
     return on;
@@ -132,11 +144,13 @@ inline bool tc_enabled() {
 template <int FMT, class Pro, class Epi>
 void launch_lin_f(const LinScratch& sc, const PackedW& W, const Pro& p, const Epi& e, int rows, cudaStream_t s) {
     const bool staged = sc.frag && rows <= sc.rows && W.K <= sc.K;
-    if constexpr (FMT == 16) {
-        if (staged && rows >= 64 && W.tc && tc_enabled()) {
-            launch_tc(W, sc, p, e, rows, s);
-            return;
-        }
+    // bf16 weights from 64 rows; quantized weights (their f16 prefill copy,
+    // f16 rows) above 64 rows, so decode batches up to 64 rows keep the
+    // 4/8-bit bytes
+    if (staged && (FMT == 16 ? rows >= 64 : rows > 64) && W.tc && W.tck <= sc.K && tc_enabled()) {
+        if (W.tck == W.K) launch_tc<FMT != 16>(W, sc, p, e, rows, s);
+        else launch_tc<FMT != 16>(W, sc, ProTwice<Pro>{p, W.K}, e, rows, s);
+        return;
     }
     // up to 64 rows of plain, RMS-normed or LayerNorm-modulated inputs: bulk.cuh
     if constexpr (std::is_same_v<Pro, ProRms> || std::is_same_v<Pro, ProPlain> || std::is_same_v<Pro, ProLnMod>) {

@@ -27,7 +27,8 @@ struct PackedW {
     const uint8_t* tiles = nullptr;
     const float* bias = nullptr;  // [ntiles*16] in packed row order, or null
     int ntiles = 0, K = 0, fmt = 16;
-    const uint8_t* tc = nullptr;  // bf16 only: swizzled weight blocks for the tcgen05 linear (tcgen05.cuh), or null
+    const uint8_t* tc = nullptr;  // swizzled weight blocks for the tcgen05 linear (tcgen05.cuh), or null
+    int tck = 0;                  // K of those blocks: K (bf16), 2 K (f16 hi | lo copy of quantized weights)
 };
 
 MING_DEV constexpr int chunk_b(int fmt) { return fmt == 4 ? 576 : (fmt == 8 ? 1088 : 2048); }

@@ -178,6 +178,17 @@ int upload_packed(ming_ctx* c, const std::vector<LinearSrc>& srcs, const std::ve
         tc_swizzle_kernel<<<dim3(pl.w.ntiles / 8, K / 64), TC_THREADS>>>(dt, K / 64, tc);
         CK(cudaGetLastError());
         pl.w.tc = tc;
+        pl.w.tck = K;
+    } else if ((fmt == 4 || fmt == 8) && pl.w.ntiles % 8 == 0 && K % 64 == 0 && c->cfg.max_prefill > 64 && tc_copies_enabled()) {
+        // the prefill copy: f16 hi | lo weight blocks dequantized once at load,
+        // so chunks of more than 64 rows run on the tcgen05 linear (4 bytes
+        // per weight in HBM beside the packed tiles)
+        uint8_t* tc = c->mem.alloc<uint8_t>((size_t)pl.w.ntiles * 16 * K * 4, &rc);
+        if (!tc) return rc;
+        tc_swizzle_dq_kernel<<<dim3(pl.w.ntiles / 8, K / 64), TC_THREADS>>>(dt, K / 64, fmt, tc);
+        CK(cudaGetLastError());
+        pl.w.tc = tc;
+        pl.w.tck = 2 * K;
     }
     pl.src_names = names;
     pl.rows = rows;
@@ -1056,6 +1067,8 @@ int ming_cuda_finalize(ming_ctx* c) {
             rows_cap = std::max(rows_cap, std::max(2 * MB * f.dit_frames, 20 * MB));  // 20 MB: 10 steps' modulation rows
             k_cap = std::max(k_cap, std::max(std::max(f.dit_hidden, f.dit_ff), std::max(f.dit_cond_dim, f.dit_freq_dim)));
         }
+        if (f.weight_bits != 16 && f.max_prefill > 64 && tc_copies_enabled())
+            k_cap = std::max(k_cap, 2 * std::max(f.hidden, f.ff));  // the prefill copies' rows, staged twice
         rows_cap = (rows_cap + 255) / 256 * 256;  // the tcgen05 linear reads whole 256-row blocks
         k_cap = (k_cap + 63) / 64 * 64;
         rc = MING_OK;

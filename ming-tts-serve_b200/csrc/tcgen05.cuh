@@ -57,11 +57,13 @@ MING_DEV uint64_t tc_desc(uint32_t saddr) {
            ((uint64_t)2 << 61);
 }
 
-// Instruction descriptor, kind::f16: f32 accumulator (1 at [4,6)), bf16 A and
-// B (1 at [7,10) and [10,13)), both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
-template <int N>
+// Instruction descriptor, kind::f16: f32 accumulator (1 at [4,6)), A and B
+// both bf16 (1 at [7,10) and [10,13)) or both f16 (0 there), both K-major,
+// N >> 3 at [17,23), M >> 4 at [24,29).
+template <int N, bool F16 = false>
 MING_DEV constexpr uint32_t tc_idesc() {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TC_M >> 4) << 24);
+    return (1u << 4) | ((F16 ? 0u : 1u) << 7) | ((F16 ? 0u : 1u) << 10) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(TC_M >> 4) << 24);
 }
 
 MING_DEV uint32_t tc_saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -99,11 +101,68 @@ static __global__ void __launch_bounds__(TC_THREADS) tc_swizzle_kernel(const uin
     }
 }
 
+// Packed 4/8-bit tiles -> swizzled f16 weight blocks over twice the K groups:
+// each weight dequantized as MLX's affine dequantize does (w = scale * q +
+// bias in f32) and split into hi = f16(w) (group g) and lo = f16(w - hi)
+// (group ng + g), so that the tcgen05 sums over the rows staged twice keep
+// ~22 significant bits of every weight: the prefill copy of a quantized
+// linear, as accurate as the exact-weight mma.sync kernels.
+static __global__ void __launch_bounds__(TC_THREADS) tc_swizzle_dq_kernel(const uint8_t* tiles, int ng, int fmt, uint8_t* out) {
+    const int mt = blockIdx.x, g = blockIdx.y, cb = fmt == 4 ? 576 : 1088;
+    uint8_t* dhi = out + ((size_t)mt * 2 * ng + g) * TC_A_BLOCK;
+    uint8_t* dlo = dhi + (size_t)ng * TC_A_BLOCK;
+    for (int e = threadIdx.x; e < 8 * 4 * 32; e += TC_THREADS) {
+        const int i = e >> 7, ks = (e >> 5) & 3, L = e & 31;
+        const uint8_t* ch = tiles + ((size_t)(mt * 8 + i) * ng + g) * cb;
+        const uint2 sc = *reinterpret_cast<const uint2*>(ch + (fmt == 4 ? 512 : 1024) + (L >> 2) * 8);
+        const float s_lo = __uint_as_float(sc.x << 16), b_lo = __uint_as_float(sc.x & 0xffff0000u);
+        const float s_hi = __uint_as_float(sc.y << 16), b_hi = __uint_as_float(sc.y & 0xffff0000u);
+        uint32_t q[4];
+        if (fmt == 4) {
+            dq4(reinterpret_cast<const uint32_t*>(ch + (size_t)L * 16)[ks], q);
+        } else {
+            const uint32_t* w8 = reinterpret_cast<const uint32_t*>(ch + ((size_t)(ks >> 1) * 32 + L) * 16 + (ks & 1) * 8);
+            dq8(w8[0], w8[1], q);
+        }
+        // q[0..3]: (row r, k..k+1), (row r+8, k..), (row r, k+8..), (row r+8, k+8..) as exact f16 codes
+        uint32_t wh[4], wl[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const float2 v = __half22float2(*reinterpret_cast<const __half2*>(&q[j]));
+            const float sj = (j & 1) ? s_hi : s_lo, bj = (j & 1) ? b_hi : b_lo;
+            const float w0 = sj * v.x + bj, w1 = sj * v.y + bj;
+            wh[j] = pack_f16x2(w0, w1);
+            const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&wh[j]));
+            wl[j] = pack_f16x2(w0 - h.x, w1 - h.y);
+        }
+        const int r0 = i * 16 + (L >> 2), k0 = ks * 16 + 2 * (L & 3);
+        const int c0 = k0 >> 3, b0 = (2 * k0) & 15;
+        const uint32_t o[4] = {tc_sw128(r0, c0) + b0, tc_sw128(r0 + 8, c0) + b0, tc_sw128(r0, c0 + 1) + b0,
+                               tc_sw128(r0 + 8, c0 + 1) + b0};
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            *reinterpret_cast<uint32_t*>(dhi + o[j]) = wh[j];
+            *reinterpret_cast<uint32_t*>(dlo + o[j]) = wl[j];
+        }
+    }
+}
+
+// The rows of a prologue over two K sections (the hi and lo weight blocks of
+// a split prefill copy): y(row, k) = pro.y(row, k mod K).
+template <class Pro>
+struct ProTwice {
+    Pro p;
+    int K;
+    MING_DEV void init(int r0, int nrows, float* aux) { p.init(r0, nrows, aux); }
+    MING_DEV float y(int row, int k) const { return p.y(row, k < K ? k : k - K); }
+    MING_DEV float post(int row) const { return p.post(row); }
+};
+
 // Rows -> swizzled activation blocks [rows / N][K / 64][N * 128 bytes]: the
 // prologue once per (row, k), with the operand rounding of the mma.sync
 // kernels (pack_bf16x2), and each row's post scale. Rows past `rows` in the
 // last block are left as they are (their outputs are never written).
-template <int N, class Pro>
+template <int N, class Pro, bool F16 = false>
 __global__ void __launch_bounds__(LIN_THREADS) stage_rows_kernel(Pro pro, int rows, int K, uint8_t* xs, float* post) {
     __shared__ float aux[8 * 32];
     const int r0 = blockIdx.x * 8, nrows = min(8, rows - r0);
@@ -134,8 +193,12 @@ __global__ void __launch_bounds__(LIN_THREADS) stage_rows_kernel(Pro pro, int ro
             for (int u = 0; u < 8; u++) y[u] = p.y(row, k + u);
         }
         uint8_t* blk = xs + ((size_t)(n / N) * ng + k / 64) * (N * 128);
-        *reinterpret_cast<uint4*>(blk + tc_sw128(n % N, (k & 63) >> 3)) =
-            make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
+        if constexpr (F16)
+            *reinterpret_cast<uint4*>(blk + tc_sw128(n % N, (k & 63) >> 3)) =
+                make_uint4(pack_f16x2(y[0], y[1]), pack_f16x2(y[2], y[3]), pack_f16x2(y[4], y[5]), pack_f16x2(y[6], y[7]));
+        else
+            *reinterpret_cast<uint4*>(blk + tc_sw128(n % N, (k & 63) >> 3)) =
+                make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
     }
     if (blockIdx.y == 0 && threadIdx.x < nrows) post[r0 + threadIdx.x] = p.post(threadIdx.x);
 }
@@ -146,7 +209,7 @@ __global__ void __launch_bounds__(LIN_THREADS) stage_rows_kernel(Pro pro, int ro
 // meet over distributed shared memory in rank order (deterministic), the
 // ranks splitting the epilogue.
 // Thread 0 produces, thread 32 issues the MMAs, all 16 warps run the epilogue.
-template <int N, class Epi>
+template <int N, class Epi, bool F16 = false>
 __global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(const uint8_t* wtc, int K, const uint8_t* xs, const float* post,
                                                                Epi epi, int rows, int nks) {
     using S = TcSmem<N>;
@@ -234,7 +297,7 @@ __global__ void __launch_bounds__(TC_THREADS) tc_linear_kernel(const uint8_t* wt
                 asm volatile(
                     "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
                     " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem),
-                    "l"(da), "l"(db), "r"(tc_idesc<N>()), "r"(acc)
+                    "l"(da), "l"(db), "r"(tc_idesc<N, F16>()), "r"(acc)
                     : "memory");
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(

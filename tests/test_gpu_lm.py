@@ -113,6 +113,20 @@ def test_prefill_bf16_many_rows(cuda_ok):
     ctx.close()
 
 
+@pytest.mark.parametrize("bits", [4, 8])
+def test_prefill_quantized_tcgen05_many_rows(cuda_ok, bits):
+    """4/8-bit weights with 200 prompt rows: chunks above 64 rows run on the
+    tcgen05 linear over the weights' f16 hi | lo prefill copies (the rows
+    staged in f16 as the mma.sync kernels stage them), gated like the other
+    multi-layer outputs."""
+    W = synth.lm_weights(seed=4, bits=bits, layers=2, qscale=QS)
+    ctx = make_ctx(W, bits, 2)
+    res = _teacher_forced(ctx, O.Lm(W), synth.normal_bf16(4, f"test.prompt.q{bits}.200", (200, 896)), 2, 3)
+    for i, (d, c, ok) in enumerate(res):
+        assert ok, f"step {i}: maxabs {d:.4g} cos {c:.6f}"
+    ctx.close()
+
+
 def test_batched_decode_ragged_prompts(q4_24):
     W, ctx, lm = q4_24
     lens = [1, 17, 40, 64, 300]
@@ -312,12 +326,15 @@ def test_errors_are_reported(q4_24):
 
 def test_q4_baseline_init_prefill(cuda_ok):
     """The benchmark's 4-bit distribution (scales U(0.005, 0.02)) on a 100-row
-    prefill of 2 layers. Its peaky attention makes the reference's own FUSED
-    and GRAPH paths differ by 0.02-0.63 max-abs on some rows (one row's
-    attention flips), so the strict 2e-2 cannot hold against either: every
-    row is gated by within_reference (the tolerance or twice that row's
-    reference spread, cosine > 0.999 or the reference's own) and is as
-    accurate as the reference against exact arithmetic (oracle F32 mode)."""
+    prefill of 2 layers (the tcgen05 linear over the f16 hi | lo prefill
+    copies). Its peaky attention makes the reference's own FUSED and GRAPH
+    paths differ by 0.02-0.63 max-abs on some rows (one row's attention
+    flips), so the strict 2e-2 cannot hold against either: every row is
+    gated by within_reference (the tolerance or twice that row's reference
+    spread, cosine > 0.999 or the reference's own) and is as accurate as the
+    reference against exact arithmetic (oracle F32 mode). Measured on the
+    flipping row (cosine to exact): tcgen05 0.8893, mma.sync 0.8856, FUSED
+    0.8891."""
     W = synth.lm_weights(seed=7, bits=4, layers=2)
     ctx = make_ctx(W, 4, 2)
     lm = O.Lm(W)
