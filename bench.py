@@ -182,8 +182,9 @@ def lm_workload(cfgid, local, steps, warmup, W=None):
     if W is None:
         W = synth.lm_weights(seed=c["seed"], bits=c["bits"], layers=24)
         log(f"[bench] weights generated in {time.time() - t0:.1f}s ({synth.nbytes(W) / 1e6:.1f} MB)")
+    # a prompt prefills in one chunk (up to 2048 rows: the tcgen05 linear's row blocks)
     cfg = M.default_cfg(weight_bits=c["bits"], dit_mode=M.DIT_NONE, agg_blocks=0, max_ctx=max_ctx, max_pages=pages,
-                        max_batch=max(B, 1), max_seqs=max(B, 1), max_prefill=512)
+                        max_batch=max(B, 1), max_seqs=max(B, 1), max_prefill=max(512, min(2048, max(lens))))
     ctx = M.Context(cfg, device=local, weights=W)
     seqs = []
     last = []
@@ -445,7 +446,7 @@ def run_loop(args, ws, rank, local):
     log(f"[bench] weights generated in {time.time() - t0:.1f}s")
     cfg = M.default_cfg(weight_bits=c["bits"], dit_mode=M.DIT_ADALN, dit_hidden=768, dit_blocks=6, dit_heads=12,
                         dit_ff=3072, dit_frames=4, dit_max_batch=B, agg_blocks=0, max_ctx=max_ctx, max_pages=pages,
-                        max_batch=B, max_seqs=B, max_prefill=512)
+                        max_batch=B, max_seqs=B, max_prefill=max(512, min(2048, P)))
     ctx = M.Context(cfg, device=local, weights={**Wl, **Wd})
     params = M.sample_params(max_steps=n_total, max_len=P + n_total, cfg=2.0, temperature=0.0)
     lp = M.Loop(ctx, B, params)
