@@ -69,6 +69,17 @@ MING_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar
                  : "memory");
 }
 MING_DEV void cbar() { asm volatile("bar.sync 1, %0;\n" ::"n"(MG_CT) : "memory"); }  // consumer warps only
+// Consumer barrier that also ORs one flag over the consumer threads: every
+// thread gets the same answer even if the producer warp sets the flag meanwhile
+MING_DEV bool cbar_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}\n"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(MG_CT)
+        : "memory");
+    return r != 0;
+}
 MING_DEV uint64_t ldr64(const void* p) {
     uint64_t v;
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];\n" : "=l"(v) : "l"(p) : "memory");
@@ -409,8 +420,9 @@ MING_DEV void stage(const Sm& sm, int nstage, int B, int H, int mode, const uint
 // Residual update from a fixed-point accumulator, fused with the RMSNorm
 // statistics of the updated rows: sX[b][f] = rb(sX + rb(acc[b][f])), then
 // inv, pre-scale and post-scale of each row for the norm weight nw. With acc
-// null the rows stay as they are (the layer-0 input).
-MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, const MegaDev& a, const unsigned long long* acc, const uint8_t* tcount,
+// null the rows stay as they are (the layer-0 input). Returns whether the
+// CTA has failed (one answer for every consumer thread).
+MING_DEV bool residual_stats(const Ctx& cx, const Sm& sm, const MegaDev& a, const unsigned long long* acc, const uint8_t* tcount,
                                const uint16_t* nw, bool f16) {
     const int H = a.H, B = a.B, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // row by row, two features per thread per pass (f = 2 tid, + 2 x 256, ...);
@@ -465,7 +477,7 @@ MING_DEV void residual_stats(const Ctx& cx, const Sm& sm, const MegaDev& a, cons
         sm.ms->scl[tid] = __int_as_float((127 - e) << 23);
         sm.ms->post[tid] = inv * __int_as_float((127 + e) << 23);
     }
-    cbar();
+    return cbar_or(*(volatile int*)cx.fail != 0);  // the caller's failure check rides on this barrier
 }
 
 enum { OUT_ACC = 0, OUT_GLU = 1 };
@@ -926,8 +938,8 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
 
 // o_proj input: the combined attention output of the heads this CTA's
 // o_proj range reads (published by each head's last chunk), into sT
-// [si][d][b].
-MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int gpt, uint32_t tag) {
+// [si][d][b]. Returns whether the CTA has failed.
+MING_DEV bool combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int gpt, uint32_t tag) {
     const MegaDev& a = *cx.a;
     Misc* ms = sm.ms;
     const int B = a.B, tot = nst * 64 * B;
@@ -938,7 +950,7 @@ MING_DEV void combine_heads(const Ctx& cx, const Sm& sm, int nst, int base, int 
         const uint64_t v = ldr64(p);
         sm.sT[e] = f2bf((uint32_t)(v >> 32) == tag ? __uint_as_float((uint32_t)v) : poll(cx, p, tag));
     }
-    cbar();
+    return cbar_or(*(volatile int*)cx.fail != 0);
 }
 
 template <int FMT, bool TR>
@@ -1104,8 +1116,7 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
     uint32_t cpar = 0;
     bool dead = false;
     auto check = [&]() -> bool {
-        cbar();  // every consumer thread sees the same answer
-        if (*(volatile int*)&ms->fail) dead = true;
+        if (cbar_or(*(volatile int*)&ms->fail != 0)) dead = true;  // every consumer thread sees the same answer
         return dead;
     };
     {
@@ -1176,11 +1187,11 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
                     const int sch = divB(rem, ms->hm);  // rem / heads (rem < 2^16: exact)
                     attention_item<TR>(cx, sm, l, tag, b, rem - sch * a.heads, sch, waited);
                     waited = true;
-                    check();
+                    check();  // the next item reuses the shared-memory areas
                 }
-                if (check()) break;
+                if (dead) break;
                 MG_STAMP(9)
-                combine_heads(cx, sm, nst, base, gpt, tag);
+                if (combine_heads(cx, sm, nst, base, gpt, tag)) dead = true;
             } else if (rows) {
                 // q 0: x(l) = x1(l-1) + down(l-1); q 2: x1 = x + o_proj
                 const unsigned long long* src =
@@ -1188,8 +1199,8 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
                 const int sp = q == 2 ? 1 : 2;  // tile counts: o_proj / down
                 if (src) hint_acc(cx, src + (size_t)(a.ph[sp == 1 ? 1 : 3].tiles - 1) * 16 + 15,
                                   ms->tcount[sp][a.ph[sp == 1 ? 1 : 3].tiles - 1]);
-                if (check()) break;
-                residual_stats(cx, sm, a, src, ms->tcount[sp], q == 0 ? ln1 : ln2, F16);
+                // (a failure seen during the hint makes the residual's polls return at once)
+                if (residual_stats(cx, sm, a, src, ms->tcount[sp], q == 0 ? ln1 : ln2, F16)) dead = true;
             } else {
                 // q 3: the SwiGLU outputs of this CTA's down range (tagged words, 4 per item)
                 if (tid == 0) {
@@ -1213,9 +1224,10 @@ __global__ void __launch_bounds__(MG_THREADS, 1) mega_kernel(const __grid_consta
                         poll4_bf16(src, dst, B, tag, cx.fail, a.err);
                     }
                 }
-                cbar();
+                check();
             }
-            if (check()) break;
+            // every branch above ended with a failure-reducing barrier
+            if (dead) break;
             MG_STAMP(1 + 2 * q)
             sm.so = 10 + 7 * q;
             stage<F16, TR>(sm, nst, B, H, rows ? 0 : 1, q == 0 ? ln1 : ln2);
