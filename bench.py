@@ -450,11 +450,12 @@ def run_loop(args, ws, rank, local):
     ctx = M.Context(cfg, device=local, weights={**Wl, **Wd})
     params = M.sample_params(max_steps=n_total, max_len=P + n_total, cfg=2.0, temperature=0.0)
     lp = M.Loop(ctx, B, params)
-    t0 = time.time()
     prompts = [synth.normal_bf16(c["seed"], f"bench.loop.prompt.{b}", (P, 896)) for b in range(B)]
+    ctx.sync()
+    t0 = time.time()
     ids = [lp.submit(prompts[b], None, seed=1000 + b) for b in range(B)]
     ctx.sync()
-    log(f"[bench] prefill of {B} x {P} tokens in {time.time() - t0:.1f}s")
+    log(f"[bench] prefill of {B} x {P} tokens in {time.time() - t0:.2f}s (submitted through the loop, host prompts)")
     for _ in range(args.warmup):
         a, q = lp.step()
         assert a == B and q == 0
