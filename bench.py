@@ -281,21 +281,24 @@ def measure_lm(cfgid, args, ws, rank, local, cpu, W=None):
         ctx.seq_truncate(s, L)
     ids = (M.ctypes.c_int * B)(*seqs)
     L_ = M.lib()
+    # --e2e-api noalloc: the same loop through the allocation-free entry point
+    dec = L_.ming_cuda_lm_decode_noalloc if args.e2e_api == "noalloc" else L_.ming_cuda_lm_decode
     for _ in range(min(args.warmup, 8)):
-        M._check(L_.ming_cuda_lm_decode(ctx._h, B, ids, M.ctypes.c_void_p(xin.data_ptr()), M.ctypes.c_void_p(hout.data_ptr()),
-                                        M.ctypes.c_void_p(hstop.data_ptr()), M.PTR_HOST))
+        M._check(dec(ctx._h, B, ids, M.ctypes.c_void_p(xin.data_ptr()), M.ctypes.c_void_p(hout.data_ptr()),
+                     M.ctypes.c_void_p(hstop.data_ptr()), M.PTR_HOST))
     for s, L in zip(seqs, lens_start):
         ctx.seq_truncate(s, L)
     dist_barrier(ws)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        M._check(L_.ming_cuda_lm_decode(ctx._h, B, ids, M.ctypes.c_void_p(xin.data_ptr()), M.ctypes.c_void_p(hout.data_ptr()),
-                                        M.ctypes.c_void_p(hstop.data_ptr()), M.PTR_HOST))
+        M._check(dec(ctx._h, B, ids, M.ctypes.c_void_p(xin.data_ptr()), M.ctypes.c_void_p(hout.data_ptr()),
+                     M.ctypes.c_void_p(hstop.data_ptr()), M.PTR_HOST))
         xin.copy_(hout)  # feed the step's output back (host side, as a caller would)
     e2e_s = time.perf_counter() - t0
     e2e_s = dist_max(e2e_s, ws)
     e2e = {"value": ws * B * args.steps / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": B * 896 * 2,
-           "d2h_bytes_per_step": B * 896 * 2 + B * 4, "api": "ming_cuda_lm_decode (pinned host buffers)"}
+           "d2h_bytes_per_step": B * 896 * 2 + B * 4,
+           "api": ("ming_cuda_lm_decode_noalloc" if args.e2e_api == "noalloc" else "ming_cuda_lm_decode") + " (pinned host buffers)"}
     cpu = cpu_baseline(cfgid, W, lens, x_last, args.cpu_seconds) if cpu else None
     launches_per_step = ctx.step_kernels(B)
     kname = ("mega_kernel (persistent decode step, one launch)" if launches_per_step == 1 else
@@ -581,6 +584,8 @@ def main():
     ap.add_argument("--no-batch32", action="store_true", help="config 2 only: skip the batch-32 (config 3) sub-measurement")
     ap.add_argument("--batch", type=int, default=None, help="override the config's batch (smaller profiling cases)")
     ap.add_argument("--prefill", type=int, default=None, help="override the config's prompt length")
+    ap.add_argument("--e2e-api", choices=["decode", "noalloc"], default="decode",
+                    help="entry point of the e2e loop (LM configs): ming_cuda_lm_decode or its allocation-free twin")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
