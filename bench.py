@@ -218,8 +218,12 @@ def run_ours(args, ws, rank, local):
         return run_loop(args, ws, rank, local)
     res, W = measure_lm(cfgid, args, ws, rank, local, cpu=rank == 0 and ws == 1 and not args.no_cpu_baseline)
     if cfgid == 2 and not args.no_batch32:
-        # the metric's second batch size: config 3 (32 sequences, ragged prompts) on the same weights
-        b32, _ = measure_lm(3, args, ws, rank, local, cpu=False, W=W)
+        # the metric's second batch size: config 3 (32 sequences, ragged prompts) on the same weights,
+        # timed over at most its own length (warm-up + timed steps within its 512 decode steps)
+        import copy
+        a3 = copy.copy(args)
+        a3.steps = max(1, min(args.steps, CONFIGS[3]["decode"] - args.warmup))
+        b32, _ = measure_lm(3, a3, ws, rank, local, cpu=False, W=W)
         res["batch32"] = {k: b32[k] for k in ("value", "unit", "ms_per_step", "steps", "warmup", "roofline", "e2e",
                                               "gpu_launches", "clocks")}
         res["batch32"]["config"] = b32["config"]
