@@ -700,6 +700,7 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
     //    mbarrier. Every thread read the barrier's phase count before the
     //    barrier that follows (thread 0 advances it there).
     const uint32_t att_par = ms->att_uses & 1u;
+    if (TR && sm.st && tid == 0) sm.st[90] = clock64();  // diagnostics: item start (page copies issued next)
     if (tid == 0) {
         const int npg = (pc - p0 + PAGE - 1) / PAGE;
         constexpr uint32_t PG = PAGE * HD * 2;
@@ -754,7 +755,9 @@ MING_DEV void attention_item(const Ctx& cx, const Sm& sm, int l, uint32_t tag, i
             kv2 = f2bf(x2);
         }
     }
+    if (TR && sm.st && tid == 0) sm.st[88] = clock64();  // diagnostics: q, k, v in registers
     if (!mbar_wait(&ms->att_bar, att_par)) atomicCAS(cx.fail, 0, 6);
+    if (TR && sm.st && tid == 0) sm.st[89] = clock64();  // diagnostics: K/V pages landed
     // 3. in the chunk holding the new position, its key and value go into
     //    their rows of sK / sV (after this thread saw the page copies land:
     //    the rows are then read like every cached one), and the group's first

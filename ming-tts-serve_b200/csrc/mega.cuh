@@ -56,7 +56,8 @@ constexpr int MG_MAX_STAGE = 32;                  // most 64-groups of activatio
 // 10-35 sub-steps of the four GEMV phases, 36-39 attention, 40-55 the end of
 // each of the first 8 warps' runs in gate|up and down, 56-63 their first
 // gate|up slot in hand, 64-87 the end of their split-K reductions in q|k|v,
-// o_proj and down
+// o_proj and down, 88-90 an attention item's q|k|v in hand, pages landed,
+// start
 constexpr int MG_TRACE = 96;
 enum { MG_ACC_QKV = 0, MG_ACC_X1 = 1, MG_ACC_X2 = 2, MG_NACC = 3 };
 constexpr int MG_MAX_TILES = 128;                 // most tiles of a split-K phase (q|k|v, o_proj, down)
