@@ -7,7 +7,8 @@ MLX-style affine 4-bit g64 weights, batch 1, a 128-token prefill, then decode
 steps feeding each step's output hidden state back as the next input. A
 "step" is one decode step of the batch (one token per sequence). Other
 configs: 1 (bf16 LM, batch 1), 3 (4-bit, batch 32, ragged prompts),
-4 (adaLN DiT head, one CFM sample of 10 Euler steps per step).
+4 (adaLN DiT head, one CFM sample of 10 Euler steps per step), 5 (the LM+DiT
+loop), 6 (the VAE decoder, one 128-latent fragment per step).
 
 value  : device-timed throughput with inputs resident in HBM (CUDA events on
          the library's stream around exactly K steps, max over ranks).
@@ -49,6 +50,10 @@ CONFIGS = {
     5: dict(name="LM+DiT loop: 4-bit LM batch 64, 2048-token prefill, then per step an LM decode step, the adaLN head "
                  "(10 Euler steps, CFG) and the latent's 64->896 projection into the next LM input (BASELINE configs[4])",
             bits=4, batch=64, prefill=2048, seed=0, loop=True),
+    6: dict(name="VAE decoder (Model.vaeDecode): one fragment of 128 latents [128][64] -> 44.1 kHz waveform of "
+                 "128 x 4 x 882 samples (10.24 s): fc1, x4 upsample, 24 Qwen2 layers (896, ff 4864, sliding window 64, "
+                 "f32 activations, bf16 weights), final norm, ISTFT head",
+            vae=True, latents=128, seed=2),
 }
 
 
@@ -216,6 +221,8 @@ def run_ours(args, ws, rank, local):
         return run_dit(args, ws, rank, local)
     if c.get("loop"):
         return run_loop(args, ws, rank, local)
+    if c.get("vae"):
+        return run_vae(args, ws, rank, local)
     res, W = measure_lm(cfgid, args, ws, rank, local, cpu=rank == 0 and ws == 1 and not args.no_cpu_baseline)
     if cfgid == 2 and not args.no_batch32:
         # the metric's second batch size: config 3 (32 sequences, ragged prompts) on the same weights,
@@ -429,6 +436,143 @@ def run_dit(args, ws, rank, local):
             "gpu_launches": launches * args.steps, "clocks": ck, "cpu_baseline": None}
 
 
+def vae_workload(c):
+    """The VAE decoder's weights (seeded random init of the real shapes) and one
+    fragment's latents."""
+    from ming_b200 import synth
+    W = synth.vae_weights(seed=c["seed"])
+    lat = synth.normal_bf16(c["seed"], "bench.vae.latents", (c["latents"], 64))
+    return W, lat
+
+
+def vae_work(W, T, window=64, heads=14):
+    """Algorithmic FLOPs and bytes of one decode of T latents: the linears (fc1
+    over T rows; the 24 layers and the head over F = 4T rows), the windowed
+    attention (scores and P.V over min(i + 1, window) positions of row i), the
+    weights read once, the latents in and the waveform out. The irfft (an FFT in
+    the reference) is not counted."""
+    F = 4 * T
+    D = "audio.decoder"
+    lin = lambda name: W[name + ".weight"].size
+    layer_params = sum(v.size for k, v in W.items() if ".decoder.layers." in k and k.endswith("_proj.weight"))
+    att = 4 * 64 * heads * sum(min(i + 1, window) for i in range(F)) * (layer_params > 0) * \
+        sum(1 for k in W if k.endswith("self_attn.q_proj.weight"))
+    flops = 2 * T * lin(D + ".fc1") + 2 * F * (layer_params + lin(D + ".head.out")) + att
+    nbytes = sum(v.nbytes for v in W.values()) + T * 64 * 2 + F * 882 * 4
+    return flops, nbytes
+
+
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        return max([i["num_threads"] for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
+    except ImportError:
+        return len(os.sched_getaffinity(0))
+
+
+def run_vae(args, ws, rank, local):
+    """The VAE decoder (Model.vaeDecode) on one fragment of T latents per step:
+    device-timed through ming_cuda_vae_decode on device buffers (CUDA events on
+    the library's stream), e2e through the same call with pinned host buffers
+    (the latents in, the waveform back). One replica per GPU. The CPU baseline
+    is the oracle's f32 restatement (numpy, BLAS on the host cores)."""
+    import torch
+
+    import ming_b200 as M
+    c = CONFIGS[args.config]
+    T = c["latents"]
+    t0 = time.time()
+    W, lat = vae_workload(c)
+    log(f"[bench] VAE weights generated in {time.time() - t0:.1f}s")
+    cfg = M.default_cfg(layers=0, dit_mode=M.DIT_NONE, agg_blocks=0, vae_layers=24, vae_ff=4864, vae_window=64,
+                        vae_max_latents=T)
+    ctx = M.Context(cfg, device=local, weights=W)
+    n_out = T * 4 * 882
+    dev = f"cuda:{local}"
+    stream = torch.cuda.ExternalStream(ctx.stream, device=local)
+    ld = torch.from_numpy(lat.view(np.int16).copy()).to(dev)
+    wd = torch.empty(n_out, dtype=torch.float32, device=dev)
+    L_ = M.lib()
+    P = lambda t: M.ctypes.c_void_p(t.data_ptr())
+
+    def step(kind=M.PTR_DEVICE, src=ld, dst=wd):
+        M._check(L_.ming_cuda_vae_decode(ctx._h, P(src), T, P(dst), kind))
+
+    for _ in range(args.warmup):
+        step()
+    ctx.sync()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = Clocks(local)
+    dist_barrier(ws)
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.3)
+    profile_range(True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    ev1.synchronize()
+    profile_range(False)
+    dist_barrier(ws)
+    ck = clocks.stop()
+    ms_local = ev0.elapsed_time(ev1)
+    value, ms = aggregate_throughput(ms_local, T, args.steps, ws)
+    flops, nbytes = vae_work(W, T)
+    hbm, tf, peak_kind = load_peaks()
+    t_call = ms_local / args.steps / 1e3
+    tensor_bound = flops / (tf * 1e12) >= nbytes / (hbm * 1e9)
+    # e2e: pinned host latents in, pinned host waveform back, one call per step
+    hl = torch.from_numpy(lat.view(np.int16).copy()).pin_memory()
+    hw = torch.empty(n_out, dtype=torch.float32).pin_memory()
+    for _ in range(min(args.warmup, 3)):
+        step(M.PTR_HOST, hl, hw)
+    dist_barrier(ws)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step(M.PTR_HOST, hl, hw)
+    e2e_s = dist_max(time.perf_counter() - t0, ws)
+    # launches per call, mirroring vae.cu and the linear dispatch: a linear over
+    # more than 8 rows is a staging kernel and a tiled one (2 launches), up to 8
+    # rows one; plus the upsample, 24 attention kernels, the spectrum and the
+    # overlap-add kernels
+    F = 4 * T
+    lin = lambda rows: 1 if rows <= 8 else 2
+    launches = lin(T) + 1 + 24 * (4 * lin(F) + 1) + lin(F) + 1 + lin(F) + 1
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        n, t0 = 0, time.perf_counter()
+        while n < 1 or (time.perf_counter() - t0 < args.cpu_seconds and n < 8):
+            O.vae_decode(W, lat, 24, window=64)
+            n += 1
+        dt = time.perf_counter() - t0
+        cpu = {"value": n * T / dt, "unit": "latents/s", "cores": blas_threads(), "kind": "port",
+               "sample": f"{n} decode(s) of the same {T} latents, 24 layers (the oracle's f32 numpy restatement, "
+                         f"BLAS on the host cores; CPU restatement, not MLX)"}
+    ctx.close()
+    audio_s = T * 4 * 882 / 44100.0
+    return {"metric": "VAE decode latents/s (one 128-latent fragment per call)", "value": value, "unit": "latents/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 activations as bf16 hi + lo parts, bf16 weights, f32 accumulation",
+            "data": "synthetic (seeded random-init weights of the real shapes, N(0,1) latents)",
+            "config": {"workload": c["name"], "latents_per_call": T, "rows_per_layer": F,
+                       "audio_seconds_per_call": audio_s, "realtime_factor": (ms / args.steps / 1e3) / audio_s,
+                       "parallelism": f"replicas x{ws} (no collective)",
+                       "l2": "inputs larger than L2: every call streams all weights (%.0f MB) from HBM" % (nbytes / 1e6)},
+            "roofline": {"bound": "tensor" if tensor_bound else "hbm", "kernel": f"VAE decode call ({launches} kernels)",
+                         "achieved": flops / t_call / 1e12 if tensor_bound else nbytes / t_call / 1e9,
+                         "peak": tf if tensor_bound else hbm, "unit": "TFLOP/s" if tensor_bound else "GB/s",
+                         "frac": (flops / t_call / 1e12 / tf) if tensor_bound else (nbytes / t_call / 1e9 / hbm),
+                         "peak_kind": peak_kind, "algorithmic_flops_per_call": flops,
+                         "algorithmic_bytes_per_call": nbytes, "hbm_frac": nbytes / t_call / 1e9 / hbm, "traffic": None},
+            "e2e": {"value": ws * T * args.steps / e2e_s, "unit": "latents/s", "h2d_bytes_per_step": T * 64 * 2,
+                    "d2h_bytes_per_step": n_out * 4, "api": "ming_cuda_vae_decode (pinned host buffers)"},
+            "gpu_launches": launches * args.steps, "clocks": ck, "cpu_baseline": cpu}
+
+
 def run_loop(args, ws, rank, local):
     """BASELINE configs[4] through the library's loop entry (ming_cuda_loop_*,
     sampleLatents over B concurrent requests): per step, for every row, the
@@ -538,6 +682,8 @@ def run_reference(args, ws, rank, local):
     O.set_threads(len(os.sched_getaffinity(0)))
     cfgid = args.config
     c = CONFIGS[cfgid]
+    if c.get("vae"):
+        return run_reference_vae(args, ws, c, O)
     if c.get("dit") or c.get("loop"):
         return {"impl": "reference", "unavailable": "reference arm implemented for the LM-only configs"}
     B = c["batch"]
@@ -574,6 +720,29 @@ def run_reference(args, ws, rank, local):
             "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": O.threads(), "kind": "port",
                              "sample": f"{n} decode steps x {nb} sequence(s) of the workload (time-bounded at {budget:.0f}s)"},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def run_reference_vae(args, ws, c, O):
+    """The VAE decoder's CPU path restated (the oracle's f32 numpy decode, BLAS
+    on all host threads): one decode of the fragment per step, time-bounded."""
+    T = c["latents"]
+    W, lat = vae_workload(c)
+    for _ in range(min(args.warmup, 1)):
+        O.vae_decode(W, lat, 24, window=64)
+    budget = float(os.environ.get("MING_REF_BUDGET_S", "150"))
+    n, t0 = 0, time.perf_counter()
+    while n < args.steps and (n < 1 or time.perf_counter() - t0 < budget):
+        O.vae_decode(W, lat, 24, window=64)
+        n += 1
+    dt = time.perf_counter() - t0
+    v = n * T / dt
+    return {"metric": "VAE decode latents/s (one 128-latent fragment per call)", "value": v, "unit": "latents/s",
+            "impl": "reference", "n_gpus": ws, "steps": n, "warmup": args.warmup, "ms_per_step": dt / n * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32 (CPU)",
+            "data": "synthetic", "config": {"workload": c["name"], "latents_per_call": T},
+            "cpu_baseline": {"value": v, "unit": "latents/s", "cores": blas_threads(), "kind": "port",
+                             "sample": f"{n} decode(s) of the workload's {T} latents (time-bounded at {budget:.0f}s)"},
+            "e2e": {"value": v, "unit": "latents/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def main():

@@ -158,43 +158,98 @@ __global__ void vae_upsample_kernel(const uint16_t* x, int T, int H, float* out)
 }
 
 // Causal sliding-window attention in f32 (slidingMask: key kp visible from
-// query qp when qp - window < kp <= qp; SDPA with scale 1/8): one warp per
-// (row, query head), a lane per two keys for the scores (window <= 64), then
-// a lane per two dims for P.V.
-__global__ void vae_attention_kernel(const float* q, const float* k, const float* v, float* o, int F, int heads, int kvh,
-                                     int window, float scale) {
+// query qp when qp - window < kp <= qp; SDPA with scale 1/8). A CTA takes
+// VA_RB consecutive query rows and one kv head: it stages the keys and values
+// of the rows' windows (at most window - 1 + VA_RB positions) and the q rows
+// of its (row, query head) pairs in shared memory once, then warp w runs the
+// pairs w, w + 8, ...: a lane per two keys for the scores (window <= 64,
+// checked at set-up), then a lane per two dims for P.V, four keys' loads in
+// flight at a time. Staging once per block instead of reading every (row,
+// head)'s window from global memory cuts the L2 traffic ~30x; the arithmetic
+// of each (row, head), summation order included, is unchanged.
+constexpr int VA_RB = 4;                 // query rows per CTA
+constexpr int VA_WARPS = 8;
+constexpr int VA_KS = HD + 4;            // row stride (floats) of the staged K/V: the float4 reads of
+                                         // 8 lanes on consecutive rows fall on distinct bank groups
+constexpr int VA_MAXK = 64 - 1 + VA_RB;  // positions of a block's windows
+constexpr int VA_MAXG = 8;               // query heads per kv head staged (the context's limit, checked at set-up)
+__global__ void __launch_bounds__(VA_WARPS * 32) vae_attention_kernel(const float* q, const float* k, const float* v,
+                                                                      float* o, int F, int heads, int kvh, int window,
+                                                                      float scale) {
+    __shared__ __align__(16) float sK[VA_MAXK * VA_KS];
+    __shared__ __align__(16) float sV[VA_MAXK * VA_KS];
+    __shared__ __align__(16) float sQ[VA_RB * VA_MAXG * HD];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int row = blockIdx.x, h = blockIdx.y * (blockDim.x >> 5) + warp;
-    if (h >= heads) return;  // warp-uniform
-    const int g = h / (heads / kvh);
-    const int j0 = max(0, row - window + 1), n = row - j0 + 1;  // n <= window <= 64
-    const float* qr = q + ((size_t)row * heads + h) * HD;
-    float s[2];
+    const int r0 = blockIdx.x * VA_RB, g = blockIdx.y, grp = heads / kvh;
+    const int k0 = max(0, r0 - window + 1), nk = min(F, r0 + VA_RB) - k0;  // nk <= VA_MAXK
+    const int nr = min(VA_RB, F - r0), np = nr * grp;                      // rows and (row, head) pairs
+    for (int e = threadIdx.x; e < nk * (HD / 4); e += blockDim.x) {
+        const int j = e / (HD / 4), c4 = e % (HD / 4);
+        const size_t src = ((size_t)(k0 + j) * kvh + g) * HD + 4 * c4;
+        *reinterpret_cast<float4*>(sK + j * VA_KS + 4 * c4) = *reinterpret_cast<const float4*>(k + src);
+        *reinterpret_cast<float4*>(sV + j * VA_KS + 4 * c4) = *reinterpret_cast<const float4*>(v + src);
+    }
+    for (int e = threadIdx.x; e < np * (HD / 4); e += blockDim.x) {
+        const int pr = e / (HD / 4), c4 = e % (HD / 4), row = r0 + pr / grp, h = g * grp + pr % grp;
+        *reinterpret_cast<float4*>(sQ + pr * HD + 4 * c4) =
+            *reinterpret_cast<const float4*>(q + ((size_t)row * heads + h) * HD + 4 * c4);
+    }
+    __syncthreads();
+    for (int pr = warp; pr < np; pr += VA_WARPS) {  // warp-uniform
+        const int row = r0 + pr / grp, h = g * grp + pr % grp;
+        const int j0 = max(0, row - window + 1), n = row - j0 + 1;  // keys j0 .. row, n <= window
+        const float* kb = sK + (j0 - k0) * VA_KS;
+        const float* vb = sV + (j0 - k0) * VA_KS;
+        const float* qs = sQ + pr * HD;
+        float s[2];
 #pragma unroll
-    for (int u = 0; u < 2; u++) {
-        const int j = lane + 32 * u;
-        s[u] = -INFINITY;
-        if (j < n) {
-            const float* kr = k + ((size_t)(j0 + j) * kvh + g) * HD;
-            float acc = 0.f;
-#pragma unroll 8
-            for (int d = 0; d < HD; d++) acc += qr[d] * kr[d];
-            s[u] = acc * scale;
+        for (int u = 0; u < 2; u++) {
+            const int j = lane + 32 * u;
+            s[u] = -INFINITY;
+            if (j < n) {
+                const float* kr = kb + j * VA_KS;
+                float acc = 0.f;
+#pragma unroll 4
+                for (int d4 = 0; d4 < HD / 4; d4++) {
+                    const float4 kk = *reinterpret_cast<const float4*>(kr + 4 * d4);
+                    const float4 qq = *reinterpret_cast<const float4*>(qs + 4 * d4);
+                    acc += qq.x * kk.x;
+                    acc += qq.y * kk.y;
+                    acc += qq.z * kk.z;
+                    acc += qq.w * kk.w;
+                }
+                s[u] = acc * scale;
+            }
         }
+        const float m = warp_max(fmaxf(s[0], s[1]));
+        const float p0 = lane < n ? expf(s[0] - m) : 0.f, p1 = lane + 32 < n ? expf(s[1] - m) : 0.f;
+        const float L = warp_sum(p0 + p1);
+        float2 acc = make_float2(0.f, 0.f);
+        int j = 0;
+        for (; j + 4 <= n; j += 4) {  // n is warp-uniform
+            float pj[4];
+            float2 vv[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                pj[u] = __shfl_sync(0xffffffffu, j + u < 32 ? p0 : p1, (j + u) & 31);
+                vv[u] = *reinterpret_cast<const float2*>(vb + (j + u) * VA_KS + 2 * lane);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                acc.x += pj[u] * vv[u].x;
+                acc.y += pj[u] * vv[u].y;
+            }
+        }
+        for (; j < n; j++) {
+            const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+            const float2 vv = *reinterpret_cast<const float2*>(vb + j * VA_KS + 2 * lane);
+            acc.x += pj * vv.x;
+            acc.y += pj * vv.y;
+        }
+        float* orow = o + ((size_t)row * heads + h) * HD;
+        orow[2 * lane] = acc.x / L;
+        orow[2 * lane + 1] = acc.y / L;
     }
-    const float m = warp_max(fmaxf(s[0], s[1]));
-    const float p0 = lane < n ? expf(s[0] - m) : 0.f, p1 = lane + 32 < n ? expf(s[1] - m) : 0.f;
-    const float L = warp_sum(p0 + p1);
-    float2 acc = make_float2(0.f, 0.f);
-    for (int j = 0; j < n; j++) {  // n is warp-uniform
-        const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
-        const float2 vv = *reinterpret_cast<const float2*>(v + ((size_t)(j0 + j) * kvh + g) * HD + 2 * lane);
-        acc.x += pj * vv.x;
-        acc.y += pj * vv.y;
-    }
-    float* orow = o + ((size_t)row * heads + h) * HD;
-    orow[2 * lane] = acc.x / L;
-    orow[2 * lane + 1] = acc.y / L;
 }
 
 // The ISTFT's spectrum from the head's output p [F][3530]: magnitude
@@ -293,6 +348,8 @@ int vae_finalize(ming_ctx* c) {
     if (f.vae_ff < 64 || f.vae_ff % 64 || f.vae_window < 1 || f.vae_window > 64 || f.vae_max_latents < 1)
         return fail(MING_ERR_INVALID,
                     "bad VAE decoder shape (vae_ff a multiple of 64, vae_window 1..64, vae_max_latents >= 1)");
+    if (f.kv_heads < 1 || f.heads % f.kv_heads || f.heads / f.kv_heads > VA_MAXG)
+        return fail(MING_ERR_INVALID, "VAE attention: heads must be a multiple of kv_heads, at most 8 per kv head");
     const int H = f.hidden, QD = f.heads * HD, KD = f.kv_heads * HD, FF = f.vae_ff;
     const std::string D = "audio.decoder";
     int rc, od = 0;
@@ -408,8 +465,8 @@ extern "C" int ming_cuda_vae_decode(ming_ctx* c, const uint16_t* latents, int T,
     for (auto& L : c->vae) {
         run_linear(c, L.qkv.w, ProRmsSplitF32{c->v_x, L.ln1, H, H, f.rms_eps, 0, nullptr},
                    EpiQKVf32{L.qkv.w.bias, c->v_q, c->v_k, c->v_v, f.heads, f.kv_heads, log2_theta}, F, s);
-        vae_attention_kernel<<<dim3(F, (f.heads + 3) / 4), 128, 0, s>>>(c->v_q, c->v_k, c->v_v, c->v_att, F, f.heads,
-                                                                        f.kv_heads, f.vae_window, 0.125f);
+        vae_attention_kernel<<<dim3((F + VA_RB - 1) / VA_RB, f.kv_heads), VA_WARPS * 32, 0, s>>>(
+            c->v_q, c->v_k, c->v_v, c->v_att, F, f.heads, f.kv_heads, f.vae_window, 0.125f);
         run_linear(c, L.o.w, ProSplitF32{c->v_att, QD, QD, 2, 2, 0}, EpiResidualF32{c->v_x, c->v_x, H}, F, s);
         run_linear(c, L.gu.w, ProRmsSplitF32{c->v_x, L.ln2, H, H, f.rms_eps, 0, nullptr}, EpiSwiGLUf32{c->v_h, f.vae_ff}, F,
                    s);

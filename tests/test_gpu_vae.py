@@ -53,3 +53,29 @@ def test_vae_decode_rejects_too_many_latents(vae):
     W, ctx = vae
     with pytest.raises(M.MingError, match="vae_max_latents"):
         ctx.vae_decode(np.zeros((65, 64), np.uint16))
+
+
+def test_vae_decode_full_size_fragment(cuda_ok):
+    """The bench's VAE workload at the real shapes: 24 layers, ff 4864, one
+    fragment of 128 latents (512 rows through every linear on the tcgen05
+    path), against the oracle under the same gate, and bit-identical on a
+    second call."""
+    T = 128
+    W = synth.vae_weights(seed=2)
+    lat = synth.normal_bf16(2, "bench.vae.latents", (T, 64))
+    ref = O.vae_decode(W, lat, 24, window=64)
+    cfg = M.default_cfg(layers=0, dit_mode=M.DIT_NONE, agg_blocks=0, vae_layers=24, vae_ff=4864, vae_window=64,
+                        vae_max_latents=T)
+    ctx = M.Context(cfg, weights=W)
+    try:
+        got = ctx.vae_decode(lat)
+        again = ctx.vae_decode(lat)
+    finally:
+        ctx.close()
+    scale = np.abs(ref).max()
+    d = np.abs(got.astype(np.float64) - ref).max()
+    cos = float((got.astype(np.float64) * ref).sum() / (np.linalg.norm(got) * np.linalg.norm(ref)))
+    print(f"vae full size T={T}: max-abs {d:.3g} ({d / scale:.3g} of the largest sample), cosine {cos:.9f}")
+    assert got.shape == ref.shape == (T * 4 * 882,)
+    assert d <= 1e-3 * scale and cos > 0.99999, (d / scale, cos)
+    assert np.array_equal(got, again)
