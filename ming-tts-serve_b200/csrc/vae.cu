@@ -164,9 +164,10 @@ __global__ void vae_upsample_kernel(const uint16_t* x, int T, int H, float* out)
 // of its (row, query head) pairs in shared memory once, then warp w runs the
 // pairs w, w + 8, ...: a lane per two keys for the scores (window <= 64,
 // checked at set-up), then a lane per two dims for P.V, four keys' loads in
-// flight at a time. Staging once per block instead of reading every (row,
-// head)'s window from global memory cuts the L2 traffic ~30x; the arithmetic
-// of each (row, head), summation order included, is unchanged.
+// flight at a time and their probabilities read from shared memory at once.
+// Staging once per block instead of reading every (row, head)'s window from
+// global memory cuts the L2 traffic ~30x; the arithmetic of each (row, head),
+// summation order included, is unchanged.
 constexpr int VA_RB = 4;                 // query rows per CTA
 constexpr int VA_WARPS = 8;
 constexpr int VA_KS = HD + 4;            // row stride (floats) of the staged K/V: the float4 reads of
@@ -179,6 +180,7 @@ __global__ void __launch_bounds__(VA_WARPS * 32) vae_attention_kernel(const floa
     __shared__ __align__(16) float sK[VA_MAXK * VA_KS];
     __shared__ __align__(16) float sV[VA_MAXK * VA_KS];
     __shared__ __align__(16) float sQ[VA_RB * VA_MAXG * HD];
+    __shared__ __align__(16) float sP[VA_WARPS][64];  // each warp's probabilities of its current pair
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int r0 = blockIdx.x * VA_RB, g = blockIdx.y, grp = heads / kvh;
     const int k0 = max(0, r0 - window + 1), nk = min(F, r0 + VA_RB) - k0;  // nk <= VA_MAXK
@@ -201,39 +203,48 @@ __global__ void __launch_bounds__(VA_WARPS * 32) vae_attention_kernel(const floa
         const float* kb = sK + (j0 - k0) * VA_KS;
         const float* vb = sV + (j0 - k0) * VA_KS;
         const float* qs = sQ + pr * HD;
-        float s[2];
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int j = lane + 32 * u;
-            s[u] = -INFINITY;
-            if (j < n) {
-                const float* kr = kb + j * VA_KS;
-                float acc = 0.f;
+        // the lane's keys j = lane and lane + 32 over the dims in order, one q
+        // load per step for both
+        const bool u0 = lane < n, u1 = lane + 32 < n;
+        const float* kr0 = kb + lane * VA_KS;
+        const float* kr1 = kb + (lane + 32) * VA_KS;
+        float a0 = 0.f, a1 = 0.f;
 #pragma unroll 4
-                for (int d4 = 0; d4 < HD / 4; d4++) {
-                    const float4 kk = *reinterpret_cast<const float4*>(kr + 4 * d4);
-                    const float4 qq = *reinterpret_cast<const float4*>(qs + 4 * d4);
-                    acc += qq.x * kk.x;
-                    acc += qq.y * kk.y;
-                    acc += qq.z * kk.z;
-                    acc += qq.w * kk.w;
-                }
-                s[u] = acc * scale;
+        for (int d4 = 0; d4 < HD / 4; d4++) {
+            const float4 qq = *reinterpret_cast<const float4*>(qs + 4 * d4);
+            if (u0) {
+                const float4 kk = *reinterpret_cast<const float4*>(kr0 + 4 * d4);
+                a0 += qq.x * kk.x;
+                a0 += qq.y * kk.y;
+                a0 += qq.z * kk.z;
+                a0 += qq.w * kk.w;
+            }
+            if (u1) {
+                const float4 kk = *reinterpret_cast<const float4*>(kr1 + 4 * d4);
+                a1 += qq.x * kk.x;
+                a1 += qq.y * kk.y;
+                a1 += qq.z * kk.z;
+                a1 += qq.w * kk.w;
             }
         }
-        const float m = warp_max(fmaxf(s[0], s[1]));
-        const float p0 = lane < n ? expf(s[0] - m) : 0.f, p1 = lane + 32 < n ? expf(s[1] - m) : 0.f;
+        const float s0 = u0 ? a0 * scale : -INFINITY, s1 = u1 ? a1 * scale : -INFINITY;
+        const float m = warp_max(fmaxf(s0, s1));
+        const float p0 = u0 ? expf(s0 - m) : 0.f, p1 = u1 ? expf(s1 - m) : 0.f;
         const float L = warp_sum(p0 + p1);
+        // P.V over the keys in order, the probabilities read four at a time
+        // from the warp's row of sP
+        float* pw = sP[warp];
+        pw[lane] = p0;
+        pw[lane + 32] = p1;
+        __syncwarp();
         float2 acc = make_float2(0.f, 0.f);
         int j = 0;
         for (; j + 4 <= n; j += 4) {  // n is warp-uniform
-            float pj[4];
+            const float4 p4 = *reinterpret_cast<const float4*>(pw + j);
+            const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
             float2 vv[4];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                pj[u] = __shfl_sync(0xffffffffu, j + u < 32 ? p0 : p1, (j + u) & 31);
-                vv[u] = *reinterpret_cast<const float2*>(vb + (j + u) * VA_KS + 2 * lane);
-            }
+            for (int u = 0; u < 4; u++) vv[u] = *reinterpret_cast<const float2*>(vb + (j + u) * VA_KS + 2 * lane);
 #pragma unroll
             for (int u = 0; u < 4; u++) {
                 acc.x += pj[u] * vv[u].x;
@@ -241,11 +252,12 @@ __global__ void __launch_bounds__(VA_WARPS * 32) vae_attention_kernel(const floa
             }
         }
         for (; j < n; j++) {
-            const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+            const float pj = pw[j];
             const float2 vv = *reinterpret_cast<const float2*>(vb + j * VA_KS + 2 * lane);
             acc.x += pj * vv.x;
             acc.y += pj * vv.y;
         }
+        __syncwarp();  // every lane read pw before the next pair overwrites it
         float* orow = o + ((size_t)row * heads + h) * HD;
         orow[2 * lane] = acc.x / L;
         orow[2 * lane + 1] = acc.y / L;
